@@ -1,0 +1,373 @@
+#!/usr/bin/env python3
+"""Benchmark of the routed-expert hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rabbit|reference]
+
+Workload (the MoE-layer decode configuration): Mixtral-shaped MoE blocks,
+hidden 4096, expert FFN 14336 SwiGLU, 8 experts top-2, group-32 int4 experts,
+fp32 router N(0, 0.02), batch 1. A step is one decode token through the MoE
+blocks of 32 distinct layers (28.2 GB of resident experts, far larger than the
+126 MB L2), h chained layer to layer: 32 launches of the fused decode kernel
+(rmsnorm + router + top-2 + gate/up + SiLU + down + combine).
+
+metric: algorithmic bytes streamed per second (GB/s): per token-layer the
+router (E*H*4 B) plus, for each selected expert, 2*B(I*H) + B(H*I) with
+B(n) = 4 + 4*ceil(n/32) + n/2 -- 220,332,056 B. tokens/s is reported beside it.
+
+N > 1: one process per GPU (torchrun); each rank decodes its own token stream
+through its own resident copy (data-parallel decode replicas, no collective
+on the data path), so per-GPU work is fixed: "scaling": "weak".
+
+--impl reference times the reference's own C (oracle/_ref, built from the
+reference sources) on the host cores, on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, I, E, TOPK = 4096, 14336, 8, 2
+LAYERS = 32
+SEED = 1
+METRIC = "MoE decode int4 expert GB/s (Mixtral-shaped layer, batch 1)"
+WORKLOAD = "Mixtral-shaped MoE layer decode x 32 distinct layers per step"
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM traffic of the decode kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("k_moe_decode_g32_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+# ------------------------------------------------------------ clocks -------
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons for one GPU while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+               "-lms", "50"]
+        if self.gpu_id:
+            cmd += ["-i", self.gpu_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU side -----
+def host_layer(seed: int = SEED):
+    """One Mixtral-shaped layer on the host (8 int4 experts, router, norm)."""
+    from rabbit_b200 import synth
+
+    return synth.moe_layer(seed, H, E, I, 0)
+
+
+def layer_bytes() -> int:
+    from rabbit_b200 import synth
+
+    return 4 * E * H + TOPK * (3 * synth.int4_nbytes(H * I))
+
+
+def time_cpu_moe(checker, layer, tokens: int, threads: int) -> tuple[float, int]:
+    """Run `tokens` moe_step calls per thread; returns (seconds, token-layers)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    recs, size, router, rms = layer
+    kw = dict(H=H, E=E, top_k=TOPK, inter=I, n_shared=0, quant=4, n_records=E,
+              expert_size=size, records=recs, rms_ffn=rms, w_router=router)
+    rng = np.random.default_rng(99)
+    hs = [rng.standard_normal(H).astype(np.float32) for _ in range(threads)]
+
+    def work(t):
+        h = hs[t]
+        for _ in range(tokens):
+            out = checker.moe_step(h, **kw)
+            h = out[0] if isinstance(out, tuple) else out
+        return h
+
+    t0 = time.perf_counter()
+    if threads == 1:
+        work(0)
+    else:
+        with ThreadPoolExecutor(threads) as ex:  # ctypes drops the GIL during the C call
+            list(ex.map(work, range(threads)))
+    return time.perf_counter() - t0, tokens * threads
+
+
+def cpu_checker():
+    """(checker, kind): the reference's own C when built, else the oracle port."""
+    from oracle.oracle import REF_SO, Oracle, Reference
+
+    if REF_SO.exists():
+        return Reference(), "reference"
+    return Oracle(), "port"
+
+
+def cpu_baseline_single(layer) -> dict:
+    chk, kind = cpu_checker()
+    secs, n = time_cpu_moe(chk, layer, tokens=8, threads=1)
+    gbs = layer_bytes() * n / secs / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{n} Mixtral-shaped token-layers (moe_step, 1 thread), {secs:.1f} s"}
+
+
+# ------------------------------------------------------------ arms ---------
+def run_reference(args) -> None:
+    """--impl reference: the reference's C on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    chk, kind = cpu_checker()
+    threads = os.cpu_count() or 1
+    layer = host_layer()
+    # one step = each thread runs one full moe_step token-layer (~1 s on one core)
+    for _ in range(args.warmup):
+        time_cpu_moe(chk, layer, 1, threads)
+    steps = args.steps
+    budget_steps = max(1, int(150 / 1.5))  # keep the whole run within a few minutes
+    timed = min(steps, budget_steps)
+    secs, n = time_cpu_moe(chk, layer, timed, threads)
+    gbs = layer_bytes() * n / secs / 1e9
+    ms = secs * 1000 / timed
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": timed, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4 weights, f32 math", "data": "synthetic",
+        "config": {"workload": "Mixtral-shaped MoE layer decode (reference C moe_step)",
+                   "hidden": H, "inter": I, "experts": E, "top_k": TOPK,
+                   "threads": threads},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{n} token-layers ({threads} threads x {timed} steps)"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "tokens_per_s": round(n / secs / LAYERS, 6),
+    }
+    if timed != steps:
+        line["note"] = f"{timed} of {steps} requested steps timed to bound the CPU run"
+    print(json.dumps(line), flush=True)
+
+
+def run_rabbit(args) -> None:
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from rabbit_b200 import capi, synth
+
+    capi.check(capi.lib().rabbit_cuda_set_device(local))
+    rng = np.random.default_rng(SEED + rank)
+    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(LAYERS)]
+    norms = [np.ones(H, np.float32) for _ in range(LAYERS)]
+    size = synth.expert_record_size(H, I)
+    pool = capi.MoePool(records=None, expert_size=size, n_layers=LAYERS, hidden=H, n_experts=E,
+                        top_k=TOPK, inter=I, quant=4, rms_ffn=norms, w_router=routers,
+                        device=local)
+    pool.fill_synthetic(SEED * 1000 + rank)
+    per_layer = pool.decode_bytes
+    step_bytes = per_layer * LAYERS
+
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+    h0 = torch.from_numpy(rng.standard_normal(H).astype(np.float32)).cuda()
+    bufs = [h0.clone(), torch.empty_like(h0)]
+    ids = torch.zeros(8, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(8, dtype=torch.float32, device="cuda")
+
+    def step():
+        for layer in range(LAYERS):
+            a, b = bufs[layer & 1], bufs[(layer + 1) & 1]
+            pool.decode_dev(layer, a.data_ptr(), b.data_ptr(), ids.data_ptr(), wts.data_ptr(), s)
+
+    for _ in range(args.warmup):
+        step()
+    pool.check(s)
+    torch.cuda.synchronize()
+
+    props = torch.cuda.get_device_properties(local)
+    clocks = ClockSampler("GPU-" + str(props.uuid))
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    pool.check(s)
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    secs = ms / 1000.0
+    value = world * step_bytes * args.steps / secs / 1e9
+    launches = args.steps * LAYERS
+    kernel_s = secs / launches
+    achieved = per_layer / kernel_s / 1e9
+    peak, peak_kind = measured_peak()
+
+    # end to end through the host-buffer C ABI (H2D of h, D2H of h + routing, per layer)
+    h_host = rng.standard_normal(H).astype(np.float32)
+    e2e_steps = max(1, min(args.steps, 50))
+    for _ in range(2):
+        for layer in range(LAYERS):
+            h_host = pool.decode(layer, h_host)[0]
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for layer in range(LAYERS):
+            h_host = pool.decode(layer, h_host)[0]
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * step_bytes * e2e_steps / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_single(host_layer())
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4 weights, f32 math", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "hidden": H, "inter": I, "experts": E,
+                       "top_k": TOPK, "layers_per_step": LAYERS, "batch": 1,
+                       "expert_bytes_resident_gb": round(pool.stats()["pool_bytes"] / 1e9, 2),
+                       "l2": "inputs larger than L2 (32 distinct layers, 28 GB of experts)",
+                       "parallelism": f"dp{world} decode replicas" if world > 1 else "single"},
+            "tokens_per_s": round(world * args.steps / secs, 2),
+            "us_per_token_layer": round(1e6 * secs / launches, 3),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profile_traffic(), "peak_kind": peak_kind,
+                         "kernel": "k_moe_decode_g32",
+                         "bytes_per_launch": per_layer},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": LAYERS * H * 4,
+                    "d2h_bytes_per_step": LAYERS * (H * 4 + TOPK * 8),
+                    "steps": e2e_steps, "api": "rabbit_cuda_moe_decode (host buffers)"},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    pool.free()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["rabbit", "reference"], default="rabbit")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_rabbit(args)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,174 @@
+/*
+ * rabbit_cuda.h -- C ABI of the B200 (sm_100a) routed-expert hot path.
+ *
+ * Plain C: pointers, sizes and status codes only. A CUDA stream is passed as
+ * `void *` (a cudaStream_t / CUstream; NULL = the library's own stream).
+ * Every entry point returns a rabbit_cuda_status; on failure
+ * rabbit_cuda_last_error() holds a one-line explanation for the calling
+ * thread. Nothing here calls exit(); nothing falls back to the CPU.
+ *
+ * Reference interfaces replaced (Stanley03-arch/Rabbit v0.4.28):
+ *   rabbit_gemv_int4_grouped        src/quant.c:152-188, src/rabbit.h:178-179
+ *   rabbit_dequant_int4_grouped     src/quant.c:123-142, src/rabbit.h:177
+ *   moe_step / expert_swiglu /
+ *     select_top_k (static)         src/forward_v2.c:248-402
+ *   expert cache + mmap fetch       src/memory.c:94-253, src/moe.c:73-117
+ *   rabbit_cache_stats_ex           src/rabbit.h:132-134
+ */
+#ifndef RABBIT_CUDA_H
+#define RABBIT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported even when the library is built with -fvisibility=hidden. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define RABBIT_CUDA_ABI_VERSION 1
+
+/* The first six values are rabbit_status (src/rabbit.h:16-23). */
+typedef enum {
+    RABBIT_CUDA_OK = 0,
+    RABBIT_CUDA_ERR_IO = 1,
+    RABBIT_CUDA_ERR_MEM = 2,
+    RABBIT_CUDA_ERR_FORMAT = 3,
+    RABBIT_CUDA_ERR_UNSUPPORTED = 4,
+    RABBIT_CUDA_ERR_ARGS = 5,
+    RABBIT_CUDA_ERR_DEVICE = 6,  /* a CUDA call failed (message has the CUDA error) */
+    RABBIT_CUDA_ERR_TIMEOUT = 7  /* a bounded device-side wait gave up */
+} rabbit_cuda_status;
+
+/* ------------------------------------------------------------- library -- */
+
+/* "rabbit-b200 <version>" */
+const char *rabbit_cuda_version(void);
+/* Text of the last failure on this thread ("" if none). */
+const char *rabbit_cuda_last_error(void);
+/* Number of visible CUDA devices (0 without a GPU; never fails on a host). */
+int rabbit_cuda_device_count(int *count);
+/* Select the device later calls on this thread use (default 0). */
+int rabbit_cuda_set_device(int device);
+/* Device-side wait limit in milliseconds for mbarrier / grid-barrier spins
+ * (default 2000). A wait that runs out sets RABBIT_CUDA_ERR_TIMEOUT. */
+int rabbit_cuda_set_wait_limit_ms(int ms);
+
+/* --------------------------------------------- stateless quant drop-ins -- */
+
+/* Drop-in for rabbit_gemv_int4_grouped (src/quant.c:152-188): y = W x with W a
+ * group-scaled int4 blob (u32 group_size | f32 scales | packed nibbles) over
+ * the flat row-major index, any shape. HOST buffers; W is copied to the device
+ * each call. An invalid group_size (0 or > 4096) writes zeros, as the
+ * reference does. Returns ARGS for NULL pointers or non-positive sizes (the
+ * reference returns silently there). */
+int rabbit_cuda_gemv_int4_grouped(const uint8_t *W, const float *x, float *y,
+                                  int out_dim, int in_dim);
+
+/* Device-buffer dequant (src/quant.c:123-142): dst[i] = (float)q_i * scale.
+ * d_blob may have any alignment. Returns FORMAT for an invalid group size. */
+int rabbit_cuda_dequant_int4_grouped_dev(const uint8_t *d_blob, float *d_dst, int n,
+                                         void *stream);
+
+/* Device-buffer GEMV over a raw blob already in device memory (any shape,
+ * any alignment), same arithmetic contract as rabbit_gemv_int4_grouped. */
+int rabbit_cuda_gemv_int4_grouped_dev(const uint8_t *d_blob, const float *d_x, float *d_y,
+                                      int out_dim, int in_dim, void *stream);
+
+/* ------------------------------------------------- resident int4 matrix -- */
+
+/* One group-32 int4 matrix kept in HBM in the GEMV layout (16-byte aligned
+ * nibble plane [rows][in/2] and scale plane [rows][in/32]). */
+typedef struct rabbit_cuda_matrix rabbit_cuda_matrix;
+
+/* Upload a host blob (.rabbit matrix format). Shapes with in_dim % 32 != 0 or
+ * group_size != 32 are kept verbatim and served by the flat-index kernel. */
+int rabbit_cuda_matrix_upload(const uint8_t *blob, int out_dim, int in_dim,
+                              rabbit_cuda_matrix **out);
+int rabbit_cuda_matrix_free(rabbit_cuda_matrix *m);
+/* y = W x with device x / y (16-byte aligned), on `stream`. */
+int rabbit_cuda_matrix_gemv_dev(const rabbit_cuda_matrix *m, const float *d_x, float *d_y,
+                                void *stream);
+/* Same with HOST x / y: copies in, GEMV, copies out, synchronises. */
+int rabbit_cuda_matrix_gemv(const rabbit_cuda_matrix *m, const float *x, float *y);
+/* Algorithmic bytes one GEMV streams: the blob (4 + 4*ceil(n/32) + n/2)
+ * plus x and y in fp32. */
+uint64_t rabbit_cuda_matrix_bytes(const rabbit_cuda_matrix *m);
+
+/* --------------------------------------------- HBM-resident expert pool -- */
+
+/* Model description for the MoE block. Mirrors the fields moe_step reads from
+ * RabbitModel / RefV2Weights (src/rabbit.h:28-97, src/forward_v2.c:106-169,
+ * src/model.c:152-189). All pointers are HOST pointers and are read only
+ * during rabbit_cuda_moe_create / rabbit_cuda_moe_upload. */
+typedef struct {
+    int n_layers;
+    int hidden;             /* H */
+    int n_experts;          /* routed experts per layer, E (router width) */
+    int experts_per_token;  /* header top-k; <= 0 means 2 (forward_v2.c:113) */
+    int inter;              /* expert FFN width I */
+    int n_shared;           /* always-on shared experts S (reserved[12..15]); 0..64 */
+    int expert_quant;       /* 0 f32, 4 group-int4, 8 int8 (forward_v2.c:297-354) */
+    uint64_t expert_size;   /* bytes per record */
+    int n_records;          /* records in expert_map */
+    int experts_per_layer;  /* records per layer (E or E+S) */
+    int experts_shared;     /* 1: one table for every layer (memory.c:230-238) */
+    const void *expert_map; /* host pointer to record 0 (e.g. the mmap'd file);
+                               NULL: records come from rabbit_cuda_moe_fill_synthetic */
+    const float *const *rms_ffn;  /* [n_layers] -> H floats */
+    const float *const *w_router; /* [n_layers] -> E*H floats */
+} rabbit_cuda_moe_desc;
+
+typedef struct rabbit_cuda_moe rabbit_cuda_moe;
+
+/* Create the pool on `device`: allocates HBM for every record (the pool is the
+ * whole expert table, resident), plus router/norm weights and scratch. */
+int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *desc, int device,
+                           rabbit_cuda_moe **out);
+/* Stage records of layers [layer_begin, layer_end) host -> pinned -> HBM on the
+ * pool's side stream (asynchronous; returns once queued). */
+int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end);
+/* Wait until every queued upload has landed. */
+int rabbit_cuda_moe_sync(rabbit_cuda_moe *p);
+/* Fill every record of a group-32 int4 pool on the device with seeded
+ * synthetic weights (nibbles uniform on [-8, 7], one scale |N(0, sigma)|/7 per
+ * 32 inputs) and mark them resident. For benchmarks and tests of models too
+ * large to stage from host memory; desc.expert_map may be NULL then.
+ * UNSUPPORTED for pools that are not in the group-32 layout. */
+int rabbit_cuda_moe_fill_synthetic(rabbit_cuda_moe *p, uint64_t seed, float scale_sigma);
+int rabbit_cuda_moe_free(rabbit_cuda_moe *p);
+
+/* One token through one layer's MoE block (moe_step, forward_v2.c:362-402):
+ * xn = rmsnorm(h); scores = W_router xn; top-k (strict '>', lower id wins
+ * ties) + softmax; h_out = h + sum_j w_j * SwiGLU_j(xn) + sum_shared SwiGLU(xn).
+ * HOST buffers: h_in/h_out [H] (may alias), ids/weights [k] (may be NULL).
+ * Returns the k used through *k_out (may be NULL). */
+int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
+                           int *ids, float *weights, int *k_out);
+/* Same on DEVICE buffers, asynchronous on `stream` (16-byte aligned h). */
+int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                               float *d_h_out, int *d_ids, float *d_weights, void *stream);
+/* Check the device error word after work on `stream` finished (TIMEOUT if a
+ * bounded wait gave up). Synchronises `stream`. */
+int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);
+
+/* Counters in the spirit of rabbit_cache_stats_ex (src/memory.c:74-92):
+ * decode calls served from HBM, records uploaded, bytes moved host->device,
+ * records resident, pool bytes. */
+int rabbit_cuda_moe_stats(const rabbit_cuda_moe *p, uint64_t *hbm_hits, uint64_t *uploads,
+                          uint64_t *h2d_bytes, int *resident_records, uint64_t *pool_bytes);
+/* Algorithmic bytes of one decode (router + selected + shared experts). */
+uint64_t rabbit_cuda_moe_decode_bytes(const rabbit_cuda_moe *p);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RABBIT_CUDA_H */

@@ -1,0 +1,228 @@
+"""ctypes binding of include/rabbit_cuda.h (librabbit_cuda.so, built in-tree).
+
+There is no CPU fallback: `lib()` raises if the shared library is missing or
+cannot be loaded, and every wrapper raises RabbitCudaError on a non-zero
+status, carrying rabbit_cuda_last_error().
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+SO = Path(__file__).resolve().parent / "librabbit_cuda.so"
+
+OK, ERR_IO, ERR_MEM, ERR_FORMAT, ERR_UNSUPPORTED, ERR_ARGS, ERR_DEVICE, ERR_TIMEOUT = range(8)
+STATUS_NAMES = ["OK", "IO", "MEM", "FORMAT", "UNSUPPORTED", "ARGS", "DEVICE", "TIMEOUT"]
+
+
+class RabbitCudaError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        name = STATUS_NAMES[status] if 0 <= status < len(STATUS_NAMES) else str(status)
+        super().__init__(f"rabbit_cuda status {name}: {msg}")
+        self.status = status
+
+
+class MoeDesc(C.Structure):
+    """rabbit_cuda_moe_desc"""
+    _fields_ = [("n_layers", C.c_int), ("hidden", C.c_int), ("n_experts", C.c_int),
+                ("experts_per_token", C.c_int), ("inter", C.c_int), ("n_shared", C.c_int),
+                ("expert_quant", C.c_int), ("expert_size", C.c_uint64),
+                ("n_records", C.c_int), ("experts_per_layer", C.c_int),
+                ("experts_shared", C.c_int), ("expert_map", C.c_void_p),
+                ("rms_ffn", C.POINTER(C.c_void_p)), ("w_router", C.POINTER(C.c_void_p))]
+
+
+_P = C.c_void_p
+_I = C.c_int
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "rabbit_cuda_version": (C.c_char_p, []),
+    "rabbit_cuda_last_error": (C.c_char_p, []),
+    "rabbit_cuda_device_count": (_I, [C.POINTER(_I)]),
+    "rabbit_cuda_set_device": (_I, [_I]),
+    "rabbit_cuda_set_wait_limit_ms": (_I, [_I]),
+    "rabbit_cuda_gemv_int4_grouped": (_I, [_P, _P, _P, _I, _I]),
+    "rabbit_cuda_dequant_int4_grouped_dev": (_I, [_P, _P, _I, _P]),
+    "rabbit_cuda_gemv_int4_grouped_dev": (_I, [_P, _P, _P, _I, _I, _P]),
+    "rabbit_cuda_matrix_upload": (_I, [_P, _I, _I, C.POINTER(_P)]),
+    "rabbit_cuda_matrix_free": (_I, [_P]),
+    "rabbit_cuda_matrix_gemv_dev": (_I, [_P, _P, _P, _P]),
+    "rabbit_cuda_matrix_gemv": (_I, [_P, _P, _P]),
+    "rabbit_cuda_matrix_bytes": (C.c_uint64, [_P]),
+    "rabbit_cuda_moe_create": (_I, [C.POINTER(MoeDesc), _I, C.POINTER(_P)]),
+    "rabbit_cuda_moe_upload": (_I, [_P, _I, _I]),
+    "rabbit_cuda_moe_sync": (_I, [_P]),
+    "rabbit_cuda_moe_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
+    "rabbit_cuda_moe_free": (_I, [_P]),
+    "rabbit_cuda_moe_decode": (_I, [_P, _I, _P, _P, _P, _P, C.POINTER(_I)]),
+    "rabbit_cuda_moe_decode_dev": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "rabbit_cuda_moe_check": (_I, [_P, _P]),
+    "rabbit_cuda_moe_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                   C.POINTER(C.c_uint64), C.POINTER(_I),
+                                   C.POINTER(C.c_uint64)]),
+    "rabbit_cuda_moe_decode_bytes": (C.c_uint64, [_P]),
+}
+
+_LIB: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    """Load librabbit_cuda.so once. Raises if it is missing (no fallback)."""
+    global _LIB
+    if _LIB is None:
+        if not SO.exists():
+            raise RuntimeError(f"{SO} is not built; run `python -m rabbit_b200.build`")
+        so = C.CDLL(str(SO))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(so, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = so
+    return _LIB
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise RabbitCudaError(status, lib().rabbit_cuda_last_error().decode(errors="replace"))
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    check(lib().rabbit_cuda_device_count(C.byref(n)))
+    return n.value
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def gemv_int4_grouped(blob: np.ndarray, x: np.ndarray, out_dim: int, in_dim: int) -> np.ndarray:
+    """Host-buffer drop-in for rabbit_gemv_int4_grouped."""
+    blob = np.ascontiguousarray(blob, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.full(max(out_dim, 1), np.nan, np.float32)
+    check(lib().rabbit_cuda_gemv_int4_grouped(_ptr(blob), _ptr(x), _ptr(y), out_dim, in_dim))
+    return y[:out_dim]
+
+
+class Matrix:
+    """A resident group-32 int4 matrix (rabbit_cuda_matrix)."""
+
+    def __init__(self, blob: np.ndarray, out_dim: int, in_dim: int):
+        blob = np.ascontiguousarray(blob, np.uint8)
+        h = C.c_void_p()
+        check(lib().rabbit_cuda_matrix_upload(_ptr(blob), out_dim, in_dim, C.byref(h)))
+        self.handle = h
+        self.out_dim, self.in_dim = out_dim, in_dim
+
+    def gemv(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros(self.out_dim, np.float32)
+        check(lib().rabbit_cuda_matrix_gemv(self.handle, _ptr(x), _ptr(y)))
+        return y
+
+    def gemv_dev(self, d_x: int, d_y: int, stream: int = 0) -> None:
+        check(lib().rabbit_cuda_matrix_gemv_dev(self.handle, d_x, d_y, stream or None))
+
+    @property
+    def nbytes(self) -> int:
+        return int(lib().rabbit_cuda_matrix_bytes(self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().rabbit_cuda_matrix_free(self.handle))
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class MoePool:
+    """HBM-resident expert pool + MoE decode (rabbit_cuda_moe)."""
+
+    def __init__(self, *, records: np.ndarray, expert_size: int, n_layers: int, hidden: int,
+                 n_experts: int, top_k: int, inter: int, n_shared: int = 0, quant: int = 4,
+                 experts_per_layer: int | None = None, experts_shared: bool = False,
+                 rms_ffn, w_router, device: int = 0, upload: bool = True):
+        if records is None:  # device-filled pool (fill_synthetic)
+            self._records = None
+            n_records = n_layers * (experts_per_layer or (n_experts + n_shared))
+            upload = False
+        else:
+            self._records = np.ascontiguousarray(records, np.uint8)
+            n_records = self._records.size // expert_size
+        self._rms = [np.ascontiguousarray(r, np.float32) for r in rms_ffn]
+        self._router = [np.ascontiguousarray(r, np.float32) for r in w_router]
+        rms_arr = (C.c_void_p * n_layers)(*[r.ctypes.data for r in self._rms])
+        rt_arr = (C.c_void_p * n_layers)(*[r.ctypes.data for r in self._router])
+        self._keep = (rms_arr, rt_arr)
+        d = MoeDesc(n_layers, hidden, n_experts, top_k, inter, n_shared, quant, expert_size,
+                    n_records, experts_per_layer or (n_experts + n_shared),
+                    1 if experts_shared else 0,
+                    None if self._records is None else self._records.ctypes.data,
+                    C.cast(rms_arr, C.POINTER(C.c_void_p)), C.cast(rt_arr, C.POINTER(C.c_void_p)))
+        h = C.c_void_p()
+        check(lib().rabbit_cuda_moe_create(C.byref(d), device, C.byref(h)))
+        self.handle = h
+        self.hidden, self.n_layers = hidden, n_layers
+        self.k = min(top_k if top_k > 0 else 2, n_experts, 8)
+        if upload:
+            self.upload(0, n_layers)
+            self.sync()
+
+    def upload(self, lb: int, le: int) -> None:
+        check(lib().rabbit_cuda_moe_upload(self.handle, lb, le))
+
+    def sync(self) -> None:
+        check(lib().rabbit_cuda_moe_sync(self.handle))
+
+    def fill_synthetic(self, seed: int, sigma: float = 0.02) -> None:
+        check(lib().rabbit_cuda_moe_fill_synthetic(self.handle, seed, sigma))
+
+    def decode(self, layer: int, h: np.ndarray):
+        """Host buffers. Returns (h_out, ids[k], weights[k])."""
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.zeros_like(h)
+        ids = np.zeros(8, np.int32)
+        w = np.zeros(8, np.float32)
+        k = C.c_int(0)
+        check(lib().rabbit_cuda_moe_decode(self.handle, layer, _ptr(h), _ptr(out), _ptr(ids),
+                                           _ptr(w), C.byref(k)))
+        return out, ids[:k.value].copy(), w[:k.value].copy()
+
+    def decode_dev(self, layer: int, d_h_in: int, d_h_out: int, d_ids: int = 0,
+                   d_w: int = 0, stream: int = 0) -> None:
+        check(lib().rabbit_cuda_moe_decode_dev(self.handle, layer, d_h_in, d_h_out,
+                                               d_ids or None, d_w or None, stream or None))
+
+    def check(self, stream: int = 0) -> None:
+        check(lib().rabbit_cuda_moe_check(self.handle, stream or None))
+
+    def stats(self) -> dict:
+        a, b, c, e = C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+        r = C.c_int()
+        check(lib().rabbit_cuda_moe_stats(self.handle, C.byref(a), C.byref(b), C.byref(c),
+                                          C.byref(r), C.byref(e)))
+        return {"hbm_hits": a.value, "uploads": b.value, "h2d_bytes": c.value,
+                "resident_records": r.value, "pool_bytes": e.value}
+
+    @property
+    def decode_bytes(self) -> int:
+        return int(lib().rabbit_cuda_moe_decode_bytes(self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().rabbit_cuda_moe_free(self.handle))
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

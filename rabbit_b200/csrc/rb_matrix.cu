@@ -1,0 +1,265 @@
+// rb_matrix.cu -- C ABI: stateless quant drop-ins and resident int4 matrices.
+#include <string.h>
+
+#include "rb_gemv.cuh"
+#include "rb_runtime.h"
+
+struct rabbit_cuda_matrix {
+    int device;
+    int rows, in_dim, rows_pad;
+    uint32_t group_size;
+    bool fast;             // plane layout + streaming kernel
+    uint8_t *nib;          // fast: [rows_pad][in/2]
+    float *sc;             // fast: [rows_pad][in/32]
+    uint8_t *raw;          // flat: verbatim blob
+    size_t blob_bytes;     // bytes of the .rabbit blob
+    rb::G32Plan plan;
+};
+
+namespace rb {
+
+static bool g_attr_set[kMaxDevices];
+
+static int launch_g32(const G32Plan &p, const uint8_t *nib, const float *sc, const float *x,
+                      float *y, DevCtx *c, cudaStream_t s) {
+    if (!g_attr_set[c->device]) {
+        RB_CUDA(cudaFuncSetAttribute(k_gemv_g32, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kMaxDynSmem));
+        g_attr_set[c->device] = true;
+    }
+    G32Args a;
+    a.nib = nib;
+    a.sc = sc;
+    a.x = x;
+    a.y = y;
+    a.rows = p.rows;
+    a.in_dim = p.in_dim;
+    a.units = p.units;
+    a.KS = p.KS;
+    a.RS = p.RS;
+    a.CR = p.CR;
+    a.nslots = p.nslots;
+    a.slot_bytes = p.slot_bytes;
+    a.rows_cta_max = p.rows_cta_max;
+    a.err = c->d_err;
+    a.wait_ns = wait_limit_ns();
+    k_gemv_g32<<<p.grid, p.block, p.smem, s>>>(a);
+    RB_CUDA(cudaGetLastError());
+    return RABBIT_CUDA_OK;
+}
+
+static int launch_flat(const uint8_t *blob, const float *x, float *y, int out_dim, int in_dim,
+                       cudaStream_t s) {
+    const int warps = 8;
+    k_gemv_flat<<<(out_dim + warps - 1) / warps, warps * 32, 0, s>>>(blob, x, y, out_dim, in_dim);
+    RB_CUDA(cudaGetLastError());
+    return RABBIT_CUDA_OK;
+}
+
+static bool blob_bytes(int out_dim, int in_dim, uint32_t gs, size_t *out) {
+    const long long n = (long long)out_dim * in_dim;
+    if (n <= 0 || n > 0x7fffffffLL) return false;  // the format indexes with int
+    const long long g = gs ? gs : 32;
+    *out = (size_t)(4 + 4 * ((n + g - 1) / g) + (n + 1) / 2);
+    return true;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" {
+
+int rabbit_cuda_gemv_int4_grouped(const uint8_t *W, const float *x, float *y, int out_dim,
+                                  int in_dim) {
+    if (!W || !x || !y || out_dim <= 0 || in_dim <= 0)
+        return fail(RABBIT_CUDA_ERR_ARGS, "gemv: NULL pointer or non-positive size");
+    uint32_t gs;
+    memcpy(&gs, W, 4);
+    if (gs == 0 || gs > 4096) {  // quant.c:158-161
+        memset(y, 0, sizeof(float) * (size_t)out_dim);
+        return ok();
+    }
+    size_t nbytes;
+    if (!blob_bytes(out_dim, in_dim, gs, &nbytes))
+        return fail(RABBIT_CUDA_ERR_ARGS, "gemv: out_dim*in_dim exceeds the format's int range");
+    int st;
+    DevCtx *c = dev_ctx(current_device(), &st);
+    if (!c) return st;
+    std::lock_guard<std::mutex> g(c->mu);
+    const size_t xb = align_up((size_t)in_dim * 4, 256), yb = align_up((size_t)out_dim * 4, 256);
+    const bool fast = gs == 32 && g32_ok(in_dim);
+    const int rows_pad = (out_dim + 3) / 4 * 4;
+    const size_t nibb = align_up((size_t)rows_pad * (in_dim / 2), 256);
+    const size_t scb = align_up((size_t)rows_pad * (in_dim / 32) * 4, 256);
+    const size_t wb = fast ? nibb + scb : align_up(nbytes, 256);
+    if ((st = ensure_dscratch(c, wb + xb + yb)) != RABBIT_CUDA_OK) return st;
+    uint8_t *dw = static_cast<uint8_t *>(c->dscratch);
+    float *dx = reinterpret_cast<float *>(dw + wb);
+    float *dy = reinterpret_cast<float *>(dw + wb + xb);
+    cudaStream_t s = c->stream;
+    RB_CUDA(cudaMemcpyAsync(dx, x, (size_t)in_dim * 4, cudaMemcpyHostToDevice, s));
+    if (fast) {
+        G32Plan p;
+        if (!plan_g32(out_dim, in_dim, c->sm_count, &p))
+            return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "gemv: no streaming plan for %dx%d", out_dim,
+                        in_dim);
+        const size_t n = (size_t)out_dim * in_dim;
+        uint8_t *dnib = dw;
+        float *dsc = reinterpret_cast<float *>(dw + nibb);
+        if (rows_pad != out_dim) RB_CUDA(cudaMemsetAsync(dw, 0, wb, s));
+        RB_CUDA(cudaMemcpyAsync(dsc, W + 4, n / 32 * 4, cudaMemcpyHostToDevice, s));
+        RB_CUDA(cudaMemcpyAsync(dnib, W + 4 + n / 32 * 4, n / 2, cudaMemcpyHostToDevice, s));
+        if ((st = launch_g32(p, dnib, dsc, dx, dy, c, s)) != RABBIT_CUDA_OK) return st;
+    } else {
+        RB_CUDA(cudaMemcpyAsync(dw, W, nbytes, cudaMemcpyHostToDevice, s));
+        if ((st = launch_flat(dw, dx, dy, out_dim, in_dim, s)) != RABBIT_CUDA_OK) return st;
+    }
+    RB_CUDA(cudaMemcpyAsync(y, dy, (size_t)out_dim * 4, cudaMemcpyDeviceToHost, s));
+    if ((st = check_device_error(c, s, "gemv")) != RABBIT_CUDA_OK) return st;
+    return ok();
+}
+
+int rabbit_cuda_dequant_int4_grouped_dev(const uint8_t *d_blob, float *d_dst, int n,
+                                         void *stream) {
+    if (!d_blob || !d_dst || n <= 0)
+        return fail(RABBIT_CUDA_ERR_ARGS, "dequant: NULL pointer or non-positive n");
+    int st;
+    DevCtx *c = dev_ctx(current_device(), &st);
+    if (!c) return st;
+    cudaStream_t s = as_stream(stream, c);
+    uint32_t gs = 0;
+    RB_CUDA(cudaMemcpyAsync(&gs, d_blob, 4, cudaMemcpyDeviceToHost, s));
+    RB_CUDA(cudaStreamSynchronize(s));
+    if (gs == 0 || gs > 4096)  // quant.c:128
+        return fail(RABBIT_CUDA_ERR_FORMAT, "dequant: invalid group_size %u", gs);
+    const int threads = 256;
+    long long blocks = ((long long)n + threads - 1) / threads;
+    if (blocks > 4L * c->sm_count * 8) blocks = 4L * c->sm_count * 8;
+    k_dequant_flat<<<(int)blocks, threads, 0, s>>>(d_blob, d_dst, n, gs);
+    RB_CUDA(cudaGetLastError());
+    return ok();
+}
+
+int rabbit_cuda_gemv_int4_grouped_dev(const uint8_t *d_blob, const float *d_x, float *d_y,
+                                      int out_dim, int in_dim, void *stream) {
+    if (!d_blob || !d_x || !d_y || out_dim <= 0 || in_dim <= 0)
+        return fail(RABBIT_CUDA_ERR_ARGS, "gemv_dev: NULL pointer or non-positive size");
+    int st;
+    DevCtx *c = dev_ctx(current_device(), &st);
+    if (!c) return st;
+    if ((st = launch_flat(d_blob, d_x, d_y, out_dim, in_dim, as_stream(stream, c))) !=
+        RABBIT_CUDA_OK)
+        return st;
+    return ok();
+}
+
+int rabbit_cuda_matrix_upload(const uint8_t *blob, int out_dim, int in_dim,
+                              rabbit_cuda_matrix **out) {
+    if (!blob || !out || out_dim <= 0 || in_dim <= 0)
+        return fail(RABBIT_CUDA_ERR_ARGS, "matrix_upload: NULL pointer or non-positive size");
+    *out = nullptr;
+    uint32_t gs;
+    memcpy(&gs, blob, 4);
+    size_t nbytes;
+    if (!blob_bytes(out_dim, in_dim, gs, &nbytes))
+        return fail(RABBIT_CUDA_ERR_ARGS, "matrix_upload: out_dim*in_dim exceeds int range");
+    int st;
+    DevCtx *c = dev_ctx(current_device(), &st);
+    if (!c) return st;
+    rabbit_cuda_matrix *m = new rabbit_cuda_matrix();
+    m->device = c->device;
+    m->rows = out_dim;
+    m->in_dim = in_dim;
+    m->rows_pad = (out_dim + 3) / 4 * 4;
+    m->group_size = gs;
+    m->blob_bytes = nbytes;
+    m->fast = gs == 32 && plan_g32(out_dim, in_dim, c->sm_count, &m->plan);
+    cudaError_t e;
+    if (m->fast) {
+        const size_t n = (size_t)out_dim * in_dim;
+        const size_t nibb = (size_t)m->rows_pad * (in_dim / 2);
+        const size_t scb = (size_t)m->rows_pad * (in_dim / 32) * 4;
+        if ((e = cudaMalloc(&m->nib, nibb)) != cudaSuccess ||
+            (e = cudaMalloc(&m->sc, scb)) != cudaSuccess ||
+            (e = cudaMemset(m->nib, 0, nibb)) != cudaSuccess ||
+            (e = cudaMemset(m->sc, 0, scb)) != cudaSuccess ||
+            (e = cudaMemcpy(m->sc, blob + 4, n / 32 * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(m->nib, blob + 4 + n / 32 * 4, n / 2, cudaMemcpyHostToDevice)) !=
+                cudaSuccess) {
+            rabbit_cuda_matrix_free(m);
+            return cuda_fail(e, "matrix_upload (planes)");
+        }
+    } else {
+        if ((e = cudaMalloc(&m->raw, nbytes)) != cudaSuccess ||
+            (e = cudaMemcpy(m->raw, blob, nbytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            rabbit_cuda_matrix_free(m);
+            return cuda_fail(e, "matrix_upload (raw)");
+        }
+    }
+    *out = m;
+    return ok();
+}
+
+int rabbit_cuda_matrix_free(rabbit_cuda_matrix *m) {
+    if (!m) return ok();
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->device);
+    if (m->nib) cudaFree(m->nib);
+    if (m->sc) cudaFree(m->sc);
+    if (m->raw) cudaFree(m->raw);
+    cudaSetDevice(prev);
+    delete m;
+    return ok();
+}
+
+int rabbit_cuda_matrix_gemv_dev(const rabbit_cuda_matrix *m, const float *d_x, float *d_y,
+                                void *stream) {
+    if (!m || !d_x || !d_y) return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_dev: NULL argument");
+    int st;
+    DevCtx *c = dev_ctx(m->device, &st);
+    if (!c) return st;
+    cudaStream_t s = as_stream(stream, c);
+    if (m->fast) {
+        if ((reinterpret_cast<uintptr_t>(d_x) & 15) != 0)
+            return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_dev: x must be 16-byte aligned");
+        st = launch_g32(m->plan, m->nib, m->sc, d_x, d_y, c, s);
+    } else if (m->group_size == 0 || m->group_size > 4096) {
+        RB_CUDA(cudaMemsetAsync(d_y, 0, (size_t)m->rows * 4, s));
+        st = RABBIT_CUDA_OK;
+    } else {
+        st = launch_flat(m->raw, d_x, d_y, m->rows, m->in_dim, s);
+    }
+    return st == RABBIT_CUDA_OK ? ok() : st;
+}
+
+int rabbit_cuda_matrix_gemv(const rabbit_cuda_matrix *m, const float *x, float *y) {
+    if (!m || !x || !y) return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv: NULL argument");
+    int st;
+    DevCtx *c = dev_ctx(m->device, &st);
+    if (!c) return st;
+    std::lock_guard<std::mutex> g(c->mu);
+    const size_t xb = align_up((size_t)m->in_dim * 4, 256), yb = (size_t)m->rows * 4;
+    if ((st = ensure_dscratch(c, xb + yb)) != RABBIT_CUDA_OK) return st;
+    if ((st = ensure_pinned(c, xb + yb)) != RABBIT_CUDA_OK) return st;
+    float *dx = static_cast<float *>(c->dscratch);
+    float *dy = reinterpret_cast<float *>(static_cast<uint8_t *>(c->dscratch) + xb);
+    float *px = static_cast<float *>(c->pin);
+    float *py = reinterpret_cast<float *>(static_cast<uint8_t *>(c->pin) + xb);
+    memcpy(px, x, (size_t)m->in_dim * 4);
+    cudaStream_t s = c->stream;
+    RB_CUDA(cudaMemcpyAsync(dx, px, (size_t)m->in_dim * 4, cudaMemcpyHostToDevice, s));
+    if ((st = rabbit_cuda_matrix_gemv_dev(m, dx, dy, s)) != RABBIT_CUDA_OK) return st;
+    RB_CUDA(cudaMemcpyAsync(py, dy, yb, cudaMemcpyDeviceToHost, s));
+    if ((st = check_device_error(c, s, "matrix_gemv")) != RABBIT_CUDA_OK) return st;
+    memcpy(y, py, yb);
+    return ok();
+}
+
+uint64_t rabbit_cuda_matrix_bytes(const rabbit_cuda_matrix *m) {
+    if (!m) return 0;
+    return (uint64_t)m->blob_bytes + 4ull * (uint64_t)m->in_dim + 4ull * (uint64_t)m->rows;
+}
+
+}  // extern "C"

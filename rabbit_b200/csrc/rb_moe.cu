@@ -1,0 +1,570 @@
+// rb_moe.cu -- C ABI: HBM-resident expert pool + MoE decode entry points.
+//
+// The pool replaces the reference's expert cache / mmap fetch
+// (memory.c:94-253, moe.c:73-117): every record of the .rabbit expert table
+// lives in HBM for the life of the pool. Records are read from the host map,
+// copied into one of two pinned staging buffers, and moved with
+// cudaMemcpyAsync on a side stream (double buffered: the host fills one
+// buffer while the other is in flight).
+//
+// Group-32 int4 records are re-laid out on the way in: each of gate / up /
+// down is split into a 256-byte aligned nibble plane [rows][in/2] and scale
+// plane [rows][in/32] -- the packed values are the same bytes, only moved --
+// so kernels can bulk-copy whole row chunks. Other formats are kept verbatim.
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "rb_gemv.cuh"
+#include "rb_moe.cuh"
+#include "rb_runtime.h"
+
+namespace {
+
+constexpr size_t kPinChunk = 32ull << 20;  // bytes per pinned staging buffer
+
+inline uint64_t nbytes_g32(uint64_t n) { return 4 + 4 * ((n + 31) / 32) + (n + 1) / 2; }
+
+inline uint64_t mix_host(uint64_t seed, uint64_t r) {
+    uint64_t z = seed * 0x100000001B3ull + r * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 33)) * 0xFF51AFD7ED558CCDull;
+    return z ^ (z >> 33);
+}
+
+struct Segment {
+    uint64_t src, len, dst;  // offsets in the host record / pool record
+};
+
+}  // namespace
+
+struct rabbit_cuda_moe {
+    int device = -1;
+    rb::DevCtx *ctx = nullptr;
+    // model
+    int L = 0, H = 0, E = 0, k = 0, I = 0, S = 0, quant = 4;
+    uint64_t expert_size = 0;
+    int n_records = 0, epl = 0, shared_table = 0;
+    const uint8_t *host_map = nullptr;
+    bool usable = false, fast = false;
+    // pool
+    uint8_t *pool = nullptr;
+    uint64_t rec_stride = 0, pool_bytes = 0;
+    uint64_t off_gnib = 0, off_unib = 0, off_dnib = 0, off_gsc = 0, off_usc = 0, off_dsc = 0;
+    std::vector<Segment> segs;
+    std::vector<uint8_t> resident;
+    // dense per-layer inputs
+    float *rms = nullptr, *router = nullptr;
+    // scratch
+    float *scores = nullptr, *mid = nullptr, *xn = nullptr, *down = nullptr;
+    float *h_in = nullptr, *h_out = nullptr, *w_int = nullptr;
+    int *ids_int = nullptr;
+    unsigned *bar = nullptr;
+    rb::Route *route = nullptr;
+    // upload machinery
+    cudaStream_t up = nullptr;
+    void *pin[2] = {nullptr, nullptr};
+    cudaEvent_t pin_ev[2] = {nullptr, nullptr};
+    int pin_next = 0;
+    // host-buffer decode staging
+    float *pin_io = nullptr;
+    // fused plan
+    rb::MoeFusedArgs plan{};
+    int grid = 0, block = 0;
+    size_t smem = 0;
+    // counters
+    uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
+};
+
+namespace rb {
+
+static bool g_moe_attr[kMaxDevices];
+
+static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_local) {
+    if (layer < 0 || layer >= p->L) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d out of range", layer);
+    if (p->shared_table) {
+        *base = 0;
+        *n_local = p->n_records;
+    } else {
+        *base = layer * p->epl;
+        *n_local = std::min(p->epl, p->n_records - *base);
+        if (*n_local < 0) *n_local = 0;
+    }
+    return RABBIT_CUDA_OK;
+}
+
+static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
+    const int H = p->H, I = p->I;
+    if (!g32_ok(H) || !g32_ok(I)) return false;
+    const int KSb = (H / 32 + 31) / 32, KSc = (I / 32 + 31) / 32;
+    int CW = std::max(8, std::max(KSb, KSc));
+    if (CW % KSb) CW = (CW / KSb + 1) * KSb;
+    if (CW > 16) CW = std::max(KSb, KSc);
+    if (CW > 16) return false;
+    MoeFusedArgs &a = p->plan;
+    a.CW = CW;
+    a.KSb = KSb;
+    a.RSb = CW / KSb;
+    a.KSc = KSc;
+    a.RSc = CW / KSc;
+    const size_t rb_b = 2 * ((size_t)H / 2 + (size_t)H / 8);  // gate+up bytes per row
+    const size_t rb_c = (size_t)I / 2 + (size_t)I / 8;
+    size_t slot = std::max<size_t>(32 * 1024, std::max(4 * rb_b, 4 * rb_c));
+    slot = align_up(slot, 128);
+    int crb = (int)(slot / rb_b) / 4 * 4, crc = (int)(slot / rb_c) / 4 * 4;
+    crb = std::min(crb, 64);
+    crc = std::min(crc, 64);
+    a.CRb = crb;
+    a.CRc = crc;
+    a.slot_bytes = (uint32_t)slot;
+    const int slots = p->k + p->S;
+    const int G = sm_count;
+    const long long UB = (long long)slots * (I / 4), UC = H / 4;
+    const long long rows_b = 4 * ((UB + G - 1) / G), rows_c = 4 * ((UC + G - 1) / G);
+    a.part_floats = (int)std::max(rows_b * 2 * KSb, rows_c * slots * KSc);
+    const size_t fixed = align_up((size_t)H * 4, 128) + 128 + 2 * kMaxSlots * 4 + 16 + 128 +
+                         align_up((size_t)a.part_floats * 4, 16);
+    long long ns = ((long long)kMaxDynSmem - (long long)fixed - 8 * 64) / (long long)slot;
+    if (ns > 12) ns = 12;
+    if (ns < 2) return false;
+    a.nslots = (int)ns;
+    p->smem = align_up(align_up((size_t)H * 4, 128) + 128 + 2 * kMaxSlots * 4 + 16, 128) +
+              (size_t)ns * slot + align_up((size_t)a.part_floats * 4, 16) + 8 * 2 * ns;
+    if (p->smem > (size_t)kMaxDynSmem) return false;
+    p->block = (CW + 1) * 32;
+    p->grid = G;
+    return true;
+}
+
+static void free_pool(rabbit_cuda_moe *p) {
+    if (p->device >= 0) cudaSetDevice(p->device);
+    if (p->up) cudaStreamSynchronize(p->up);
+    void *bufs[] = {p->pool,  p->rms, p->router,  p->scores, p->mid, p->xn,    p->down,
+                    p->h_in, p->h_out, p->w_int, p->ids_int, p->bar, p->route};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    for (int i = 0; i < 2; ++i) {
+        if (p->pin[i]) cudaFreeHost(p->pin[i]);
+        if (p->pin_ev[i]) cudaEventDestroy(p->pin_ev[i]);
+    }
+    if (p->pin_io) cudaFreeHost(p->pin_io);
+    if (p->up) cudaStreamDestroy(p->up);
+    delete p;
+}
+
+static int upload_record(rabbit_cuda_moe *p, int gid) {
+    const uint8_t *src = p->host_map + (uint64_t)gid * p->expert_size;
+    uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
+    for (const Segment &sg : p->segs) {
+        for (uint64_t done = 0; done < sg.len;) {
+            const uint64_t n = std::min<uint64_t>(kPinChunk, sg.len - done);
+            const int b = p->pin_next;
+            p->pin_next ^= 1;
+            RB_CUDA(cudaEventSynchronize(p->pin_ev[b]));  // buffer b free again
+            memcpy(p->pin[b], src + sg.src + done, n);
+            RB_CUDA(cudaMemcpyAsync(dst + sg.dst + done, p->pin[b], n, cudaMemcpyHostToDevice,
+                                    p->up));
+            RB_CUDA(cudaEventRecord(p->pin_ev[b], p->up));
+            p->h2d_bytes += n;
+            done += n;
+        }
+    }
+    p->resident[gid] = 1;
+    p->uploads++;
+    return RABBIT_CUDA_OK;
+}
+
+// splitmix64: a stateless hash of (seed, index) for device-side random init.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Uniform random bytes (two uniform nibbles each) over [dst, dst + n).
+__global__ void k_fill_bytes(uint8_t *dst, uint64_t n, uint64_t seed) {
+    const uint64_t n8 = n / 8;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
+         i += (uint64_t)gridDim.x * blockDim.x)
+        reinterpret_cast<uint64_t *>(dst)[i] = mix64(seed ^ (i * 0xD1B54A32D192ED03ull));
+}
+
+// |N(0, sigma)| / 7 per element (Box-Muller on two hashed uniforms).
+__global__ void k_fill_scales(float *dst, uint64_t n, uint64_t seed, float sigma) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t h = mix64(seed ^ (i * 0xA24BAED4963EE407ull));
+        const float u1 = ((uint32_t)(h >> 40) + 1) * (1.0f / 16777217.0f);
+        const float u2 = (uint32_t)(h & 0xFFFFFF) * (1.0f / 16777216.0f);
+        const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        dst[i] = fabsf(z) * sigma / 7.0f;
+    }
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" {
+
+int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cuda_moe **out) {
+    if (!d || !out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_create: NULL argument");
+    *out = nullptr;
+    if (d->n_layers <= 0 || d->hidden <= 0 || d->n_experts <= 0 || d->inter <= 0 ||
+        d->expert_size == 0 || d->n_records <= 0 || !d->rms_ffn || !d->w_router)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_create: incomplete model description");
+    for (int l = 0; l < d->n_layers; ++l)
+        if (!d->rms_ffn[l] || !d->w_router[l])
+            return fail(RABBIT_CUDA_ERR_ARGS, "moe_create: layer %d has no norm/router", l);
+    int st;
+    DevCtx *c = dev_ctx(device, &st);
+    if (!c) return st;
+
+    rabbit_cuda_moe *p = new rabbit_cuda_moe();
+    p->device = device;
+    p->ctx = c;
+    p->L = d->n_layers;
+    p->H = d->hidden;
+    p->E = d->n_experts;
+    p->I = d->inter;
+    int k = d->experts_per_token > 0 ? d->experts_per_token : 2;  // forward_v2.c:113
+    k = std::min(k, p->E);
+    k = std::min(k, 8);  // forward_v2.c:366-367
+    p->k = k;
+    p->S = (d->n_shared > 0 && d->n_shared <= 64) ? d->n_shared : 0;  // forward_v2.c:392
+    p->quant = d->expert_quant;
+    p->expert_size = d->expert_size;
+    p->n_records = d->n_records;
+    p->epl = d->experts_per_layer > 0 ? d->experts_per_layer : d->n_experts;
+    p->shared_table = d->experts_shared ? 1 : 0;
+    p->host_map = static_cast<const uint8_t *>(d->expert_map);
+
+    const uint64_t mat = (uint64_t)p->H * p->I;
+    uint64_t need;
+    if (p->quant == 0)
+        need = (2 * mat + mat) * 4;
+    else if (p->quant == 4)
+        need = 2 * nbytes_g32(mat) + nbytes_g32(mat);
+    else
+        need = 3 * (4 + mat);
+    p->usable = p->expert_size >= need;  // forward_v2.c:299,319,335: else experts add nothing
+
+    // Fast layout only when every blob carries group 32.
+    p->fast = p->quant == 4 && p->usable && mat <= 0x7fffffffull;
+    if (p->fast && p->host_map) {
+        const uint64_t nb = nbytes_g32(mat);
+        for (int r = 0; r < p->n_records && p->fast; ++r) {
+            const uint8_t *rec = p->host_map + (uint64_t)r * p->expert_size;
+            for (int m = 0; m < 3; ++m) {
+                uint32_t gs;
+                memcpy(&gs, rec + m * nb, 4);
+                if (gs != 32) {
+                    p->fast = false;
+                    break;
+                }
+            }
+        }
+    }
+    if (p->fast && !plan_fused(p, c->sm_count)) p->fast = false;
+
+    cudaError_t e = cudaSuccess;
+    if (p->fast) {
+        const uint64_t hn = mat / 2, hs = mat / 8, nb = nbytes_g32(mat);
+        p->off_gnib = 0;
+        p->off_unib = align_up(hn, 256);
+        p->off_dnib = p->off_unib + align_up(hn, 256);
+        p->off_gsc = p->off_dnib + align_up(hn, 256);
+        p->off_usc = p->off_gsc + align_up(hs, 256);
+        p->off_dsc = p->off_usc + align_up(hs, 256);
+        p->rec_stride = p->off_dsc + align_up(hs, 256);
+        p->segs = {{4, hs, p->off_gsc},          {4 + hs, hn, p->off_gnib},
+                   {nb + 4, hs, p->off_usc},     {nb + 4 + hs, hn, p->off_unib},
+                   {2 * nb + 4, hs, p->off_dsc}, {2 * nb + 4 + hs, hn, p->off_dnib}};
+    } else {
+        p->rec_stride = align_up(p->expert_size, 256);
+        p->segs = {{0, p->expert_size, 0}};
+    }
+    p->pool_bytes = p->rec_stride * (uint64_t)p->n_records;
+    p->resident.assign(p->n_records, 0);
+
+    const int slots = p->k + p->S;
+    const size_t HE = (size_t)p->H * p->E;
+    if ((e = cudaMalloc(&p->pool, p->pool_bytes)) != cudaSuccess) {
+        free_pool(p);
+        return fail(RABBIT_CUDA_ERR_MEM, "moe_create: cannot allocate %.2f GB expert pool: %s",
+                    p->pool_bytes / 1e9, cudaGetErrorString(e));
+    }
+    if ((e = cudaMalloc(&p->rms, sizeof(float) * (size_t)p->H * p->L)) != cudaSuccess ||
+        (e = cudaMalloc(&p->router, sizeof(float) * HE * p->L)) != cudaSuccess ||
+        (e = cudaMalloc(&p->scores, sizeof(float) * p->E)) != cudaSuccess ||
+        (e = cudaMalloc(&p->mid, sizeof(float) * (size_t)std::max(slots, 1) * p->I)) !=
+            cudaSuccess ||
+        (e = cudaMalloc(&p->xn, sizeof(float) * p->H)) != cudaSuccess ||
+        (e = cudaMalloc(&p->down, sizeof(float) * (size_t)std::max(slots, 1) * p->H)) !=
+            cudaSuccess ||
+        (e = cudaMalloc(&p->h_in, sizeof(float) * p->H)) != cudaSuccess ||
+        (e = cudaMalloc(&p->h_out, sizeof(float) * p->H)) != cudaSuccess ||
+        (e = cudaMalloc(&p->w_int, sizeof(float) * 8)) != cudaSuccess ||
+        (e = cudaMalloc(&p->ids_int, sizeof(int) * 8)) != cudaSuccess ||
+        (e = cudaMalloc(&p->bar, sizeof(unsigned) * 2)) != cudaSuccess ||
+        (e = cudaMalloc(&p->route, sizeof(Route))) != cudaSuccess ||
+        (e = cudaMemset(p->bar, 0, sizeof(unsigned) * 2)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 16))) !=
+            cudaSuccess) {
+        free_pool(p);
+        return cuda_fail(e, "moe_create: scratch");
+    }
+    const uint64_t pin_bytes = std::min<uint64_t>(kPinChunk, align_up(p->expert_size, 4096));
+    for (int i = 0; i < 2; ++i) {
+        if ((e = cudaMallocHost(&p->pin[i], pin_bytes)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&p->pin_ev[i], cudaEventDisableTiming)) !=
+                cudaSuccess ||
+            (e = cudaEventRecord(p->pin_ev[i], p->up)) != cudaSuccess) {
+            free_pool(p);
+            return cuda_fail(e, "moe_create: pinned staging");
+        }
+    }
+    for (int l = 0; l < p->L; ++l) {
+        if ((e = cudaMemcpy(p->rms + (size_t)l * p->H, d->rms_ffn[l], sizeof(float) * p->H,
+                            cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(p->router + HE * l, d->w_router[l], sizeof(float) * HE,
+                            cudaMemcpyHostToDevice)) != cudaSuccess) {
+            free_pool(p);
+            return cuda_fail(e, "moe_create: router/norm upload");
+        }
+    }
+    if (p->fast && !g_moe_attr[device]) {
+        if ((e = cudaFuncSetAttribute(k_moe_decode_g32, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kMaxDynSmem)) != cudaSuccess) {
+            free_pool(p);
+            return cuda_fail(e, "moe_create: smem attribute");
+        }
+        g_moe_attr[device] = true;
+    }
+    if (p->fast) {
+        int per_sm = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode_g32,
+                                                               p->block, p->smem)) !=
+                cudaSuccess ||
+            per_sm < 1) {
+            free_pool(p);
+            return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_create: fused kernel does not fit an SM");
+        }
+    }
+    *out = p;
+    return ok();
+}
+
+int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: NULL pool");
+    if (layer_begin < 0 || layer_end > p->L || layer_begin >= layer_end)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: bad layer range [%d, %d)", layer_begin,
+                    layer_end);
+    if (!p->host_map)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: pool was created without a host map");
+    RB_CUDA(cudaSetDevice(p->device));
+    for (int l = layer_begin; l < layer_end; ++l) {
+        int base, n;
+        int st = layer_map(p, l, &base, &n);
+        if (st) return st;
+        for (int r = 0; r < n; ++r)
+            if (!p->resident[base + r] && (st = upload_record(p, base + r)) != RABBIT_CUDA_OK)
+                return st;
+    }
+    return ok();
+}
+
+int rabbit_cuda_moe_sync(rabbit_cuda_moe *p) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_sync: NULL pool");
+    RB_CUDA(cudaSetDevice(p->device));
+    RB_CUDA(cudaStreamSynchronize(p->up));
+    return ok();
+}
+
+int rabbit_cuda_moe_fill_synthetic(rabbit_cuda_moe *p, uint64_t seed, float scale_sigma) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_fill_synthetic: NULL pool");
+    if (!p->fast)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_fill_synthetic: pool is not in the group-32 layout");
+    RB_CUDA(cudaSetDevice(p->device));
+    const uint64_t mat = (uint64_t)p->H * p->I;
+    const int blocks = p->ctx->sm_count * 8;
+    for (int r = 0; r < p->n_records; ++r) {
+        uint8_t *rec = p->pool + (uint64_t)r * p->rec_stride;
+        const uint64_t s0 = mix_host(seed, (uint64_t)r);
+        const uint64_t nibs[3] = {p->off_gnib, p->off_unib, p->off_dnib};
+        const uint64_t scs[3] = {p->off_gsc, p->off_usc, p->off_dsc};
+        for (int m = 0; m < 3; ++m) {
+            k_fill_bytes<<<blocks, 256, 0, p->up>>>(rec + nibs[m], mat / 2, s0 + 2 * m);
+            k_fill_scales<<<blocks, 256, 0, p->up>>>(reinterpret_cast<float *>(rec + scs[m]),
+                                                     mat / 32, s0 + 2 * m + 1, scale_sigma);
+        }
+        p->resident[r] = 1;
+    }
+    RB_CUDA(cudaGetLastError());
+    RB_CUDA(cudaStreamSynchronize(p->up));
+    return ok();
+}
+
+int rabbit_cuda_moe_free(rabbit_cuda_moe *p) {
+    if (p) free_pool(p);
+    return ok();
+}
+
+int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                               float *d_h_out, int *d_ids, float *d_weights, void *stream) {
+    if (!p || !d_h_in || !d_h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: NULL argument");
+    int base, n_local;
+    int st = layer_map(p, layer, &base, &n_local);
+    if (st) return st;
+    for (int r = 0; r < n_local; ++r)
+        if (!p->resident[base + r])
+            return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: layer %d not uploaded", layer);
+    RB_CUDA(cudaSetDevice(p->device));
+    cudaStream_t s = as_stream(stream, p->ctx);
+    int *ids = d_ids ? d_ids : p->ids_int;
+    float *w = d_weights ? d_weights : p->w_int;
+    const float *rms = p->rms + (size_t)layer * p->H;
+    const float *router = p->router + (size_t)layer * p->H * p->E;
+    if (p->fast) {
+        if ((reinterpret_cast<uintptr_t>(d_h_in) & 15) || (reinterpret_cast<uintptr_t>(d_h_out) & 15))
+            return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: h must be 16-byte aligned");
+        MoeFusedArgs a = p->plan;
+        a.h_in = d_h_in;
+        a.h_out = d_h_out;
+        a.ids_out = ids;
+        a.w_out = w;
+        a.rms = rms;
+        a.router = router;
+        a.pool = p->pool;
+        a.rec_stride = p->rec_stride;
+        a.off_gnib = p->off_gnib;
+        a.off_unib = p->off_unib;
+        a.off_dnib = p->off_dnib;
+        a.off_gsc = p->off_gsc;
+        a.off_usc = p->off_usc;
+        a.off_dsc = p->off_dsc;
+        a.rec_base = base;
+        a.n_local = n_local;
+        a.H = p->H;
+        a.E = p->E;
+        a.k = p->k;
+        a.I = p->I;
+        a.S = p->S;
+        a.usable = p->usable ? 1 : 0;
+        a.scores = p->scores;
+        a.mid = p->mid;
+        a.bar = p->bar;
+        a.err = p->ctx->d_err;
+        a.wait_ns = wait_limit_ns();
+        void *args[] = {&a};
+        RB_CUDA(cudaLaunchCooperativeKernel((const void *)k_moe_decode_g32, dim3(p->grid),
+                                            dim3(p->block), args, p->smem, s));
+    } else {
+        MoeGenericArgs a;
+        a.h_in = d_h_in;
+        a.h_out = d_h_out;
+        a.ids_out = ids;
+        a.w_out = w;
+        a.rms = rms;
+        a.router = router;
+        a.pool = p->pool;
+        a.rec_stride = p->rec_stride;
+        a.expert_size = p->expert_size;
+        a.rec_base = base;
+        a.n_local = n_local;
+        a.H = p->H;
+        a.E = p->E;
+        a.k = p->k;
+        a.I = p->I;
+        a.S = p->S;
+        a.quant = p->quant;
+        a.usable = p->usable ? 1 : 0;
+        a.xn = p->xn;
+        a.scores = p->scores;
+        a.mid = p->mid;
+        a.down = p->down;
+        a.route = p->route;
+        const int slots = std::max(1, p->k + p->S);
+        k_moe_route<<<1, 512, 0, s>>>(a);
+        k_moe_up_generic<<<dim3((p->I + 7) / 8, slots), 256, 0, s>>>(a);
+        k_moe_down_generic<<<dim3((p->H + 7) / 8, slots), 256, 0, s>>>(a);
+        k_moe_combine<<<(p->H + 255) / 256, 256, 0, s>>>(a);
+        RB_CUDA(cudaGetLastError());
+    }
+    p->hbm_hits++;
+    return ok();
+}
+
+int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_check: NULL pool");
+    RB_CUDA(cudaSetDevice(p->device));
+    cudaStream_t s = as_stream(stream, p->ctx);
+    int st = check_device_error(p->ctx, s, "moe_decode");
+    if (st != RABBIT_CUDA_OK) {
+        // a barrier that gave up may have left arrivals behind: start clean
+        cudaMemsetAsync(p->bar, 0, sizeof(unsigned) * 2, s);
+        cudaStreamSynchronize(s);
+        return st;
+    }
+    return ok();
+}
+
+int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
+                           int *ids, float *weights, int *k_out) {
+    if (!p || !h_in || !h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: NULL argument");
+    std::lock_guard<std::mutex> g(p->ctx->mu);
+    RB_CUDA(cudaSetDevice(p->device));
+    cudaStream_t s = p->ctx->stream;
+    const size_t hb = sizeof(float) * p->H;
+    float *pin_h = p->pin_io;
+    float *pin_w = p->pin_io + 2 * (size_t)p->H;
+    int *pin_ids = reinterpret_cast<int *>(pin_w + 8);
+    memcpy(pin_h, h_in, hb);
+    RB_CUDA(cudaMemcpyAsync(p->h_in, pin_h, hb, cudaMemcpyHostToDevice, s));
+    int st = rabbit_cuda_moe_decode_dev(p, layer, p->h_in, p->h_out, p->ids_int, p->w_int, s);
+    if (st) return st;
+    RB_CUDA(cudaMemcpyAsync(pin_h + p->H, p->h_out, hb, cudaMemcpyDeviceToHost, s));
+    if (p->k > 0) {
+        RB_CUDA(cudaMemcpyAsync(pin_ids, p->ids_int, sizeof(int) * p->k, cudaMemcpyDeviceToHost, s));
+        RB_CUDA(cudaMemcpyAsync(pin_w, p->w_int, sizeof(float) * p->k, cudaMemcpyDeviceToHost, s));
+    }
+    if ((st = rabbit_cuda_moe_check(p, s)) != RABBIT_CUDA_OK) return st;
+    memcpy(h_out, pin_h + p->H, hb);
+    if (ids) memcpy(ids, pin_ids, sizeof(int) * p->k);
+    if (weights) memcpy(weights, pin_w, sizeof(float) * p->k);
+    if (k_out) *k_out = p->k;
+    return ok();
+}
+
+int rabbit_cuda_moe_stats(const rabbit_cuda_moe *p, uint64_t *hbm_hits, uint64_t *uploads,
+                          uint64_t *h2d_bytes, int *resident_records, uint64_t *pool_bytes) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_stats: NULL pool");
+    if (hbm_hits) *hbm_hits = p->hbm_hits;
+    if (uploads) *uploads = p->uploads;
+    if (h2d_bytes) *h2d_bytes = p->h2d_bytes;
+    if (resident_records) {
+        int n = 0;
+        for (uint8_t r : p->resident) n += r;
+        *resident_records = n;
+    }
+    if (pool_bytes) *pool_bytes = p->pool_bytes;
+    return ok();
+}
+
+uint64_t rabbit_cuda_moe_decode_bytes(const rabbit_cuda_moe *p) {
+    if (!p) return 0;
+    const uint64_t mat = (uint64_t)p->H * p->I;
+    uint64_t per;
+    if (p->quant == 0)
+        per = 3 * mat * 4;
+    else if (p->quant == 4)
+        per = 3 * nbytes_g32(mat);
+    else
+        per = 3 * (4 + mat);
+    return 4ull * p->E * p->H + (uint64_t)(p->k + p->S) * per;
+}
+
+}  // extern "C"
