@@ -2,7 +2,9 @@
  * rabbit_cuda.h -- C ABI of the B200 (sm_100a) routed-expert hot path.
  *
  * Plain C: pointers, sizes and status codes only. A CUDA stream is passed as
- * `void *` (a cudaStream_t / CUstream; NULL = the library's own stream).
+ * `void *` (a cudaStream_t / CUstream; NULL = the default stream). Entry
+ * points that take HOST buffers use a stream of the library's own and return
+ * after the result is on the host.
  * Every entry point returns a rabbit_cuda_status; on failure
  * rabbit_cuda_last_error() holds a one-line explanation for the calling
  * thread. Nothing here calls exit(); nothing falls back to the CPU.

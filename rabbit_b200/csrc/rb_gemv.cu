@@ -1,103 +1,181 @@
 // rb_gemv.cu -- group-32 int4 GEMV on B200.
 //
-// Streaming kernel (k_gemv_g32), one persistent CTA per SM, contiguous row
-// range per CTA:
-//   warp CW (producer): one lane issues cp.async.bulk copies of row chunks
-//       (nibbles + scales) into a ring of shared-memory stages, gated by
-//       full/empty mbarriers; x is bulk-copied once.
-//   warps 0..CW-1 (consumers): warp w owns k-slice w % KS (lane = one group
-//       of 32 inputs, x for that group held in 32 registers for the whole
-//       kernel) and row subset w / KS. Each lane computes its group's dot
-//       product on packed fp32, scales it, and eight rows at a time are
-//       reduced across the warp with a transposed butterfly. Partials per
-//       (row, k-slice) go to shared memory and are summed once at the end.
-// Arithmetic: per group, sum_i (q_i/64) x_i, times 64*scale; rows summed over
-// groups in a fixed order (within tolerance of the reference's serial fp32
-// sum, quant.c:181-184).
+// Streaming kernel (k_gemv_g32), one persistent CTA per SM, a contiguous
+// range of row tiles per CTA (tile = TR rows of nibbles + scales, one
+// contiguous block in HBM):
+//   warp CW (producer): one lane issues one cp.async.bulk per tile into a
+//       ring of shared-memory stages, gated by full/empty mbarriers.
+//   warps 0..CW-1 (consumers, at most eight): warp w owns k-slice w % KS
+//       (lane = J groups of 32 inputs, held as integer planes in registers
+//       for the whole kernel) and ROWS rows of every tile from
+//       (w / KS) * ROWS. ROWS and J are compile-time, so a warp does exactly
+//       its ROWS x J dots per tile: it loads them, releases the stage, then
+//       computes, and the ROWS values are reduced across the warp together
+//       with a transposed butterfly.
+//       Partials per (row, k-slice) go to shared memory and are summed once
+//       at the end.
+// Arithmetic: per group an exact integer dot of the nibbles with the
+// activations' 23-bit block-floating-point planes (dp4a), times the group
+// scale; rows summed over groups in a fixed order (within tolerance of the
+// reference's serial fp32 sum, quant.c:181-184).
+#include <string.h>
+
+#include <algorithm>
+
 #include "rb_gemv.cuh"
 #include "rb_runtime.h"
 
 namespace rb {
 
+// Per-SM streaming rate and fixed cost of one bulk copy issued by one
+// thread, used to size tiles (measured on B200: 16-40 KB single copies stream
+// at 6.6-7 TB/s; 8 KB copies from one issuing thread at ~3.3 TB/s, i.e.
+// ~0.35 us per copy per SM).
+constexpr double kSmBytesPerUs = 44.0e3;
+constexpr double kCopyUs = 0.35;
+// Consumer-side fixed work per tile (wait, release, cross-lane reduction,
+// partial stores), not hidden behind the copies.
+constexpr double kTileFixedUs = 0.15;
+const double kTileSmBytesPerUs = kSmBytesPerUs, kTileCopyUs = kCopyUs;
+
+int choose_rows(int rows, int mats, bool spread, int ctas, size_t row_bytes, int NG, int max_rows,
+                size_t max_bytes) {
+    int best = 1;
+    double best_cost = 1e30;
+    for (int R = 1; R <= max_rows; R *= 2) {
+        const int TR = NG * R;
+        if (R > 1 && (size_t)TR * row_bytes > max_bytes) break;
+        const long long tiles = (rows + TR - 1) / TR;
+        const long long per =
+            spread ? (mats * tiles + ctas - 1) / ctas : mats * ((tiles + ctas - 1) / ctas);
+        const double cost = std::max((double)per * TR * row_bytes / kSmBytesPerUs, per * kCopyUs) +
+                             per * kTileFixedUs;
+        if (cost < best_cost * 0.98 || (cost <= best_cost * 1.02 && R > best)) {
+            if (cost < best_cost) best_cost = cost;
+            best = R;
+        }
+    }
+    return best;
+}
+
+void tile_blob_host(const uint8_t *blob, const Tiling &t, uint8_t *dst) {
+    const size_t n = (size_t)t.rows * t.in_dim;
+    const size_t half = t.in_dim / 2, scb = t.in_dim / 8;  // bytes per row
+    const uint8_t *sc = blob + 4;
+    const uint8_t *nib = blob + 4 + n / 32 * 4;
+    for (int ti = 0; ti < t.ntiles; ++ti) {
+        uint8_t *d = dst + (size_t)ti * t.tile_stride;
+        const int r0 = ti * t.TR, nr = std::min(t.TR, t.rows - r0);
+        memset(d, 0, t.tile_stride);
+        memcpy(d, nib + (size_t)r0 * half, (size_t)nr * half);
+        memcpy(d + (size_t)t.TR * half, sc + (size_t)r0 * scb, (size_t)nr * scb);
+    }
+}
+
+void tile_pair_host(const uint8_t *a, const uint8_t *b, const Tiling &t2, uint8_t *dst) {
+    const size_t n = (size_t)t2.rows * t2.in_dim;
+    const size_t half = t2.in_dim / 2, scb = t2.in_dim / 8;
+    const uint8_t *srcs[2] = {a, b};
+    for (int ti = 0; ti < t2.ntiles; ++ti) {
+        uint8_t *d = dst + (size_t)ti * t2.tile_stride;
+        const int r0 = ti * t2.TR, nr = std::min(t2.TR, t2.rows - r0);
+        memset(d, 0, t2.tile_stride);
+        for (int m = 0; m < 2; ++m) {
+            const uint8_t *sc = srcs[m] + 4;
+            const uint8_t *nib = srcs[m] + 4 + n / 32 * 4;
+            memcpy(d + (size_t)m * t2.TR * half, nib + (size_t)r0 * half, (size_t)nr * half);
+            memcpy(d + 2 * (size_t)t2.TR * half + (size_t)m * t2.TR * scb, sc + (size_t)r0 * scb,
+                   (size_t)nr * scb);
+        }
+    }
+}
+
 bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p) {
     if (rows <= 0 || !g32_ok(in_dim)) return false;
     const int G = in_dim / 32;
-    p->rows = rows;
-    p->in_dim = in_dim;
-    p->units = (rows + 3) / 4;
-    p->KS = (G + 31) / 32;
-    p->RS = p->KS >= 8 ? 1 : 8 / p->KS;
+    p->J = lane_groups(G);
+    p->KS = kslices(G, p->J);
+    p->NG = std::max(1, kConsumerWarps / p->KS);
     const size_t row_bytes = (size_t)in_dim / 2 + (size_t)in_dim / 8;
-    int cr = (int)((32 * 1024) / row_bytes) / 4 * 4;
-    if (cr < 4) cr = 4;
-    if (cr > 64) cr = 64;
-    p->CR = cr;
-    p->slot_bytes = (uint32_t)align_up((size_t)cr * row_bytes, 128);
-    p->grid = p->units < sm_count ? p->units : sm_count;
-    p->rows_cta_max = 4 * ((p->units + p->grid - 1) / p->grid);
-    const int CW = p->KS * p->RS;
+    p->ROWS = choose_rows(rows, 1, true, sm_count, row_bytes, p->NG, 8, 48 * 1024);
+    const int TR = p->NG * p->ROWS;
+    p->til = make_tiling(rows, in_dim, TR);
+    p->grid = p->til.ntiles < sm_count ? p->til.ntiles : sm_count;
+    p->tiles_cta_max = (p->til.ntiles + p->grid - 1) / p->grid;
+    const int CW = p->KS * p->NG;
     p->block = (CW + 1) * 32;
-    const size_t fixed = align_up((size_t)in_dim * 4, 128) +
-                         align_up((size_t)p->rows_cta_max * p->KS * 4, 16);
-    int ns = (int)((kMaxDynSmem - fixed - 8 * 64) / p->slot_bytes);
-    if (ns > 16) ns = 16;
+    const size_t part = align_up((size_t)p->tiles_cta_max * TR * p->KS * 4, 16);
+    long long ns =
+        ((long long)kMaxDynSmem - (long long)part - 16 * 24 - 128) / p->til.tile_stride;
+    if (ns > 24) ns = 24;
     if (ns < 2) return false;
-    p->nslots = ns;
-    p->smem = fixed + (size_t)ns * p->slot_bytes + 8 * (2 * ns + 1);
+    p->nslots = (int)ns;
+    p->smem = (size_t)ns * p->til.tile_stride + part + 16 * (size_t)ns + 4 * 32;
     return p->smem <= (size_t)kMaxDynSmem;
 }
 
-__global__ void __launch_bounds__(17 * 32, 1) k_gemv_g32(G32Args a) {
+// The consumer loop of one warp over the CTA's nt tiles: ROWS rows of every
+// tile starting at rbase, J groups per lane. False when a wait ran out.
+template <int J, int ROWS>
+__device__ __forceinline__ bool gemv_tiles(const G32Args &a, const uint8_t *ring, float *part,
+                                           uint64_t *full, uint64_t *empty, uint32_t *sink,
+                                           int nt, int ks, int rbase, int g0,
+                                           const bool (&act)[J], const XPlanes (&xg)[J]) {
+    const int G = a.til.in_dim >> 5, half = a.til.in_dim >> 1, TR = a.til.TR, KS = a.KS;
+    const uint32_t stride = a.til.tile_stride;
+    for (int i = 0; i < nt; ++i) {
+        const int s = i % a.nslots, n = i / a.nslots;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) return false;
+        const int lb = i * TR + rbase;
+        chunk_dot<1, ROWS, J>(ring + (size_t)s * stride, TR, rbase, half, G, g0, act, xg,
+                              [=](int, int r) { return (lb + r) * KS + ks; }, part, &empty[s],
+                              1u, sink);
+    }
+    return true;
+}
+
+template <int J>
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_gemv_g32(G32Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int CW = a.KS * a.RS;
+    const int CW = a.KS * a.NG;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int in = a.in_dim, G = in >> 5;
-    const int half = in >> 1;  // nibble bytes per row
+    const int G = a.til.in_dim >> 5;
+    const int TR = a.til.TR;
+    const uint32_t stride = a.til.tile_stride;
 
-    float *xs = reinterpret_cast<float *>(smem);
-    uint8_t *ring = smem + align_up((size_t)in * 4, 128);
-    float *part = reinterpret_cast<float *>(ring + (size_t)a.nslots * a.slot_bytes);
+    uint8_t *ring = smem;
+    float *part = reinterpret_cast<float *>(ring + (size_t)a.nslots * stride);
     uint64_t *full = reinterpret_cast<uint64_t *>(
-        reinterpret_cast<uint8_t *>(part) + align_up((size_t)a.rows_cta_max * a.KS * 4, 16));
+        reinterpret_cast<uint8_t *>(part) + align_up((size_t)a.tiles_cta_max * TR * a.KS * 4, 16));
     uint64_t *empty = full + a.nslots;
-    uint64_t *xbar = empty + a.nslots;
+    uint32_t *sink = reinterpret_cast<uint32_t *>(empty + a.nslots);  // one word per warp
 
-    const int u0 = (int)((long long)blockIdx.x * a.units / gridDim.x);
-    const int u1 = (int)((long long)(blockIdx.x + 1) * a.units / gridDim.x);
-    const int r0 = 4 * u0, r1 = 4 * u1, nrows = r1 - r0;
-    const int nchunks = (nrows + a.CR - 1) / a.CR;
+    const int t0 = (int)((long long)blockIdx.x * a.til.ntiles / gridDim.x);
+    const int t1 = (int)((long long)(blockIdx.x + 1) * a.til.ntiles / gridDim.x);
+    const int nt = t1 - t0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nslots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CW);
+            mbar_init(&empty[s], CW);  // every consumer warp releases every stage
         }
-        mbar_init(xbar, 1);
         mbar_init_fence();
     }
     __syncthreads();
 
     if (warp == CW) {  // ---------------------------------------- producer
         if (lane == 0) {
-            const uint64_t pol_w = policy_evict_first();
-            const uint64_t pol_x = policy_evict_last();
-            mbar_arrive_expect_tx(xbar, (uint32_t)in * 4);
-            bulk_g2s(xs, a.x, (uint32_t)in * 4, xbar, pol_x);
+            const uint64_t pol = policy_evict_first();
             int issued = 0;
-            for (int i = 0; i < nchunks; ++i) {
+            for (int i = 0; i < nt; ++i) {
                 const int s = i % a.nslots, n = i / a.nslots;
-                if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err)) break;
-                const int row0 = r0 + i * a.CR;
-                const int rows = min(a.CR, r1 - row0);
-                const uint32_t nb = (uint32_t)rows * half, sb = (uint32_t)rows * (in >> 3);
-                uint8_t *dst = ring + (size_t)s * a.slot_bytes;
-                mbar_arrive_expect_tx(&full[s], nb + sb);
-                bulk_g2s(dst, a.nib + (size_t)row0 * half, nb, &full[s], pol_w);
-                bulk_g2s(dst + (size_t)a.CR * half, a.sc + (size_t)row0 * G, sb, &full[s], pol_w);
+                if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) break;
+                mbar_arrive_expect_tx(&full[s], a.til.tile_bytes);
+                bulk_g2s(ring + (size_t)s * stride, a.tiles + (size_t)(t0 + i) * stride,
+                         a.til.tile_bytes, &full[s], pol);
                 ++issued;
             }
             // Never leave the CTA while a copy we issued may still be landing.
-            mbar_wait(xbar, 0, a.wait_ns, a.err);
             for (int i = issued > a.nslots ? issued - a.nslots : 0; i < issued; ++i)
                 mbar_wait(&full[i % a.nslots], (i / a.nslots) & 1, a.wait_ns, a.err);
         }
@@ -105,69 +183,43 @@ __global__ void __launch_bounds__(17 * 32, 1) k_gemv_g32(G32Args a) {
     }
 
     // ----------------------------------------------------------- consumers
-    const int ks = warp % a.KS, rsub = warp / a.KS;
-    const int g = ks * 32 + lane;
-    const bool active = g < G;
+    // Warp group q = warp / KS (KS warps cover one row, J groups of 32
+    // inputs per lane) takes rows [q*ROWS, (q+1)*ROWS) of every tile. Every
+    // consumer waits for and releases every stage, so the ring's phases stay
+    // in step.
+    const int ks = warp % a.KS, grp = warp / a.KS;
+    const int g0 = ks * 32 * J + lane;
+    bool act[J];
+    XPlanes xg[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        act[j] = g0 + 32 * j < G;
+        load_xplanes_global(xg[j], a.x + (size_t)(g0 + 32 * j) * 32, act[j]);
+    }
+    const int rbase = grp * a.ROWS;
     // A wait that runs out marks the CTA failed; every consumer still reaches
     // the named barrier below (a warp that left would stall the others).
-    bool good = __all_sync(0xffffffffu, mbar_wait(xbar, 0, a.wait_ns, a.err));
-    float xr[32];
-    if (active) {
-        const float4 *xp = reinterpret_cast<const float4 *>(xs + g * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float4 t = xp[j];
-            xr[4 * j] = t.x;
-            xr[4 * j + 1] = t.y;
-            xr[4 * j + 2] = t.z;
-            xr[4 * j + 3] = t.w;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) xr[j] = 0.f;
-    }
-
-    for (int i = 0; good && i < nchunks; ++i) {
-        const int s = i % a.nslots, n = i / a.nslots;
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) {
-            good = false;
-            break;
-        }
-        const int row0 = r0 + i * a.CR;
-        const int rows = min(a.CR, r1 - row0);
-        const uint8_t *sn = ring + (size_t)s * a.slot_bytes;
-        const float *ss = reinterpret_cast<const float *>(sn + (size_t)a.CR * half);
-        for (int rb = rsub; rb < rows; rb += 8 * a.RS) {
-            float v[8];
-#pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const int r = rb + b * a.RS;
-                v[b] = 0.f;
-                if (active && r < rows) {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(sn + (size_t)r * half + g * 16);
-                    const float sc64 = ss[r * G + g] * 64.f;
-                    v[b] = dot32_q64(w, xr) * sc64;
-                }
-            }
-            const float tot = warp_reduce8(v);
-            if ((lane & 3) == 0) {
-                const int r = rb + (lane >> 2) * a.RS;
-                if (r < rows) part[(row0 - r0 + r) * a.KS + ks] = tot;
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+    bool good;
+    switch (a.ROWS) {
+        case 1: good = gemv_tiles<J, 1>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        case 2: good = gemv_tiles<J, 2>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        case 4: good = gemv_tiles<J, 4>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        default: good = gemv_tiles<J, 8>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
     }
     named_sync(1, CW * 32);
     if (!good) return;
-    for (int lr = threadIdx.x; lr < nrows; lr += CW * 32) {
-        const int row = r0 + lr;
-        if (row < a.rows) {
+    for (int lr = threadIdx.x; lr < nt * TR; lr += CW * 32) {
+        const int row = t0 * TR + lr;
+        if (row < a.til.rows) {
             float acc = 0.f;
             for (int k = 0; k < a.KS; ++k) acc += part[lr * a.KS + k];
             a.y[row] = acc;
         }
     }
+}
+
+const void *gemv_g32_kernel(int J) {
+    return J == 2 ? (const void *)k_gemv_g32<2> : (const void *)k_gemv_g32<1>;
 }
 
 // --------------------------------------------------------- flat kernels --

@@ -1,16 +1,17 @@
 // rb_matrix.cu -- C ABI: stateless quant drop-ins and resident int4 matrices.
 #include <string.h>
 
+#include <vector>
+
 #include "rb_gemv.cuh"
 #include "rb_runtime.h"
 
 struct rabbit_cuda_matrix {
     int device;
-    int rows, in_dim, rows_pad;
+    int rows, in_dim;
     uint32_t group_size;
-    bool fast;             // plane layout + streaming kernel
-    uint8_t *nib;          // fast: [rows_pad][in/2]
-    float *sc;             // fast: [rows_pad][in/32]
+    bool fast;             // tiled layout + streaming kernel
+    uint8_t *tiles;        // fast: plan.til.ntiles tiles of plan.til.tile_stride bytes
     uint8_t *raw;          // flat: verbatim blob
     size_t blob_bytes;     // bytes of the .rabbit blob
     rb::G32Plan plan;
@@ -20,31 +21,28 @@ namespace rb {
 
 static bool g_attr_set[kMaxDevices];
 
-static int launch_g32(const G32Plan &p, const uint8_t *nib, const float *sc, const float *x,
-                      float *y, DevCtx *c, cudaStream_t s) {
+static int launch_g32(const G32Plan &p, const uint8_t *tiles, const float *x, float *y, DevCtx *c,
+                      cudaStream_t s) {
     if (!g_attr_set[c->device]) {
-        RB_CUDA(cudaFuncSetAttribute(k_gemv_g32, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kMaxDynSmem));
+        for (int J = 1; J <= 2; ++J)
+            RB_CUDA(cudaFuncSetAttribute(gemv_g32_kernel(J),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
         g_attr_set[c->device] = true;
     }
     G32Args a;
-    a.nib = nib;
-    a.sc = sc;
+    a.tiles = tiles;
     a.x = x;
     a.y = y;
-    a.rows = p.rows;
-    a.in_dim = p.in_dim;
-    a.units = p.units;
+    a.til = p.til;
     a.KS = p.KS;
-    a.RS = p.RS;
-    a.CR = p.CR;
+    a.NG = p.NG;
+    a.ROWS = p.ROWS;
     a.nslots = p.nslots;
-    a.slot_bytes = p.slot_bytes;
-    a.rows_cta_max = p.rows_cta_max;
+    a.tiles_cta_max = p.tiles_cta_max;
     a.err = c->d_err;
     a.wait_ns = wait_limit_ns();
-    k_gemv_g32<<<p.grid, p.block, p.smem, s>>>(a);
-    RB_CUDA(cudaGetLastError());
+    void *args[] = {&a};
+    RB_CUDA(cudaLaunchKernel(gemv_g32_kernel(p.J), dim3(p.grid), dim3(p.block), args, p.smem, s));
     return RABBIT_CUDA_OK;
 }
 
@@ -88,11 +86,10 @@ int rabbit_cuda_gemv_int4_grouped(const uint8_t *W, const float *x, float *y, in
     if (!c) return st;
     std::lock_guard<std::mutex> g(c->mu);
     const size_t xb = align_up((size_t)in_dim * 4, 256), yb = align_up((size_t)out_dim * 4, 256);
-    const bool fast = gs == 32 && g32_ok(in_dim);
-    const int rows_pad = (out_dim + 3) / 4 * 4;
-    const size_t nibb = align_up((size_t)rows_pad * (in_dim / 2), 256);
-    const size_t scb = align_up((size_t)rows_pad * (in_dim / 32) * 4, 256);
-    const size_t wb = fast ? nibb + scb : align_up(nbytes, 256);
+    G32Plan p;
+    const bool fast = gs == 32 && plan_g32(out_dim, in_dim, c->sm_count, &p);
+    const size_t tb = fast ? (size_t)p.til.ntiles * p.til.tile_stride : 0;
+    const size_t wb = fast ? align_up(tb, 256) : align_up(nbytes, 256);
     if ((st = ensure_dscratch(c, wb + xb + yb)) != RABBIT_CUDA_OK) return st;
     uint8_t *dw = static_cast<uint8_t *>(c->dscratch);
     float *dx = reinterpret_cast<float *>(dw + wb);
@@ -100,17 +97,12 @@ int rabbit_cuda_gemv_int4_grouped(const uint8_t *W, const float *x, float *y, in
     cudaStream_t s = c->stream;
     RB_CUDA(cudaMemcpyAsync(dx, x, (size_t)in_dim * 4, cudaMemcpyHostToDevice, s));
     if (fast) {
-        G32Plan p;
-        if (!plan_g32(out_dim, in_dim, c->sm_count, &p))
-            return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "gemv: no streaming plan for %dx%d", out_dim,
-                        in_dim);
-        const size_t n = (size_t)out_dim * in_dim;
-        uint8_t *dnib = dw;
-        float *dsc = reinterpret_cast<float *>(dw + nibb);
-        if (rows_pad != out_dim) RB_CUDA(cudaMemsetAsync(dw, 0, wb, s));
-        RB_CUDA(cudaMemcpyAsync(dsc, W + 4, n / 32 * 4, cudaMemcpyHostToDevice, s));
-        RB_CUDA(cudaMemcpyAsync(dnib, W + 4 + n / 32 * 4, n / 2, cudaMemcpyHostToDevice, s));
-        if ((st = launch_g32(p, dnib, dsc, dx, dy, c, s)) != RABBIT_CUDA_OK) return st;
+        // tile on the host into pinned memory, one copy to the device
+        if ((st = ensure_pinned(c, tb)) != RABBIT_CUDA_OK) return st;
+        RB_CUDA(cudaStreamSynchronize(s));  // pinned buffer is free
+        tile_blob_host(W, p.til, static_cast<uint8_t *>(c->pin));
+        RB_CUDA(cudaMemcpyAsync(dw, c->pin, tb, cudaMemcpyHostToDevice, s));
+        if ((st = launch_g32(p, dw, dx, dy, c, s)) != RABBIT_CUDA_OK) return st;
     } else {
         RB_CUDA(cudaMemcpyAsync(dw, W, nbytes, cudaMemcpyHostToDevice, s));
         if ((st = launch_flat(dw, dx, dy, out_dim, in_dim, s)) != RABBIT_CUDA_OK) return st;
@@ -171,24 +163,18 @@ int rabbit_cuda_matrix_upload(const uint8_t *blob, int out_dim, int in_dim,
     m->device = c->device;
     m->rows = out_dim;
     m->in_dim = in_dim;
-    m->rows_pad = (out_dim + 3) / 4 * 4;
     m->group_size = gs;
     m->blob_bytes = nbytes;
     m->fast = gs == 32 && plan_g32(out_dim, in_dim, c->sm_count, &m->plan);
     cudaError_t e;
     if (m->fast) {
-        const size_t n = (size_t)out_dim * in_dim;
-        const size_t nibb = (size_t)m->rows_pad * (in_dim / 2);
-        const size_t scb = (size_t)m->rows_pad * (in_dim / 32) * 4;
-        if ((e = cudaMalloc(&m->nib, nibb)) != cudaSuccess ||
-            (e = cudaMalloc(&m->sc, scb)) != cudaSuccess ||
-            (e = cudaMemset(m->nib, 0, nibb)) != cudaSuccess ||
-            (e = cudaMemset(m->sc, 0, scb)) != cudaSuccess ||
-            (e = cudaMemcpy(m->sc, blob + 4, n / 32 * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(m->nib, blob + 4 + n / 32 * 4, n / 2, cudaMemcpyHostToDevice)) !=
-                cudaSuccess) {
+        const size_t tb = (size_t)m->plan.til.ntiles * m->plan.til.tile_stride;
+        std::vector<uint8_t> img(tb);
+        tile_blob_host(blob, m->plan.til, img.data());
+        if ((e = cudaMalloc(&m->tiles, tb)) != cudaSuccess ||
+            (e = cudaMemcpy(m->tiles, img.data(), tb, cudaMemcpyHostToDevice)) != cudaSuccess) {
             rabbit_cuda_matrix_free(m);
-            return cuda_fail(e, "matrix_upload (planes)");
+            return cuda_fail(e, "matrix_upload (tiles)");
         }
     } else {
         if ((e = cudaMalloc(&m->raw, nbytes)) != cudaSuccess ||
@@ -206,8 +192,7 @@ int rabbit_cuda_matrix_free(rabbit_cuda_matrix *m) {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(m->device);
-    if (m->nib) cudaFree(m->nib);
-    if (m->sc) cudaFree(m->sc);
+    if (m->tiles) cudaFree(m->tiles);
     if (m->raw) cudaFree(m->raw);
     cudaSetDevice(prev);
     delete m;
@@ -224,7 +209,7 @@ int rabbit_cuda_matrix_gemv_dev(const rabbit_cuda_matrix *m, const float *d_x, f
     if (m->fast) {
         if ((reinterpret_cast<uintptr_t>(d_x) & 15) != 0)
             return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_dev: x must be 16-byte aligned");
-        st = launch_g32(m->plan, m->nib, m->sc, d_x, d_y, c, s);
+        st = launch_g32(m->plan, m->tiles, d_x, d_y, c, s);
     } else if (m->group_size == 0 || m->group_size > 4096) {
         RB_CUDA(cudaMemsetAsync(d_y, 0, (size_t)m->rows * 4, s));
         st = RABBIT_CUDA_OK;

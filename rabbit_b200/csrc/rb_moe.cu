@@ -7,13 +7,15 @@
 // cudaMemcpyAsync on a side stream (double buffered: the host fills one
 // buffer while the other is in flight).
 //
-// Group-32 int4 records are re-laid out on the way in: each of gate / up /
-// down is split into a 256-byte aligned nibble plane [rows][in/2] and scale
-// plane [rows][in/32] -- the packed values are the same bytes, only moved --
-// so kernels can bulk-copy whole row chunks. Other formats are kept verbatim.
+// Group-32 int4 records are re-laid out on the way in -- the packed values
+// are the same bytes, only moved -- into row tiles the kernels fetch with one
+// bulk copy each: [GU tiles: TRb rows of gate nibbles | up nibbles | gate
+// scales | up scales] over the I rows, then [D tiles: TRc rows of down
+// nibbles | scales] over the H rows. Other formats are kept verbatim.
 #include <string.h>
 
 #include <algorithm>
+#include <numeric>
 #include <vector>
 
 #include "rb_gemv.cuh"
@@ -32,10 +34,6 @@ inline uint64_t mix_host(uint64_t seed, uint64_t r) {
     return z ^ (z >> 33);
 }
 
-struct Segment {
-    uint64_t src, len, dst;  // offsets in the host record / pool record
-};
-
 }  // namespace
 
 struct rabbit_cuda_moe {
@@ -50,8 +48,7 @@ struct rabbit_cuda_moe {
     // pool
     uint8_t *pool = nullptr;
     uint64_t rec_stride = 0, pool_bytes = 0;
-    uint64_t off_gnib = 0, off_unib = 0, off_dnib = 0, off_gsc = 0, off_usc = 0, off_dsc = 0;
-    std::vector<Segment> segs;
+    uint64_t off_d = 0;  // GU tiles at 0, D tiles at off_d (group-32 layout)
     std::vector<uint8_t> resident;
     // dense per-layer inputs
     float *rms = nullptr, *router = nullptr;
@@ -59,11 +56,12 @@ struct rabbit_cuda_moe {
     float *scores = nullptr, *mid = nullptr, *xn = nullptr, *down = nullptr;
     float *h_in = nullptr, *h_out = nullptr, *w_int = nullptr;
     int *ids_int = nullptr;
-    unsigned *bar = nullptr;
+    unsigned long long *bar = nullptr;
     rb::Route *route = nullptr;
     // upload machinery
     cudaStream_t up = nullptr;
     void *pin[2] = {nullptr, nullptr};
+    uint64_t pin_cap = 0;  // bytes per pinned staging buffer
     cudaEvent_t pin_ev[2] = {nullptr, nullptr};
     int pin_next = 0;
     // host-buffer decode staging
@@ -74,6 +72,7 @@ struct rabbit_cuda_moe {
     size_t smem = 0;
     // counters
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
+    std::vector<uint8_t> img;  // host image of one record in the tiled layout
 };
 
 namespace rb {
@@ -93,46 +92,61 @@ static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_loca
     return RABBIT_CUDA_OK;
 }
 
+// Shared-memory bytes in front of the ring, in the order k_moe_decode_g32
+// carves them: xn, reduction scratch, slot records/weights, flags, scores.
+static size_t fused_head_bytes(int H, int E) {
+    size_t off = align_up((size_t)(H / 32) * 33 * 4, 128);
+    off += 128 + 2 * (size_t)kMaxSlots * 4;
+    off = align_up(off + 16, 128);
+    off = align_up(off + (size_t)E * 4, 128);
+    return off;
+}
+
 static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     const int H = p->H, I = p->I;
     if (!g32_ok(H) || !g32_ok(I)) return false;
-    const int KSb = (H / 32 + 31) / 32, KSc = (I / 32 + 31) / 32;
-    int CW = std::max(8, std::max(KSb, KSc));
-    if (CW % KSb) CW = (CW / KSb + 1) * KSb;
-    if (CW > 16) CW = std::max(KSb, KSc);
-    if (CW > 16) return false;
     MoeFusedArgs &a = p->plan;
+    a.JB = lane_groups(H / 32);
+    a.KSb = kslices(H / 32, a.JB);
+    a.NGb = std::max(1, kConsumerWarps / a.KSb);  // warp groups in phase B
+    a.JC = lane_groups(I / 32);
+    a.KSc = kslices(I / 32, a.JC);
+    a.NGc = std::max(1, kConsumerWarps / a.KSc);  // warp groups in phase C
+    const int CW = std::max(a.KSb * a.NGb, a.KSc * a.NGc);
     a.CW = CW;
-    a.KSb = KSb;
-    a.RSb = CW / KSb;
-    a.KSc = KSc;
-    a.RSc = CW / KSc;
-    const size_t rb_b = 2 * ((size_t)H / 2 + (size_t)H / 8);  // gate+up bytes per row
-    const size_t rb_c = (size_t)I / 2 + (size_t)I / 8;
-    size_t slot = std::max<size_t>(32 * 1024, std::max(4 * rb_b, 4 * rb_c));
-    slot = align_up(slot, 128);
-    int crb = (int)(slot / rb_b) / 4 * 4, crc = (int)(slot / rb_c) / 4 * 4;
-    crb = std::min(crb, 64);
-    crc = std::min(crc, 64);
-    a.CRb = crb;
-    a.CRc = crc;
-    a.slot_bytes = (uint32_t)slot;
-    const int slots = p->k + p->S;
+    const int slots = std::max(1, p->k + p->S);
     const int G = sm_count;
-    const long long UB = (long long)slots * (I / 4), UC = H / 4;
-    const long long rows_b = 4 * ((UB + G - 1) / G), rows_c = 4 * ((UC + G - 1) / G);
-    a.part_floats = (int)std::max(rows_b * 2 * KSb, rows_c * slots * KSc);
-    const size_t fixed = align_up((size_t)H * 4, 128) + 128 + 2 * kMaxSlots * 4 + 16 + 128 +
-                         align_up((size_t)a.part_floats * 4, 16);
-    long long ns = ((long long)kMaxDynSmem - (long long)fixed - 8 * 64) / (long long)slot;
-    if (ns > 12) ns = 12;
+    const size_t rb_b = (size_t)H / 2 + (size_t)H / 8;  // bytes per row, one matrix
+    const size_t rb_c = (size_t)I / 2 + (size_t)I / 8;
+    // gate+up tiles: the slots' tiles are dealt out over the CTAs; at most 4
+    // rows per warp group (8 values per warp)
+    a.ROWSb = choose_rows(I, slots, true, G, 2 * rb_b, a.NGb, 4, 48 * 1024);
+    // down tiles: CTAs own H rows for every slot
+    a.ROWSc = choose_rows(H, slots, false, G, rb_c, a.NGc, 8, 48 * 1024);
+    const int TRb = a.NGb * a.ROWSb, TRc = a.NGc * a.ROWSc;
+    const int KSb = a.KSb, KSc = a.KSc;
+    a.tb = make_tiling(I, H, TRb);
+    a.tb.tile_bytes *= 2;  // a GU tile holds gate and up rows
+    a.tb.tile_stride = (uint32_t)align_up(a.tb.tile_bytes, 128);
+    a.tc = make_tiling(H, I, TRc);
+    const size_t slot = std::max(a.tb.tile_stride, a.tc.tile_stride);
+    a.slot_bytes = (uint32_t)slot;
+    const long long ub_max = ((long long)slots * a.tb.ntiles + G - 1) / G;
+    const long long tc_max = ((long long)a.tc.ntiles + G - 1) / G;
+    a.part_floats = (int)std::max(ub_max * TRb * 2 * KSb, tc_max * TRc * slots * KSc);
+    const size_t head = fused_head_bytes(H, p->E);
+    const size_t tail = align_up((size_t)a.part_floats * 4, 16);
+    long long ns =
+        ((long long)kMaxDynSmem - (long long)(head + tail) - 16 * 24 - 128) / (long long)slot;
+    if (ns > 24) ns = 24;
     if (ns < 2) return false;
     a.nslots = (int)ns;
-    p->smem = align_up(align_up((size_t)H * 4, 128) + 128 + 2 * kMaxSlots * 4 + 16, 128) +
-              (size_t)ns * slot + align_up((size_t)a.part_floats * 4, 16) + 8 * 2 * ns;
+    p->smem = head + (size_t)ns * slot + tail + 16 * (size_t)ns + 4 * 32;
     if (p->smem > (size_t)kMaxDynSmem) return false;
     p->block = (CW + 1) * 32;
     p->grid = G;
+    p->off_d = align_up((size_t)a.tb.ntiles * a.tb.tile_stride, 256);
+    p->rec_stride = p->off_d + align_up((size_t)a.tc.ntiles * a.tc.tile_stride, 256);
     return true;
 }
 
@@ -152,23 +166,39 @@ static void free_pool(rabbit_cuda_moe *p) {
     delete p;
 }
 
+// Copy `n` host bytes to device memory through the two pinned staging
+// buffers on the side stream (the host fills one while the other is in flight).
+static int stage_h2d(rabbit_cuda_moe *p, uint8_t *dst, const uint8_t *src, uint64_t n) {
+    for (uint64_t done = 0; done < n;) {
+        const uint64_t m = std::min<uint64_t>(p->pin_cap, n - done);
+        const int b = p->pin_next;
+        p->pin_next ^= 1;
+        RB_CUDA(cudaEventSynchronize(p->pin_ev[b]));  // buffer b free again
+        memcpy(p->pin[b], src + done, m);
+        RB_CUDA(cudaMemcpyAsync(dst + done, p->pin[b], m, cudaMemcpyHostToDevice, p->up));
+        RB_CUDA(cudaEventRecord(p->pin_ev[b], p->up));
+        p->h2d_bytes += m;
+        done += m;
+    }
+    return RABBIT_CUDA_OK;
+}
+
 static int upload_record(rabbit_cuda_moe *p, int gid) {
     const uint8_t *src = p->host_map + (uint64_t)gid * p->expert_size;
     uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
-    for (const Segment &sg : p->segs) {
-        for (uint64_t done = 0; done < sg.len;) {
-            const uint64_t n = std::min<uint64_t>(kPinChunk, sg.len - done);
-            const int b = p->pin_next;
-            p->pin_next ^= 1;
-            RB_CUDA(cudaEventSynchronize(p->pin_ev[b]));  // buffer b free again
-            memcpy(p->pin[b], src + sg.src + done, n);
-            RB_CUDA(cudaMemcpyAsync(dst + sg.dst + done, p->pin[b], n, cudaMemcpyHostToDevice,
-                                    p->up));
-            RB_CUDA(cudaEventRecord(p->pin_ev[b], p->up));
-            p->h2d_bytes += n;
-            done += n;
-        }
+    int st;
+    if (p->fast) {
+        // gate / up / down blobs -> [GU tiles][D tiles] in a host image
+        const uint64_t nb = nbytes_g32((uint64_t)p->H * p->I);
+        p->img.resize(p->rec_stride);
+        Tiling t2 = p->plan.tb;
+        tile_pair_host(src, src + nb, t2, p->img.data());
+        tile_blob_host(src + 2 * nb, p->plan.tc, p->img.data() + p->off_d);
+        st = stage_h2d(p, dst, p->img.data(), p->rec_stride);
+    } else {
+        st = stage_h2d(p, dst, src, p->expert_size);
     }
+    if (st != RABBIT_CUDA_OK) return st;
     p->resident[gid] = 1;
     p->uploads++;
     return RABBIT_CUDA_OK;
@@ -190,15 +220,20 @@ __global__ void k_fill_bytes(uint8_t *dst, uint64_t n, uint64_t seed) {
         reinterpret_cast<uint64_t *>(dst)[i] = mix64(seed ^ (i * 0xD1B54A32D192ED03ull));
 }
 
-// |N(0, sigma)| / 7 per element (Box-Muller on two hashed uniforms).
-__global__ void k_fill_scales(float *dst, uint64_t n, uint64_t seed, float sigma) {
+// |N(0, sigma)| / 7 per scale (Box-Muller on two hashed uniforms); the scales
+// of tile t are n_per_tile floats at base + t*stride + off.
+__global__ void k_fill_scales(uint8_t *base, int ntiles, uint32_t stride, uint32_t off,
+                              uint32_t n_per_tile, uint64_t seed, float sigma) {
+    const uint64_t n = (uint64_t)ntiles * n_per_tile;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
+        float *dst = reinterpret_cast<float *>(base + (i / n_per_tile) * stride + off) +
+                     i % n_per_tile;
         const uint64_t h = mix64(seed ^ (i * 0xA24BAED4963EE407ull));
         const float u1 = ((uint32_t)(h >> 40) + 1) * (1.0f / 16777217.0f);
         const float u2 = (uint32_t)(h & 0xFFFFFF) * (1.0f / 16777216.0f);
         const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-        dst[i] = fabsf(z) * sigma / 7.0f;
+        *dst = fabsf(z) * sigma / 7.0f;
     }
 }
 
@@ -269,22 +304,7 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     if (p->fast && !plan_fused(p, c->sm_count)) p->fast = false;
 
     cudaError_t e = cudaSuccess;
-    if (p->fast) {
-        const uint64_t hn = mat / 2, hs = mat / 8, nb = nbytes_g32(mat);
-        p->off_gnib = 0;
-        p->off_unib = align_up(hn, 256);
-        p->off_dnib = p->off_unib + align_up(hn, 256);
-        p->off_gsc = p->off_dnib + align_up(hn, 256);
-        p->off_usc = p->off_gsc + align_up(hs, 256);
-        p->off_dsc = p->off_usc + align_up(hs, 256);
-        p->rec_stride = p->off_dsc + align_up(hs, 256);
-        p->segs = {{4, hs, p->off_gsc},          {4 + hs, hn, p->off_gnib},
-                   {nb + 4, hs, p->off_usc},     {nb + 4 + hs, hn, p->off_unib},
-                   {2 * nb + 4, hs, p->off_dsc}, {2 * nb + 4 + hs, hn, p->off_dnib}};
-    } else {
-        p->rec_stride = align_up(p->expert_size, 256);
-        p->segs = {{0, p->expert_size, 0}};
-    }
+    if (!p->fast) p->rec_stride = align_up(p->expert_size, 256);  // verbatim records
     p->pool_bytes = p->rec_stride * (uint64_t)p->n_records;
     p->resident.assign(p->n_records, 0);
 
@@ -307,16 +327,19 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         (e = cudaMalloc(&p->h_out, sizeof(float) * p->H)) != cudaSuccess ||
         (e = cudaMalloc(&p->w_int, sizeof(float) * 8)) != cudaSuccess ||
         (e = cudaMalloc(&p->ids_int, sizeof(int) * 8)) != cudaSuccess ||
-        (e = cudaMalloc(&p->bar, sizeof(unsigned) * 2)) != cudaSuccess ||
+        (e = cudaMalloc(&p->bar, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaMalloc(&p->route, sizeof(Route))) != cudaSuccess ||
-        (e = cudaMemset(p->bar, 0, sizeof(unsigned) * 2)) != cudaSuccess ||
+        (e = cudaMemset(p->bar, 0, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 16))) !=
             cudaSuccess) {
         free_pool(p);
         return cuda_fail(e, "moe_create: scratch");
     }
-    const uint64_t pin_bytes = std::min<uint64_t>(kPinChunk, align_up(p->expert_size, 4096));
+    // staging holds up to one record image (verbatim or tiled, whichever is larger)
+    const uint64_t pin_bytes =
+        std::min<uint64_t>(kPinChunk, align_up(std::max<uint64_t>(p->expert_size, p->rec_stride), 4096));
+    p->pin_cap = pin_bytes;
     for (int i = 0; i < 2; ++i) {
         if ((e = cudaMallocHost(&p->pin[i], pin_bytes)) != cudaSuccess ||
             (e = cudaEventCreateWithFlags(&p->pin_ev[i], cudaEventDisableTiming)) !=
@@ -336,17 +359,19 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         }
     }
     if (p->fast && !g_moe_attr[device]) {
-        if ((e = cudaFuncSetAttribute(k_moe_decode_g32, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kMaxDynSmem)) != cudaSuccess) {
-            free_pool(p);
-            return cuda_fail(e, "moe_create: smem attribute");
-        }
+        for (const void *k : {moe_fused_kernel(1, 1), moe_fused_kernel(1, 2), moe_fused_kernel(2, 1),
+                              moe_fused_kernel(2, 2)})
+            if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kMaxDynSmem)) != cudaSuccess) {
+                free_pool(p);
+                return cuda_fail(e, "moe_create: smem attribute");
+            }
         g_moe_attr[device] = true;
     }
     if (p->fast) {
         int per_sm = 0;
-        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode_g32,
-                                                               p->block, p->smem)) !=
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                 &per_sm, moe_fused_kernel(p->plan.JB, p->plan.JC), p->block, p->smem)) !=
                 cudaSuccess ||
             per_sm < 1) {
             free_pool(p);
@@ -389,18 +414,19 @@ int rabbit_cuda_moe_fill_synthetic(rabbit_cuda_moe *p, uint64_t seed, float scal
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_fill_synthetic: pool is not in the group-32 layout");
     RB_CUDA(cudaSetDevice(p->device));
-    const uint64_t mat = (uint64_t)p->H * p->I;
     const int blocks = p->ctx->sm_count * 8;
+    const Tiling &tb = p->plan.tb, &tc = p->plan.tc;
     for (int r = 0; r < p->n_records; ++r) {
         uint8_t *rec = p->pool + (uint64_t)r * p->rec_stride;
         const uint64_t s0 = mix_host(seed, (uint64_t)r);
-        const uint64_t nibs[3] = {p->off_gnib, p->off_unib, p->off_dnib};
-        const uint64_t scs[3] = {p->off_gsc, p->off_usc, p->off_dsc};
-        for (int m = 0; m < 3; ++m) {
-            k_fill_bytes<<<blocks, 256, 0, p->up>>>(rec + nibs[m], mat / 2, s0 + 2 * m);
-            k_fill_scales<<<blocks, 256, 0, p->up>>>(reinterpret_cast<float *>(rec + scs[m]),
-                                                     mat / 32, s0 + 2 * m + 1, scale_sigma);
-        }
+        // nibbles everywhere (uniform bytes), then the scale blocks of each tile
+        k_fill_bytes<<<blocks, 256, 0, p->up>>>(rec, p->rec_stride, s0);
+        k_fill_scales<<<blocks, 256, 0, p->up>>>(rec, tb.ntiles, tb.tile_stride,
+                                                 (uint32_t)(2 * (size_t)tb.TR * (p->H / 2)),
+                                                 2 * tb.TR * (p->H / 32), s0 + 1, scale_sigma);
+        k_fill_scales<<<blocks, 256, 0, p->up>>>(rec + p->off_d, tc.ntiles, tc.tile_stride,
+                                                 (uint32_t)((size_t)tc.TR * (p->I / 2)),
+                                                 tc.TR * (p->I / 32), s0 + 2, scale_sigma);
         p->resident[r] = 1;
     }
     RB_CUDA(cudaGetLastError());
@@ -440,12 +466,7 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         a.router = router;
         a.pool = p->pool;
         a.rec_stride = p->rec_stride;
-        a.off_gnib = p->off_gnib;
-        a.off_unib = p->off_unib;
-        a.off_dnib = p->off_dnib;
-        a.off_gsc = p->off_gsc;
-        a.off_usc = p->off_usc;
-        a.off_dsc = p->off_dsc;
+        a.off_d = p->off_d;
         a.rec_base = base;
         a.n_local = n_local;
         a.H = p->H;
@@ -460,7 +481,7 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         a.err = p->ctx->d_err;
         a.wait_ns = wait_limit_ns();
         void *args[] = {&a};
-        RB_CUDA(cudaLaunchCooperativeKernel((const void *)k_moe_decode_g32, dim3(p->grid),
+        RB_CUDA(cudaLaunchCooperativeKernel(moe_fused_kernel(a.JB, a.JC), dim3(p->grid),
                                             dim3(p->block), args, p->smem, s));
     } else {
         MoeGenericArgs a;
@@ -505,7 +526,7 @@ int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream) {
     int st = check_device_error(p->ctx, s, "moe_decode");
     if (st != RABBIT_CUDA_OK) {
         // a barrier that gave up may have left arrivals behind: start clean
-        cudaMemsetAsync(p->bar, 0, sizeof(unsigned) * 2, s);
+        cudaMemsetAsync(p->bar, 0, sizeof(unsigned long long), s);
         cudaStreamSynchronize(s);
         return st;
     }

@@ -3,6 +3,7 @@
 #include <stdint.h>
 
 #include "rb_device.cuh"
+#include "rb_gemv.cuh"
 
 namespace rb {
 
@@ -24,23 +25,29 @@ struct MoeFusedArgs {
     const float *router;  // [E, H]
     const uint8_t *pool;
     uint64_t rec_stride;
-    uint64_t off_gnib, off_unib, off_dnib, off_gsc, off_usc, off_dsc;
+    uint64_t off_d;  // record = [GU tiles (gate+up pairs over I rows)] [D tiles over H rows]
+    Tiling tb;       // GU tiling: rows I, in H, tile_bytes/stride of the gate+up pair
+    Tiling tc;       // D tiling: rows H, in I
     int rec_base;  // global record of local expert 0 in this layer
     int n_local;   // local ids >= n_local have no record (skipped)
     int H, E, k, I, S;
     int usable;    // 0: records too small, experts add nothing (forward_v2.c:319-322)
     float *scores; // scratch [E]
     float *mid;    // scratch [k+S][I]
-    unsigned *bar; // scratch [2]: arrival count, generation
+    unsigned long long *bar; // scratch: grid-barrier arrival counter
     int *err;
     uint64_t wait_ns;
-    // plan
-    int CW, KSb, RSb, CRb, KSc, RSc, CRc, nslots;
+    // plan: CW consumer warps; phase B (gate/up, in = H) uses KSb warps per
+    // row, NGb warp groups of ROWSb rows per tile, JB groups per lane; phase C
+    // (down, in = I) likewise with KSc, NGc, ROWSc, JC
+    int CW, KSb, NGb, ROWSb, JB, KSc, NGc, ROWSc, JC, nslots;
     uint32_t slot_bytes;
     int part_floats;
 };
 
-__global__ void k_moe_decode_g32(MoeFusedArgs a);
+// k_moe_decode_g32<JB, JC> for JB / JC groups of 32 per lane in phases B / C
+// (1 or 2 each); cooperative launch with one MoeFusedArgs argument.
+const void *moe_fused_kernel(int JB, int JC);
 
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine
 struct MoeGenericArgs {

@@ -6,13 +6,14 @@
 //      rows c, c+grid, ... -> scores.            [grid barrier 1]
 //      every CTA: top-k + softmax on the scores (identical in all CTAs), the
 //      active slot list (routed in rank order, then shared experts).
-//   B. gate/up: the active slots' gate and up rows, flattened and split evenly
-//      over CTAs in units of 4 rows; the producer warp bulk-copies chunks of
-//      gate+up rows (nibbles + scales) into the shared-memory ring; consumer
-//      warps dot them against xn held in registers (one group of 32 per lane);
-//      mid = silu(gate) * up goes to global scratch.
-//   C. down + combine: each CTA owns 4-row units of the H outputs for every
-//      active slot; the producer keeps issuing these W2 chunks as soon as
+//   B. gate/up: the active slots' GU tiles (TRb rows of gate and of up,
+//      nibbles + scales, one contiguous block) dealt out evenly over the
+//      CTAs; the producer warp bulk-copies them into the shared-memory ring;
+//      eight consumer warps dot them against xn held in registers (JB groups
+//      of 32 per lane, ROWSb rows per warp group and tile, both fixed at
+//      compile time); mid = silu(gate) * up goes to global scratch.
+//   C. down + combine: each CTA owns D tiles (TRc rows of the H outputs) for
+//      every active slot; the producer keeps issuing these W2 chunks as soon as
 //      ring stages free up -- before and during grid barrier 2 -- so the down
 //      weights are in flight while the last gate/up rows finish. Consumers
 //      reload x = mid[slot] per slot and combine h_out = h + sum_j w_j down_j
@@ -24,32 +25,46 @@
 
 namespace rb {
 
+#ifdef RB_PHASE_TIMERS
+// Diagnostic build only: per-CTA %globaltimer stamps at phase boundaries, and
+// for CTA 0 the producer's issue time and consumer warp 0's wait / ready /
+// done times of each of the first 64 chunks.
+__device__ uint64_t g_phase_ns[1024 * 8];
+__device__ uint64_t g_chunk_ns[4 * 64];
+#define RB_CHUNK(kind, i)                                                              \
+    do {                                                                               \
+        if (blockIdx.x == 0 && (i) < 64) g_chunk_ns[(kind) * 64 + (i)] = globaltimer_ns(); \
+    } while (0)
+#define RB_STAMP(i)                                                        \
+    do {                                                                   \
+        if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = globaltimer_ns(); \
+    } while (0)
+#else
+#define RB_STAMP(i) \
+    do {            \
+    } while (0)
+#define RB_CHUNK(kind, i) \
+    do {                  \
+    } while (0)
+#endif
+
 // ---------------------------------------------------------- grid barrier --
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// One thread per CTA. bar[0] counts arrivals, bar[1] is the generation.
-__device__ bool grid_barrier(unsigned *bar, unsigned nblocks, uint64_t wait_ns, int *err) {
-    const unsigned gen = ld_acquire_u32(bar + 1);
-    __threadfence();
-    const unsigned prev = atomicAdd(bar, 1u);
-    if (prev == nblocks - 1) {
-        atomicExch(bar, 0u);
-        __threadfence();
-        st_release_u32(bar + 1, gen + 1);
-        return true;
-    }
+// One thread per CTA. *count is a monotonic 64-bit arrival counter (zeroed at
+// pool creation and after any failed wait); every barrier adds exactly
+// gridDim.x, so the round ends at the next multiple of nblocks. One
+// release-atomic to arrive, acquire loads to wait: a single L2 round trip on
+// the critical path.
+__device__ bool grid_barrier(unsigned long long *count, unsigned nblocks, uint64_t wait_ns,
+                             int *err) {
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(count) : "memory");
+    const unsigned long long target = old - old % nblocks + nblocks;
     const uint64_t t0 = globaltimer_ns();
-    for (unsigned it = 1;; ++it) {
-        if (ld_acquire_u32(bar + 1) != gen) return true;
-        if ((it & 31u) == 0 && globaltimer_ns() - t0 > wait_ns) {
+    for (unsigned it = 0;; ++it) {
+        unsigned long long v;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(count) : "memory");
+        if (v >= target) return true;
+        if ((it & 15u) == 15u && globaltimer_ns() - t0 > wait_ns) {
             set_error(err, RB_ERR_TIMEOUT);
             return false;
         }
@@ -65,7 +80,7 @@ __device__ void topk_softmax(const float *scores, int E, int k, int *ids, float 
         w[i] = -1e30f;
     }
     for (int e = 0; e < E; ++e) {
-        const float s = __ldcg(scores + e);
+        const float s = scores[e];
         int slot = 0;
         while (slot < k && !(s > w[slot])) ++slot;
         if (slot == k) continue;
@@ -114,45 +129,78 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return (g * sg) * u;
 }
 
-// Phase-B cursor: 4-row units over the flattened (slot, row) space of I rows
-// per slot; a chunk never crosses a slot boundary.
-__device__ __forceinline__ bool next_b(int &u, int ub1, int I, int CR, int &slot, int &r,
-                                       int &rows) {
-    if (u >= ub1) return false;
-    const int per = I >> 2;
-    slot = u / per;
-    r = (u - slot * per) * 4;
-    rows = min(CR, min(4 * (ub1 - u), I - r));
-    u += rows >> 2;
+// Release a stage this warp has no rows of (its wait has completed).
+__device__ __forceinline__ void release_stage(uint64_t *empty) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(empty, 1);
+}
+
+// Phase B for one consumer warp: the CTA's units [ub0, ub1) (slot, GU tile),
+// ROWS rows of gate and of up per tile from rbase. `i` counts ring stages.
+template <int J, int ROWS>
+__device__ __forceinline__ bool moe_gate_up(const MoeFusedArgs &a, const uint8_t *ring,
+                                            float *part, uint64_t *full, uint64_t *empty,
+                                            uint32_t *sink, int ub0, int ub1, int &i, int ks,
+                                            int rbase, bool mine, int g0, const bool (&act)[J],
+                                            const XPlanes (&xg)[J]) {
+    const int KS = a.KSb, TRb = a.tb.TR, Hh = a.H >> 1, Gb = a.H >> 5;
+    for (int u = ub0; u < ub1; ++u, ++i) {
+        const int s = i % a.nslots, n = i / a.nslots;
+        if (threadIdx.x == 0) RB_CHUNK(1, i);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) return false;
+        if (threadIdx.x == 0) RB_CHUNK(2, i);
+        const int lb = (u - ub0) * TRb + rbase;
+        if (mine)
+            chunk_dot<2, ROWS, J>(ring + (size_t)s * a.slot_bytes, TRb, rbase, Hh, Gb, g0, act, xg,
+                                  [=](int m, int r) { return ((lb + r) * 2 + m) * KS + ks; },
+                                  part, &empty[s], 1u, sink);
+        else
+            release_stage(&empty[s]);
+        if (threadIdx.x == 0) RB_CHUNK(3, i);
+    }
     return true;
 }
 
-__device__ __forceinline__ void load_x32(float (&xr)[32], const float *src, bool act, bool l2) {
-    if (act) {
-        const float4 *p = reinterpret_cast<const float4 *>(src);
+// Phase C for one consumer warp: for every active slot, the CTA's D tiles
+// [c0, c1), ROWS rows of each from rbase, x = mid of the slot.
+template <int J, int ROWS>
+__device__ __forceinline__ bool moe_down(const MoeFusedArgs &a, const uint8_t *ring, float *part,
+                                         uint64_t *full, uint64_t *empty, uint32_t *sink,
+                                         int nact, int c0, int c1, int &i, int ks, int rbase,
+                                         bool mine, int g0, const bool (&act)[J]) {
+    const int KS = a.KSc, TRc = a.tc.TR, Ih = a.I >> 1, Gc = a.I >> 5;
+    XPlanes xg[J];
+    for (int j = 0; j < nact; ++j) {
+        // x = mid of this slot (written by all CTAs before grid barrier 2)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float4 t = l2 ? __ldcg(p + j) : p[j];
-            xr[4 * j] = t.x;
-            xr[4 * j + 1] = t.y;
-            xr[4 * j + 2] = t.z;
-            xr[4 * j + 3] = t.w;
+        for (int q = 0; q < J; ++q)
+            load_xplanes_global(xg[q], a.mid + (size_t)j * a.I + (size_t)(g0 + 32 * q) * 32, act[q]);
+        for (int t = c0; t < c1; ++t, ++i) {
+            const int s = i % a.nslots, n = i / a.nslots;
+            if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err)))
+                return false;
+            const int lb = (t - c0) * TRc + rbase;
+            if (mine)
+                chunk_dot<1, ROWS, J>(ring + (size_t)s * a.slot_bytes, TRc, rbase, Ih, Gc, g0, act,
+                                      xg, [=](int, int r) { return ((lb + r) * nact + j) * KS + ks; },
+                                      part, &empty[s], 1u, sink);
+            else
+                release_stage(&empty[s]);
         }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) xr[j] = 0.f;
     }
+    return true;
 }
 
-__global__ void __launch_bounds__(17 * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
+template <int JB, int JC>
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nthr = blockDim.x;
     const int H = a.H, I = a.I, CW = a.CW;
-    const int Hh = H >> 1, Ih = I >> 1, Gb = H >> 5, Gc = I >> 5;
+    const int Gb = H >> 5, Gc = I >> 5;
 
     size_t off = 0;
-    float *xn = reinterpret_cast<float *>(smem);
-    off = align_up((size_t)H * 4, 128);
+    float *xn = reinterpret_cast<float *>(smem);  // padded: 33 floats per group of 32
+    off = align_up((size_t)Gb * 33 * 4, 128);
     float *red = reinterpret_cast<float *>(smem + off);
     off += 128;
     int *s_rec = reinterpret_cast<int *>(smem + off);
@@ -161,17 +209,21 @@ __global__ void __launch_bounds__(17 * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     off += kMaxSlots * 4;
     int *s_misc = reinterpret_cast<int *>(smem + off);  // [0] nact [1] abort A [2] abort B
     off = align_up(off + 16, 128);
+    float *s_sc = reinterpret_cast<float *>(smem + off);  // router scores for top-k
+    off = align_up(off + (size_t)a.E * 4, 128);
     uint8_t *ring = smem + off;
     off += (size_t)a.nslots * a.slot_bytes;
     float *part = reinterpret_cast<float *>(smem + off);
     off += align_up((size_t)a.part_floats * 4, 16);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + off);
     uint64_t *empty = full + a.nslots;
+    uint32_t *sink = reinterpret_cast<uint32_t *>(empty + a.nslots);  // one word per warp
 
+    RB_STAMP(0);
     if (tid == 0) {
         for (int s = 0; s < a.nslots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CW);
+            mbar_init(&empty[s], CW);  // every consumer warp releases every stage
         }
         mbar_init_fence();
     }
@@ -193,12 +245,12 @@ __global__ void __launch_bounds__(17 * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     }
     __syncthreads();
     const float inv = red[31];
-    for (int i = tid; i < H; i += nthr) xn[i] = (a.h_in[i] * inv) * a.rms[i];
+    for (int i = tid; i < H; i += nthr) xn[xpad(i)] = (a.h_in[i] * inv) * a.rms[i];
     __syncthreads();
     for (int e = blockIdx.x; e < a.E; e += gridDim.x) {
         const float *wr = a.router + (size_t)e * H;
         float d = 0.f;
-        for (int i = tid; i < H; i += nthr) d += wr[i] * xn[i];
+        for (int i = tid; i < H; i += nthr) d += wr[i] * xn[xpad(i)];
         d = warp_sum(d);
         if (lane == 0) red[warp] = d;
         __syncthreads();
@@ -209,80 +261,71 @@ __global__ void __launch_bounds__(17 * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
         }
         __syncthreads();
     }
+    RB_STAMP(1);
     if (tid == 0) {
-        __threadfence();
         s_misc[1] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
         s_misc[2] = 0;
-        if (!s_misc[1]) {
-            int ids[8];
-            float w[8];
-            topk_softmax(a.scores, a.E, a.k, ids, w);
-            if (blockIdx.x == 0) {
-                for (int i = 0; i < a.k; ++i) {
-                    a.ids_out[i] = ids[i];
-                    a.w_out[i] = w[i];
-                }
-            }
-            s_misc[0] =
-                build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
-        }
     }
     __syncthreads();
     if (s_misc[1]) return;  // nothing in flight yet
+    for (int e = tid; e < a.E; e += nthr) s_sc[e] = __ldcg(a.scores + e);
+    __syncthreads();
+    if (tid == 0) {
+        int ids[8];
+        float w[8];
+        topk_softmax(s_sc, a.E, a.k, ids, w);
+        if (blockIdx.x == 0) {
+            for (int i = 0; i < a.k; ++i) {
+                a.ids_out[i] = ids[i];
+                a.w_out[i] = w[i];
+            }
+        }
+        s_misc[0] = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+    }
+    __syncthreads();
+    RB_STAMP(2);
     const int nact = s_misc[0];
     if (nact == 0) {
         for (int i = blockIdx.x * nthr + tid; i < H; i += gridDim.x * nthr) a.h_out[i] = a.h_in[i];
         return;
     }
 
-    const int UB = nact * (I >> 2);
+    const int ntb = a.tb.ntiles, TRb = a.tb.TR, ntc = a.tc.ntiles, TRc = a.tc.TR;
+    const int UB = nact * ntb;  // phase B units: (slot, GU tile)
     const int ub0 = (int)((long long)blockIdx.x * UB / gridDim.x);
     const int ub1 = (int)((long long)(blockIdx.x + 1) * UB / gridDim.x);
-    const int UC = H >> 2;
-    const int uc0 = (int)((long long)blockIdx.x * UC / gridDim.x);
-    const int uc1 = (int)((long long)(blockIdx.x + 1) * UC / gridDim.x);
-    const int c0 = 4 * uc0, c1 = 4 * uc1;
+    const int c0 = (int)((long long)blockIdx.x * ntc / gridDim.x);  // phase C: D tiles over H
+    const int c1 = (int)((long long)(blockIdx.x + 1) * ntc / gridDim.x);
+    const uint32_t sb = a.tb.tile_stride, sc = a.tc.tile_stride;
 
     if (warp == CW) {  // -------------------------------------------- producer
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             int i = 0;
             bool okp = true;
-            int u = ub0, slot, r, rows;
-            while (okp && next_b(u, ub1, I, a.CRb, slot, r, rows)) {
+            for (int u = ub0; okp && u < ub1; ++u, ++i) {
                 const int s = i % a.nslots, n = i / a.nslots;
-                if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err)) {
+                if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) {
                     okp = false;
                     break;
                 }
-                const uint8_t *rec = a.pool + (size_t)s_rec[slot] * a.rec_stride;
-                const uint32_t nb = (uint32_t)rows * Hh, sb = (uint32_t)rows * (H >> 3);
-                uint8_t *dst = ring + (size_t)s * a.slot_bytes;
-                const size_t cn = (size_t)a.CRb * Hh, cs = (size_t)a.CRb * (H >> 3);
-                mbar_arrive_expect_tx(&full[s], 2 * (nb + sb));
-                bulk_g2s(dst, rec + a.off_gnib + (size_t)r * Hh, nb, &full[s], pol);
-                bulk_g2s(dst + cn, rec + a.off_unib + (size_t)r * Hh, nb, &full[s], pol);
-                bulk_g2s(dst + 2 * cn, rec + a.off_gsc + (size_t)r * (H >> 3), sb, &full[s], pol);
-                bulk_g2s(dst + 2 * cn + cs, rec + a.off_usc + (size_t)r * (H >> 3), sb, &full[s],
-                         pol);
-                ++i;
+                const int slot = u / ntb, t = u - slot * ntb;
+                const uint8_t *src = a.pool + (size_t)s_rec[slot] * a.rec_stride + (size_t)t * sb;
+                RB_CHUNK(0, i);
+                mbar_arrive_expect_tx(&full[s], a.tb.tile_bytes);
+                bulk_g2s(ring + (size_t)s * a.slot_bytes, src, a.tb.tile_bytes, &full[s], pol);
             }
             for (int j = 0; okp && j < nact; ++j) {
-                const uint8_t *rec = a.pool + (size_t)s_rec[j] * a.rec_stride;
-                for (int rr = c0; rr < c1; rr += a.CRc) {
+                const uint8_t *rec = a.pool + (size_t)s_rec[j] * a.rec_stride + a.off_d;
+                for (int t = c0; t < c1; ++t, ++i) {
                     const int s = i % a.nslots, n = i / a.nslots;
-                    if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err)) {
+                    if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) {
                         okp = false;
                         break;
                     }
-                    const int rws = min(a.CRc, c1 - rr);
-                    const uint32_t nb = (uint32_t)rws * Ih, sb = (uint32_t)rws * (I >> 3);
-                    uint8_t *dst = ring + (size_t)s * a.slot_bytes;
-                    mbar_arrive_expect_tx(&full[s], nb + sb);
-                    bulk_g2s(dst, rec + a.off_dnib + (size_t)rr * Ih, nb, &full[s], pol);
-                    bulk_g2s(dst + (size_t)a.CRc * Ih, rec + a.off_dsc + (size_t)rr * (I >> 3), sb,
+                    mbar_arrive_expect_tx(&full[s], a.tc.tile_bytes);
+                    bulk_g2s(ring + (size_t)s * a.slot_bytes, rec + (size_t)t * sc, a.tc.tile_bytes,
                              &full[s], pol);
-                    ++i;
                 }
             }
             // drain: the last use of every stage must have landed before exit
@@ -293,133 +336,108 @@ __global__ void __launch_bounds__(17 * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     }
 
     // ---------------------------------------------------------- consumers --
+    // Warp group q = warp / KS covers one row (KS warps, J groups of 32 inputs
+    // per lane) and takes rows [q*ROWS, (q+1)*ROWS) of every tile; warps past
+    // the phase's NG groups only release. Every consumer waits for and
+    // releases every stage (weight 1), so the ring's phases stay in step
+    // across both phases.
     bool good = true;
     int i = 0;
     {  // B: gate + up
-        const int ks = warp % a.KSb, rsub = warp / a.KSb;
-        const int g = ks * 32 + lane;
-        const bool wact = rsub < a.RSb;
-        const bool act = wact && g < Gb;
-        float xr[32];
-        load_x32(xr, xn + g * 32, act, false);
-        const size_t cn = (size_t)a.CRb * Hh, cs = (size_t)a.CRb * (H >> 3);
-        int u = ub0, slot, r, rows;
-        while (next_b(u, ub1, I, a.CRb, slot, r, rows)) {
-            const int s = i % a.nslots, n = i / a.nslots;
-            if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) {
-                good = false;
-                break;
-            }
-            const uint8_t *st = ring + (size_t)s * a.slot_bytes;
-            const float *gsc = reinterpret_cast<const float *>(st + 2 * cn);
-            const float *usc = reinterpret_cast<const float *>(st + 2 * cn + cs);
-            const int lbase = slot * I + r - 4 * ub0;
-            if (wact) {
-                for (int rb = rsub; rb < rows; rb += 4 * a.RSb) {
-                    float v[8];
+        const int ks = warp % a.KSb, grp = warp / a.KSb;
+        const int g0 = ks * 32 * JB + lane;
+        const bool mine = grp < a.NGb;
+        bool act[JB];
+        XPlanes xg[JB];
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const int rr = rb + b * a.RSb;
-                        v[b] = 0.f;
-                        v[b + 4] = 0.f;
-                        if (act && rr < rows) {
-                            const uint4 wg =
-                                *reinterpret_cast<const uint4 *>(st + (size_t)rr * Hh + g * 16);
-                            const uint4 wu =
-                                *reinterpret_cast<const uint4 *>(st + cn + (size_t)rr * Hh + g * 16);
-                            v[b] = dot32_q64(wg, xr) * (gsc[rr * Gb + g] * 64.f);
-                            v[b + 4] = dot32_q64(wu, xr) * (usc[rr * Gb + g] * 64.f);
-                        }
-                    }
-                    const float tot = warp_reduce8(v);
-                    if ((lane & 3) == 0) {
-                        const int idx = lane >> 2;  // 0..3 gate rows, 4..7 up rows
-                        const int rr = rb + (idx & 3) * a.RSb;
-                        if (rr < rows)
-                            part[((lbase + rr) * 2 + (idx >> 2)) * a.KSb + ks] = tot;
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            ++i;
+        for (int q = 0; q < JB; ++q) {
+            act[q] = mine && g0 + 32 * q < Gb;
+            load_xplanes_padded(xg[q], xn, g0 + 32 * q, act[q]);
+        }
+        const int rbase = grp * a.ROWSb;
+        switch (a.ROWSb) {
+            case 1: good = moe_gate_up<JB, 1>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
+            case 2: good = moe_gate_up<JB, 2>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
+            default: good = moe_gate_up<JB, 4>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
         }
     }
     named_sync(1, CW * 32);
     if (good) {
-        const int nrb = 4 * (ub1 - ub0);
+        const int nrb = (ub1 - ub0) * TRb;
         for (int lr = tid; lr < nrb; lr += CW * 32) {
+            const int u = ub0 + lr / TRb;
+            const int slot = u / ntb, row = (u - slot * ntb) * TRb + lr % TRb;
+            if (row >= I) continue;
             float gs = 0.f, us = 0.f;
             for (int k = 0; k < a.KSb; ++k) {
                 gs += part[(lr * 2) * a.KSb + k];
                 us += part[(lr * 2 + 1) * a.KSb + k];
             }
-            a.mid[4 * ub0 + lr] = silu_mul(gs, us);
+            a.mid[(size_t)slot * I + row] = silu_mul(gs, us);
         }
     }
     __threadfence();
     named_sync(1, CW * 32);
+    RB_STAMP(3);
     if (tid == 0) s_misc[2] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
     named_sync(1, CW * 32);
+    RB_STAMP(4);
     good = good && !s_misc[2];
 
-    {  // C: down + combine
-        const int ks = warp % a.KSc, rsub = warp / a.KSc;
-        const int g = ks * 32 + lane;
-        const bool wact = rsub < a.RSc;
-        const bool act = wact && g < Gc;
-        float xr[32];
-        const size_t cn = (size_t)a.CRc * Ih;
-        for (int j = 0; good && j < nact; ++j) {
-            load_x32(xr, a.mid + (size_t)j * I + g * 32, act, true);
-            for (int rr0 = c0; rr0 < c1; rr0 += a.CRc) {
-                const int rows = min(a.CRc, c1 - rr0);
-                const int s = i % a.nslots, n = i / a.nslots;
-                if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) {
-                    good = false;
-                    break;
-                }
-                const uint8_t *st = ring + (size_t)s * a.slot_bytes;
-                const float *dsc = reinterpret_cast<const float *>(st + cn);
-                if (wact) {
-                    for (int rb = rsub; rb < rows; rb += 8 * a.RSc) {
-                        float v[8];
+    if (good) {  // C: down + combine
+        const int ks = warp % a.KSc, grp = warp / a.KSc;
+        const int g0 = ks * 32 * JC + lane;
+        const bool mine = grp < a.NGc;
+        bool act[JC];
 #pragma unroll
-                        for (int b = 0; b < 8; ++b) {
-                            const int rr = rb + b * a.RSc;
-                            v[b] = 0.f;
-                            if (act && rr < rows) {
-                                const uint4 w =
-                                    *reinterpret_cast<const uint4 *>(st + (size_t)rr * Ih + g * 16);
-                                v[b] = dot32_q64(w, xr) * (dsc[rr * Gc + g] * 64.f);
-                            }
-                        }
-                        const float tot = warp_reduce8(v);
-                        if ((lane & 3) == 0) {
-                            const int rr = rb + (lane >> 2) * a.RSc;
-                            if (rr < rows)
-                                part[((rr0 - c0 + rr) * nact + j) * a.KSc + ks] = tot;
-                        }
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-                ++i;
-            }
+        for (int q = 0; q < JC; ++q) act[q] = mine && g0 + 32 * q < Gc;
+        const int rbase = grp * a.ROWSc;
+        switch (a.ROWSc) {
+            case 1: good = moe_down<JC, 1>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
+            case 2: good = moe_down<JC, 2>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
+            case 4: good = moe_down<JC, 4>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
+            default: good = moe_down<JC, 8>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
         }
     }
     named_sync(1, CW * 32);
+    RB_STAMP(5);
     if (!good) return;
-    for (int lr = tid; lr < c1 - c0; lr += CW * 32) {
+    for (int lr = tid; lr < (c1 - c0) * TRc; lr += CW * 32) {
+        const int row = c0 * TRc + lr;
+        if (row >= H) continue;
         float delta = 0.f;
         for (int j = 0; j < nact; ++j) {
             float d = 0.f;
             for (int k = 0; k < a.KSc; ++k) d += part[(lr * nact + j) * a.KSc + k];
             delta += s_w[j] * d;
         }
-        a.h_out[c0 + lr] = a.h_in[c0 + lr] + delta;
+        a.h_out[row] = a.h_in[row] + delta;
     }
+    RB_STAMP(6);
 }
+
+const void *moe_fused_kernel(int JB, int JC) {
+    if (JB == 2)
+        return JC == 2 ? (const void *)k_moe_decode_g32<2, 2> : (const void *)k_moe_decode_g32<2, 1>;
+    return JC == 2 ? (const void *)k_moe_decode_g32<1, 2> : (const void *)k_moe_decode_g32<1, 1>;
+}
+
+#ifdef RB_PHASE_TIMERS
+}  // namespace rb
+extern "C" __attribute__((visibility("default"))) int rabbit_cuda_debug_phase_ns(uint64_t *out,
+                                                                                 int n) {
+    return cudaMemcpyFromSymbol(out, rb::g_phase_ns, sizeof(uint64_t) * n) == cudaSuccess ? 0 : 6;
+}
+extern "C" __attribute__((visibility("default"))) int rabbit_cuda_debug_dot_ns(uint64_t *out) {
+    int z = 0;
+    cudaMemcpyToSymbol(rb::rb_dbg_i, &z, sizeof(int));
+    return cudaMemcpyFromSymbol(out, rb::rb_dbg_ns, sizeof(uint64_t) * 128) == cudaSuccess ? 0 : 6;
+}
+extern "C" __attribute__((visibility("default"))) int rabbit_cuda_debug_chunk_ns(uint64_t *out) {
+    return cudaMemcpyFromSymbol(out, rb::g_chunk_ns, sizeof(uint64_t) * 256) == cudaSuccess ? 0 : 6;
+}
+namespace rb {
+#endif
 
 // ======================================================= generic path ====
 __device__ __forceinline__ uint32_t ldu32(const uint8_t *p) {

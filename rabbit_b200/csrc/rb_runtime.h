@@ -54,8 +54,8 @@ uint64_t wait_limit_ns();
 // Read and clear the device error word of ctx after synchronising `s`.
 int check_device_error(DevCtx *c, cudaStream_t s, const char *what);
 
-inline cudaStream_t as_stream(void *s, DevCtx *c) {
-    return s ? static_cast<cudaStream_t>(s) : c->stream;
-}
+// A NULL stream argument is the default (legacy) stream, as in CUDA itself,
+// so a caller's stream-0 work and ours stay ordered.
+inline cudaStream_t as_stream(void *s, DevCtx *) { return static_cast<cudaStream_t>(s); }
 
 }  // namespace rb
