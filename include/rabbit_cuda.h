@@ -154,6 +154,27 @@ int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, flo
 /* Same on DEVICE buffers, asynchronous on `stream` (16-byte aligned h). */
 int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                float *d_h_out, int *d_ids, float *d_weights, void *stream);
+/* No counterpart in the reference (its moe_step runs on the CPU). The same
+ * decode as rabbit_cuda_moe_decode_dev, for callers that must not allocate
+ * device memory while they decode: an engine that has already split the
+ * device's memory between its own arenas, or a serving loop that cannot take
+ * the device-wide synchronisation a cudaMalloc/cudaFree brings. The call
+ * allocates nothing and frees nothing; its scratch (router scores, the SwiGLU
+ * activations and a grid-barrier counter) is a fixed 1 MiB array inside this
+ * library, present on every device that loads it until the process exits.
+ * Models whose scratch does not fit -- 256 + E*4 (rounded up to 256) +
+ * (k + S) * I * 4 bytes -- are rejected with RABBIT_CUDA_ERR_ARGS, pools not
+ * in the group-32 layout with RABBIT_CUDA_ERR_UNSUPPORTED. The first call on
+ * each device looks up the array's device address (once, with that device
+ * current); make that first call before any stream capture. Every call uses
+ * the same array, which keeps what the last call left there: the call clears
+ * the counter on `stream` before its kernel, and calls that overlap on the
+ * GPU (other streams, other pools on the same device) race on the array and
+ * give wrong results. d_ids / d_weights may be NULL. Errors surface through
+ * rabbit_cuda_moe_check as for rabbit_cuda_moe_decode_dev. */
+int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                                       float *d_h_out, int *d_ids, float *d_weights,
+                                       void *stream);
 /* Check the device error word after work on `stream` finished (TIMEOUT if a
  * bounded wait gave up). Synchronises `stream`. */
 int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);

@@ -58,6 +58,7 @@ SIGNATURES = {
     "rabbit_cuda_moe_free": (_I, [_P]),
     "rabbit_cuda_moe_decode": (_I, [_P, _I, _P, _P, _P, _P, C.POINTER(_I)]),
     "rabbit_cuda_moe_decode_dev": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "rabbit_cuda_moe_decode_dev_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "rabbit_cuda_moe_check": (_I, [_P, _P]),
     "rabbit_cuda_moe_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
                                    C.POINTER(C.c_uint64), C.POINTER(_I),
@@ -200,6 +201,14 @@ class MoePool:
                    d_w: int = 0, stream: int = 0) -> None:
         check(lib().rabbit_cuda_moe_decode_dev(self.handle, layer, d_h_in, d_h_out,
                                                d_ids or None, d_w or None, stream or None))
+
+    def decode_dev_noalloc(self, layer: int, d_h_in: int, d_h_out: int, d_ids: int = 0,
+                           d_w: int = 0, stream: int = 0) -> None:
+        """decode_dev with the library's fixed scratch array instead of the
+        pool's; allocates nothing (one call at a time per device)."""
+        check(lib().rabbit_cuda_moe_decode_dev_noalloc(self.handle, layer, d_h_in, d_h_out,
+                                                       d_ids or None, d_w or None,
+                                                       stream or None))
 
     def check(self, stream: int = 0) -> None:
         check(lib().rabbit_cuda_moe_check(self.handle, stream or None))

@@ -519,6 +519,92 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
     return ok();
 }
 
+// ------------------------------------------------------- no-alloc decode --
+// Scratch for rabbit_cuda_moe_decode_dev_noalloc, in a fixed array of this
+// module instead of the pool: [0, 256) grid-barrier counter (u64 at 0),
+// routed ids at 64 and weights at 128 when the caller passes none; then the
+// router scores (E floats, 256-aligned); then mid ((k + S) x I floats). Every
+// device that loads the library holds these bytes until the process exits.
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// g_noalloc_scratch names the array only on the host side; its device address
+// on each device, looked up once per device with that device current.
+static uint8_t *g_noalloc_ptr[kMaxDevices];
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(int device, uint8_t **out) {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_decode_noalloc: scratch address");
+        g_noalloc_ptr[device] = static_cast<uint8_t *>(ptr);
+    }
+    *out = g_noalloc_ptr[device];
+    return RABBIT_CUDA_OK;
+}
+
+int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                                       float *d_h_out, int *d_ids, float *d_weights,
+                                       void *stream) {
+    if (!p || !d_h_in || !d_h_out)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: NULL argument");
+    if (!p->fast)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_decode_noalloc: pool is not in the group-32 fused layout");
+    if ((reinterpret_cast<uintptr_t>(d_h_in) & 15) || (reinterpret_cast<uintptr_t>(d_h_out) & 15))
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: h must be 16-byte aligned");
+    const size_t off_scores = 256;
+    const size_t off_mid = off_scores + align_up((size_t)p->E * 4, 256);
+    const size_t need = off_mid + (size_t)std::max(1, p->k + p->S) * p->I * 4;
+    if (need > kNoAllocScratchBytes)
+        return fail(RABBIT_CUDA_ERR_ARGS,
+                    "moe_decode_noalloc: this model needs %zu bytes of scratch, more than the "
+                    "%zu-byte limit",
+                    need, kNoAllocScratchBytes);
+    int base, n_local;
+    int st = layer_map(p, layer, &base, &n_local);
+    if (st) return st;
+    for (int r = 0; r < n_local; ++r)
+        if (!p->resident[base + r])
+            return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: layer %d not uploaded", layer);
+    RB_CUDA(cudaSetDevice(p->device));
+    uint8_t *scratch = nullptr;
+    if ((st = noalloc_scratch(p->device, &scratch)) != RABBIT_CUDA_OK) return st;
+    cudaStream_t s = as_stream(stream, p->ctx);
+    // The counter keeps the last call's value, which a call that gave up may
+    // have left between rounds: every call starts it from zero.
+    RB_CUDA(cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), s));
+    MoeFusedArgs a = p->plan;
+    a.h_in = d_h_in;
+    a.h_out = d_h_out;
+    a.ids_out = d_ids ? d_ids : reinterpret_cast<int *>(scratch + 64);
+    a.w_out = d_weights ? d_weights : reinterpret_cast<float *>(scratch + 128);
+    a.rms = p->rms + (size_t)layer * p->H;
+    a.router = p->router + (size_t)layer * p->H * p->E;
+    a.pool = p->pool;
+    a.rec_stride = p->rec_stride;
+    a.off_d = p->off_d;
+    a.rec_base = base;
+    a.n_local = n_local;
+    a.H = p->H;
+    a.E = p->E;
+    a.k = p->k;
+    a.I = p->I;
+    a.S = p->S;
+    a.usable = p->usable ? 1 : 0;
+    a.scores = reinterpret_cast<float *>(scratch + off_scores);
+    a.mid = reinterpret_cast<float *>(scratch + off_mid);
+    a.bar = reinterpret_cast<unsigned long long *>(scratch);
+    a.err = p->ctx->d_err;
+    a.wait_ns = wait_limit_ns();
+    void *args[] = {&a};
+    RB_CUDA(cudaLaunchCooperativeKernel(moe_fused_kernel(a.JB, a.JC), dim3(p->grid),
+                                        dim3(p->block), args, p->smem, s));
+    p->hbm_hits++;
+    return ok();
+}
+
 int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream) {
     if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_check: NULL pool");
     RB_CUDA(cudaSetDevice(p->device));
