@@ -71,6 +71,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking: has phase `parity` of `bar` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete; false (and *err set) after
 // `limit_ns` nanoseconds. Consumers back off with __nanosleep (doubling up to
 // `max_sleep_ns`) so warps that wait do not spin on the issue slots of the
@@ -129,26 +142,35 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
 // ------------------------------------------------------- int4 dot product --
 // The 32 activations of one group are turned into a 23-bit block-floating-
 // point integer vector: X_i = rint(x_i * 2^(22-e)) with 2^e > max|x_i|, so
-// |X_i| <= 2^22 and the rounding error is at most 2^(e-23) per element. X is
-// split into three signed 8-bit planes, X = P2*2^16 + P1*2^8 + P0 (P0, P1 in
-// [-128, 127], P2 in [-64, 64]). The weights stay unsigned nibbles (bias 8):
-// w & 0x0F0F0F0F holds the even elements of a word as bytes, (w >> 4) &
-// 0x0F0F0F0F the odd ones, and dp4a (u8 x s8) accumulates exact integer plane
-// sums S_p = sum nib_i * P_p,i (|S_p| <= 61440). Then
+// |X_i| <= 2^22 and the rounding error is at most 2^(e-23) per element. The
+// planes are the bytes of X_i's two's-complement form:
+//   X = B2 * 2^16 + B1 * 2^8 + B0,  B0, B1 = bytes 0, 1 (unsigned, 0..255),
+//   B2 = X >> 16 = byte 2 read as a signed int8 (in [-64, 64]).
+// The weights stay unsigned nibbles (bias 8): w & 0x0F0F0F0F holds the even
+// elements of a word as bytes, (w >> 4) & 0x0F0F0F0F the odd ones, and dp4a
+// accumulates exact plane sums S_p = sum nib_i * B_p,i (u8 x u8 for planes 0
+// and 1, |S| <= 122400; u8 x s8 for plane 2, |S2| <= 30720). Then
 //   sum_i q_i X_i = S2 * 65536 + (S1 * 256 + S0 - 8 * sum_i X_i)
 // with the bracket exact in int32; two int->float conversions and one FFMA
 // give the group's dot product, times unit = 2^(e-22).
 struct XPlanes {
-    int lo[3][4];  // plane p, word j: bytes P_p of elements 8j, 8j+2, 8j+4, 8j+6
-    int hi[3][4];  // plane p, word j: bytes P_p of elements 8j+1, 8j+3, 8j+5, 8j+7
-    int m8sum;     // -8 * sum_i X_i  (|.| <= 2^30)
-    float unit;    // 2^(e-22)
+    uint32_t lo[3][4];  // plane p, word j: byte p of X for elements 8j, 8j+2, 8j+4, 8j+6
+    uint32_t hi[3][4];  // plane p, word j: byte p of X for elements 8j+1, 8j+3, 8j+5, 8j+7
+    int m8sum;          // -8 * sum_i X_i  (|.| <= 2^30)
+    float unit;         // 2^(e-22)
 };
 
-// Four small ints -> bytes of one word (b0 in the low byte).
-__device__ __forceinline__ int pack4(int b0, int b1, int b2, int b3) {
-    return (int)__byte_perm(__byte_perm((uint32_t)b0, (uint32_t)b1, 0x0040u),
-                            __byte_perm((uint32_t)b2, (uint32_t)b3, 0x0040u), 0x5410u);
+// Planes 0..2 of four integers a, b, c, d (bytes p of each, a in the low
+// byte): seven byte permutes for the three planes.
+__device__ __forceinline__ void planes4(int a, int b, int c, int d, uint32_t &p0, uint32_t &p1,
+                                        uint32_t &p2) {
+    const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x5140u);  // a0 b0 a1 b1
+    const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x5140u);  // c0 d0 c1 d1
+    p0 = __byte_perm(ab, cd, 0x5410u);
+    p1 = __byte_perm(ab, cd, 0x7632u);
+    const uint32_t ab2 = __byte_perm((uint32_t)a, (uint32_t)b, 0x0062u);  // a2 b2
+    const uint32_t cd2 = __byte_perm((uint32_t)c, (uint32_t)d, 0x0062u);  // c2 d2
+    p2 = __byte_perm(ab2, cd2, 0x5410u);
 }
 
 __device__ __forceinline__ void make_xplanes(XPlanes &g, const float (&x)[32]) {
@@ -160,31 +182,31 @@ __device__ __forceinline__ void make_xplanes(XPlanes &g, const float (&x)[32]) {
     if (e < -100) e = -100;
     const float scale = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e)
     g.unit = __int_as_float((127 - 22 + e) << 23);             // 2^(e-22)
-    int P[3][32];
+    int X[32];
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
         // rint via the 1.5*2^23 shift: exact for |x*scale| <= 2^22
-        const int X = __float_as_int(fmaf(x[i], scale, 12582912.0f)) - 0x4B400000;
-        sum += X;
-        const int p0 = (X << 24) >> 24;
-        const int r = (X - p0) >> 8;
-        const int p1 = (r << 24) >> 24;
-        P[0][i] = p0;
-        P[1][i] = p1;
-        P[2][i] = (r - p1) >> 8;
+        X[i] = __float_as_int(fmaf(x[i], scale, 12582912.0f)) - 0x4B400000;
+        sum += X[i];
     }
     g.m8sum = -8 * sum;
 #pragma unroll
-    for (int p = 0; p < 3; ++p)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            g.lo[p][j] = pack4(P[p][8 * j], P[p][8 * j + 2], P[p][8 * j + 4], P[p][8 * j + 6]);
-            g.hi[p][j] = pack4(P[p][8 * j + 1], P[p][8 * j + 3], P[p][8 * j + 5], P[p][8 * j + 7]);
-        }
+    for (int j = 0; j < 4; ++j) {
+        planes4(X[8 * j], X[8 * j + 2], X[8 * j + 4], X[8 * j + 6], g.lo[0][j], g.lo[1][j],
+                g.lo[2][j]);
+        planes4(X[8 * j + 1], X[8 * j + 3], X[8 * j + 5], X[8 * j + 7], g.hi[0][j], g.hi[1][j],
+                g.hi[2][j]);
+    }
 }
 
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
@@ -199,11 +221,11 @@ __device__ __forceinline__ float dot32(const uint4 w, const XPlanes &g) {
     for (int j = 0; j < 4; ++j) {
         const uint32_t lo = wv[j] & 0x0F0F0F0Fu;
         const uint32_t hi = (wv[j] >> 4) & 0x0F0F0F0Fu;
-        s0 = dp4a_us(lo, g.lo[0][j], s0);
-        s1 = dp4a_us(lo, g.lo[1][j], s1);
+        s0 = dp4a_uu(lo, g.lo[0][j], s0);
+        s1 = dp4a_uu(lo, g.lo[1][j], s1);
         s2 = dp4a_us(lo, g.lo[2][j], s2);
-        s0 = dp4a_us(hi, g.hi[0][j], s0);
-        s1 = dp4a_us(hi, g.hi[1][j], s1);
+        s0 = dp4a_uu(hi, g.hi[0][j], s0);
+        s1 = dp4a_uu(hi, g.hi[1][j], s1);
         s2 = dp4a_us(hi, g.hi[2][j], s2);
     }
     const int low = s1 * 256 + s0 + g.m8sum;
@@ -336,7 +358,7 @@ __device__ __forceinline__ void chunk_dot(const uint8_t *st, int TR, int rbase, 
                                           const XPlanes (&xg)[J], PIdx pidx, float *part,
                                           uint64_t *empty, uint32_t wgt, uint32_t *sink) {
     constexpr int V = NMAT * ROWS;  // values per warp: 1..8
-    static_assert(V >= 1 && V <= 8, "at most 8 values per warp");
+    static_assert(V >= 1 && V * J <= 8, "at most 8 dots per lane and tile");
     const int lane = threadIdx.x & 31;
     const float *scb = reinterpret_cast<const float *>(st + (size_t)NMAT * TR * half);
     uint4 w[V][J];

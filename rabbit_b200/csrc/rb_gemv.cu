@@ -61,15 +61,25 @@ int choose_rows(int rows, int mats, bool spread, int ctas, size_t row_bytes, int
 void tile_blob_host(const uint8_t *blob, const Tiling &t, uint8_t *dst) {
     const size_t n = (size_t)t.rows * t.in_dim;
     const size_t half = t.in_dim / 2, scb = t.in_dim / 8;  // bytes per row
+    const size_t chalf = t.cols / 2, cscb = t.cols / 8;    // bytes per row of one chunk
     const uint8_t *sc = blob + 4;
     const uint8_t *nib = blob + 4 + n / 32 * 4;
-    for (int ti = 0; ti < t.ntiles; ++ti) {
-        uint8_t *d = dst + (size_t)ti * t.tile_stride;
-        const int r0 = ti * t.TR, nr = std::min(t.TR, t.rows - r0);
-        memset(d, 0, t.tile_stride);
-        memcpy(d, nib + (size_t)r0 * half, (size_t)nr * half);
-        memcpy(d + (size_t)t.TR * half, sc + (size_t)r0 * scb, (size_t)nr * scb);
-    }
+    for (int c = 0; c < t.KC; ++c)
+        for (int ti = 0; ti < t.rtiles; ++ti) {
+            uint8_t *d = dst + (size_t)(c * t.rtiles + ti) * t.tile_stride;
+            const int r0 = ti * t.TR, nr = std::min(t.TR, t.rows - r0);
+            memset(d, 0, t.tile_stride);
+            if (t.KC == 1) {
+                memcpy(d, nib + (size_t)r0 * half, (size_t)nr * half);
+                memcpy(d + (size_t)t.TR * half, sc + (size_t)r0 * scb, (size_t)nr * scb);
+                continue;
+            }
+            for (int r = 0; r < nr; ++r) {
+                memcpy(d + (size_t)r * chalf, nib + (size_t)(r0 + r) * half + c * chalf, chalf);
+                memcpy(d + (size_t)t.TR * chalf + (size_t)r * cscb,
+                       sc + (size_t)(r0 + r) * scb + c * cscb, cscb);
+            }
+        }
 }
 
 void tile_pair_host(const uint8_t *a, const uint8_t *b, const Tiling &t2, uint8_t *dst) {
@@ -97,7 +107,7 @@ bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p) {
     p->KS = kslices(G, p->J);
     p->NG = std::max(1, kConsumerWarps / p->KS);
     const size_t row_bytes = (size_t)in_dim / 2 + (size_t)in_dim / 8;
-    p->ROWS = choose_rows(rows, 1, true, sm_count, row_bytes, p->NG, 8, 48 * 1024);
+    p->ROWS = choose_rows(rows, 1, true, sm_count, row_bytes, p->NG, 8 / p->J, 48 * 1024);
     const int TR = p->NG * p->ROWS;
     p->til = make_tiling(rows, in_dim, TR);
     p->grid = p->til.ntiles < sm_count ? p->til.ntiles : sm_count;
@@ -204,7 +214,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_gemv_g32(G32Ar
         case 1: good = gemv_tiles<J, 1>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
         case 2: good = gemv_tiles<J, 2>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
         case 4: good = gemv_tiles<J, 4>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
-        default: good = gemv_tiles<J, 8>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        // ROWS * J <= 8 (the planner never asks for more)
+        default: good = gemv_tiles<J, 8 / J>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
     }
     named_sync(1, CW * 32);
     if (!good) return;

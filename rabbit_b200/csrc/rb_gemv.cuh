@@ -9,23 +9,29 @@ namespace rb {
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // --------------------------------------------------------------- tiling --
-// A matrix [rows, in] in HBM as tiles of TR rows; tile t holds rows
-// [t*TR, t*TR + TR): the packed nibbles (TR x in/2 bytes, row-major) followed by
-// the group scales (TR x in/32 fp32). Tiles sit tile_stride bytes apart; rows
-// past the end of the matrix are zero. One tile is one bulk copy.
+// A matrix [rows, in] in HBM as tiles of TR rows x cols = in / KC inputs
+// (KC column chunks, 1 unless stated): tile (c, t), at index c * rtiles + t,
+// holds rows [t*TR, t*TR + TR) of input columns [c*cols, (c+1)*cols): the
+// packed nibbles (TR x cols/2 bytes, row-major) followed by the group scales
+// (TR x cols/32 fp32). Tiles sit tile_stride bytes apart; rows past the end
+// of the matrix are zero. One tile is one bulk copy.
 struct Tiling {
     int rows, in_dim, TR, ntiles;
-    uint32_t tile_bytes;   // TR * (in/2 + in/8)
+    int KC, cols, rtiles;  // column chunks, inputs per chunk, row tiles per chunk
+    uint32_t tile_bytes;   // TR * (cols/2 + cols/8)
     uint32_t tile_stride;  // tile_bytes rounded up to 128
 };
 
-__host__ __device__ inline Tiling make_tiling(int rows, int in_dim, int TR) {
+__host__ __device__ inline Tiling make_tiling(int rows, int in_dim, int TR, int KC = 1) {
     Tiling t;
     t.rows = rows;
     t.in_dim = in_dim;
     t.TR = TR;
-    t.ntiles = (rows + TR - 1) / TR;
-    t.tile_bytes = (uint32_t)((size_t)TR * ((size_t)in_dim / 2 + (size_t)in_dim / 8));
+    t.KC = KC;
+    t.cols = in_dim / KC;
+    t.rtiles = (rows + TR - 1) / TR;
+    t.ntiles = t.rtiles * KC;
+    t.tile_bytes = (uint32_t)((size_t)TR * ((size_t)t.cols / 2 + (size_t)t.cols / 8));
     t.tile_stride = (uint32_t)align_up(t.tile_bytes, 128);
     return t;
 }

@@ -57,6 +57,8 @@ struct rabbit_cuda_moe {
     float *h_in = nullptr, *h_out = nullptr, *w_int = nullptr;
     int *ids_int = nullptr;
     unsigned long long *bar = nullptr;
+    unsigned *flags = nullptr;  // fused path: per-CTA "h read" tags
+    unsigned seq = 1;           // tag of the next fused launch (never 0)
     rb::Route *route = nullptr;
     // upload machinery
     cudaStream_t up = nullptr;
@@ -92,6 +94,30 @@ static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_loca
     return RABBIT_CUDA_OK;
 }
 
+// Bytes per element of the mid / down scratch: the fused kernel tags every
+// value with its launch ({float, seq}, 8 bytes); the generic kernels use
+// plain floats.
+static size_t scratch_elt(const rabbit_cuda_moe *p) { return p->fast ? 8 : 4; }
+static size_t mid_bytes(const rabbit_cuda_moe *p) {
+    return scratch_elt(p) * (size_t)std::max(1, p->k + p->S) * p->I;
+}
+static size_t down_bytes(const rabbit_cuda_moe *p) {
+    return scratch_elt(p) * (size_t)std::max(1, p->k + p->S) * (p->fast ? p->plan.tc.KC : 1) *
+           p->H;
+}
+
+// The next launch tag. Tags never repeat while the scratch lives: on wrap the
+// tagged buffers are cleared (on the launch's stream) and tags restart at 1.
+static unsigned next_seq(unsigned *seq, void *tagged[], const size_t bytes[], int n,
+                         cudaStream_t s) {
+    if (*seq == 0) *seq = 1;  // 0 is the tag of zeroed memory
+    if (*seq == 0xFFFFFFFFu) {
+        for (int i = 0; i < n; ++i) cudaMemsetAsync(tagged[i], 0, bytes[i], s);
+        *seq = 1;
+    }
+    return (*seq)++;
+}
+
 // Shared-memory bytes in front of the ring, in the order k_moe_decode_g32
 // carves them: xn, reduction scratch, slot records/weights, flags, scores.
 static size_t fused_head_bytes(int H, int E) {
@@ -109,41 +135,65 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     a.JB = lane_groups(H / 32);
     a.KSb = kslices(H / 32, a.JB);
     a.NGb = std::max(1, kConsumerWarps / a.KSb);  // warp groups in phase B
-    a.JC = lane_groups(I / 32);
-    a.KSc = kslices(I / 32, a.JC);
+    // W2 is split into column chunks of CG groups: the largest divisor of I/32
+    // up to 32 (1024 inputs), at most 16 chunks. A CTA then needs only its
+    // chunk of mid, not all of it.
+    const int Gc = I / 32;
+    int CG = 0;
+    for (int g = std::min(Gc, 32); g >= 1 && !CG; --g)
+        if (Gc % g == 0) CG = g;
+    const int KCc = Gc / CG;
+    if (KCc > 16) return false;
+    a.JC = lane_groups(CG);
+    a.KSc = kslices(CG, a.JC);
     a.NGc = std::max(1, kConsumerWarps / a.KSc);  // warp groups in phase C
     const int CW = std::max(a.KSb * a.NGb, a.KSc * a.NGc);
     a.CW = CW;
+
     const int slots = std::max(1, p->k + p->S);
     const int G = sm_count;
     const size_t rb_b = (size_t)H / 2 + (size_t)H / 8;  // bytes per row, one matrix
-    const size_t rb_c = (size_t)I / 2 + (size_t)I / 8;
-    // gate+up tiles: the slots' tiles are dealt out over the CTAs; at most 4
-    // rows per warp group (8 values per warp)
-    a.ROWSb = choose_rows(I, slots, true, G, 2 * rb_b, a.NGb, 4, 48 * 1024);
-    // down tiles: CTAs own H rows for every slot
-    a.ROWSc = choose_rows(H, slots, false, G, rb_c, a.NGc, 8, 48 * 1024);
+    const size_t rb_c = (size_t)CG * 32 / 2 + (size_t)CG * 32 / 8;  // one chunk row
+    // gate+up tiles: the slots' tiles are dealt out over the CTAs; at most 8
+    // dots per lane and tile (rows * 2 matrices * groups per lane)
+    a.ROWSb = choose_rows(I, slots, true, G, 2 * rb_b, a.NGb, 4 / a.JB, 48 * 1024);
+    // down tiles: the slots' tiles are dealt out over the CTAs as well
+    a.ROWSc = choose_rows(H, slots * KCc, true, G, rb_c, a.NGc, 8 / a.JC, 48 * 1024);
     const int TRb = a.NGb * a.ROWSb, TRc = a.NGc * a.ROWSc;
     const int KSb = a.KSb, KSc = a.KSc;
     a.tb = make_tiling(I, H, TRb);
     a.tb.tile_bytes *= 2;  // a GU tile holds gate and up rows
     a.tb.tile_stride = (uint32_t)align_up(a.tb.tile_bytes, 128);
-    a.tc = make_tiling(H, I, TRc);
+    a.tc = make_tiling(H, I, TRc, KCc);
     const size_t slot = std::max(a.tb.tile_stride, a.tc.tile_stride);
     a.slot_bytes = (uint32_t)slot;
-    const long long ub_max = ((long long)slots * a.tb.ntiles + G - 1) / G;
-    const long long tc_max = ((long long)a.tc.ntiles + G - 1) / G;
-    a.part_floats = (int)std::max(ub_max * TRb * 2 * KSb, tc_max * TRc * slots * KSc);
+    // one partial region holds one unit's per-(row, k-slice) sums
+    a.part_floats = std::max(TRb * 2 * KSb, TRc * KSc);
     const size_t head = fused_head_bytes(H, p->E);
-    const size_t tail = align_up((size_t)a.part_floats * 4, 16);
+    // partial regions, then two staging buffers for chunks of mid (padded)
+    const size_t tail = align_up((size_t)kPartRing * a.part_floats * 4, 16) +
+                        align_up((size_t)2 * (CG * 33) * 4, 16);
+    // ring barriers (16 per stage), one sink word per warp (128), the two
+    // staging barriers (16), the partial-region barriers (16 per region),
+    // the mid staging barriers (32)
+    const size_t bars = 128 + 16 + 16 * (size_t)kPartRing + 32;
     long long ns =
-        ((long long)kMaxDynSmem - (long long)(head + tail) - 16 * 24 - 128) / (long long)slot;
+        ((long long)kMaxDynSmem - (long long)(head + tail + bars) - 16 * 24) / (long long)slot;
     if (ns > 24) ns = 24;
     if (ns < 2) return false;
     a.nslots = (int)ns;
-    p->smem = head + (size_t)ns * slot + tail + 16 * (size_t)ns + 4 * 32;
+    p->smem = head + (size_t)ns * slot + tail + 16 * (size_t)ns + bars;
+    // Until routing is done the ring is idle and stages h and the norm
+    // weights (8 H bytes); routers up to 256 KB that fit in front of them are
+    // staged too and scored by every CTA; larger ones are split over the CTAs
+    // behind a grid barrier.
+    const size_t ring = (size_t)ns * slot, router_bytes = (size_t)p->E * H * 4;
+    if ((size_t)8 * H > ring) return false;
+    a.route_local =
+        router_bytes <= 256 * 1024 && align_up(router_bytes, 128) + (size_t)8 * H <= ring ? 1 : 0;
     if (p->smem > (size_t)kMaxDynSmem) return false;
-    p->block = (CW + 1) * 32;
+    p->block = (CW + 3) * 32;  // consumers, producer, epilogue, scout
+    if (G > kMaxGrid) return false;
     p->grid = G;
     p->off_d = align_up((size_t)a.tb.ntiles * a.tb.tile_stride, 256);
     p->rec_stride = p->off_d + align_up((size_t)a.tc.ntiles * a.tc.tile_stride, 256);
@@ -153,8 +203,8 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
 static void free_pool(rabbit_cuda_moe *p) {
     if (p->device >= 0) cudaSetDevice(p->device);
     if (p->up) cudaStreamSynchronize(p->up);
-    void *bufs[] = {p->pool,  p->rms, p->router,  p->scores, p->mid, p->xn,    p->down,
-                    p->h_in, p->h_out, p->w_int, p->ids_int, p->bar, p->route};
+    void *bufs[] = {p->pool,  p->rms,  p->router, p->scores,  p->mid, p->xn,  p->down,
+                    p->h_in,  p->h_out, p->w_int, p->ids_int, p->bar, p->route, p->flags};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int i = 0; i < 2; ++i) {
@@ -308,7 +358,6 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     p->pool_bytes = p->rec_stride * (uint64_t)p->n_records;
     p->resident.assign(p->n_records, 0);
 
-    const int slots = p->k + p->S;
     const size_t HE = (size_t)p->H * p->E;
     if ((e = cudaMalloc(&p->pool, p->pool_bytes)) != cudaSuccess) {
         free_pool(p);
@@ -318,11 +367,13 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     if ((e = cudaMalloc(&p->rms, sizeof(float) * (size_t)p->H * p->L)) != cudaSuccess ||
         (e = cudaMalloc(&p->router, sizeof(float) * HE * p->L)) != cudaSuccess ||
         (e = cudaMalloc(&p->scores, sizeof(float) * p->E)) != cudaSuccess ||
-        (e = cudaMalloc(&p->mid, sizeof(float) * (size_t)std::max(slots, 1) * p->I)) !=
-            cudaSuccess ||
+        (e = cudaMalloc(&p->mid, mid_bytes(p))) != cudaSuccess ||
+        (e = cudaMemset(p->mid, 0, mid_bytes(p))) != cudaSuccess ||
         (e = cudaMalloc(&p->xn, sizeof(float) * p->H)) != cudaSuccess ||
-        (e = cudaMalloc(&p->down, sizeof(float) * (size_t)std::max(slots, 1) * p->H)) !=
-            cudaSuccess ||
+        (e = cudaMalloc(&p->down, down_bytes(p))) != cudaSuccess ||
+        (e = cudaMemset(p->down, 0, down_bytes(p))) != cudaSuccess ||
+        (e = cudaMalloc(&p->flags, sizeof(unsigned) * kMaxGrid)) != cudaSuccess ||
+        (e = cudaMemset(p->flags, 0, sizeof(unsigned) * kMaxGrid)) != cudaSuccess ||
         (e = cudaMalloc(&p->h_in, sizeof(float) * p->H)) != cudaSuccess ||
         (e = cudaMalloc(&p->h_out, sizeof(float) * p->H)) != cudaSuccess ||
         (e = cudaMalloc(&p->w_int, sizeof(float) * 8)) != cudaSuccess ||
@@ -425,8 +476,8 @@ int rabbit_cuda_moe_fill_synthetic(rabbit_cuda_moe *p, uint64_t seed, float scal
                                                  (uint32_t)(2 * (size_t)tb.TR * (p->H / 2)),
                                                  2 * tb.TR * (p->H / 32), s0 + 1, scale_sigma);
         k_fill_scales<<<blocks, 256, 0, p->up>>>(rec + p->off_d, tc.ntiles, tc.tile_stride,
-                                                 (uint32_t)((size_t)tc.TR * (p->I / 2)),
-                                                 tc.TR * (p->I / 32), s0 + 2, scale_sigma);
+                                                 (uint32_t)((size_t)tc.TR * (tc.cols / 2)),
+                                                 tc.TR * (tc.cols / 32), s0 + 2, scale_sigma);
         p->resident[r] = 1;
     }
     RB_CUDA(cudaGetLastError());
@@ -476,8 +527,15 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         a.S = p->S;
         a.usable = p->usable ? 1 : 0;
         a.scores = p->scores;
-        a.mid = p->mid;
+        a.mid = reinterpret_cast<unsigned long long *>(p->mid);
+        a.down = reinterpret_cast<unsigned long long *>(p->down);
+        a.flags = p->flags;
         a.bar = p->bar;
+        {
+            void *tagged[] = {p->mid, p->down, p->flags};
+            const size_t bytes[] = {mid_bytes(p), down_bytes(p), sizeof(unsigned) * kMaxGrid};
+            a.seq = next_seq(&p->seq, tagged, bytes, 3, s);
+        }
         a.err = p->ctx->d_err;
         a.wait_ns = wait_limit_ns();
         void *args[] = {&a};
@@ -523,10 +581,13 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
 // Scratch for rabbit_cuda_moe_decode_dev_noalloc, in a fixed array of this
 // module instead of the pool: [0, 256) grid-barrier counter (u64 at 0),
 // routed ids at 64 and weights at 128 when the caller passes none; then the
-// router scores (E floats, 256-aligned); then mid ((k + S) x I floats). Every
+// per-CTA flags; the router scores (E floats); mid ((k + S) x I tagged
+// values, 8 bytes each); the down rows per column chunk of W2 ((k + S) x KC
+// x H tagged values), each part 256-aligned. Every
 // device that loads the library holds these bytes until the process exits.
-constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB
+constexpr size_t kNoAllocScratchBytes = 2u << 20;  // 2 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static unsigned g_noalloc_seq[kMaxDevices] = {};  // next launch tag per device (0: unset)
 // g_noalloc_scratch names the array only on the host side; its device address
 // on each device, looked up once per device with that device current.
 static uint8_t *g_noalloc_ptr[kMaxDevices];
@@ -554,9 +615,11 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
                     "moe_decode_noalloc: pool is not in the group-32 fused layout");
     if ((reinterpret_cast<uintptr_t>(d_h_in) & 15) || (reinterpret_cast<uintptr_t>(d_h_out) & 15))
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: h must be 16-byte aligned");
-    const size_t off_scores = 256;
+    const size_t off_flags = 256;
+    const size_t off_scores = off_flags + align_up(sizeof(unsigned) * kMaxGrid, 256);
     const size_t off_mid = off_scores + align_up((size_t)p->E * 4, 256);
-    const size_t need = off_mid + (size_t)std::max(1, p->k + p->S) * p->I * 4;
+    const size_t off_down = off_mid + align_up(mid_bytes(p), 256);
+    const size_t need = off_down + down_bytes(p);
     if (need > kNoAllocScratchBytes)
         return fail(RABBIT_CUDA_ERR_ARGS,
                     "moe_decode_noalloc: this model needs %zu bytes of scratch, more than the "
@@ -572,8 +635,10 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     uint8_t *scratch = nullptr;
     if ((st = noalloc_scratch(p->device, &scratch)) != RABBIT_CUDA_OK) return st;
     cudaStream_t s = as_stream(stream, p->ctx);
-    // The counter keeps the last call's value, which a call that gave up may
-    // have left between rounds: every call starts it from zero.
+    // The grid-barrier counter keeps the last call's value (a call that gave
+    // up may have left it anywhere): every call starts it from zero. Values
+    // shared between CTAs are tagged with the call's sequence number, which
+    // is new on every call on this device.
     RB_CUDA(cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), s));
     MoeFusedArgs a = p->plan;
     a.h_in = d_h_in;
@@ -594,8 +659,16 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     a.S = p->S;
     a.usable = p->usable ? 1 : 0;
     a.scores = reinterpret_cast<float *>(scratch + off_scores);
-    a.mid = reinterpret_cast<float *>(scratch + off_mid);
+    a.mid = reinterpret_cast<unsigned long long *>(scratch + off_mid);
+    a.down = reinterpret_cast<unsigned long long *>(scratch + off_down);
+    a.flags = reinterpret_cast<unsigned *>(scratch + off_flags);
     a.bar = reinterpret_cast<unsigned long long *>(scratch);
+    {
+        std::lock_guard<std::mutex> g(g_noalloc_mu);
+        void *tagged[] = {scratch + off_flags};
+        const size_t bytes[] = {kNoAllocScratchBytes - off_flags};
+        a.seq = next_seq(&g_noalloc_seq[p->device], tagged, bytes, 1, s);
+    }
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
     void *args[] = {&a};
@@ -611,7 +684,8 @@ int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream) {
     cudaStream_t s = as_stream(stream, p->ctx);
     int st = check_device_error(p->ctx, s, "moe_decode");
     if (st != RABBIT_CUDA_OK) {
-        // a barrier that gave up may have left arrivals behind: start clean
+        // a barrier wait that gave up may have left arrivals behind: start
+        // clean (tagged scratch needs nothing: the next launch has a new tag)
         cudaMemsetAsync(p->bar, 0, sizeof(unsigned long long), s);
         cudaStreamSynchronize(s);
         return st;

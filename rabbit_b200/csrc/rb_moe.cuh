@@ -8,6 +8,8 @@
 namespace rb {
 
 constexpr int kMaxSlots = 72;  // top-k (<= 8) + shared (<= 64)
+constexpr int kPartRing = 8;   // partial-sum regions between consumers and epilogue
+constexpr int kMaxGrid = 1024; // CTAs of the fused kernel (one per SM)
 
 // Routing result shared by the generic kernels (device memory).
 struct Route {
@@ -27,14 +29,19 @@ struct MoeFusedArgs {
     uint64_t rec_stride;
     uint64_t off_d;  // record = [GU tiles (gate+up pairs over I rows)] [D tiles over H rows]
     Tiling tb;       // GU tiling: rows I, in H, tile_bytes/stride of the gate+up pair
-    Tiling tc;       // D tiling: rows H, in I
+    Tiling tc;       // D tiling: rows H, in I, KC column chunks
     int rec_base;  // global record of local expert 0 in this layer
     int n_local;   // local ids >= n_local have no record (skipped)
     int H, E, k, I, S;
     int usable;    // 0: records too small, experts add nothing (forward_v2.c:319-322)
-    float *scores; // scratch [E]
-    float *mid;    // scratch [k+S][I]
-    unsigned long long *bar; // scratch: grid-barrier arrival counter
+    int route_local;  // 1: every CTA computes all router rows (no grid barrier 1)
+    float *scores; // scratch [E] (route_local == 0)
+    // scratch shared between CTAs, every value tagged {float, seq} (64-bit)
+    unsigned long long *mid;   // [k+S][I]
+    unsigned long long *down;  // [k+S][tc.KC][H]: down rows per slot and column chunk
+    unsigned *flags;           // [grid]: seq once the CTA has read h
+    unsigned seq;              // this launch's tag (never 0)
+    unsigned long long *bar;   // grid-barrier arrival counter (large routers)
     int *err;
     uint64_t wait_ns;
     // plan: CW consumer warps; phase B (gate/up, in = H) uses KSb warps per
@@ -42,7 +49,7 @@ struct MoeFusedArgs {
     // (down, in = I) likewise with KSc, NGc, ROWSc, JC
     int CW, KSb, NGb, ROWSb, JB, KSc, NGc, ROWSc, JC, nslots;
     uint32_t slot_bytes;
-    int part_floats;
+    int part_floats;  // floats per partial region
 };
 
 // k_moe_decode_g32<JB, JC> for JB / JC groups of 32 per lane in phases B / C

@@ -2,22 +2,35 @@
 // routed + shared SwiGLU experts (forward_v2.c:280-402).
 //
 // Fused group-32 kernel (k_moe_decode_g32), cooperative launch, one CTA per SM:
-//   A. every CTA: rmsnorm(h) -> xn in shared memory; CTA c computes router
-//      rows c, c+grid, ... -> scores.            [grid barrier 1]
+//   A. every CTA: rmsnorm(h) -> xn in shared memory; router scores: for
+//      routers up to 256 KB every CTA computes all E rows itself (same code
+//      and order everywhere, so the same scores); larger routers are split
+//      over the CTAs and published through a grid barrier.
 //      every CTA: top-k + softmax on the scores (identical in all CTAs), the
 //      active slot list (routed in rank order, then shared experts).
 //   B. gate/up: the active slots' GU tiles (TRb rows of gate and of up,
-//      nibbles + scales, one contiguous block) dealt out evenly over the
+//      nibbles + scales, one contiguous block) dealt out round-robin over the
 //      CTAs; the producer warp bulk-copies them into the shared-memory ring;
 //      eight consumer warps dot them against xn held in registers (JB groups
 //      of 32 per lane, ROWSb rows per warp group and tile, both fixed at
-//      compile time); mid = silu(gate) * up goes to global scratch.
-//   C. down + combine: each CTA owns D tiles (TRc rows of the H outputs) for
-//      every active slot; the producer keeps issuing these W2 chunks as soon as
-//      ring stages free up -- before and during grid barrier 2 -- so the down
-//      weights are in flight while the last gate/up rows finish. Consumers
-//      reload x = mid[slot] per slot and combine h_out = h + sum_j w_j down_j
-//      in slot order (forward_v2.c:356-357, 398-399).
+//      compile time) and leave per-k-slice partials in shared memory; the
+//      epilogue warp stores mid = silu(gate) * up to global scratch, each
+//      value tagged with the launch's sequence number.
+//   C. down: W2 is tiled as (column chunk of up to 1024 inputs, row tile of
+//      TRc rows); the active slots' tiles are dealt out in contiguous ranges
+//      over the CTAs in (slot, chunk, row tile) order, so a CTA reads only one
+//      or two chunks of mid. The producer issues them right after the CTA's
+//      gate/up tiles, so the down
+//      weights are in flight while the last gate/up rows finish. A scout warp
+//      reads the CTA's chunks of mid once all their values carry this
+//      launch's tag and stages them in shared memory; consumers build x
+//      planes from there when (slot, chunk) changes; the epilogue warp stores
+//      the tagged partial down rows per chunk.
+//      combine: row tile t is owned by CTA t % grid, which reads its partials
+//      once tagged: down_j = the sum of its chunks in chunk order, h_out =
+//      h + sum_j w_j down_j in slot order (forward_v2.c:356-357, 398-399).
+// There are no grid barriers between the phases (one before top-k for
+// routers too large to stage): CTAs wait only for the data they read.
 // Every wait (mbarrier or grid barrier) is bounded by a %globaltimer limit;
 // a timeout records RB_ERR_TIMEOUT and the CTA drains its copies and exits.
 #include "rb_gemv.cuh"
@@ -31,15 +44,26 @@ namespace rb {
 // done times of each of the first 64 chunks.
 __device__ uint64_t g_phase_ns[1024 * 8];
 __device__ uint64_t g_chunk_ns[4 * 64];
-#define RB_CHUNK(kind, i)                                                              \
-    do {                                                                               \
-        if (blockIdx.x == 0 && (i) < 64) g_chunk_ns[(kind) * 64 + (i)] = globaltimer_ns(); \
+#ifndef RB_CHUNK_CTA
+#define RB_CHUNK_CTA 0
+#endif
+#define RB_CHUNK(kind, i)                                                     \
+    do {                                                                      \
+        if (blockIdx.x == RB_CHUNK_CTA && (i) < 64)                           \
+            g_chunk_ns[(kind) * 64 + (i)] = globaltimer_ns();                 \
     } while (0)
 #define RB_STAMP(i)                                                        \
     do {                                                                   \
         if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = globaltimer_ns(); \
     } while (0)
+#define RB_DBG(k)                                                                  \
+    do {                                                                           \
+        if (blockIdx.x == RB_CHUNK_CTA && threadIdx.x == 0) rb_dbg_ns[(k)] = globaltimer_ns(); \
+    } while (0)
 #else
+#define RB_DBG(k) \
+    do {          \
+    } while (0)
 #define RB_STAMP(i) \
     do {            \
     } while (0)
@@ -72,6 +96,20 @@ __device__ bool grid_barrier(unsigned long long *count, unsigned nblocks, uint64
 }
 
 // --------------------------------------------------------------- top-k ----
+// Softmax over the k selected scores in place (max-subtracted, expf).
+__device__ __forceinline__ void softmax_k(float *w, int k) {
+    float m = w[0];
+    for (int i = 1; i < k; ++i)
+        if (w[i] > m) m = w[i];
+    float z = 0.f;
+    for (int i = 0; i < k; ++i) {
+        w[i] = expf(w[i] - m);
+        z += w[i];
+    }
+    if (z > 0.f)
+        for (int i = 0; i < k; ++i) w[i] = w[i] / z;
+}
+
 // forward_v2.c:248-278: insertion into a descending list seeded (-1, -1e30),
 // strict '>' (lower index wins ties, NaN never enters), softmax over the k.
 __device__ void topk_softmax(const float *scores, int E, int k, int *ids, float *w) {
@@ -91,16 +129,37 @@ __device__ void topk_softmax(const float *scores, int E, int k, int *ids, float 
         ids[slot] = e;
         w[slot] = s;
     }
-    float m = w[0];
-    for (int i = 1; i < k; ++i)
-        if (w[i] > m) m = w[i];
-    float z = 0.f;
-    for (int i = 0; i < k; ++i) {
-        w[i] = expf(w[i] - m);
-        z += w[i];
+    softmax_k(w, k);
+}
+
+// forward_v2.c:248-278 by one warp: an expert with a score above the -1e30
+// seed (NaN never qualifies) takes place r = the number of qualifying experts
+// with a larger score, or an equal score and a lower index -- the order the
+// strict-'>' insertion builds. Places past the qualifying count keep (-1,
+// -1e30). ids / w in shared memory; every lane of the warp calls it.
+__device__ void topk_softmax_warp(const float *scores, int E, int k, int *ids, float *w) {
+    const int lane = threadIdx.x & 31;
+    if (lane < k) {
+        ids[lane] = -1;
+        w[lane] = -1e30f;
     }
-    if (z > 0.f)
-        for (int i = 0; i < k; ++i) w[i] = w[i] / z;
+    __syncwarp();
+    for (int e = lane; e < E; e += 32) {
+        const float s = scores[e];
+        if (!(s > -1e30f)) continue;
+        int r = 0;
+        for (int f = 0; f < E; ++f) {
+            const float t = scores[f];
+            r += (t > s || (t == s && f < e)) ? 1 : 0;
+        }
+        if (r < k) {
+            ids[r] = e;
+            w[r] = s;
+        }
+    }
+    __syncwarp();
+    if (lane == 0) softmax_k(w, k);
+    __syncwarp();
 }
 
 // Active slot list: routed experts in rank order, then shared experts with
@@ -135,68 +194,148 @@ __device__ __forceinline__ void release_stage(uint64_t *empty) {
     if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(empty, 1);
 }
 
-// Phase B for one consumer warp: the CTA's units [ub0, ub1) (slot, GU tile),
-// ROWS rows of gate and of up per tile from rbase. `i` counts ring stages.
+// Values shared between CTAs carry the launch's sequence number: {value,
+// seq} in one 64-bit word, stored and loaded as one aligned relaxed 64-bit
+// access (single-copy atomic). A reader takes a value once its tag matches
+// the current launch -- no counter, no fence. Buffers start zeroed and
+// sequence numbers start at 1.
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, unsigned seq) {
+    const unsigned long long w = ((unsigned long long)seq << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+__device__ __forceinline__ bool tag_ok(unsigned long long w, unsigned seq) {
+    return (unsigned)(w >> 32) == seq;
+}
+
+__device__ __forceinline__ float tag_val(unsigned long long w) {
+    return __uint_as_float((unsigned)w);
+}
+
+// Wait until every CTA has published seq in flags[0, n) (every lane polls).
+__device__ __forceinline__ bool wait_flags(const unsigned *flags, int n, unsigned seq,
+                                           uint64_t limit_ns, int *err) {
+    const uint64_t t0 = globaltimer_ns();
+    for (unsigned it = 0;; ++it) {
+        bool ok = true;
+        for (int b = threadIdx.x & 31; b < n; b += 32) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + b) : "memory");
+            ok = ok && v == seq;
+        }
+        if (__all_sync(0xffffffffu, ok)) return true;
+        if ((it & 7u) == 7u && globaltimer_ns() - t0 > limit_ns) {
+            set_error(err, RB_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(128);
+    }
+}
+
+// Partial sums of one unit go to part region i % kPartRing; the warp first
+// waits until the epilogue warp has emptied that region (unit i - kPartRing),
+// and signals `done` when its partials are written.
+__device__ __forceinline__ bool part_acquire(uint64_t *pfree, int i, const MoeFusedArgs &a) {
+    if (i < kPartRing) return true;
+    return __all_sync(0xffffffffu, mbar_wait(&pfree[i % kPartRing], ((i / kPartRing) - 1) & 1,
+                                             a.wait_ns, a.err));
+}
+
+__device__ __forceinline__ void part_done(uint64_t *done, int i) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&done[i % kPartRing]);
+}
+
+// Phase B for one consumer warp: the CTA's gate/up units u = blockIdx.x +
+// n * gridDim.x (n < nB), ROWS rows of gate and of up per tile from rbase.
+// `i` counts the CTA's units (ring stages and partial regions).
 template <int J, int ROWS>
 __device__ __forceinline__ bool moe_gate_up(const MoeFusedArgs &a, const uint8_t *ring,
                                             float *part, uint64_t *full, uint64_t *empty,
-                                            uint32_t *sink, int ub0, int ub1, int &i, int ks,
-                                            int rbase, bool mine, int g0, const bool (&act)[J],
-                                            const XPlanes (&xg)[J]) {
+                                            uint64_t *done, uint64_t *pfree, uint32_t *sink,
+                                            int nB, int &i, int ks, int rbase, bool mine, int g0,
+                                            const bool (&act)[J], const XPlanes (&xg)[J]) {
     const int KS = a.KSb, TRb = a.tb.TR, Hh = a.H >> 1, Gb = a.H >> 5;
-    for (int u = ub0; u < ub1; ++u, ++i) {
-        const int s = i % a.nslots, n = i / a.nslots;
+    for (int n = 0; n < nB; ++n, ++i) {
+        const int s = i % a.nslots, ph = i / a.nslots;
         if (threadIdx.x == 0) RB_CHUNK(1, i);
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph & 1, a.wait_ns, a.err))) return false;
         if (threadIdx.x == 0) RB_CHUNK(2, i);
-        const int lb = (u - ub0) * TRb + rbase;
+        if (!part_acquire(pfree, i, a)) return false;
+        float *pp = part + (size_t)(i % kPartRing) * a.part_floats;
         if (mine)
             chunk_dot<2, ROWS, J>(ring + (size_t)s * a.slot_bytes, TRb, rbase, Hh, Gb, g0, act, xg,
-                                  [=](int m, int r) { return ((lb + r) * 2 + m) * KS + ks; },
-                                  part, &empty[s], 1u, sink);
+                                  [=](int m, int r) { return ((rbase + r) * 2 + m) * KS + ks; },
+                                  pp, &empty[s], 1u, sink);
         else
             release_stage(&empty[s]);
+        part_done(done, i);
         if (threadIdx.x == 0) RB_CHUNK(3, i);
     }
     return true;
 }
 
-// Phase C for one consumer warp: for every active slot, the CTA's D tiles
-// [c0, c1), ROWS rows of each from rbase, x = mid of the slot.
+// Phase C for one consumer warp: the CTA's units [uc0, uc1), unit u = slot
+// u / ntiles, tile u % ntiles of the slot's W2 (column chunk c, row tile t);
+// ROWS rows of each tile from rbase. x = the chunk's slice of the slot's mid,
+// staged in shared memory by the scout warp (buffer kk & 1 for the CTA's
+// kk-th (slot, chunk) key); planes are rebuilt when the key changes (units
+// run in key order, so once or twice per CTA).
 template <int J, int ROWS>
 __device__ __forceinline__ bool moe_down(const MoeFusedArgs &a, const uint8_t *ring, float *part,
-                                         uint64_t *full, uint64_t *empty, uint32_t *sink,
-                                         int nact, int c0, int c1, int &i, int ks, int rbase,
-                                         bool mine, int g0, const bool (&act)[J]) {
-    const int KS = a.KSc, TRc = a.tc.TR, Ih = a.I >> 1, Gc = a.I >> 5;
+                                         uint64_t *full, uint64_t *empty, uint64_t *done,
+                                         uint64_t *pfree, uint32_t *sink, const float *xbuf,
+                                         int xb, uint64_t *xfull, uint64_t *xfree, int key0,
+                                         int uc0, int uc1, int &i, int ks, int rbase, bool mine,
+                                         int g0, const bool (&act)[J]) {
+    const int KS = a.KSc, TRc = a.tc.TR, ntc = a.tc.ntiles, rt = a.tc.rtiles;
+    const int cols = a.tc.cols, Gk = cols >> 5, half = cols >> 1;
     XPlanes xg[J];
-    for (int j = 0; j < nact; ++j) {
-        // x = mid of this slot (written by all CTAs before grid barrier 2)
-#pragma unroll
-        for (int q = 0; q < J; ++q)
-            load_xplanes_global(xg[q], a.mid + (size_t)j * a.I + (size_t)(g0 + 32 * q) * 32, act[q]);
-        for (int t = c0; t < c1; ++t, ++i) {
-            const int s = i % a.nslots, n = i / a.nslots;
-            if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err)))
+    int cur = -1;
+    RB_DBG(5);
+    for (int u = uc0; u < uc1; ++u, ++i) {
+        const int j = u / ntc, kk = j * a.tc.KC + (u - j * ntc) / rt - key0;
+        if (kk != cur) {
+            cur = kk;
+            const int b = kk & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&xfull[b], (kk >> 1) & 1, a.wait_ns, a.err)))
                 return false;
-            const int lb = (t - c0) * TRc + rbase;
-            if (mine)
-                chunk_dot<1, ROWS, J>(ring + (size_t)s * a.slot_bytes, TRc, rbase, Ih, Gc, g0, act,
-                                      xg, [=](int, int r) { return ((lb + r) * nact + j) * KS + ks; },
-                                      part, &empty[s], 1u, sink);
-            else
-                release_stage(&empty[s]);
+#pragma unroll
+            for (int q = 0; q < J; ++q) load_xplanes_padded(xg[q], xbuf + b * xb, g0 + 32 * q, act[q]);
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) mbar_arrive(&xfree[b]);
+            RB_DBG(6);
         }
+        const int s = i % a.nslots, ph = i / a.nslots;
+        if (threadIdx.x == 0) RB_CHUNK(1, i);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph & 1, a.wait_ns, a.err))) return false;
+        if (threadIdx.x == 0) RB_CHUNK(2, i);
+        if (!part_acquire(pfree, i, a)) return false;
+        float *pp = part + (size_t)(i % kPartRing) * a.part_floats;
+        if (mine)
+            chunk_dot<1, ROWS, J>(ring + (size_t)s * a.slot_bytes, TRc, rbase, half, Gk, g0, act,
+                                  xg, [=](int, int r) { return (rbase + r) * KS + ks; }, pp,
+                                  &empty[s], 1u, sink);
+        else
+            release_stage(&empty[s]);
+        part_done(done, i);
+        if (threadIdx.x == 0) RB_CHUNK(3, i);
     }
     return true;
 }
 
 template <int JB, int JC>
-__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
+__global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nthr = blockDim.x;
     const int H = a.H, I = a.I, CW = a.CW;
-    const int Gb = H >> 5, Gc = I >> 5;
+    const int Gb = H >> 5;
 
     size_t off = 0;
     float *xn = reinterpret_cast<float *>(smem);  // padded: 33 floats per group of 32
@@ -213,11 +352,24 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
     off = align_up(off + (size_t)a.E * 4, 128);
     uint8_t *ring = smem + off;
     off += (size_t)a.nslots * a.slot_bytes;
-    float *part = reinterpret_cast<float *>(smem + off);
-    off += align_up((size_t)a.part_floats * 4, 16);
+    float *part = reinterpret_cast<float *>(smem + off);  // kPartRing regions
+    off += align_up((size_t)kPartRing * a.part_floats * 4, 16);
+    const int xb = (a.tc.cols >> 5) * 33;  // one padded chunk of mid
+    float *xbuf = reinterpret_cast<float *>(smem + off);  // [2][xb]
+    off += align_up((size_t)2 * xb * 4, 16);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + off);
     uint64_t *empty = full + a.nslots;
     uint32_t *sink = reinterpret_cast<uint32_t *>(empty + a.nslots);  // one word per warp
+    uint64_t *rbar = reinterpret_cast<uint64_t *>(sink + 32);  // router staging barrier
+    uint64_t *hbar = rbar + 1;                                  // h / rms staging barrier
+    uint64_t *done = hbar + 1;                                  // [kPartRing] partials written
+    uint64_t *pfree = done + kPartRing;                         // [kPartRing] partials consumed
+    uint64_t *xfull = pfree + kPartRing;                        // [2] chunk of mid staged
+    uint64_t *xfree = xfull + 2;                                // [2] its planes taken
+    const uint32_t router_bytes = (uint32_t)a.E * (uint32_t)H * 4u;
+    // the ring is idle until routing is done: [router (route_local)] [h] [rms]
+    float *hs = reinterpret_cast<float *>(ring + (a.route_local ? align_up(router_bytes, 128) : 0));
+    float *rs = hs + H;
 
     RB_STAMP(0);
     if (tid == 0) {
@@ -225,13 +377,49 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);  // every consumer warp releases every stage
         }
+        mbar_init(rbar, 1);
+        mbar_init(hbar, 1);
+        for (int d = 0; d < kPartRing; ++d) {
+            mbar_init(&done[d], CW);  // every consumer warp, after its partials
+            mbar_init(&pfree[d], 1);  // the epilogue warp
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&xfull[b], 1);   // the scout warp
+            mbar_init(&xfree[b], CW);  // every consumer warp, after its planes
+        }
         mbar_init_fence();
+        // h and the norm weights, behind the router block in the idle ring
+        mbar_arrive_expect_tx(hbar, 8u * (uint32_t)H);
+        const uint64_t pol_h = policy_evict_last();
+        bulk_g2s(hs, a.h_in, 4u * (uint32_t)H, hbar, pol_h);
+        bulk_g2s(rs, a.rms, 4u * (uint32_t)H, hbar, pol_h);
+        if (a.route_local) {
+            // The ring is idle until routing is done: stage the layer's router
+            // block [E, H] there while the CTA computes the norm.
+            mbar_arrive_expect_tx(rbar, router_bytes);
+            const uint64_t pol = policy_evict_last();  // every CTA reads it
+            for (uint32_t o = 0; o < router_bytes; o += 32768u)
+                bulk_g2s(ring + o, reinterpret_cast<const uint8_t *>(a.router) + o,
+                         router_bytes - o < 32768u ? router_bytes - o : 32768u, rbar, pol);
+        }
     }
 
     // ------------------------------------------------ A: rmsnorm + router --
+    // no thread may touch a barrier before thread 0 has initialised it
+    __syncthreads();
+    RB_DBG(0);
+    {
+        const bool okh = mbar_wait(hbar, 0, a.wait_ns, a.err);
+        if (__syncthreads_or(!okh)) {
+            if (!okh) mbar_wait(hbar, 0, a.wait_ns, a.err);  // let the copies land first
+            if (a.route_local) mbar_wait(rbar, 0, a.wait_ns, a.err);
+            return;
+        }
+    }
+    RB_DBG(1);
     float ss = 0.f;
     for (int i = tid; i < H; i += nthr) {
-        const float v = a.h_in[i];
+        const float v = hs[i];
         ss += v * v;
     }
     ss = warp_sum(ss);
@@ -245,35 +433,79 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
     }
     __syncthreads();
     const float inv = red[31];
-    for (int i = tid; i < H; i += nthr) xn[xpad(i)] = (a.h_in[i] * inv) * a.rms[i];
+    for (int i = tid; i < H; i += nthr) xn[xpad(i)] = (hs[i] * inv) * rs[i];
     __syncthreads();
-    for (int e = blockIdx.x; e < a.E; e += gridDim.x) {
-        const float *wr = a.router + (size_t)e * H;
-        float d = 0.f;
-        for (int i = tid; i < H; i += nthr) d += wr[i] * xn[xpad(i)];
-        d = warp_sum(d);
-        if (lane == 0) red[warp] = d;
+    if (tid == 0)  // this CTA is done with h_in (it may be h_out)
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.flags + blockIdx.x), "r"(a.seq)
+                     : "memory");
+    RB_DBG(2);
+    if (a.route_local) {
+        // Every CTA scores every expert itself from the staged router: warp w
+        // takes rows w, w + 9, ...; lane l sums inputs 4l + 128t in order,
+        // then a fixed butterfly. The code and order are the same in every
+        // CTA, so every CTA gets the same scores and the same top-k, and no
+        // grid barrier is needed.
+        const bool okr = mbar_wait(rbar, 0, a.wait_ns, a.err);
+        if (__syncthreads_or(!okr)) {
+            if (!okr) mbar_wait(rbar, 0, a.wait_ns, a.err);  // let the copy land first
+            return;
+        }
+        RB_DBG(3);
+        const float *rt = reinterpret_cast<const float *>(ring);
+        for (int e = warp; e < a.E; e += nthr >> 5) {
+            const float4 *wr = reinterpret_cast<const float4 *>(rt + (size_t)e * H);
+            float d = 0.f;
+            for (int i4 = lane; i4 < (H >> 2); i4 += 32) {
+                const float4 w = wr[i4];
+                const float *xp = xn + xpad(i4 * 4);
+                d = fmaf(w.x, xp[0], d);
+                d = fmaf(w.y, xp[1], d);
+                d = fmaf(w.z, xp[2], d);
+                d = fmaf(w.w, xp[3], d);
+            }
+            d = warp_sum(d);
+            if (lane == 0) s_sc[e] = d;
+        }
+        if (tid == 0) s_misc[2] = 0;
         __syncthreads();
+        RB_STAMP(1);
+    } else {
+        // Router rows spread over the CTAs, published through global scratch.
+        for (int e = blockIdx.x; e < a.E; e += gridDim.x) {
+            const float *wr = a.router + (size_t)e * H;
+            float d = 0.f;
+            for (int i = tid; i < H; i += nthr) d += wr[i] * xn[xpad(i)];
+            d = warp_sum(d);
+            if (lane == 0) red[warp] = d;
+            __syncthreads();
+            if (tid == 0) {
+                float t = 0.f;
+                for (int w = 0; w < (nthr >> 5); ++w) t += red[w];
+                a.scores[e] = t;
+            }
+            __syncthreads();
+        }
+        RB_STAMP(1);
         if (tid == 0) {
-            float t = 0.f;
-            for (int w = 0; w < (nthr >> 5); ++w) t += red[w];
-            a.scores[e] = t;
+            s_misc[1] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
+            s_misc[2] = 0;
         }
         __syncthreads();
+        if (s_misc[1]) return;  // nothing in flight yet
+        for (int e = tid; e < a.E; e += nthr) s_sc[e] = __ldcg(a.scores + e);
+        __syncthreads();
     }
-    RB_STAMP(1);
-    if (tid == 0) {
-        s_misc[1] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
-        s_misc[2] = 0;
+    RB_DBG(4);
+    if (warp == 0) {
+        // top-k lists in shared memory (the norm's reduction words are free
+        // by now)
+        int *ids = reinterpret_cast<int *>(red);
+        float *w = red + 8;
+        topk_softmax_warp(s_sc, a.E, a.k, ids, w);
     }
-    __syncthreads();
-    if (s_misc[1]) return;  // nothing in flight yet
-    for (int e = tid; e < a.E; e += nthr) s_sc[e] = __ldcg(a.scores + e);
-    __syncthreads();
     if (tid == 0) {
-        int ids[8];
-        float w[8];
-        topk_softmax(s_sc, a.E, a.k, ids, w);
+        const int *ids = reinterpret_cast<const int *>(red);
+        const float *w = red + 8;
         if (blockIdx.x == 0) {
             for (int i = 0; i < a.k; ++i) {
                 a.ids_out[i] = ids[i];
@@ -291,47 +523,196 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
     }
 
     const int ntb = a.tb.ntiles, TRb = a.tb.TR, ntc = a.tc.ntiles, TRc = a.tc.TR;
-    const int UB = nact * ntb;  // phase B units: (slot, GU tile)
-    const int ub0 = (int)((long long)blockIdx.x * UB / gridDim.x);
-    const int ub1 = (int)((long long)(blockIdx.x + 1) * UB / gridDim.x);
-    const int c0 = (int)((long long)blockIdx.x * ntc / gridDim.x);  // phase C: D tiles over H
-    const int c1 = (int)((long long)(blockIdx.x + 1) * ntc / gridDim.x);
+    const int G = (int)gridDim.x, bx = (int)blockIdx.x;
+    const int UB = nact * ntb;  // gate/up units (slot, GU tile), dealt round-robin
+    const int nB = UB > bx ? (UB - bx + G - 1) / G : 0;
+    const int UC = nact * ntc;  // down units (slot, chunk, row tile), contiguous ranges
+    const int uc0 = (int)((long long)bx * UC / G);
+    const int uc1 = (int)((long long)(bx + 1) * UC / G);
     const uint32_t sb = a.tb.tile_stride, sc = a.tc.tile_stride;
 
     if (warp == CW) {  // -------------------------------------------- producer
         if (lane == 0) {
+            // the ring may have held the router, read through the generic proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             const uint64_t pol = policy_evict_first();
             int i = 0;
             bool okp = true;
-            for (int u = ub0; okp && u < ub1; ++u, ++i) {
-                const int s = i % a.nslots, n = i / a.nslots;
-                if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) {
+            for (int n = 0; okp && n < nB; ++n, ++i) {
+                const int s = i % a.nslots, ph = i / a.nslots;
+                if (ph > 0 && !mbar_wait(&empty[s], (ph - 1) & 1, a.wait_ns, a.err, 0)) {
                     okp = false;
                     break;
                 }
-                const int slot = u / ntb, t = u - slot * ntb;
+                const int u = bx + n * G, slot = u / ntb, t = u - slot * ntb;
                 const uint8_t *src = a.pool + (size_t)s_rec[slot] * a.rec_stride + (size_t)t * sb;
                 RB_CHUNK(0, i);
                 mbar_arrive_expect_tx(&full[s], a.tb.tile_bytes);
                 bulk_g2s(ring + (size_t)s * a.slot_bytes, src, a.tb.tile_bytes, &full[s], pol);
             }
-            for (int j = 0; okp && j < nact; ++j) {
-                const uint8_t *rec = a.pool + (size_t)s_rec[j] * a.rec_stride + a.off_d;
-                for (int t = c0; t < c1; ++t, ++i) {
-                    const int s = i % a.nslots, n = i / a.nslots;
-                    if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) {
-                        okp = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&full[s], a.tc.tile_bytes);
-                    bulk_g2s(ring + (size_t)s * a.slot_bytes, rec + (size_t)t * sc, a.tc.tile_bytes,
-                             &full[s], pol);
+            for (int u = uc0; okp && u < uc1; ++u, ++i) {
+                const int s = i % a.nslots, ph = i / a.nslots;
+                if (ph > 0 && !mbar_wait(&empty[s], (ph - 1) & 1, a.wait_ns, a.err, 0)) {
+                    okp = false;
+                    break;
                 }
+                const int slot = u / ntc, t = u - slot * ntc;
+                const uint8_t *src =
+                    a.pool + (size_t)s_rec[slot] * a.rec_stride + a.off_d + (size_t)t * sc;
+                RB_CHUNK(0, i);
+                mbar_arrive_expect_tx(&full[s], a.tc.tile_bytes);
+                bulk_g2s(ring + (size_t)s * a.slot_bytes, src, a.tc.tile_bytes, &full[s], pol);
             }
             // drain: the last use of every stage must have landed before exit
             for (int t = i > a.nslots ? i - a.nslots : 0; t < i; ++t)
                 mbar_wait(&full[t % a.nslots], (t / a.nslots) & 1, a.wait_ns, a.err);
         }
+        return;
+    }
+
+    const int KC = a.tc.KC;
+    const int rt_c = a.tc.rtiles;
+    // (slot, chunk) key of down unit u; the CTA's keys are key0 .. key of uc1-1
+    auto key_of = [&](int u) { const int j = u / ntc; return j * KC + (u - j * ntc) / rt_c; };
+    const int key0 = uc0 < uc1 ? key_of(uc0) : 0;
+
+    if (warp == CW + 2) {  // --------------------------------------------- scout
+        // For each of the CTA's (slot, chunk) keys in order: once the
+        // consumers have taken the planes of key kk - 2 from staging buffer
+        // kk & 1, read that chunk of mid until every value carries this
+        // launch's tag and copy the values there in the padded layout (33
+        // floats per group). Runs while the CTA is still on its gate/up
+        // units, so the down units find x ready.
+        if (uc0 >= uc1) return;
+        const int nkeys = key_of(uc1 - 1) - key0 + 1;
+        const int cols = a.tc.cols;
+        for (int kk = 0; kk < nkeys; ++kk) {
+            const int key = key0 + kk, b = kk & 1;
+            if (kk >= 2 &&
+                !__all_sync(0xffffffffu, mbar_wait(&xfree[b], ((kk >> 1) - 1) & 1, a.wait_ns, a.err)))
+                return;
+            // poll the chunk until every value carries this launch's tag
+            const unsigned long long *src =
+                a.mid + (size_t)(key / KC) * I + (size_t)(key % KC) * cols;
+            float *dst = xbuf + b * xb;
+            const uint64_t t0 = globaltimer_ns();
+            for (int e0 = 0; e0 < cols; e0 += 32 * 16) {
+                for (unsigned it = 0;; ++it) {
+                    unsigned long long w[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        const int e = e0 + lane + 32 * q;
+                        w[q] = e < cols ? ld_tagged(src + e) : (unsigned long long)a.seq << 32;
+                    }
+                    bool ok = true;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) ok = ok && tag_ok(w[q], a.seq);
+                    if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const int e = e0 + lane + 32 * q;
+                            if (e < cols) dst[xpad(e)] = tag_val(w[q]);
+                        }
+                        break;
+                    }
+                    if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                        set_error(a.err, RB_ERR_TIMEOUT);
+                        return;
+                    }
+                    __nanosleep(128);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xfull[b]);
+        }
+        return;
+    }
+
+    if (warp == CW + 1) {  // ------------------------------------------ epilogue
+        // Unit by unit, in the consumers' order: sum the KS partials of each
+        // row and store mid (gate/up units) or the chunk's down rows (down
+        // units) tagged with this launch, then free the partial region. Then
+        // combine the row tiles this CTA owns (t = blockIdx.x, + grid, ...):
+        // h_out = h + sum_j w_j sum_c down_jc, slots and chunks in order
+        // (forward_v2.c:356-357, 398-399), reading each partial once its tag
+        // matches and once every CTA has read h (h_out may be h_in).
+        const int rt = a.tc.rtiles;
+        const int nU = nB + (uc1 - uc0);
+        for (int i = 0; i < nU; ++i) {
+            const int d = i % kPartRing;
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&done[d], (i / kPartRing) & 1, a.wait_ns, a.err)))
+                return;
+            const float *pp = part + (size_t)d * a.part_floats;
+            if (i < nB) {
+                const int u = bx + i * G, slot = u / ntb, t = u - slot * ntb;
+                for (int r = lane; r < TRb; r += 32) {
+                    const int row = t * TRb + r;
+                    if (row >= I) continue;
+                    float gs = 0.f, us = 0.f;
+                    for (int k = 0; k < a.KSb; ++k) {
+                        gs += pp[(r * 2) * a.KSb + k];
+                        us += pp[(r * 2 + 1) * a.KSb + k];
+                    }
+                    st_tagged(a.mid + (size_t)slot * I + row, silu_mul(gs, us), a.seq);
+                }
+            } else {
+                const int u = uc0 + (i - nB);
+                const int slot = u / ntc, ti = u - slot * ntc, c = ti / rt, t = ti - c * rt;
+                for (int r = lane; r < TRc; r += 32) {
+                    const int row = t * TRc + r;
+                    if (row >= H) continue;
+                    float dsum = 0.f;
+                    for (int k = 0; k < a.KSc; ++k) dsum += pp[r * a.KSc + k];
+                    st_tagged(a.down + ((size_t)slot * KC + c) * H + row, dsum, a.seq);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfree[d]);
+        }
+        bool flags_seen = false;
+        for (int t = bx; t < rt; t += G) {
+            if (!flags_seen) {
+                if (!wait_flags(a.flags, G, a.seq, a.wait_ns, a.err)) return;
+                flags_seen = true;
+            }
+            const uint64_t t0 = globaltimer_ns();
+            for (int r = lane; r < TRc; r += 32) {
+                const int row = t * TRc + r;
+                if (row >= H) continue;
+                float delta = 0.f;
+                bool ok = true;
+                for (int j = 0; ok && j < nact; ++j) {
+                    const unsigned long long *dp = a.down + (size_t)j * KC * H + row;
+                    unsigned long long w[16];  // KC <= 16: all loads in flight at once
+                    for (unsigned it = 0;; ++it) {
+                        bool all = true;
+#pragma unroll
+                        for (int cc = 0; cc < 16; ++cc) {
+                            w[cc] = cc < KC ? ld_tagged(dp + (size_t)cc * H)
+                                            : (unsigned long long)a.seq << 32;
+                            all = all && tag_ok(w[cc], a.seq);
+                        }
+                        if (all) break;
+                        if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                            set_error(a.err, RB_ERR_TIMEOUT);
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(128);
+                    }
+                    float dj = 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < 16; ++cc)
+                        if (cc < KC) dj += tag_val(w[cc]);
+                    delta += s_w[j] * dj;
+                }
+                if (ok) a.h_out[row] = a.h_in[row] + delta;
+            }
+        }
+#ifdef RB_PHASE_TIMERS
+        if (lane == 0) g_phase_ns[blockIdx.x * 8 + 5] = globaltimer_ns();
+#endif
         return;
     }
 
@@ -341,8 +722,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
     // the phase's NG groups only release. Every consumer waits for and
     // releases every stage (weight 1), so the ring's phases stay in step
     // across both phases.
-    bool good = true;
     int i = 0;
+    bool good;
     {  // B: gate + up
         const int ks = warp % a.KSb, grp = warp / a.KSb;
         const int g0 = ks * 32 * JB + lane;
@@ -354,66 +735,34 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_moe_decode_g32
             act[q] = mine && g0 + 32 * q < Gb;
             load_xplanes_padded(xg[q], xn, g0 + 32 * q, act[q]);
         }
+        RB_DBG(7);
         const int rbase = grp * a.ROWSb;
         switch (a.ROWSb) {
-            case 1: good = moe_gate_up<JB, 1>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
-            case 2: good = moe_gate_up<JB, 2>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
-            default: good = moe_gate_up<JB, 4>(a, ring, part, full, empty, sink + warp, ub0, ub1, i, ks, rbase, mine, g0, act, xg); break;
+            // ROWS * 2 matrices * JB <= 8 (the planner never asks for more)
+            case 1: good = moe_gate_up<JB, 1>(a, ring, part, full, empty, done, pfree, sink + warp, nB, i, ks, rbase, mine, g0, act, xg); break;
+            case 2: good = moe_gate_up<JB, 2>(a, ring, part, full, empty, done, pfree, sink + warp, nB, i, ks, rbase, mine, g0, act, xg); break;
+            default: good = moe_gate_up<JB, 4 / JB>(a, ring, part, full, empty, done, pfree, sink + warp, nB, i, ks, rbase, mine, g0, act, xg); break;
         }
     }
-    named_sync(1, CW * 32);
-    if (good) {
-        const int nrb = (ub1 - ub0) * TRb;
-        for (int lr = tid; lr < nrb; lr += CW * 32) {
-            const int u = ub0 + lr / TRb;
-            const int slot = u / ntb, row = (u - slot * ntb) * TRb + lr % TRb;
-            if (row >= I) continue;
-            float gs = 0.f, us = 0.f;
-            for (int k = 0; k < a.KSb; ++k) {
-                gs += part[(lr * 2) * a.KSb + k];
-                us += part[(lr * 2 + 1) * a.KSb + k];
-            }
-            a.mid[(size_t)slot * I + row] = silu_mul(gs, us);
-        }
-    }
-    __threadfence();
-    named_sync(1, CW * 32);
     RB_STAMP(3);
-    if (tid == 0) s_misc[2] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
-    named_sync(1, CW * 32);
-    RB_STAMP(4);
-    good = good && !s_misc[2];
-
-    if (good) {  // C: down + combine
+    if (!good) return;
+    {  // C: down
         const int ks = warp % a.KSc, grp = warp / a.KSc;
         const int g0 = ks * 32 * JC + lane;
         const bool mine = grp < a.NGc;
         bool act[JC];
 #pragma unroll
-        for (int q = 0; q < JC; ++q) act[q] = mine && g0 + 32 * q < Gc;
+        for (int q = 0; q < JC; ++q) act[q] = mine && g0 + 32 * q < (a.tc.cols >> 5);
         const int rbase = grp * a.ROWSc;
         switch (a.ROWSc) {
-            case 1: good = moe_down<JC, 1>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
-            case 2: good = moe_down<JC, 2>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
-            case 4: good = moe_down<JC, 4>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
-            default: good = moe_down<JC, 8>(a, ring, part, full, empty, sink + warp, nact, c0, c1, i, ks, rbase, mine, g0, act); break;
+            case 1: moe_down<JC, 1>(a, ring, part, full, empty, done, pfree, sink + warp, xbuf, xb, xfull, xfree, key0, uc0, uc1, i, ks, rbase, mine, g0, act); break;
+            case 2: moe_down<JC, 2>(a, ring, part, full, empty, done, pfree, sink + warp, xbuf, xb, xfull, xfree, key0, uc0, uc1, i, ks, rbase, mine, g0, act); break;
+            case 4: moe_down<JC, 4>(a, ring, part, full, empty, done, pfree, sink + warp, xbuf, xb, xfull, xfree, key0, uc0, uc1, i, ks, rbase, mine, g0, act); break;
+            // ROWS * JC <= 8 (the planner never asks for more)
+            default: moe_down<JC, 8 / JC>(a, ring, part, full, empty, done, pfree, sink + warp, xbuf, xb, xfull, xfree, key0, uc0, uc1, i, ks, rbase, mine, g0, act); break;
         }
     }
-    named_sync(1, CW * 32);
-    RB_STAMP(5);
-    if (!good) return;
-    for (int lr = tid; lr < (c1 - c0) * TRc; lr += CW * 32) {
-        const int row = c0 * TRc + lr;
-        if (row >= H) continue;
-        float delta = 0.f;
-        for (int j = 0; j < nact; ++j) {
-            float d = 0.f;
-            for (int k = 0; k < a.KSc; ++k) d += part[(lr * nact + j) * a.KSc + k];
-            delta += s_w[j] * d;
-        }
-        a.h_out[row] = a.h_in[row] + delta;
-    }
-    RB_STAMP(6);
+    RB_STAMP(4);
 }
 
 const void *moe_fused_kernel(int JB, int JC) {
