@@ -39,10 +39,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 H, I, E, TOPK = 4096, 14336, 8, 2
-LAYERS = 32
+LAYERS = 32  # distinct layers per step (--layers)
 SEED = 1
 METRIC = "MoE decode int4 expert GB/s (Mixtral-shaped layer, batch 1)"
-WORKLOAD = "Mixtral-shaped MoE layer decode x 32 distinct layers per step"
+WORKLOAD = "Mixtral-shaped MoE layer decode x {} distinct layers per step"
 
 
 def measured_peak():
@@ -184,6 +184,43 @@ def cpu_baseline_single(layer) -> dict:
             "sample": f"{n} Mixtral-shaped token-layers (moe_step, 1 thread), {secs:.1f} s"}
 
 
+# ------------------------------------------------------------ GEMV ---------
+GEMV_ROWS = GEMV_COLS = 4096  # the single int4 grouped GEMV (quant.c:152-188)
+
+
+def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 200) -> dict:
+    """The batch-1 group-32 int4 GEMV W[4096, 4096] x fp32 x, resident matrices
+    in the tiled layout, `copies` distinct ones in rotation (168 MB > L2),
+    back to back on `stream`, timed with CUDA events."""
+    import torch
+
+    rng = np.random.default_rng(0)
+    mats = [capi.Matrix(synth.int4_blob(rng, GEMV_ROWS, GEMV_COLS), GEMV_ROWS, GEMV_COLS)
+            for _ in range(copies)]
+    x = torch.from_numpy(rng.standard_normal(GEMV_COLS).astype(np.float32)).cuda()
+    y = torch.empty(GEMV_ROWS, device="cuda")
+    s = stream.cuda_stream
+    for m in mats:
+        m.gemv_dev(x.data_ptr(), y.data_ptr(), s)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(iters):
+        mats[i % copies].gemv_dev(x.data_ptr(), y.data_ptr(), s)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    sec = ev0.elapsed_time(ev1) / 1e3 / iters
+    nbytes = synth.int4_nbytes(GEMV_ROWS * GEMV_COLS) + 4 * (GEMV_ROWS + GEMV_COLS)
+    for m in mats:
+        m.free()
+    gbs = nbytes / sec / 1e9
+    return {"metric": "int4 expert GEMV GB/s (4096x4096, batch 1)", "value": round(gbs, 1),
+            "unit": "GB/s", "us_per_gemv": round(sec * 1e6, 3), "bytes_per_gemv": nbytes,
+            "frac_of_hbm_peak": round(gbs / peak, 4), "launches": iters,
+            "l2": f"{copies} distinct matrices in rotation ({copies * nbytes / 1e6:.0f} MB)",
+            "kernel": "k_gemv_g32"}
+
+
 # ------------------------------------------------------------ arms ---------
 def run_reference(args) -> None:
     """--impl reference: the reference's C on all host cores."""
@@ -240,17 +277,19 @@ def run_rabbit(args) -> None:
                                 device_id=torch.device("cuda", local))
     from rabbit_b200 import capi, synth
 
+    L = args.layers
+
     capi.check(capi.lib().rabbit_cuda_set_device(local))
     rng = np.random.default_rng(SEED + rank)
-    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(LAYERS)]
-    norms = [np.ones(H, np.float32) for _ in range(LAYERS)]
+    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
+    norms = [np.ones(H, np.float32) for _ in range(L)]
     size = synth.expert_record_size(H, I)
-    pool = capi.MoePool(records=None, expert_size=size, n_layers=LAYERS, hidden=H, n_experts=E,
+    pool = capi.MoePool(records=None, expert_size=size, n_layers=L, hidden=H, n_experts=E,
                         top_k=TOPK, inter=I, quant=4, rms_ffn=norms, w_router=routers,
                         device=local)
     pool.fill_synthetic(SEED * 1000 + rank)
     per_layer = pool.decode_bytes
-    step_bytes = per_layer * LAYERS
+    step_bytes = per_layer * L
 
     stream = torch.cuda.current_stream()
     s = stream.cuda_stream
@@ -260,7 +299,7 @@ def run_rabbit(args) -> None:
     wts = torch.zeros(8, dtype=torch.float32, device="cuda")
 
     def step():
-        for layer in range(LAYERS):
+        for layer in range(L):
             a, b = bufs[layer & 1], bufs[(layer + 1) & 1]
             pool.decode_dev(layer, a.data_ptr(), b.data_ptr(), ids.data_ptr(), wts.data_ptr(), s)
 
@@ -292,7 +331,7 @@ def run_rabbit(args) -> None:
         ms = float(t.item())
     secs = ms / 1000.0
     value = world * step_bytes * args.steps / secs / 1e9
-    launches = args.steps * LAYERS
+    launches = args.steps * L
     kernel_s = secs / launches
     achieved = per_layer / kernel_s / 1e9
     peak, peak_kind = measured_peak()
@@ -301,13 +340,13 @@ def run_rabbit(args) -> None:
     h_host = rng.standard_normal(H).astype(np.float32)
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(2):
-        for layer in range(LAYERS):
+        for layer in range(L):
             h_host = pool.decode(layer, h_host)[0]
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        for layer in range(LAYERS):
+        for layer in range(L):
             h_host = pool.decode(layer, h_host)[0]
     e2e_s = time.perf_counter() - t0
     if dist:
@@ -315,6 +354,8 @@ def run_rabbit(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_value = world * step_bytes * e2e_steps / e2e_s / 1e9
+
+    gemv = None if args.no_gemv else gemv_item(capi, synth, stream, measured_peak()[0])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -326,10 +367,11 @@ def run_rabbit(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u4 weights, f32 math", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "hidden": H, "inter": I, "experts": E,
-                       "top_k": TOPK, "layers_per_step": LAYERS, "batch": 1,
+            "config": {"workload": WORKLOAD.format(L), "hidden": H, "inter": I, "experts": E,
+                       "top_k": TOPK, "layers_per_step": L, "batch": 1,
                        "expert_bytes_resident_gb": round(pool.stats()["pool_bytes"] / 1e9, 2),
-                       "l2": "inputs larger than L2 (32 distinct layers, 28 GB of experts)",
+                       "l2": (f"inputs larger than L2 ({L} distinct layers, "
+                              f"{pool.stats()['pool_bytes'] / 1e9:.1f} GB of experts)"),
                        "parallelism": f"dp{world} decode replicas" if world > 1 else "single"},
             "tokens_per_s": round(world * args.steps / secs, 2),
             "us_per_token_layer": round(1e6 * secs / launches, 3),
@@ -339,10 +381,11 @@ def run_rabbit(args) -> None:
                          "kernel": "k_moe_decode_g32",
                          "bytes_per_launch": per_layer},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": LAYERS * H * 4,
-                    "d2h_bytes_per_step": LAYERS * (H * 4 + TOPK * 8),
+                    "h2d_bytes_per_step": L * H * 4,
+                    "d2h_bytes_per_step": L * (H * 4 + TOPK * 8),
                     "steps": e2e_steps, "api": "rabbit_cuda_moe_decode (host buffers)"},
             "gpu_launches": launches,
+            "gemv": gemv,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -359,6 +402,9 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["rabbit", "reference"], default="rabbit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="distinct layers per step (small values: profiling cases)")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV line item")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

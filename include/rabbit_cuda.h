@@ -160,19 +160,21 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
  * device's memory between its own arenas, or a serving loop that cannot take
  * the device-wide synchronisation a cudaMalloc/cudaFree brings. The call
  * allocates nothing and frees nothing; its scratch (router scores, the SwiGLU
- * activations, the down-projection rows, a grid-barrier counter and the
- * kernel's work counters) is a fixed 1 MiB array inside this library,
- * present on every device that loads it until the process exits. Models
- * whose scratch does not fit -- about 256 + E*4 + (k + S) * (I + C * H) * 4
- * bytes plus a few KB of counters, with C = I / 1024 when I is a multiple of
- * 1024, else 1 -- are rejected with RABBIT_CUDA_ERR_ARGS, pools not
+ * activations, the down-projection rows, per-CTA flags and a grid-barrier
+ * counter) is a fixed 2 MiB array inside this library, present on every
+ * device that loads it until the process exits. Models whose scratch does not
+ * fit -- about 5 KB + E*4 + (k + S) * (I + C * H) * 8 bytes, with C the number
+ * of column chunks of W2 (I / 1024 when I is a multiple of 1024) -- are
+ * rejected with RABBIT_CUDA_ERR_ARGS, pools not
  * in the group-32 layout with RABBIT_CUDA_ERR_UNSUPPORTED. The first call on
  * each device looks up the array's device address (once, with that device
  * current); make that first call before any stream capture. Every call uses
  * the same array, which keeps what the last call left there: the call clears
- * the counters on `stream` before its kernel, and calls that overlap on the
- * GPU (other streams, other pools on the same device) race on the array and
- * give wrong results. d_ids / d_weights may be NULL. Errors surface through
+ * the grid-barrier counter on `stream` before its kernel, and the values its
+ * CTAs share carry a tag new to each call, so leftovers are never read. Calls
+ * that overlap on the GPU (other streams, other pools on the same device) race
+ * on the array and give wrong results. d_ids / d_weights may be NULL. Errors
+ * surface through
  * rabbit_cuda_moe_check as for rabbit_cuda_moe_decode_dev. */
 int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                        float *d_h_out, int *d_ids, float *d_weights,
