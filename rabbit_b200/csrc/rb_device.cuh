@@ -134,6 +134,19 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     return p;
 }
 
+// Programmatic dependent launch. `launch_dependents`: this CTA no longer
+// holds back the launch of the next kernel on the stream (it launches once
+// every CTA has said so or exited). `wait_prerequisite`: block until the
+// preceding kernel on the stream has completed and its memory is visible.
+// Both are no-ops for a launch without the programmatic-serialization
+// attribute.
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_prerequisite() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Named barrier among `threads` threads (a multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -115,13 +115,14 @@ bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p) {
     const int CW = p->KS * p->NG;
     p->block = (CW + 1) * 32;
     const size_t part = align_up((size_t)p->tiles_cta_max * TR * p->KS * 4, 16);
-    long long ns =
-        ((long long)kMaxDynSmem - (long long)part - 16 * 24 - 128) / p->til.tile_stride;
+    // J == 1: two CTAs per SM (consecutive launches overlap), 113 KB each
+    const long long cap = p->J == 1 ? 113 * 1024 : kMaxDynSmem;
+    long long ns = (cap - (long long)part - 16 * 24 - 128) / p->til.tile_stride;
     if (ns > 24) ns = 24;
     if (ns < 2) return false;
     p->nslots = (int)ns;
     p->smem = (size_t)ns * p->til.tile_stride + part + 16 * (size_t)ns + 4 * 32;
-    return p->smem <= (size_t)kMaxDynSmem;
+    return p->smem <= (size_t)cap;
 }
 
 // The consumer loop of one warp over the CTA's nt tiles: ROWS rows of every
@@ -144,8 +145,11 @@ __device__ __forceinline__ bool gemv_tiles(const G32Args &a, const uint8_t *ring
     return true;
 }
 
+// J == 1 (rows up to 8192 inputs): two CTAs per SM (<= 113 KB of shared
+// memory, <= 113 registers a thread), so a launch that follows this one on
+// the stream can stream its weights while this one finishes.
 template <int J>
-__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_gemv_g32(G32Args a) {
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, J == 1 ? 2 : 1) k_gemv_g32(G32Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int CW = a.KS * a.NG;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -171,6 +175,9 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_gemv_g32(G32Ar
         }
         mbar_init_fence();
     }
+    // The next kernel on the stream may launch now; it waits for this one to
+    // complete before it touches its own x / y (wait_prerequisite below).
+    launch_dependents();
     __syncthreads();
 
     if (warp == CW) {  // ---------------------------------------- producer
@@ -201,6 +208,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, 1) k_gemv_g32(G32Ar
     const int g0 = ks * 32 * J + lane;
     bool act[J];
     XPlanes xg[J];
+    // x may be the output of the preceding kernel, and y may still be read by
+    // it: nothing below touches either before that kernel has completed. The
+    // weights (uploaded by copies, not written by a kernel) are already
+    // streaming in.
+    wait_prerequisite();
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         act[j] = g0 + 32 * j < G;

@@ -41,8 +41,21 @@ static int launch_g32(const G32Plan &p, const uint8_t *tiles, const float *x, fl
     a.tiles_cta_max = p.tiles_cta_max;
     a.err = c->d_err;
     a.wait_ns = wait_limit_ns();
+    // Programmatic dependent launch: this GEMV may start (and stream its
+    // weights) while the kernel before it on the stream finishes; it waits
+    // for that kernel before reading x or writing y.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(p.block);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     void *args[] = {&a};
-    RB_CUDA(cudaLaunchKernel(gemv_g32_kernel(p.J), dim3(p.grid), dim3(p.block), args, p.smem, s));
+    RB_CUDA(cudaLaunchKernelExC(&cfg, gemv_g32_kernel(p.J), args));
     return RABBIT_CUDA_OK;
 }
 
