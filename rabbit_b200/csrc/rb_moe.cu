@@ -118,6 +118,27 @@ static unsigned next_seq(unsigned *seq, void *tagged[], const size_t bytes[], in
     return (*seq)++;
 }
 
+// One fused decode launch: cooperative (all CTAs resident: they wait on one
+// another's data) and programmatic-dependent (it may start while the kernel
+// before it on the stream finishes; it waits for that kernel before reading h
+// or touching scratch).
+static cudaError_t launch_fused(const rabbit_cuda_moe *p, MoeFusedArgs &a, cudaStream_t s) {
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p->grid);
+    cfg.blockDim = dim3(p->block);
+    cfg.dynamicSmemBytes = p->smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    void *args[] = {&a};
+    return cudaLaunchKernelExC(&cfg, moe_fused_kernel(a.JB, a.JC), args);
+}
+
 // Shared-memory bytes in front of the ring, in the order k_moe_decode_g32
 // carves them: xn, reduction scratch, slot records/weights, flags, scores.
 static size_t fused_head_bytes(int H, int E) {
@@ -134,7 +155,7 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     MoeFusedArgs &a = p->plan;
     a.JB = lane_groups(H / 32);
     a.KSb = kslices(H / 32, a.JB);
-    a.NGb = std::max(1, kConsumerWarps / a.KSb);  // warp groups in phase B
+    a.NGb = std::max(1, kMoeConsumerWarps / a.KSb);  // warp groups in phase B
     // W2 is split into column chunks of CG groups: the largest divisor of I/32
     // up to 32 (1024 inputs), at most 16 chunks. A CTA then needs only its
     // chunk of mid, not all of it.
@@ -146,7 +167,7 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     if (KCc > 16) return false;
     a.JC = lane_groups(CG);
     a.KSc = kslices(CG, a.JC);
-    a.NGc = std::max(1, kConsumerWarps / a.KSc);  // warp groups in phase C
+    a.NGc = std::max(1, kMoeConsumerWarps / a.KSc);  // warp groups in phase C
     const int CW = std::max(a.KSb * a.NGb, a.KSc * a.NGc);
     a.CW = CW;
 
@@ -538,9 +559,7 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         }
         a.err = p->ctx->d_err;
         a.wait_ns = wait_limit_ns();
-        void *args[] = {&a};
-        RB_CUDA(cudaLaunchCooperativeKernel(moe_fused_kernel(a.JB, a.JC), dim3(p->grid),
-                                            dim3(p->block), args, p->smem, s));
+        RB_CUDA(launch_fused(p, a, s));
     } else {
         MoeGenericArgs a;
         a.h_in = d_h_in;
@@ -671,9 +690,7 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     }
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
-    void *args[] = {&a};
-    RB_CUDA(cudaLaunchCooperativeKernel(moe_fused_kernel(a.JB, a.JC), dim3(p->grid),
-                                        dim3(p->block), args, p->smem, s));
+    RB_CUDA(launch_fused(p, a, s));
     p->hbm_hits++;
     return ok();
 }

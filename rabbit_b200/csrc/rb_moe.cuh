@@ -10,6 +10,7 @@ namespace rb {
 constexpr int kMaxSlots = 72;  // top-k (<= 8) + shared (<= 64)
 constexpr int kPartRing = 8;   // partial-sum regions between consumers and epilogue
 constexpr int kMaxGrid = 1024; // CTAs of the fused kernel (one per SM)
+constexpr int kMoeConsumerWarps = 8;  // consumer warps of the fused kernel (2 per SM sub-partition)
 
 // Routing result shared by the generic kernels (device memory).
 struct Route {

@@ -299,8 +299,14 @@ __device__ __forceinline__ bool moe_down(const MoeFusedArgs &a, const uint8_t *r
     XPlanes xg[J];
     int cur = -1;
     RB_DBG(5);
+    // (slot, chunk) key of unit u, relative to the CTA's first, tracked
+    // incrementally: units run in (slot, chunk, row tile) order
+    int kk = 0, t_in_key = (uc0 % ntc) % rt;
     for (int u = uc0; u < uc1; ++u, ++i) {
-        const int j = u / ntc, kk = j * a.tc.KC + (u - j * ntc) / rt - key0;
+        if (u > uc0 && ++t_in_key == rt) {
+            t_in_key = 0;
+            ++kk;
+        }
         if (kk != cur) {
             cur = kk;
             const int b = kk & 1;
@@ -331,7 +337,7 @@ __device__ __forceinline__ bool moe_down(const MoeFusedArgs &a, const uint8_t *r
 }
 
 template <int JB, int JC>
-__global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
+__global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nthr = blockDim.x;
     const int H = a.H, I = a.I, CW = a.CW;
@@ -388,21 +394,26 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
             mbar_init(&xfree[b], CW);  // every consumer warp, after its planes
         }
         mbar_init_fence();
-        // h and the norm weights, behind the router block in the idle ring
-        mbar_arrive_expect_tx(hbar, 8u * (uint32_t)H);
+        // The norm weights and (small routers) the router block go to the
+        // idle ring at once: they are weights, not written by the kernel
+        // before this one on the stream. h is: its copy waits for that kernel
+        // (programmatic dependent launch; a no-op for a plain launch).
         const uint64_t pol_h = policy_evict_last();
-        bulk_g2s(hs, a.h_in, 4u * (uint32_t)H, hbar, pol_h);
+        mbar_arrive_expect_tx(hbar, 8u * (uint32_t)H);
         bulk_g2s(rs, a.rms, 4u * (uint32_t)H, hbar, pol_h);
         if (a.route_local) {
-            // The ring is idle until routing is done: stage the layer's router
-            // block [E, H] there while the CTA computes the norm.
             mbar_arrive_expect_tx(rbar, router_bytes);
             const uint64_t pol = policy_evict_last();  // every CTA reads it
             for (uint32_t o = 0; o < router_bytes; o += 32768u)
                 bulk_g2s(ring + o, reinterpret_cast<const uint8_t *>(a.router) + o,
                          router_bytes - o < 32768u ? router_bytes - o : 32768u, rbar, pol);
         }
+        wait_prerequisite();
+        bulk_g2s(hs, a.h_in, 4u * (uint32_t)H, hbar, pol_h);
     }
+    // The next kernel on the stream may launch now (it waits for this one
+    // before it reads h or touches scratch).
+    launch_dependents();
 
     // ------------------------------------------------ A: rmsnorm + router --
     // no thread may touch a barrier before thread 0 has initialised it
@@ -417,32 +428,38 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
         }
     }
     RB_DBG(1);
+    // rmsnorm (forward_v2.c:61-69): x * (1 / sqrt(mean(x^2) + 1e-5)) * w
+    const float4 *hs4 = reinterpret_cast<const float4 *>(hs);
+    const float4 *rs4 = reinterpret_cast<const float4 *>(rs);
     float ss = 0.f;
-    for (int i = tid; i < H; i += nthr) {
-        const float v = hs[i];
-        ss += v * v;
+    for (int i4 = tid; i4 < (H >> 2); i4 += nthr) {
+        const float4 v = hs4[i4];
+        ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
     }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
-    if (tid == 0) {
-        float t = 0.f;
-        for (int w = 0; w < (nthr >> 5); ++w) t += red[w];
-        t /= (float)H;
-        red[31] = 1.0f / sqrtf(t + 1e-5f);  // forward_v2.c:61-69
+    if (warp == 0) {
+        float t = lane < (nthr >> 5) ? red[lane] : 0.f;
+        t = warp_sum(t);
+        if (lane == 0) red[31] = 1.0f / sqrtf(t / (float)H + 1e-5f);
     }
     __syncthreads();
     const float inv = red[31];
-    for (int i = tid; i < H; i += nthr) xn[xpad(i)] = (hs[i] * inv) * rs[i];
+    for (int i4 = tid; i4 < (H >> 2); i4 += nthr) {
+        const float4 v = hs4[i4], w = rs4[i4];
+        float *xp = xn + xpad(i4 * 4);  // four floats of one group
+        xp[0] = (v.x * inv) * w.x;
+        xp[1] = (v.y * inv) * w.y;
+        xp[2] = (v.z * inv) * w.z;
+        xp[3] = (v.w * inv) * w.w;
+    }
     __syncthreads();
-    if (tid == 0)  // this CTA is done with h_in (it may be h_out)
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.flags + blockIdx.x), "r"(a.seq)
-                     : "memory");
     RB_DBG(2);
     if (a.route_local) {
         // Every CTA scores every expert itself from the staged router: warp w
-        // takes rows w, w + 9, ...; lane l sums inputs 4l + 128t in order,
-        // then a fixed butterfly. The code and order are the same in every
+        // takes rows w, w + 11, ...; lane l sums inputs 4l + 128t in four
+        // chains, then a fixed butterfly. The code and order are the same in every
         // CTA, so every CTA gets the same scores and the same top-k, and no
         // grid barrier is needed.
         const bool okr = mbar_wait(rbar, 0, a.wait_ns, a.err);
@@ -452,18 +469,22 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
         }
         RB_DBG(3);
         const float *rt = reinterpret_cast<const float *>(ring);
+        // lane l reads inputs 4l + 128t (t < nq): padded xn index xpad(4l) + 132t
+        const float *xl = xn + xpad(4 * lane);
+        const int nq = (H >> 2) > lane ? ((H >> 2) - lane + 31) >> 5 : 0;
         for (int e = warp; e < a.E; e += nthr >> 5) {
-            const float4 *wr = reinterpret_cast<const float4 *>(rt + (size_t)e * H);
-            float d = 0.f;
-            for (int i4 = lane; i4 < (H >> 2); i4 += 32) {
-                const float4 w = wr[i4];
-                const float *xp = xn + xpad(i4 * 4);
-                d = fmaf(w.x, xp[0], d);
-                d = fmaf(w.y, xp[1], d);
-                d = fmaf(w.z, xp[2], d);
-                d = fmaf(w.w, xp[3], d);
+            const float4 *wr = reinterpret_cast<const float4 *>(rt + (size_t)e * H) + lane;
+            const float *xp = xl;
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four independent chains
+#pragma unroll 4
+            for (int t = 0; t < nq; ++t, wr += 32, xp += 132) {
+                const float4 w = *wr;
+                d0 = fmaf(w.x, xp[0], d0);
+                d1 = fmaf(w.y, xp[1], d1);
+                d2 = fmaf(w.z, xp[2], d2);
+                d3 = fmaf(w.w, xp[3], d3);
             }
-            d = warp_sum(d);
+            const float d = warp_sum((d0 + d1) + (d2 + d3));
             if (lane == 0) s_sc[e] = d;
         }
         if (tid == 0) s_misc[2] = 0;
@@ -502,6 +523,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
         int *ids = reinterpret_cast<int *>(red);
         float *w = red + 8;
         topk_softmax_warp(s_sc, a.E, a.k, ids, w);
+        RB_DBG(8);
     }
     if (tid == 0) {
         const int *ids = reinterpret_cast<const int *>(red);
@@ -513,6 +535,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
             }
         }
         s_misc[0] = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+        RB_DBG(9);
     }
     __syncthreads();
     RB_STAMP(2);
@@ -527,8 +550,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
     const int UB = nact * ntb;  // gate/up units (slot, GU tile), dealt round-robin
     const int nB = UB > bx ? (UB - bx + G - 1) / G : 0;
     const int UC = nact * ntc;  // down units (slot, chunk, row tile), contiguous ranges
-    const int uc0 = (int)((long long)bx * UC / G);
-    const int uc1 = (int)((long long)(bx + 1) * UC / G);
+    const int uc0 = bx * UC / G;  // bx * UC < 2^31: UC <= 72 * 16 * 16384 / 1
+    const int uc1 = (bx + 1) * UC / G;
     const uint32_t sb = a.tb.tile_stride, sc = a.tc.tile_stride;
 
     if (warp == CW) {  // -------------------------------------------- producer
@@ -636,6 +659,12 @@ __global__ void __launch_bounds__((kConsumerWarps + 3) * 32, 1) k_moe_decode_g32
         // h_out = h + sum_j w_j sum_c down_jc, slots and chunks in order
         // (forward_v2.c:356-357, 398-399), reading each partial once its tag
         // matches and once every CTA has read h (h_out may be h_in).
+        // This CTA has read h_in (its copy landed before the norm), and
+        // h_out may be h_in: tell the combine owners.
+        if (lane == 0)
+            asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.flags + blockIdx.x),
+                         "r"(a.seq)
+                         : "memory");
         const int rt = a.tc.rtiles;
         const int nU = nB + (uc1 - uc0);
         for (int i = 0; i < nU; ++i) {
