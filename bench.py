@@ -382,7 +382,8 @@ def run_rabbit(args) -> None:
                          "bytes_per_launch": per_layer},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": L * H * 4,
-                    "d2h_bytes_per_step": L * (H * 4 + TOPK * 8),
+                    # one copy per layer: h_out, ids[8], weights[8], error word
+                    "d2h_bytes_per_step": L * (H * 4 + 80),
                     "steps": e2e_steps, "api": "rabbit_cuda_moe_decode (host buffers)"},
             "gpu_launches": launches,
             "gemv": gemv,

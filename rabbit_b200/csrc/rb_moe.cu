@@ -54,8 +54,12 @@ struct rabbit_cuda_moe {
     float *rms = nullptr, *router = nullptr;
     // scratch
     float *scores = nullptr, *mid = nullptr, *xn = nullptr, *down = nullptr;
+    // host-buffer decode: h_in, and one block [h_out (H) | ids (8) | weights
+    // (8) | error word (4)] that comes back to the host in one copy
     float *h_in = nullptr, *h_out = nullptr, *w_int = nullptr;
-    int *ids_int = nullptr;
+    int *ids_int = nullptr, *err_io = nullptr;
+    uint8_t *dio = nullptr;
+    size_t dio_bytes = 0;
     unsigned long long *bar = nullptr;
     unsigned *flags = nullptr;  // fused path: per-CTA "h read" tags
     unsigned seq = 1;           // tag of the next fused launch (never 0)
@@ -225,7 +229,7 @@ static void free_pool(rabbit_cuda_moe *p) {
     if (p->device >= 0) cudaSetDevice(p->device);
     if (p->up) cudaStreamSynchronize(p->up);
     void *bufs[] = {p->pool,  p->rms,  p->router, p->scores,  p->mid, p->xn,  p->down,
-                    p->h_in,  p->h_out, p->w_int, p->ids_int, p->bar, p->route, p->flags};
+                    p->h_in,  p->dio,   p->bar,   p->route,   p->flags};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int i = 0; i < 2; ++i) {
@@ -396,18 +400,22 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         (e = cudaMalloc(&p->flags, sizeof(unsigned) * kMaxGrid)) != cudaSuccess ||
         (e = cudaMemset(p->flags, 0, sizeof(unsigned) * kMaxGrid)) != cudaSuccess ||
         (e = cudaMalloc(&p->h_in, sizeof(float) * p->H)) != cudaSuccess ||
-        (e = cudaMalloc(&p->h_out, sizeof(float) * p->H)) != cudaSuccess ||
-        (e = cudaMalloc(&p->w_int, sizeof(float) * 8)) != cudaSuccess ||
-        (e = cudaMalloc(&p->ids_int, sizeof(int) * 8)) != cudaSuccess ||
+        (e = cudaMalloc(&p->dio, p->dio_bytes = sizeof(float) * (size_t)p->H + 80)) !=
+            cudaSuccess ||
+        (e = cudaMemset(p->dio, 0, p->dio_bytes)) != cudaSuccess ||
         (e = cudaMalloc(&p->bar, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaMalloc(&p->route, sizeof(Route))) != cudaSuccess ||
         (e = cudaMemset(p->bar, 0, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking)) != cudaSuccess ||
-        (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 16))) !=
+        (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 32))) !=
             cudaSuccess) {
         free_pool(p);
         return cuda_fail(e, "moe_create: scratch");
     }
+    p->h_out = reinterpret_cast<float *>(p->dio);
+    p->ids_int = reinterpret_cast<int *>(p->dio + sizeof(float) * (size_t)p->H);
+    p->w_int = reinterpret_cast<float *>(p->ids_int + 8);
+    p->err_io = reinterpret_cast<int *>(p->w_int + 8);
     // staging holds up to one record image (verbatim or tiled, whichever is larger)
     const uint64_t pin_bytes =
         std::min<uint64_t>(kPinChunk, align_up(std::max<uint64_t>(p->expert_size, p->rec_stride), 4096));
@@ -511,9 +519,13 @@ int rabbit_cuda_moe_free(rabbit_cuda_moe *p) {
     return ok();
 }
 
-int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
-                               float *d_h_out, int *d_ids, float *d_weights, void *stream) {
-    if (!p || !d_h_in || !d_h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: NULL argument");
+}  // extern "C"
+
+namespace rb {
+// The body of rabbit_cuda_moe_decode_dev; `err` is the device word the fused
+// kernel records a failed wait in.
+static int decode_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                       int *d_ids, float *d_weights, cudaStream_t s, int *err) {
     int base, n_local;
     int st = layer_map(p, layer, &base, &n_local);
     if (st) return st;
@@ -521,7 +533,6 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         if (!p->resident[base + r])
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: layer %d not uploaded", layer);
     RB_CUDA(cudaSetDevice(p->device));
-    cudaStream_t s = as_stream(stream, p->ctx);
     int *ids = d_ids ? d_ids : p->ids_int;
     float *w = d_weights ? d_weights : p->w_int;
     const float *rms = p->rms + (size_t)layer * p->H;
@@ -552,12 +563,12 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
         a.down = reinterpret_cast<unsigned long long *>(p->down);
         a.flags = p->flags;
         a.bar = p->bar;
+        a.err = err;
         {
             void *tagged[] = {p->mid, p->down, p->flags};
             const size_t bytes[] = {mid_bytes(p), down_bytes(p), sizeof(unsigned) * kMaxGrid};
             a.seq = next_seq(&p->seq, tagged, bytes, 3, s);
         }
-        a.err = p->ctx->d_err;
         a.wait_ns = wait_limit_ns();
         RB_CUDA(launch_fused(p, a, s));
     } else {
@@ -594,6 +605,16 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
     }
     p->hbm_hits++;
     return ok();
+}
+}  // namespace rb
+
+extern "C" {
+
+int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                               float *d_h_out, int *d_ids, float *d_weights, void *stream) {
+    if (!p || !d_h_in || !d_h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: NULL argument");
+    return decode_impl(p, layer, d_h_in, d_h_out, d_ids, d_weights, as_stream(stream, p->ctx),
+                       p->ctx->d_err);
 }
 
 // ------------------------------------------------------- no-alloc decode --
@@ -717,22 +738,29 @@ int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, flo
     RB_CUDA(cudaSetDevice(p->device));
     cudaStream_t s = p->ctx->stream;
     const size_t hb = sizeof(float) * p->H;
+    // pinned: [h_in (H)] [h_out (H) | ids (8) | weights (8) | error word], the
+    // second part a mirror of the device block p->dio
     float *pin_h = p->pin_io;
-    float *pin_w = p->pin_io + 2 * (size_t)p->H;
-    int *pin_ids = reinterpret_cast<int *>(pin_w + 8);
+    uint8_t *pin_o = reinterpret_cast<uint8_t *>(p->pin_io + p->H);
     memcpy(pin_h, h_in, hb);
     RB_CUDA(cudaMemcpyAsync(p->h_in, pin_h, hb, cudaMemcpyHostToDevice, s));
-    int st = rabbit_cuda_moe_decode_dev(p, layer, p->h_in, p->h_out, p->ids_int, p->w_int, s);
+    int st = decode_impl(p, layer, p->h_in, p->h_out, p->ids_int, p->w_int, s, p->err_io);
     if (st) return st;
-    RB_CUDA(cudaMemcpyAsync(pin_h + p->H, p->h_out, hb, cudaMemcpyDeviceToHost, s));
-    if (p->k > 0) {
-        RB_CUDA(cudaMemcpyAsync(pin_ids, p->ids_int, sizeof(int) * p->k, cudaMemcpyDeviceToHost, s));
-        RB_CUDA(cudaMemcpyAsync(pin_w, p->w_int, sizeof(float) * p->k, cudaMemcpyDeviceToHost, s));
+    RB_CUDA(cudaMemcpyAsync(pin_o, p->dio, p->dio_bytes, cudaMemcpyDeviceToHost, s));
+    RB_CUDA(cudaStreamSynchronize(s));
+    const int err = *reinterpret_cast<const int *>(pin_o + (p->dio_bytes - 16));
+    if (err != 0) {
+        // a wait that gave up may have left grid-barrier arrivals behind
+        cudaMemsetAsync(p->err_io, 0, sizeof(int), s);
+        cudaMemsetAsync(p->bar, 0, sizeof(unsigned long long), s);
+        cudaStreamSynchronize(s);
+        if (err == RB_ERR_TIMEOUT)
+            return fail(RABBIT_CUDA_ERR_TIMEOUT, "moe_decode: a bounded device wait ran out");
+        return fail(RABBIT_CUDA_ERR_DEVICE, "moe_decode: device error code %d", err);
     }
-    if ((st = rabbit_cuda_moe_check(p, s)) != RABBIT_CUDA_OK) return st;
-    memcpy(h_out, pin_h + p->H, hb);
-    if (ids) memcpy(ids, pin_ids, sizeof(int) * p->k);
-    if (weights) memcpy(weights, pin_w, sizeof(float) * p->k);
+    memcpy(h_out, pin_o, hb);
+    if (ids) memcpy(ids, pin_o + hb, sizeof(int) * p->k);
+    if (weights) memcpy(weights, pin_o + hb + 32, sizeof(float) * p->k);
     if (k_out) *k_out = p->k;
     return ok();
 }
