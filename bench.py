@@ -211,14 +211,34 @@ def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 2
     torch.cuda.synchronize()
     sec = ev0.elapsed_time(ev1) / 1e3 / iters
     nbytes = synth.int4_nbytes(GEMV_ROWS * GEMV_COLS) + 4 * (GEMV_ROWS + GEMV_COLS)
+    gbs = nbytes / sec / 1e9
+    # the same matrices as one launch of `copies` independent GEMVs sharing x
+    # (rabbit_cuda_matrix_gemv_batch_dev); each launch streams all of them
+    ys = [torch.empty(GEMV_ROWS, device="cuda") for _ in range(copies)]
+    xp, yp = [x.data_ptr()] * copies, [t.data_ptr() for t in ys]
+    for _ in range(3):
+        capi.gemv_batch_dev(mats, xp, yp, s)
+    torch.cuda.synchronize()
+    biters = max(1, iters // copies)
+    ev0.record(stream)
+    for _ in range(biters):
+        capi.gemv_batch_dev(mats, xp, yp, s)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    bsec = ev0.elapsed_time(ev1) / 1e3 / (biters * copies)
+    bgbs = nbytes / bsec / 1e9
     for m in mats:
         m.free()
-    gbs = nbytes / sec / 1e9
     return {"metric": "int4 expert GEMV GB/s (4096x4096, batch 1)", "value": round(gbs, 1),
             "unit": "GB/s", "us_per_gemv": round(sec * 1e6, 3), "bytes_per_gemv": nbytes,
             "frac_of_hbm_peak": round(gbs / peak, 4), "launches": iters,
             "l2": f"{copies} distinct matrices in rotation ({copies * nbytes / 1e6:.0f} MB)",
-            "kernel": "k_gemv_g32"}
+            "kernel": "k_gemv_g32", "mode": "one GEMV per launch, each after the previous",
+            "batched": {"value": round(bgbs, 1), "unit": "GB/s",
+                        "us_per_gemv": round(bsec * 1e6, 3),
+                        "frac_of_hbm_peak": round(bgbs / peak, 4),
+                        "mode": f"{copies} independent GEMVs (shared x) per launch, "
+                                "rabbit_cuda_matrix_gemv_batch_dev", "launches": biters}}
 
 
 # ------------------------------------------------------------ arms ---------

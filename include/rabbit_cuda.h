@@ -97,6 +97,15 @@ int rabbit_cuda_matrix_gemv_dev(const rabbit_cuda_matrix *m, const float *d_x, f
                                 void *stream);
 /* Same with HOST x / y: copies in, GEMV, copies out, synchronises. */
 int rabbit_cuda_matrix_gemv(const rabbit_cuda_matrix *m, const float *x, float *y);
+/* n independent GEMVs in one launch (no counterpart in the reference, which
+ * calls rabbit_gemv_int4_grouped once per matrix): d_y[i] = m[i] d_x[i] for
+ * 1 <= n <= 32 resident matrices of one device, shape and format, e.g. the
+ * projections that share one input. The matrices' tiles stream back to back
+ * through every SM, so the fixed cost of a launch and of its dependency on
+ * the previous kernel is paid once; x planes are built once when every d_x[i]
+ * is the same pointer. Same conventions as rabbit_cuda_matrix_gemv_dev. */
+int rabbit_cuda_matrix_gemv_batch_dev(const rabbit_cuda_matrix *const *m, int n,
+                                      const float *const *d_x, float *const *d_y, void *stream);
 /* Algorithmic bytes one GEMV streams: the blob (4 + 4*ceil(n/32) + n/2)
  * plus x and y in fp32. */
 uint64_t rabbit_cuda_matrix_bytes(const rabbit_cuda_matrix *m);

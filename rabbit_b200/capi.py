@@ -49,6 +49,7 @@ SIGNATURES = {
     "rabbit_cuda_matrix_upload": (_I, [_P, _I, _I, C.POINTER(_P)]),
     "rabbit_cuda_matrix_free": (_I, [_P]),
     "rabbit_cuda_matrix_gemv_dev": (_I, [_P, _P, _P, _P]),
+    "rabbit_cuda_matrix_gemv_batch_dev": (_I, [_P, _I, _P, _P, _P]),
     "rabbit_cuda_matrix_gemv": (_I, [_P, _P, _P]),
     "rabbit_cuda_matrix_bytes": (C.c_uint64, [_P]),
     "rabbit_cuda_moe_create": (_I, [C.POINTER(MoeDesc), _I, C.POINTER(_P)]),
@@ -142,6 +143,16 @@ class Matrix:
             self.free()
         except Exception:
             pass
+
+
+def gemv_batch_dev(mats, d_xs, d_ys, stream: int = 0) -> None:
+    """d_ys[i] = mats[i] @ d_xs[i] in one launch (rabbit_cuda_matrix_gemv_batch_dev);
+    device pointers as ints, one shape for all matrices."""
+    n = len(mats)
+    hs = (C.c_void_p * n)(*[m.handle.value for m in mats])
+    xs = (C.c_void_p * n)(*d_xs)
+    ys = (C.c_void_p * n)(*d_ys)
+    check(lib().rabbit_cuda_matrix_gemv_batch_dev(hs, n, xs, ys, stream or None))
 
 
 class MoePool:

@@ -27,6 +27,23 @@
 
 namespace rb {
 
+#ifdef RB_PHASE_TIMERS
+// Diagnostic build only: for CTA 0 of each launch, %globaltimer at kernel
+// start, after the wait for the preceding kernel, at the first tile and at
+// the end; a ring of 64 launches.
+__device__ uint64_t g_gemv_ns[64 * 4];
+__device__ unsigned g_gemv_launch;
+#define RB_GEMV_STAMP(slot, k)                                              \
+    do {                                                                    \
+        if (blockIdx.x == 0 && threadIdx.x == 0)                            \
+            g_gemv_ns[((slot) & 63) * 4 + (k)] = globaltimer_ns();          \
+    } while (0)
+#else
+#define RB_GEMV_STAMP(slot, k) \
+    do {                       \
+    } while (0)
+#endif
+
 // Per-SM streaming rate and fixed cost of one bulk copy issued by one
 // thread, used to size tiles (measured on B200: 16-40 KB single copies stream
 // at 6.6-7 TB/s; 8 KB copies from one issuing thread at ~3.3 TB/s, i.e.
@@ -110,9 +127,15 @@ bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p) {
     p->ROWS = choose_rows(rows, 1, true, sm_count, row_bytes, p->NG, 8 / p->J, 48 * 1024);
     const int TR = p->NG * p->ROWS;
     p->til = make_tiling(rows, in_dim, TR);
-    p->grid = p->til.ntiles < sm_count ? p->til.ntiles : sm_count;
-    p->tiles_cta_max = (p->til.ntiles + p->grid - 1) / p->grid;
-    const int CW = p->KS * p->NG;
+    return plan_g32_batch(*p, 1, sm_count, p);
+}
+
+bool plan_g32_batch(const G32Plan &one, int nmat, int sm_count, G32Plan *p) {
+    *p = one;
+    const long long total = (long long)nmat * p->til.ntiles;
+    p->grid = total < sm_count ? (int)total : sm_count;
+    p->tiles_cta_max = (int)((total + p->grid - 1) / p->grid);
+    const int CW = p->KS * p->NG, TR = p->til.TR;
     p->block = (CW + 1) * 32;
     const size_t part = align_up((size_t)p->tiles_cta_max * TR * p->KS * 4, 16);
     // J == 1: two CTAs per SM (consecutive launches overlap), 113 KB each
@@ -125,16 +148,30 @@ bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p) {
     return p->smem <= (size_t)cap;
 }
 
-// The consumer loop of one warp over the CTA's nt tiles: ROWS rows of every
-// tile starting at rbase, J groups per lane. False when a wait ran out.
+// The consumer loop of one warp over the CTA's tiles [t0, t0 + nt) of the
+// launch's matrix-major tile range: ROWS rows of every tile starting at
+// rbase, J groups per lane, x planes (re)built when the matrix changes (once
+// if x is shared). False when a wait ran out.
 template <int J, int ROWS>
 __device__ __forceinline__ bool gemv_tiles(const G32Args &a, const uint8_t *ring, float *part,
                                            uint64_t *full, uint64_t *empty, uint32_t *sink,
-                                           int nt, int ks, int rbase, int g0,
-                                           const bool (&act)[J], const XPlanes (&xg)[J]) {
+                                           int t0, int nt, int ks, int rbase, int g0,
+                                           const bool (&act)[J]) {
     const int G = a.til.in_dim >> 5, half = a.til.in_dim >> 1, TR = a.til.TR, KS = a.KS;
     const uint32_t stride = a.til.tile_stride;
-    for (int i = 0; i < nt; ++i) {
+    XPlanes xg[J];
+    int mcur = -1, m = t0 / a.til.ntiles, tin = t0 - m * a.til.ntiles;
+    for (int i = 0; i < nt; ++i, ++tin) {
+        if (tin == a.til.ntiles) {
+            tin = 0;
+            ++m;
+        }
+        if (m != mcur && (mcur < 0 || !a.shared_x)) {
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                load_xplanes_global(xg[j], a.x[m] + (size_t)(g0 + 32 * j) * 32, act[j]);
+        }
+        mcur = m;
         const int s = i % a.nslots, n = i / a.nslots;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], n & 1, a.wait_ns, a.err))) return false;
         const int lb = i * TR + rbase;
@@ -154,6 +191,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, J == 1 ? 2 : 1) k_g
     const int CW = a.KS * a.NG;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.til.in_dim >> 5;
+#ifdef RB_PHASE_TIMERS
+    unsigned slot = 0;
+    if (blockIdx.x == 0 && threadIdx.x == 0) slot = atomicAdd(&g_gemv_launch, 1u);
+#endif
+    RB_GEMV_STAMP(slot, 0);
     const int TR = a.til.TR;
     const uint32_t stride = a.til.tile_stride;
 
@@ -164,8 +206,9 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, J == 1 ? 2 : 1) k_g
     uint64_t *empty = full + a.nslots;
     uint32_t *sink = reinterpret_cast<uint32_t *>(empty + a.nslots);  // one word per warp
 
-    const int t0 = (int)((long long)blockIdx.x * a.til.ntiles / gridDim.x);
-    const int t1 = (int)((long long)(blockIdx.x + 1) * a.til.ntiles / gridDim.x);
+    const long long total = (long long)a.nmat * a.til.ntiles;  // matrix-major tile range
+    const int t0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int t1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
     const int nt = t1 - t0;
 
     if (threadIdx.x == 0) {
@@ -184,11 +227,16 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, J == 1 ? 2 : 1) k_g
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             int issued = 0;
-            for (int i = 0; i < nt; ++i) {
+            int m = t0 / a.til.ntiles, tin = t0 - m * a.til.ntiles;
+            for (int i = 0; i < nt; ++i, ++tin) {
+                if (tin == a.til.ntiles) {
+                    tin = 0;
+                    ++m;
+                }
                 const int s = i % a.nslots, n = i / a.nslots;
                 if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.wait_ns, a.err, 0)) break;
                 mbar_arrive_expect_tx(&full[s], a.til.tile_bytes);
-                bulk_g2s(ring + (size_t)s * stride, a.tiles + (size_t)(t0 + i) * stride,
+                bulk_g2s(ring + (size_t)s * stride, a.tiles[m] + (size_t)tin * stride,
                          a.til.tile_bytes, &full[s], pol);
                 ++issued;
             }
@@ -207,39 +255,47 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, J == 1 ? 2 : 1) k_g
     const int ks = warp % a.KS, grp = warp / a.KS;
     const int g0 = ks * 32 * J + lane;
     bool act[J];
-    XPlanes xg[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) act[j] = g0 + 32 * j < G;
     // x may be the output of the preceding kernel, and y may still be read by
     // it: nothing below touches either before that kernel has completed. The
     // weights (uploaded by copies, not written by a kernel) are already
     // streaming in.
     wait_prerequisite();
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        act[j] = g0 + 32 * j < G;
-        load_xplanes_global(xg[j], a.x + (size_t)(g0 + 32 * j) * 32, act[j]);
-    }
+    RB_GEMV_STAMP(slot, 1);
     const int rbase = grp * a.ROWS;
     // A wait that runs out marks the CTA failed; every consumer still reaches
     // the named barrier below (a warp that left would stall the others).
     bool good;
     switch (a.ROWS) {
-        case 1: good = gemv_tiles<J, 1>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
-        case 2: good = gemv_tiles<J, 2>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
-        case 4: good = gemv_tiles<J, 4>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        case 1: good = gemv_tiles<J, 1>(a, ring, part, full, empty, sink + warp, t0, nt, ks, rbase, g0, act); break;
+        case 2: good = gemv_tiles<J, 2>(a, ring, part, full, empty, sink + warp, t0, nt, ks, rbase, g0, act); break;
+        case 4: good = gemv_tiles<J, 4>(a, ring, part, full, empty, sink + warp, t0, nt, ks, rbase, g0, act); break;
         // ROWS * J <= 8 (the planner never asks for more)
-        default: good = gemv_tiles<J, 8 / J>(a, ring, part, full, empty, sink + warp, nt, ks, rbase, g0, act, xg); break;
+        default: good = gemv_tiles<J, 8 / J>(a, ring, part, full, empty, sink + warp, t0, nt, ks, rbase, g0, act); break;
     }
+    RB_GEMV_STAMP(slot, 2);
     named_sync(1, CW * 32);
     if (!good) return;
     for (int lr = threadIdx.x; lr < nt * TR; lr += CW * 32) {
-        const int row = t0 * TR + lr;
+        const int gt = t0 + lr / TR, m = gt / a.til.ntiles;
+        const int row = (gt - m * a.til.ntiles) * TR + lr % TR;
         if (row < a.til.rows) {
             float acc = 0.f;
             for (int k = 0; k < a.KS; ++k) acc += part[lr * a.KS + k];
-            a.y[row] = acc;
+            a.y[m][row] = acc;
         }
     }
+    RB_GEMV_STAMP(slot, 3);
 }
+
+#ifdef RB_PHASE_TIMERS
+}  // namespace rb
+extern "C" __attribute__((visibility("default"))) int rabbit_cuda_debug_gemv_ns(uint64_t *out) {
+    return cudaMemcpyFromSymbol(out, rb::g_gemv_ns, sizeof(uint64_t) * 256) == cudaSuccess ? 0 : 6;
+}
+namespace rb {
+#endif
 
 const void *gemv_g32_kernel(int J) {
     return J == 2 ? (const void *)k_gemv_g32<2> : (const void *)k_gemv_g32<1>;

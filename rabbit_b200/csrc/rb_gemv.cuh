@@ -77,11 +77,19 @@ struct G32Plan {
 };
 
 bool plan_g32(int rows, int in_dim, int sm_count, G32Plan *p);
+// The same tiling and warp layout for a launch over `nmat` matrices.
+bool plan_g32_batch(const G32Plan &one, int nmat, int sm_count, G32Plan *p);
 
+constexpr int kMaxBatch = 32;  // matrices of one shape per GEMV launch
+
+// One launch: y[m] = W[m] x[m] for nmat matrices of one tiling, their tiles
+// dealt out to the CTAs as one range (matrix-major).
 struct G32Args {
-    const uint8_t *tiles;
-    const float *x;
-    float *y;
+    const uint8_t *tiles[kMaxBatch];
+    const float *x[kMaxBatch];
+    float *y[kMaxBatch];
+    int nmat;
+    int shared_x;  // 1: every x[m] is x[0], planes are built once
     Tiling til;
     int KS, NG, ROWS, nslots, tiles_cta_max;
     int *err;

@@ -21,24 +21,33 @@ namespace rb {
 
 static bool g_attr_set[kMaxDevices];
 
-static int launch_g32(const G32Plan &p, const uint8_t *tiles, const float *x, float *y, DevCtx *c,
-                      cudaStream_t s) {
+// One launch over n matrices of plan p's tiling (n == 1: a single GEMV).
+static int launch_g32(const G32Plan &p, int n, const uint8_t *const *tiles,
+                      const float *const *x, float *const *y, DevCtx *c, cudaStream_t s) {
     if (!g_attr_set[c->device]) {
         for (int J = 1; J <= 2; ++J)
             RB_CUDA(cudaFuncSetAttribute(gemv_g32_kernel(J),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
         g_attr_set[c->device] = true;
     }
+    G32Plan pb;
+    if (!plan_g32_batch(p, n, c->sm_count, &pb))
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "gemv: no launch plan for %d matrices", n);
     G32Args a;
-    a.tiles = tiles;
-    a.x = x;
-    a.y = y;
-    a.til = p.til;
-    a.KS = p.KS;
-    a.NG = p.NG;
-    a.ROWS = p.ROWS;
-    a.nslots = p.nslots;
-    a.tiles_cta_max = p.tiles_cta_max;
+    a.nmat = n;
+    a.shared_x = 1;
+    for (int m = 0; m < n; ++m) {
+        a.tiles[m] = tiles[m];
+        a.x[m] = x[m];
+        a.y[m] = y[m];
+        if (x[m] != x[0]) a.shared_x = 0;
+    }
+    a.til = pb.til;
+    a.KS = pb.KS;
+    a.NG = pb.NG;
+    a.ROWS = pb.ROWS;
+    a.nslots = pb.nslots;
+    a.tiles_cta_max = pb.tiles_cta_max;
     a.err = c->d_err;
     a.wait_ns = wait_limit_ns();
     // Programmatic dependent launch: this GEMV may start (and stream its
@@ -48,15 +57,20 @@ static int launch_g32(const G32Plan &p, const uint8_t *tiles, const float *x, fl
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid);
-    cfg.blockDim = dim3(p.block);
-    cfg.dynamicSmemBytes = p.smem;
+    cfg.gridDim = dim3(pb.grid);
+    cfg.blockDim = dim3(pb.block);
+    cfg.dynamicSmemBytes = pb.smem;
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     void *args[] = {&a};
-    RB_CUDA(cudaLaunchKernelExC(&cfg, gemv_g32_kernel(p.J), args));
+    RB_CUDA(cudaLaunchKernelExC(&cfg, gemv_g32_kernel(pb.J), args));
     return RABBIT_CUDA_OK;
+}
+
+static int launch_g32(const G32Plan &p, const uint8_t *tiles, const float *x, float *y, DevCtx *c,
+                      cudaStream_t s) {
+    return launch_g32(p, 1, &tiles, &x, &y, c, s);
 }
 
 static int launch_flat(const uint8_t *blob, const float *x, float *y, int out_dim, int in_dim,
@@ -210,6 +224,39 @@ int rabbit_cuda_matrix_free(rabbit_cuda_matrix *m) {
     cudaSetDevice(prev);
     delete m;
     return ok();
+}
+
+int rabbit_cuda_matrix_gemv_batch_dev(const rabbit_cuda_matrix *const *m, int n,
+                                      const float *const *d_x, float *const *d_y, void *stream) {
+    if (!m || !d_x || !d_y || n < 1 || n > kMaxBatch)
+        return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_batch_dev: need 1..%d matrices", kMaxBatch);
+    for (int i = 0; i < n; ++i) {
+        if (!m[i] || !d_x[i] || !d_y[i])
+            return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_batch_dev: NULL entry %d", i);
+        if (m[i]->device != m[0]->device || m[i]->rows != m[0]->rows ||
+            m[i]->in_dim != m[0]->in_dim || m[i]->fast != m[0]->fast ||
+            m[i]->group_size != m[0]->group_size)
+            return fail(RABBIT_CUDA_ERR_ARGS,
+                        "matrix_gemv_batch_dev: matrix %d differs in device, shape or format", i);
+    }
+    if (!m[0]->fast) {  // one flat-index launch per matrix
+        for (int i = 0; i < n; ++i) {
+            const int st = rabbit_cuda_matrix_gemv_dev(m[i], d_x[i], d_y[i], stream);
+            if (st != RABBIT_CUDA_OK) return st;
+        }
+        return ok();
+    }
+    int st;
+    DevCtx *c = dev_ctx(m[0]->device, &st);
+    if (!c) return st;
+    const uint8_t *tiles[kMaxBatch];
+    for (int i = 0; i < n; ++i) {
+        if ((reinterpret_cast<uintptr_t>(d_x[i]) & 15) != 0)
+            return fail(RABBIT_CUDA_ERR_ARGS, "matrix_gemv_batch_dev: x must be 16-byte aligned");
+        tiles[i] = m[i]->tiles;
+    }
+    st = launch_g32(m[0]->plan, n, tiles, d_x, d_y, c, as_stream(stream, c));
+    return st == RABBIT_CUDA_OK ? ok() : st;
 }
 
 int rabbit_cuda_matrix_gemv_dev(const rabbit_cuda_matrix *m, const float *d_x, float *d_y,

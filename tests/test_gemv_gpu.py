@@ -154,3 +154,42 @@ def test_matrix_gemv_dev_linearity_full_size(rc, dev):
 def test_wait_limit_setting(rc):
     assert rc.lib().rabbit_cuda_set_wait_limit_ms(500) == rc.OK
     assert rc.lib().rabbit_cuda_set_wait_limit_ms(2000) == rc.OK
+
+
+@pytest.mark.parametrize("shape,n,shared", [((300, 4096), 5, False), ((300, 4096), 5, True),
+                                            ((64, 14336), 3, False), ((96, 160), 32, True)],
+                         ids=["300x4096-n5", "300x4096-n5-shared-x", "64x14336-n3", "96x160-n32"])
+def test_matrix_gemv_batch_vs_oracle(rc, dev, oracle, shape, n, shared):
+    """n GEMVs in one launch (ragged row counts, long rows, the 32-matrix maximum,
+    shared and distinct inputs) against the oracle, twice in a row."""
+    r, c = shape
+    rng = np.random.default_rng(r + c + n)
+    blobs = [synth.int4_blob(rng, r, c) for _ in range(n)]
+    mats = [rc.Matrix(b, r, c) for b in blobs]
+    for _ in range(2):
+        xs = [rng.standard_normal(c).astype(np.float32) for _ in range(1 if shared else n)]
+        dxs = [dev.put(x) for x in xs]
+        dys = [dev.empty(r, dev.torch.float32) for _ in range(n)]
+        rc.gemv_batch_dev(mats, [dxs[0 if shared else i].data_ptr() for i in range(n)],
+                          [d.data_ptr() for d in dys], dev.stream)
+        dev.torch.cuda.synchronize()
+        for i in range(n):
+            ref = oracle.gemv_int4_grouped(blobs[i], xs[0 if shared else i], r, c)
+            np.testing.assert_allclose(dys[i].cpu().numpy(), ref, rtol=RTOL, atol=ATOL,
+                                       err_msg=f"matrix {i}")
+    for m in mats:
+        m.free()
+
+
+def test_matrix_gemv_batch_rejects_bad_batches(rc, dev):
+    rng = np.random.default_rng(5)
+    a = rc.Matrix(synth.int4_blob(rng, 64, 256), 64, 256)
+    b = rc.Matrix(synth.int4_blob(rng, 32, 256), 32, 256)
+    dx = dev.put(rng.standard_normal(256).astype(np.float32))
+    dy = dev.empty(64, dev.torch.float32)
+    with pytest.raises(rc.RabbitCudaError, match="differs"):
+        rc.gemv_batch_dev([a, b], [dx.data_ptr()] * 2, [dy.data_ptr()] * 2, dev.stream)
+    with pytest.raises(rc.RabbitCudaError, match="1..32"):
+        rc.gemv_batch_dev([a] * 33, [dx.data_ptr()] * 33, [dy.data_ptr()] * 33, dev.stream)
+    a.free()
+    b.free()
