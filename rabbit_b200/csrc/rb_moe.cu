@@ -122,23 +122,27 @@ static unsigned next_seq(unsigned *seq, void *tagged[], const size_t bytes[], in
     return (*seq)++;
 }
 
-// One fused decode launch: cooperative (all CTAs resident: they wait on one
-// another's data) and programmatic-dependent (it may start while the kernel
-// before it on the stream finishes; it waits for that kernel before reading h
-// or touching scratch).
+// One fused decode launch, programmatic-dependent: it may start while the
+// kernel before it on the stream finishes (it waits for that kernel before it
+// reads h or touches scratch), which hides the launch gap between layers.
+// Its CTAs wait on one another's data, so all of them must be resident: the
+// grid is one CTA per SM and the shared memory admits exactly one per SM
+// (checked at pool creation), and the next launch on the stream starts only
+// after every CTA of this one has started. The cooperative-launch attribute
+// would state that guarantee but keeps consecutive launches from overlapping;
+// if the device is shared and some CTAs cannot be placed, the bounded waits
+// end the launch with RABBIT_CUDA_ERR_TIMEOUT.
 static cudaError_t launch_fused(const rabbit_cuda_moe *p, MoeFusedArgs &a, cudaStream_t s) {
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p->grid);
     cfg.blockDim = dim3(p->block);
     cfg.dynamicSmemBytes = p->smem;
     cfg.stream = s;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     void *args[] = {&a};
     return cudaLaunchKernelExC(&cfg, moe_fused_kernel(a.JB, a.JC), args);
 }
