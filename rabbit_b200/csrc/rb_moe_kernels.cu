@@ -10,7 +10,7 @@
 //      active slot list (routed in rank order, then shared experts).
 //   B. gate/up: the active slots' GU tiles (TRb rows of gate and of up,
 //      nibbles + scales, one contiguous block) dealt out round-robin over the
-//      CTAs; the producer warp bulk-copies them into the shared-memory ring;
+//      CTAs (in reverse CTA order); the producer warp bulk-copies them into the shared-memory ring;
 //      eight consumer warps dot them against xn held in registers (JB groups
 //      of 32 per lane, ROWSb rows per warp group and tile, both fixed at
 //      compile time) and leave per-k-slice partials in shared memory; the
@@ -548,7 +548,12 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
     const int ntb = a.tb.ntiles, TRb = a.tb.TR, ntc = a.tc.ntiles, TRc = a.tc.TR;
     const int G = (int)gridDim.x, bx = (int)blockIdx.x;
     const int UB = nact * ntb;  // gate/up units (slot, GU tile), dealt round-robin
-    const int nB = UB > bx ? (UB - bx + G - 1) / G : 0;
+    // gate/up unit n of this CTA is vb + n * G with vb = G - 1 - bx: the last,
+    // partial round goes to the highest CTAs, which hold the down units of the
+    // last chunks of mid -- the CTAs that finish gate/up last are the ones
+    // that would wait for those chunks anyway
+    const int vb = G - 1 - bx;
+    const int nB = UB > vb ? (UB - vb + G - 1) / G : 0;
     const int UC = nact * ntc;  // down units (slot, chunk, row tile), contiguous ranges
     const int uc0 = bx * UC / G;  // bx * UC < 2^31: UC <= 72 * 16 * 16384 / 1
     const int uc1 = (bx + 1) * UC / G;
@@ -567,7 +572,7 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
                     okp = false;
                     break;
                 }
-                const int u = bx + n * G, slot = u / ntb, t = u - slot * ntb;
+                const int u = vb + n * G, slot = u / ntb, t = u - slot * ntb;
                 const uint8_t *src = a.pool + (size_t)s_rec[slot] * a.rec_stride + (size_t)t * sb;
                 RB_CHUNK(0, i);
                 mbar_arrive_expect_tx(&full[s], a.tb.tile_bytes);
@@ -674,7 +679,7 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
                 return;
             const float *pp = part + (size_t)d * a.part_floats;
             if (i < nB) {
-                const int u = bx + i * G, slot = u / ntb, t = u - slot * ntb;
+                const int u = vb + i * G, slot = u / ntb, t = u - slot * ntb;
                 for (int r = lane; r < TRb; r += 32) {
                     const int row = t * TRb + r;
                     if (row >= I) continue;
