@@ -200,6 +200,61 @@ int rabbit_cuda_moe_stats(const rabbit_cuda_moe *p, uint64_t *hbm_hits, uint64_t
 /* Algorithmic bytes of one decode (router + selected + shared experts). */
 uint64_t rabbit_cuda_moe_decode_bytes(const rabbit_cuda_moe *p);
 
+/* ------------------------------------- incremental ref-v2 decode context -- */
+
+/* The dense (fp32) weights of a ref-v2 model, in the layout parse_weights
+ * reads from the .rabbit dense block (src/forward_v2.c:106-169). HOST
+ * pointers, read only during rabbit_cuda_refv2_create; embed == NULL: every
+ * dense weight is left for rabbit_cuda_refv2_fill_synthetic. */
+typedef struct {
+    int n_layers, hidden, vocab;
+    int n_heads, n_kv_heads, head_dim;  /* n_heads * head_dim may differ from hidden */
+    int max_ctx;                        /* KV window, 1..256 (forward_v2.c:16-26) */
+    const float *embed;                 /* [vocab, hidden] */
+    const float *lm_head;               /* [hidden, vocab] */
+    const float *final_norm;            /* [hidden] */
+    const float *const *rms_attn;       /* [n_layers] -> [hidden] */
+    const float *const *w_q;            /* [n_layers] -> [n_heads * head_dim, hidden] */
+    const float *const *w_k;            /* [n_layers] -> [n_kv_heads * head_dim, hidden] */
+    const float *const *w_v;            /* [n_layers] -> [n_kv_heads * head_dim, hidden] */
+    const float *const *w_o;            /* [n_layers] -> [hidden, n_heads * head_dim] */
+} rabbit_cuda_dense_desc;
+
+typedef struct rabbit_cuda_refv2 rabbit_cuda_refv2;
+
+/* The device-resident form of RabbitRefV2Ctx (src/rabbit.h:160-167, declared
+ * but not implemented in the reference): dense weights and a per-layer KV
+ * cache in HBM, the MoE blocks from `moe` (a pool of the same model on the
+ * same device; it must outlive the context). One decode step follows
+ * rabbit_ref_v2_forward's per-token loop (forward_v2.c:457-471):
+ * h = embed[id % vocab]; per layer attention_step then moe_step; then the
+ * final rmsnorm and logits = lm_head^T h (forward_v2.c:404-413, 473-484).
+ * The KV cache stops growing at max_ctx, as attention_step does. */
+int rabbit_cuda_refv2_create(const rabbit_cuda_dense_desc *desc, rabbit_cuda_moe *moe,
+                             rabbit_cuda_refv2 **out);
+/* Seeded synthetic dense weights on the device: embed, projections, lm_head
+ * uniform with standard deviation `sigma`, norms 1. */
+int rabbit_cuda_refv2_fill_synthetic(rabbit_cuda_refv2 *c, uint64_t seed, float sigma);
+int rabbit_cuda_refv2_free(rabbit_cuda_refv2 *c);
+/* Empty the KV cache and restart at position 0 (rabbit_ref_v2_ctx_reset). */
+int rabbit_cuda_refv2_reset(rabbit_cuda_refv2 *c);
+/* One token at the next position (rabbit_ref_v2_ctx_step). HOST outputs, each
+ * may be NULL: logits [vocab], hidden [hidden] (the final-normed h, as
+ * rabbit_ref_v2_forward's out_hidden), argmax (lowest index among equal
+ * maxima, forward_v2.c:415-421). Synchronous. */
+int rabbit_cuda_refv2_step(rabbit_cuda_refv2 *c, int token_id, float *logits, float *hidden,
+                           int *argmax);
+/* n tokens in order (rabbit_ref_v2_ctx_prefill); outputs as for the last one. */
+int rabbit_cuda_refv2_prefill(rabbit_cuda_refv2 *c, const int *token_ids, int n_tokens,
+                              float *logits, float *hidden, int *argmax);
+/* Greedy continuation (as rabbit_ref_v2_greedy, without re-running the
+ * prefix): n_new tokens, each the argmax of the previous step, chained on the
+ * device with no host round trip; out_ids[n_new] (host). Needs a step before
+ * it; n_new <= 4096. */
+int rabbit_cuda_refv2_generate(rabbit_cuda_refv2 *c, int n_new, int *out_ids);
+/* Tokens processed since the last reset. */
+int rabbit_cuda_refv2_position(const rabbit_cuda_refv2 *c);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

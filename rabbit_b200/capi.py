@@ -34,6 +34,16 @@ class MoeDesc(C.Structure):
                 ("rms_ffn", C.POINTER(C.c_void_p)), ("w_router", C.POINTER(C.c_void_p))]
 
 
+class DenseDesc(C.Structure):
+    """rabbit_cuda_dense_desc"""
+    _fields_ = [("n_layers", C.c_int), ("hidden", C.c_int), ("vocab", C.c_int),
+                ("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("max_ctx", C.c_int), ("embed", C.c_void_p), ("lm_head", C.c_void_p),
+                ("final_norm", C.c_void_p), ("rms_attn", C.POINTER(C.c_void_p)),
+                ("w_q", C.POINTER(C.c_void_p)), ("w_k", C.POINTER(C.c_void_p)),
+                ("w_v", C.POINTER(C.c_void_p)), ("w_o", C.POINTER(C.c_void_p))]
+
+
 _P = C.c_void_p
 _I = C.c_int
 # name -> (restype, argtypes)
@@ -65,6 +75,14 @@ SIGNATURES = {
                                    C.POINTER(C.c_uint64), C.POINTER(_I),
                                    C.POINTER(C.c_uint64)]),
     "rabbit_cuda_moe_decode_bytes": (C.c_uint64, [_P]),
+    "rabbit_cuda_refv2_create": (_I, [C.POINTER(DenseDesc), _P, C.POINTER(_P)]),
+    "rabbit_cuda_refv2_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
+    "rabbit_cuda_refv2_free": (_I, [_P]),
+    "rabbit_cuda_refv2_reset": (_I, [_P]),
+    "rabbit_cuda_refv2_step": (_I, [_P, _I, _P, _P, C.POINTER(_I)]),
+    "rabbit_cuda_refv2_prefill": (_I, [_P, _P, _I, _P, _P, C.POINTER(_I)]),
+    "rabbit_cuda_refv2_generate": (_I, [_P, _I, _P]),
+    "rabbit_cuda_refv2_position": (_I, [_P]),
 }
 
 _LIB: C.CDLL | None = None
@@ -239,6 +257,83 @@ class MoePool:
     def free(self) -> None:
         if self.handle:
             check(lib().rabbit_cuda_moe_free(self.handle))
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class RefV2:
+    """Device-resident incremental ref-v2 decode (rabbit_cuda_refv2): dense
+    weights + KV cache in HBM, the MoE blocks from `pool` (which must outlive
+    this object).
+
+    weights=None leaves the dense weights for fill_synthetic(); otherwise a
+    dict with embed [V, H], lm_head [H, V], final_norm [H] and per-layer lists
+    rms_attn, w_q, w_k, w_v, w_o (row-major, as the .rabbit dense block).
+    """
+
+    def __init__(self, pool: MoePool, *, vocab: int, n_heads: int, n_kv_heads: int,
+                 head_dim: int, max_ctx: int = 256, weights: dict | None = None):
+        L, H = pool.n_layers, pool.hidden
+        self.pool, self.vocab, self.hidden = pool, vocab, H
+        null = C.POINTER(C.c_void_p)()
+        if weights is None:
+            d = DenseDesc(L, H, vocab, n_heads, n_kv_heads, head_dim, max_ctx, None, None, None,
+                          null, null, null, null, null)
+            keep = ()
+        else:
+            f32 = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+            glob = [f32(weights[n]) for n in ("embed", "lm_head", "final_norm")]
+            per = {n: [f32(a) for a in weights[n]] for n in ("rms_attn", "w_q", "w_k", "w_v",
+                                                              "w_o")}
+            arrs = {n: (C.c_void_p * L)(*[a.ctypes.data for a in per[n]]) for n in per}
+            keep = (glob, per, arrs)
+            d = DenseDesc(L, H, vocab, n_heads, n_kv_heads, head_dim, max_ctx,
+                          *[a.ctypes.data for a in glob],
+                          *[C.cast(arrs[n], C.POINTER(C.c_void_p)) for n in ("rms_attn", "w_q",
+                                                                              "w_k", "w_v",
+                                                                              "w_o")])
+        h = C.c_void_p()
+        check(lib().rabbit_cuda_refv2_create(C.byref(d), pool.handle, C.byref(h)))
+        del keep  # the weights are on the device now
+        self.handle = h
+
+    def fill_synthetic(self, seed: int, sigma: float = 0.02) -> None:
+        check(lib().rabbit_cuda_refv2_fill_synthetic(self.handle, seed, sigma))
+
+    def reset(self) -> None:
+        check(lib().rabbit_cuda_refv2_reset(self.handle))
+
+    @property
+    def position(self) -> int:
+        return int(lib().rabbit_cuda_refv2_position(self.handle))
+
+    def prefill(self, ids, want_logits: bool = True, want_hidden: bool = True):
+        """Returns (logits[V] or None, hidden[H] or None, argmax)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.full(self.vocab, np.nan, np.float32) if want_logits else None
+        hidden = np.full(self.hidden, np.nan, np.float32) if want_hidden else None
+        am = C.c_int(-1)
+        check(lib().rabbit_cuda_refv2_prefill(
+            self.handle, ids.ctypes.data, ids.size, None if logits is None else _ptr(logits),
+            None if hidden is None else _ptr(hidden), C.byref(am)))
+        return logits, hidden, am.value
+
+    def step(self, token_id: int, want_logits: bool = True, want_hidden: bool = True):
+        return self.prefill([token_id], want_logits, want_hidden)
+
+    def generate(self, n_new: int) -> np.ndarray:
+        out = np.full(n_new, -1, np.int32)
+        check(lib().rabbit_cuda_refv2_generate(self.handle, n_new, _ptr(out)))
+        return out
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().rabbit_cuda_refv2_free(self.handle))
             self.handle = C.c_void_p()
 
     def __del__(self):

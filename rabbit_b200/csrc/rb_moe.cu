@@ -318,6 +318,14 @@ __global__ void k_fill_scales(uint8_t *base, int ntiles, uint32_t stride, uint32
 
 }  // namespace rb
 
+namespace rb {
+void moe_shape(const rabbit_cuda_moe *p, int *device, int *n_layers, int *hidden) {
+    *device = p->device;
+    *n_layers = p->L;
+    *hidden = p->H;
+}
+}  // namespace rb
+
 using namespace rb;
 
 extern "C" {

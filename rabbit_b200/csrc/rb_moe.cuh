@@ -5,6 +5,8 @@
 #include "rb_device.cuh"
 #include "rb_gemv.cuh"
 
+struct rabbit_cuda_moe;
+
 namespace rb {
 
 constexpr int kMaxSlots = 72;  // top-k (<= 8) + shared (<= 64)
@@ -81,5 +83,9 @@ __global__ void k_moe_route(MoeGenericArgs a);
 __global__ void k_moe_up_generic(MoeGenericArgs a);
 __global__ void k_moe_down_generic(MoeGenericArgs a);
 __global__ void k_moe_combine(MoeGenericArgs a);
+
+// Device, layer count and hidden size of a pool (for code that runs a pool's
+// layers as part of a larger model).
+void moe_shape(const struct ::rabbit_cuda_moe *p, int *device, int *n_layers, int *hidden);
 
 }  // namespace rb
