@@ -241,6 +241,128 @@ def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 2
                                 "rabbit_cuda_matrix_gemv_batch_dev", "launches": biters}}
 
 
+# ------------------------------------------------------------ full decode --
+# The OLMoE-shaped full decode (ref-v2 model, random init): 16 layers, hidden
+# 2048, 16 heads x 128 (no GQA), RoPE, 64 experts top-8 with SwiGLU FFN 1024
+# int4 group-32, fp32 dense weights N(0, 0.02)-scaled, KV window 256, vocab
+# 50304; a random 16-id prompt, then 128 greedy tokens.
+OL = dict(L=16, H=2048, nh=16, nkv=16, hd=128, E=64, k=8, I=1024, V=50304, ctx=256)
+OL_PROMPT, OL_NEW = 16, 128
+
+
+def olmoe_dense_bytes(kv_len: int) -> int:
+    """Algorithmic bytes of one token's dense part at KV length kv_len (after
+    the append): per layer rms_attn + W_q/W_k/W_v/W_o + the K/V rows read and
+    the row written; the embedding row, final norm and lm_head once."""
+    L, H, V = OL["L"], OL["H"], OL["V"]
+    qd, kvd = OL["nh"] * OL["hd"], OL["nkv"] * OL["hd"]
+    per_layer = H + qd * H + 2 * kvd * H + H * qd + 2 * kvd * (kv_len + 1)
+    return 4 * (L * per_layer + 2 * H + H * V)
+
+
+def olmoe_cpu_sample(seconds: float = 6.0) -> dict:
+    """The reference's own C (or the oracle port) on one host thread: one
+    layer's attention_step + moe_step at KV length ~ the run's middle, repeated
+    for about `seconds`, and one lm_head pass; a token = 16 layers + lm_head."""
+    from rabbit_b200 import synth
+
+    chk, kind = cpu_checker()
+    L, H, V, E, k, I = OL["L"], OL["H"], OL["V"], OL["E"], OL["k"], OL["I"]
+    nh, nkv, hd = OL["nh"], OL["nkv"], OL["hd"]
+    rng = np.random.default_rng(SEED + 11)
+    f = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)  # noqa: E731
+    w = dict(rms_attn=np.ones(H, np.float32), w_q=f(nh * hd, H), w_k=f(nkv * hd, H),
+             w_v=f(nkv * hd, H), w_o=f(H, nh * hd))
+    recs, size, router, rms = synth.moe_layer(SEED + 12, H, E, I)
+    kv_len = OL_PROMPT + OL_NEW // 2
+    kc = np.zeros((OL["ctx"], nkv * hd), np.float32)
+    vc = np.zeros_like(kc)
+    kc[:kv_len] = rng.standard_normal((kv_len, nkv * hd), dtype=np.float32)
+    vc[:kv_len] = rng.standard_normal((kv_len, nkv * hd), dtype=np.float32)
+    h = rng.standard_normal(H, dtype=np.float32)
+    n, t_layer = 0, 0.0
+    while t_layer < seconds or n < 2:
+        t0 = time.perf_counter()
+        h, _ = chk.attention_step(h, kc, vc, kv_len, kv_len, n_heads=nh, n_kv_heads=nkv,
+                                  head_dim=hd, **w)
+        out = chk.moe_step(h, H=H, E=E, top_k=k, inter=I, n_shared=0, quant=4, n_records=E,
+                           expert_size=size, records=recs, rms_ffn=rms, w_router=router)
+        h = out[0] if isinstance(out, tuple) else out
+        t_layer += time.perf_counter() - t0
+        n += 1
+    lm = f(H, V)
+    t0 = time.perf_counter()
+    chk.logits(lm, chk.rmsnorm(h, np.ones(H, np.float32)))
+    t_lm = time.perf_counter() - t0
+    per_token = L * t_layer / n + t_lm
+    steps = sum(OL_PROMPT + t for t in range(OL_NEW))  # forward passes of its greedy loop
+    return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": 1, "kind": kind,
+            "sample": f"{n} layer steps (attention_step + moe_step, KV length {kv_len}) + 1 "
+                      f"lm_head pass on one thread, {t_layer + t_lm:.1f} s; a token = "
+                      f"{L} layers + lm_head",
+            "greedy_tokens_per_s": round(OL_NEW / (per_token * steps), 6),
+            "greedy_note": ("rabbit_ref_v2_greedy re-runs the whole prefix for every new token "
+                            f"({steps} token passes for {OL_NEW} tokens after a {OL_PROMPT}-id "
+                            "prompt)")}
+
+
+def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True) -> dict:
+    """Device-resident full decode through rabbit_cuda_refv2: prefill a random
+    prompt, then generate 128 tokens chained on the device; device time from
+    CUDA events around the generate call's kernels, e2e from the host call."""
+    L, H, V, E, k, I = OL["L"], OL["H"], OL["V"], OL["E"], OL["k"], OL["I"]
+    rng = np.random.default_rng(SEED + 5)
+    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
+    pool = capi.MoePool(records=None, expert_size=synth.expert_record_size(H, I), n_layers=L,
+                        hidden=H, n_experts=E, top_k=k, inter=I, quant=4,
+                        rms_ffn=[np.ones(H, np.float32)] * L, w_router=routers)
+    pool.fill_synthetic(SEED * 1000 + 77)
+    ctx = capi.RefV2(pool, vocab=V, n_heads=OL["nh"], n_kv_heads=OL["nkv"],
+                     head_dim=OL["hd"], max_ctx=OL["ctx"])
+    ctx.fill_synthetic(SEED * 1000 + 78, 0.02)
+    prompt = rng.integers(0, V, OL_PROMPT)
+    dev, wall = [], []
+    for r in range(runs + 1):  # the first run warms up
+        ctx.reset()
+        ctx.prefill(prompt, want_logits=False, want_hidden=False)
+        t0 = time.perf_counter()
+        out = ctx.generate(OL_NEW)
+        t = time.perf_counter() - t0
+        if r:
+            dev.append(ctx.device_ms / 1e3)
+            wall.append(t)
+    assert ((out >= 0) & (out < V)).all()
+    moe_bytes = pool.decode_bytes * L
+    gen_bytes = sum(olmoe_dense_bytes(OL_PROMPT + i) for i in range(OL_NEW)) + OL_NEW * moe_bytes
+    dsec, wsec = statistics.median(dev), statistics.median(wall)
+    achieved = gen_bytes / dsec / 1e9
+    item = {
+        "metric": "full decode tokens/s (OLMoE-shaped, batch 1)",
+        "value": round(OL_NEW / dsec, 2), "unit": "tokens/s",
+        "ms_per_token": round(1e3 * dsec / OL_NEW, 4),
+        "config": {"workload": (f"OLMoE-shaped ref-v2 decode: {L} layers, hidden {H}, "
+                                f"{OL['nh']}x{OL['hd']} heads, {E} experts top-{k}, inter {I}, "
+                                f"vocab {V}, KV window {OL['ctx']}; {OL_PROMPT}-id random "
+                                f"prompt, {OL_NEW} greedy tokens"),
+                   "l2": "inputs larger than L2 (1.5 GB fp32 dense + 0.46 GB experts per token)",
+                   "runs": runs},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "bytes_per_token": round(gen_bytes / OL_NEW),
+                     "moe_bytes_per_token": moe_bytes,
+                     "what": "every weight byte a token needs read once, over the whole chain"},
+        "e2e": {"value": round(OL_NEW / wsec, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * OL_NEW,
+                "api": "rabbit_cuda_refv2_generate (host output ids)"},
+        "gpu_launches_per_token": 4 * L + 3,
+    }
+    ctx.free()
+    pool.free()
+    if cpu:
+        item["cpu_baseline"] = olmoe_cpu_sample()
+    return item
+
+
 # ------------------------------------------------------------ arms ---------
 def run_reference(args) -> None:
     """--impl reference: the reference's C on all host cores."""
@@ -376,6 +498,9 @@ def run_rabbit(args) -> None:
     e2e_value = world * step_bytes * e2e_steps / e2e_s / 1e9
 
     gemv = None if args.no_gemv else gemv_item(capi, synth, stream, measured_peak()[0])
+    full = None
+    if world == 1 and not args.no_full_decode:
+        full = full_decode_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -407,6 +532,7 @@ def run_rabbit(args) -> None:
                     "steps": e2e_steps, "api": "rabbit_cuda_moe_decode (host buffers)"},
             "gpu_launches": launches,
             "gemv": gemv,
+            "full_decode": full,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -426,6 +552,8 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="distinct layers per step (small values: profiling cases)")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV line item")
+    ap.add_argument("--no-full-decode", action="store_true",
+                    help="skip the OLMoE-shaped full decode line item")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

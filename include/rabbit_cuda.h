@@ -56,7 +56,7 @@ const char *rabbit_cuda_last_error(void);
 int rabbit_cuda_device_count(int *count);
 /* Select the device later calls on this thread use (default 0). */
 int rabbit_cuda_set_device(int device);
-/* Device-side wait limit in milliseconds for mbarrier / grid-barrier spins
+/* Device-side wait limit in milliseconds for mbarrier / inter-CTA spins
  * (default 2000). A wait that runs out sets RABBIT_CUDA_ERR_TIMEOUT. */
 int rabbit_cuda_set_wait_limit_ms(int ms);
 
@@ -169,17 +169,15 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
  * device's memory between its own arenas, or a serving loop that cannot take
  * the device-wide synchronisation a cudaMalloc/cudaFree brings. The call
  * allocates nothing and frees nothing; its scratch (router scores, the SwiGLU
- * activations, the down-projection rows, per-CTA flags and a grid-barrier
- * counter) is a fixed 2 MiB array inside this library, present on every
+ * activations, the down-projection rows and per-CTA flags) is a fixed 2 MiB array inside this library, present on every
  * device that loads it until the process exits. Models whose scratch does not
- * fit -- about 5 KB + E*4 + (k + S) * (I + C * H) * 8 bytes, with C the number
+ * fit -- about 5 KB + E*8 + (k + S) * (I + C * H) * 8 bytes, with C the number
  * of column chunks of W2 (I / 1024 when I is a multiple of 1024) -- are
  * rejected with RABBIT_CUDA_ERR_ARGS, pools not
  * in the group-32 layout with RABBIT_CUDA_ERR_UNSUPPORTED. The first call on
  * each device looks up the array's device address (once, with that device
  * current); make that first call before any stream capture. Every call uses
- * the same array, which keeps what the last call left there: the call clears
- * the grid-barrier counter on `stream` before its kernel, and the values its
+ * the same array, which keeps what the last call left there: the values its
  * CTAs share carry a tag new to each call, so leftovers are never read. Calls
  * that overlap on the GPU (other streams, other pools on the same device) race
  * on the array and give wrong results. d_ids / d_weights may be NULL. Errors
@@ -254,6 +252,10 @@ int rabbit_cuda_refv2_prefill(rabbit_cuda_refv2 *c, const int *token_ids, int n_
 int rabbit_cuda_refv2_generate(rabbit_cuda_refv2 *c, int n_new, int *out_ids);
 /* Tokens processed since the last reset. */
 int rabbit_cuda_refv2_position(const rabbit_cuda_refv2 *c);
+/* Device time (CUDA events on the context's stream) from the first kernel to
+ * the last one of the latest successful prefill / step / generate call, in ms;
+ * the copies of its outputs to the host are outside it. */
+int rabbit_cuda_refv2_device_ms(const rabbit_cuda_refv2 *c, float *ms);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -83,6 +83,7 @@ SIGNATURES = {
     "rabbit_cuda_refv2_prefill": (_I, [_P, _P, _I, _P, _P, C.POINTER(_I)]),
     "rabbit_cuda_refv2_generate": (_I, [_P, _I, _P]),
     "rabbit_cuda_refv2_position": (_I, [_P]),
+    "rabbit_cuda_refv2_device_ms": (_I, [_P, C.POINTER(C.c_float)]),
 }
 
 _LIB: C.CDLL | None = None
@@ -325,6 +326,13 @@ class RefV2:
 
     def step(self, token_id: int, want_logits: bool = True, want_hidden: bool = True):
         return self.prefill([token_id], want_logits, want_hidden)
+
+    @property
+    def device_ms(self) -> float:
+        """Device time of the kernels of the latest prefill/step/generate (ms)."""
+        ms = C.c_float()
+        check(lib().rabbit_cuda_refv2_device_ms(self.handle, C.byref(ms)))
+        return ms.value
 
     def generate(self, n_new: int) -> np.ndarray:
         out = np.full(n_new, -1, np.int32)

@@ -46,58 +46,115 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 }
 
 // ------------------------------------------------------------ fp32 GEMV --
-// One warp per row, grid-stride over the rows of all matrices; lanes read
-// the row as float4 (eight loads in flight each) against x staged in shared
-// memory.
-__global__ void __launch_bounds__(512, 2) k_gemv_f32(GemvF32Args a) {
-    extern __shared__ __align__(16) float xs[];
+__device__ __forceinline__ void fma4(float &acc, const float4 w, const float4 x) {
+    acc = fmaf(w.x, x.x, acc);
+    acc = fmaf(w.y, x.y, acc);
+    acc = fmaf(w.z, x.z, acc);
+    acc = fmaf(w.w, x.w, acc);
+}
+
+__device__ __forceinline__ const float4 *gemv_row_ptr(const GemvF32Args &a, int r) {
+    int m = 0;
+    while (r >= a.rows[m]) r -= a.rows[m++];
+    return reinterpret_cast<const float4 *>(a.W[m] + (size_t)r * a.in_dim);
+}
+
+template <int XK>
+__global__ void __launch_bounds__(kGemvF32Threads, XK >= 8 ? 1 : 2) k_gemv_f32(GemvF32Args a) {
+    // rows per group: 8 float4 loads per thread in flight whatever XK
+    constexpr int RG = kGemvF32Rows / XK, NW = kGemvF32Threads / 32;
+    __shared__ float part[2][NW][kGemvF32Rows];  // per-warp row sums, double-buffered
     __shared__ float red[32];
     launch_dependents();
-    wait_prerequisite();
-    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int in = a.in_dim, in4 = in >> 2;
-    for (int i = tid; i < in; i += nthr) xs[i] = a.x[i];
-    if (a.norm_w) {
-        __syncthreads();
-        float ss = 0.f;
-        for (int i = tid; i < in; i += nthr) ss += xs[i] * xs[i];
-        ss = block_sum(ss, red);
-        const float inv = 1.0f / sqrtf(ss / (float)in + 1e-5f);
-        for (int i = tid; i < in; i += nthr) xs[i] = (xs[i] * inv) * a.norm_w[i];
-    }
-    __syncthreads();
-    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
     int total = 0;
     for (int m = 0; m < a.nmat; ++m) total += a.rows[m];
-    const int nw = nthr >> 5;
-    for (int r = blockIdx.x * nw + warp; r < total; r += gridDim.x * nw) {
-        int m = 0, row = r;
-        while (row >= a.rows[m]) row -= a.rows[m++];
-        const float4 *w4 = reinterpret_cast<const float4 *>(a.W[m] + (size_t)row * in);
-        float acc = 0.f;
-        int j = lane;
-        for (; j + 7 * 32 < in4; j += 8 * 32) {
-            float4 w[8];
+    const int r0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int r1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    float4 w[RG][XK];
+    auto load_group = [&](int rb) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) w[u] = __ldcs(w4 + j + 32 * u);
+        for (int u = 0; u < RG; ++u) {
+            const float4 *p = rb + u < r1 ? gemv_row_ptr(a, rb + u) : nullptr;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float4 x = x4[j + 32 * u];
-                acc = fmaf(w[u].x, x.x, acc);
-                acc = fmaf(w[u].y, x.y, acc);
-                acc = fmaf(w[u].z, x.z, acc);
-                acc = fmaf(w[u].w, x.w, acc);
+            for (int k = 0; k < XK; ++k) {
+                const int c = tid + k * kGemvF32Threads;
+                w[u][k] = p && c < in4 ? __ldcs(p + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-        for (; j < in4; j += 32) {
-            const float4 w = __ldcs(w4 + j), x = x4[j];
-            acc = fmaf(w.x, x.x, acc);
-            acc = fmaf(w.y, x.y, acc);
-            acc = fmaf(w.z, x.z, acc);
-            acc = fmaf(w.w, x.w, acc);
+    };
+    if (r0 < r1) load_group(r0);
+    wait_prerequisite();
+    if (r0 >= r1 && !(a.embed && blockIdx.x == 0)) return;
+    const float *x = a.x;
+    if (a.embed) {
+        int t = a.idp ? *a.idp : a.id;
+        t %= a.V;
+        if (t < 0) t = 0;
+        x = a.embed + (size_t)t * in;
+    }
+    const float4 *x4g = reinterpret_cast<const float4 *>(x);
+    float4 xv[XK];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < XK; ++k) {
+        const int c = tid + k * kGemvF32Threads;
+        xv[k] = c < in4 ? x4g[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += (xv[k].x * xv[k].x + xv[k].y * xv[k].y) + (xv[k].z * xv[k].z + xv[k].w * xv[k].w);
+        if (a.embed && blockIdx.x == 0 && c < in4) reinterpret_cast<float4 *>(a.h)[c] = xv[k];
+    }
+    if (a.norm_w) {
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / (float)in + 1e-5f);
+        const float4 *n4 = reinterpret_cast<const float4 *>(a.norm_w);
+#pragma unroll
+        for (int k = 0; k < XK; ++k) {
+            const int c = tid + k * kGemvF32Threads;
+            if (c < in4) {
+                const float4 nw = n4[c];
+                xv[k].x = (xv[k].x * inv) * nw.x;
+                xv[k].y = (xv[k].y * inv) * nw.y;
+                xv[k].z = (xv[k].z * inv) * nw.z;
+                xv[k].w = (xv[k].w * inv) * nw.w;
+            }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) a.y[m][row] = (a.res[m] ? a.res[m][row] : 0.f) + acc;
+    }
+    int buf = 0;
+    for (int rb = r0; rb < r1; rb += RG, buf ^= 1) {
+        if (rb != r0) load_group(rb);
+        float v[kGemvF32Rows];
+#pragma unroll
+        for (int u = 0; u < kGemvF32Rows; ++u) {
+            float acc = 0.f;
+            if (u < RG) {
+#pragma unroll
+                for (int k = 0; k < XK; ++k) fma4(acc, w[u][k], xv[k]);
+            }
+            v[u] = acc;
+        }
+        const float tot = warp_reduce8(v);  // lane 4u holds row u's warp sum
+        if ((lane & 3) == 0) part[buf][warp][lane >> 2] = tot;
+        __syncthreads();
+        if (tid < RG && rb + tid < r1) {
+            float sum = 0.f;
+#pragma unroll
+            for (int wi = 0; wi < NW; ++wi) sum += part[buf][wi][tid];
+            int m = 0, row = rb + tid;
+            while (row >= a.rows[m]) row -= a.rows[m++];
+            a.y[m][row] = (a.res[m] ? a.res[m][row] : 0.f) + sum;
+        }
+    }
+}
+
+const void *gemv_f32_kernel(int in) {
+    const int xk = (in / 4 + kGemvF32Threads - 1) / kGemvF32Threads;
+    switch (xk) {
+        case 1: return (const void *)k_gemv_f32<1>;
+        case 2: return (const void *)k_gemv_f32<2>;
+        case 3: case 4: return (const void *)k_gemv_f32<4>;
+        case 5: case 6: case 7: case 8: return (const void *)k_gemv_f32<8>;
+        default: return nullptr;
     }
 }
 
@@ -115,60 +172,124 @@ __device__ __forceinline__ void rope_pairs(float *x, int hd, int pos) {
     }
 }
 
-__global__ void __launch_bounds__(256) k_attention(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
+    __shared__ bool last;
     launch_dependents();
     wait_prerequisite();
-    const int j = blockIdx.x, hd = a.hd, kv_dim = a.nkv * hd;
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarp = nthr >> 5;
+    const int head = blockIdx.x, split = blockIdx.y, hd = a.hd, kvd = a.nkv * hd;
     const int rep = a.nh / a.nkv;  // nh is a multiple of nkv (checked at creation)
-    float *qs = sm;       // [hd]
-    float *sc = sm + hd;  // [max_len]
-    float *kh = a.k + (size_t)j * hd;
-    rope_pairs(kh, hd, a.pos);
-    __syncthreads();
-    const int len = a.len < a.max_len ? a.len + 1 : a.len;
-    if (a.len < a.max_len)
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            a.kc[(size_t)a.len * kv_dim + (size_t)j * hd + i] = kh[i];
-            a.vc[(size_t)a.len * kv_dim + (size_t)j * hd + i] = a.v[(size_t)j * hd + i];
-        }
-    __syncthreads();
-    const float scale = 1.0f / sqrtf((float)hd);
-    for (int r = 0; r < rep; ++r) {
-        const int head = j * rep + r;
-        float *qh = a.q + (size_t)head * hd;
-        rope_pairs(qh, hd, a.pos);
-        __syncthreads();
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = qh[i];
-        __syncthreads();
-        for (int t = threadIdx.x; t < len; t += blockDim.x) {
-            const float *kt = a.kc + (size_t)t * kv_dim + (size_t)j * hd;
-            float dot = 0.f;
-            for (int i = 0; i < hd; ++i) dot += qs[i] * kt[i];
-            sc[t] = dot * scale;
-        }
-        __syncthreads();
-        float mx = -INFINITY;
-        for (int t = threadIdx.x; t < len; t += blockDim.x) mx = fmaxf(mx, sc[t]);
-        mx = block_max(mx, red);
-        float sum = 0.f;
-        for (int t = threadIdx.x; t < len; t += blockDim.x) {
-            const float e = expf(sc[t] - mx);
-            sc[t] = e;
-            sum += e;
-        }
-        sum = block_sum(sum, red);
-        if (sum > 0.f)
-            for (int t = threadIdx.x; t < len; t += blockDim.x) sc[t] = sc[t] / sum;
-        __syncthreads();
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            float acc = 0.f;
-            for (int t = 0; t < len; ++t) acc += sc[t] * a.vc[(size_t)t * kv_dim + (size_t)j * hd + i];
-            a.out[(size_t)head * hd + i] = acc;
-        }
-        __syncthreads();
+    const int j = head / rep;
+    const int groups = hd < nthr ? nthr / hd : 1;
+    float *qs = sm;                // [hd]
+    float *ks = qs + hd;           // [hd] this token's k (RoPE applied)
+    float *sc = ks + hd;           // [max_len]
+    float *pv = sc + a.max_len;    // [groups][hd]
+    for (int i = tid; i < hd; i += nthr) {
+        qs[i] = a.q[(size_t)head * hd + i];
+        ks[i] = a.k[(size_t)j * hd + i];
     }
+    __syncthreads();
+    rope_pairs(qs, hd, a.pos);
+    rope_pairs(ks, hd, a.pos);
+    __syncthreads();
+    const bool append = a.len < a.max_len;
+    const int len = append ? a.len + 1 : a.len;
+    const float *vnew = a.v + (size_t)j * hd;
+    if (append && head % rep == 0 && split == 0)
+        for (int i = tid; i < hd; i += nthr) {
+            a.kc[(size_t)a.len * kvd + (size_t)j * hd + i] = ks[i];
+            a.vc[(size_t)a.len * kvd + (size_t)j * hd + i] = vnew[i];
+        }
+    // this CTA's positions [p0, p1); the appended one reads this CTA's own
+    // k / v (another CTA writes the cache row)
+    const int p0 = (int)((long long)split * len / a.splits);
+    const int p1 = (int)((long long)(split + 1) * len / a.splits);
+    const int n = p1 - p0;
+    const float scale = 1.0f / sqrtf((float)hd);
+    // scores: a warp per position, lanes across the head, four at a time
+    for (int t0 = warp * 4; t0 < n; t0 += nwarp * 4) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const float *kt[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = p0 + min(t0 + u, n - 1);
+            kt[u] = append && t == a.len ? ks : a.kc + (size_t)t * kvd + (size_t)j * hd;
+        }
+        for (int i = lane; i < hd; i += 32) {
+            const float qi = qs[i];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) d[u] = fmaf(qi, kt[u][i], d[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float v = warp_sum(d[u]);
+            if (lane == 0 && t0 + u < n) sc[t0 + u] = v * scale;
+        }
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int t = tid; t < n; t += nthr) mx = fmaxf(mx, sc[t]);
+    mx = block_max(mx, red);
+    float sum = 0.f;
+    for (int t = tid; t < n; t += nthr) {
+        const float e = expf(sc[t] - mx);
+        sc[t] = e;
+        sum += e;
+    }
+    sum = block_sum(sum, red);  // ends with a barrier: sc is complete
+    // values: thread (g, i) sums positions g, g + groups, ... of column i
+    for (int c = tid; c < groups * hd; c += nthr) {
+        const int g = c / hd, i = c - g * hd;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int t = g; t < n; t += groups) {
+            const int tp = p0 + t;
+            const float vt = append && tp == a.len ? vnew[i]
+                                                  : a.vc[(size_t)tp * kvd + (size_t)j * hd + i];
+            acc = fmaf(sc[t], vt, acc);
+        }
+        pv[c] = acc;
+    }
+    __syncthreads();
+    float *mine = a.part + ((size_t)head * kAttnMaxSplits + split) * (hd + 2);
+    for (int i = tid; i < hd; i += nthr) {
+        float o = 0.f;
+        for (int g = 0; g < groups; ++g) o += pv[g * hd + i];
+        mine[i] = o;
+    }
+    if (tid == 0) {
+        mine[hd] = mx;
+        mine[hd + 1] = sum;
+    }
+    // the last CTA of this head merges the splits:
+    // out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(a.count + head, 1u) == (unsigned)a.splits - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float *ph = a.part + (size_t)head * kAttnMaxSplits * (hd + 2);
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < a.splits; ++s2) M = fmaxf(M, __ldcg(ph + (size_t)s2 * (hd + 2) + hd));
+    float L = 0.f;
+    for (int s2 = 0; s2 < a.splits; ++s2) {
+        const float *q2 = ph + (size_t)s2 * (hd + 2);
+        L += __ldcg(q2 + hd + 1) * expf(__ldcg(q2 + hd) - M);
+    }
+    for (int i = tid; i < hd; i += nthr) {
+        float o = 0.f;
+        for (int s2 = 0; s2 < a.splits; ++s2) {
+            const float *q2 = ph + (size_t)s2 * (hd + 2);
+            o = fmaf(__ldcg(q2 + i), expf(__ldcg(q2 + hd) - M), o);
+        }
+        a.out[(size_t)head * hd + i] = L > 0.f ? o / L : o;
+    }
+    if (tid == 0) a.count[head] = 0u;  // ready for the next launch
 }
 
 // -------------------------------------------------------------- lm_head --
@@ -292,17 +413,6 @@ __global__ void __launch_bounds__(256) k_logits_argmax(const float *partial, int
         *argmax_out = si[0] == 0x7fffffff ? 0 : si[0];
         *done_ctr = 0u;  // ready for the next launch
     }
-}
-
-// ---------------------------------------------------------------- embed --
-__global__ void k_embed(const float *embed, int V, int H, const int *idp, int id, float *h) {
-    launch_dependents();
-    wait_prerequisite();
-    int t = idp ? *idp : id;
-    t %= V;
-    if (t < 0) t = 0;
-    const float *e = embed + (size_t)t * H;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) h[i] = e[i];
 }
 
 // ----------------------------------------------------------------- fill --

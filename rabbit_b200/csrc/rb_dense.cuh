@@ -11,6 +11,17 @@ constexpr int kMaxGemvMats = 4;
 // y_m = W_m x for up to 4 row-major fp32 matrices [rows_m, in] sharing x.
 // norm_w != nullptr: x is first replaced by rmsnorm(x) * norm_w
 // (forward_v2.c:61-69). res_m != nullptr: y_m = res_m + W_m x (res_m may be y_m).
+// embed != nullptr: x is row id % V of embed [V, in] (id from *idp, or `id`
+// when idp is nullptr; negative -> row 0, forward_v2.c:459-461), and the raw
+// row is also written to h (the token's residual stream).
+//
+// CTA b owns the stacked rows [b R / G, (b + 1) R / G) (R rows, G CTAs) and
+// walks them in groups of 8 / XK; thread t owns the float4 columns t,
+// t + 512, ... (XK of them) of x, held in registers, so each row is one
+// fully coalesced sweep of the CTA. The loads of the first group go out
+// before the wait for the kernel before (weights are not written by it).
+constexpr int kGemvF32Threads = 512;
+constexpr int kGemvF32Rows = 8;  // float4 loads per thread and group
 struct GemvF32Args {
     const float *W[kMaxGemvMats];
     float *y[kMaxGemvMats];
@@ -19,21 +30,48 @@ struct GemvF32Args {
     int nmat, in_dim;
     const float *x;
     const float *norm_w;
+    const float *embed;
+    const int *idp;
+    int id, V;
+    float *h;
 };
 
-__global__ void k_gemv_f32(GemvF32Args a);
+// The kernel for rows of `in` floats: XK = ceil(in / 4 / 512) float4 columns
+// per thread rounded up to 1, 2, 4 or 8 (in <= 16384); nullptr past that.
+const void *gemv_f32_kernel(int in);
 
-// One CTA per KV head: RoPE on its k, append k / v at position `len` of the
-// cache when len < max_len, then for each of its query heads RoPE on q,
-// scores over the cache, softmax, weighted sum of values (forward_v2.c:171-246).
+
+// Grid (nh, splits): CTA (h, s) takes query head h and the s-th of `splits`
+// equal ranges of the cached positions. Every CTA applies RoPE to its q and
+// to its KV head's k; the first CTA of each group (h % rep == 0, s == 0)
+// appends the k / v row at position `len` when len < max_len. Each CTA
+// leaves its range's max score, sum of exponentials and unnormalised
+// weighted values in `part`; the last CTA of a head to finish merges them
+// into out (forward_v2.c:171-246: scores scaled by 1/sqrt(hd), softmax,
+// weighted sum of values).
+constexpr int kAttnMaxSplits = 8;
+constexpr int kAttnThreads = 256;
 struct AttnArgs {
-    float *q;             // [nh * hd] (RoPE applied in place)
-    float *k;             // [nkv * hd] (RoPE applied in place)
+    const float *q;       // [nh * hd] (before RoPE)
+    const float *k;       // [nkv * hd] (before RoPE)
     const float *v;       // [nkv * hd]
     float *kc, *vc;       // cache [max_len, nkv * hd]
     float *out;           // [nh * hd]
-    int nh, nkv, hd, pos, len, max_len;
+    float *part;          // [nh][kAttnMaxSplits][hd + 2]
+    unsigned *count;      // [nh] arrivals, zero between launches
+    int nh, nkv, hd, pos, len, max_len, splits;
 };
+
+// Splits for a window of n positions (after the append): ranges of >= 32.
+inline int attention_splits(int n) {
+    const int s = (n + 31) / 32;
+    return s < 1 ? 1 : (s > kAttnMaxSplits ? kAttnMaxSplits : s);
+}
+// Dynamic shared memory of k_attention.
+inline size_t attention_smem(int hd, int max_len) {
+    const int groups = hd < kAttnThreads ? kAttnThreads / hd : 1;
+    return sizeof(float) * (size_t)(2 * hd + max_len + groups * hd);
+}
 
 __global__ void k_attention(AttnArgs a);
 
@@ -55,10 +93,6 @@ __global__ void k_lm_head_partial(LmHeadArgs a);
 __global__ void k_logits_argmax(const float *partial, int nchunk, int V, float *logits,
                                 int *block_best, float *block_val, int *argmax_out,
                                 unsigned *done_ctr);
-
-// h = embed[id % V] (id < 0 -> 0; forward_v2.c:459-461). id from *idp when
-// idp != nullptr, else `id`.
-__global__ void k_embed(const float *embed, int V, int H, const int *idp, int id, float *h);
 
 // Seeded synthetic fill: p[i] uniform with standard deviation `sigma`
 // (sigma == 0: every element = `value`).

@@ -60,7 +60,6 @@ struct rabbit_cuda_moe {
     int *ids_int = nullptr, *err_io = nullptr;
     uint8_t *dio = nullptr;
     size_t dio_bytes = 0;
-    unsigned long long *bar = nullptr;
     unsigned *flags = nullptr;  // fused path: per-CTA "h read" tags
     unsigned seq = 1;           // tag of the next fused launch (never 0)
     rb::Route *route = nullptr;
@@ -214,12 +213,17 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     p->smem = head + (size_t)ns * slot + tail + 16 * (size_t)ns + bars;
     // Until routing is done the ring is idle and stages h and the norm
     // weights (8 H bytes); routers up to 256 KB that fit in front of them are
-    // staged too and scored by every CTA; larger ones are split over the CTAs
-    // behind a grid barrier.
+    // staged too and scored by every CTA; larger ones are split over the CTAs,
+    // which publish the scores as tagged values.
     const size_t ring = (size_t)ns * slot, router_bytes = (size_t)p->E * H * 4;
     if ((size_t)8 * H > ring) return false;
     a.route_local =
         router_bytes <= 256 * 1024 && align_up(router_bytes, 128) + (size_t)8 * H <= ring ? 1 : 0;
+    // split routing: a CTA scores ceil(E / grid) rows at most (one when E <
+    // grid); they are staged with h before the wait for the kernel before
+    const size_t own_rows = p->E < G ? 1 : (size_t)(p->E + G - 1) / G;
+    a.route_stage =
+        !a.route_local && align_up(own_rows * H * 4, 128) + (size_t)8 * H <= ring ? 1 : 0;
     if (p->smem > (size_t)kMaxDynSmem) return false;
     p->block = (CW + 3) * 32;  // consumers, producer, epilogue, scout
     if (G > kMaxGrid) return false;
@@ -233,7 +237,7 @@ static void free_pool(rabbit_cuda_moe *p) {
     if (p->device >= 0) cudaSetDevice(p->device);
     if (p->up) cudaStreamSynchronize(p->up);
     void *bufs[] = {p->pool,  p->rms,  p->router, p->scores,  p->mid, p->xn,  p->down,
-                    p->h_in,  p->dio,   p->bar,   p->route,   p->flags};
+                    p->h_in,  p->dio,   p->route,   p->flags};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int i = 0; i < 2; ++i) {
@@ -403,7 +407,7 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     }
     if ((e = cudaMalloc(&p->rms, sizeof(float) * (size_t)p->H * p->L)) != cudaSuccess ||
         (e = cudaMalloc(&p->router, sizeof(float) * HE * p->L)) != cudaSuccess ||
-        (e = cudaMalloc(&p->scores, sizeof(float) * p->E)) != cudaSuccess ||
+        (e = cudaMalloc(&p->scores, sizeof(unsigned long long) * p->E)) != cudaSuccess ||
         (e = cudaMalloc(&p->mid, mid_bytes(p))) != cudaSuccess ||
         (e = cudaMemset(p->mid, 0, mid_bytes(p))) != cudaSuccess ||
         (e = cudaMalloc(&p->xn, sizeof(float) * p->H)) != cudaSuccess ||
@@ -415,9 +419,7 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         (e = cudaMalloc(&p->dio, p->dio_bytes = sizeof(float) * (size_t)p->H + 80)) !=
             cudaSuccess ||
         (e = cudaMemset(p->dio, 0, p->dio_bytes)) != cudaSuccess ||
-        (e = cudaMalloc(&p->bar, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaMalloc(&p->route, sizeof(Route))) != cudaSuccess ||
-        (e = cudaMemset(p->bar, 0, sizeof(unsigned long long))) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 32))) !=
             cudaSuccess) {
@@ -570,16 +572,16 @@ static int decode_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float
         a.I = p->I;
         a.S = p->S;
         a.usable = p->usable ? 1 : 0;
-        a.scores = p->scores;
+        a.scores = reinterpret_cast<unsigned long long *>(p->scores);
         a.mid = reinterpret_cast<unsigned long long *>(p->mid);
         a.down = reinterpret_cast<unsigned long long *>(p->down);
         a.flags = p->flags;
-        a.bar = p->bar;
         a.err = err;
         {
-            void *tagged[] = {p->mid, p->down, p->flags};
-            const size_t bytes[] = {mid_bytes(p), down_bytes(p), sizeof(unsigned) * kMaxGrid};
-            a.seq = next_seq(&p->seq, tagged, bytes, 3, s);
+            void *tagged[] = {p->mid, p->down, p->flags, p->scores};
+            const size_t bytes[] = {mid_bytes(p), down_bytes(p), sizeof(unsigned) * kMaxGrid,
+                                    sizeof(unsigned long long) * p->E};
+            a.seq = next_seq(&p->seq, tagged, bytes, 4, s);
         }
         a.wait_ns = wait_limit_ns();
         RB_CUDA(launch_fused(p, a, s));
@@ -631,9 +633,9 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
 
 // ------------------------------------------------------- no-alloc decode --
 // Scratch for rabbit_cuda_moe_decode_dev_noalloc, in a fixed array of this
-// module instead of the pool: [0, 256) grid-barrier counter (u64 at 0),
-// routed ids at 64 and weights at 128 when the caller passes none; then the
-// per-CTA flags; the router scores (E floats); mid ((k + S) x I tagged
+// module instead of the pool: [0, 256) routed ids at 64 and weights at 128
+// when the caller passes none; then the per-CTA flags; the router scores (E
+// tagged values, 8 bytes each); mid ((k + S) x I tagged
 // values, 8 bytes each); the down rows per column chunk of W2 ((k + S) x KC
 // x H tagged values), each part 256-aligned. Every
 // device that loads the library holds these bytes until the process exits.
@@ -669,7 +671,7 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: h must be 16-byte aligned");
     const size_t off_flags = 256;
     const size_t off_scores = off_flags + align_up(sizeof(unsigned) * kMaxGrid, 256);
-    const size_t off_mid = off_scores + align_up((size_t)p->E * 4, 256);
+    const size_t off_mid = off_scores + align_up((size_t)p->E * 8, 256);
     const size_t off_down = off_mid + align_up(mid_bytes(p), 256);
     const size_t need = off_down + down_bytes(p);
     if (need > kNoAllocScratchBytes)
@@ -687,11 +689,9 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     uint8_t *scratch = nullptr;
     if ((st = noalloc_scratch(p->device, &scratch)) != RABBIT_CUDA_OK) return st;
     cudaStream_t s = as_stream(stream, p->ctx);
-    // The grid-barrier counter keeps the last call's value (a call that gave
-    // up may have left it anywhere): every call starts it from zero. Values
-    // shared between CTAs are tagged with the call's sequence number, which
-    // is new on every call on this device.
-    RB_CUDA(cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), s));
+    // Values shared between CTAs are tagged with the call's sequence number,
+    // which is new on every call on this device: what an earlier call left in
+    // the array is never read.
     MoeFusedArgs a = p->plan;
     a.h_in = d_h_in;
     a.h_out = d_h_out;
@@ -710,11 +710,10 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     a.I = p->I;
     a.S = p->S;
     a.usable = p->usable ? 1 : 0;
-    a.scores = reinterpret_cast<float *>(scratch + off_scores);
+    a.scores = reinterpret_cast<unsigned long long *>(scratch + off_scores);
     a.mid = reinterpret_cast<unsigned long long *>(scratch + off_mid);
     a.down = reinterpret_cast<unsigned long long *>(scratch + off_down);
     a.flags = reinterpret_cast<unsigned *>(scratch + off_flags);
-    a.bar = reinterpret_cast<unsigned long long *>(scratch);
     {
         std::lock_guard<std::mutex> g(g_noalloc_mu);
         void *tagged[] = {scratch + off_flags};
@@ -733,14 +732,9 @@ int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream) {
     RB_CUDA(cudaSetDevice(p->device));
     cudaStream_t s = as_stream(stream, p->ctx);
     int st = check_device_error(p->ctx, s, "moe_decode");
-    if (st != RABBIT_CUDA_OK) {
-        // a barrier wait that gave up may have left arrivals behind: start
-        // clean (tagged scratch needs nothing: the next launch has a new tag)
-        cudaMemsetAsync(p->bar, 0, sizeof(unsigned long long), s);
-        cudaStreamSynchronize(s);
-        return st;
-    }
-    return ok();
+    // after a wait that gave up, scratch needs no cleaning: everything the
+    // CTAs share is tagged, and the next launch has a new tag
+    return st != RABBIT_CUDA_OK ? st : ok();
 }
 
 int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
@@ -762,9 +756,7 @@ int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, flo
     RB_CUDA(cudaStreamSynchronize(s));
     const int err = *reinterpret_cast<const int *>(pin_o + (p->dio_bytes - 16));
     if (err != 0) {
-        // a wait that gave up may have left grid-barrier arrivals behind
         cudaMemsetAsync(p->err_io, 0, sizeof(int), s);
-        cudaMemsetAsync(p->bar, 0, sizeof(unsigned long long), s);
         cudaStreamSynchronize(s);
         if (err == RB_ERR_TIMEOUT)
             return fail(RABBIT_CUDA_ERR_TIMEOUT, "moe_decode: a bounded device wait ran out");

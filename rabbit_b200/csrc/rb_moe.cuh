@@ -37,14 +37,14 @@ struct MoeFusedArgs {
     int n_local;   // local ids >= n_local have no record (skipped)
     int H, E, k, I, S;
     int usable;    // 0: records too small, experts add nothing (forward_v2.c:319-322)
-    int route_local;  // 1: every CTA computes all router rows (no grid barrier 1)
-    float *scores; // scratch [E] (route_local == 0)
+    int route_local;  // 1: every CTA computes all router rows from shared memory
+    int route_stage;  // route_local == 0: 1 = each CTA's own rows staged in shared memory
+    unsigned long long *scores;  // [E] tagged router scores (route_local == 0)
     // scratch shared between CTAs, every value tagged {float, seq} (64-bit)
     unsigned long long *mid;   // [k+S][I]
     unsigned long long *down;  // [k+S][tc.KC][H]: down rows per slot and column chunk
     unsigned *flags;           // [grid]: seq once the CTA has read h
     unsigned seq;              // this launch's tag (never 0)
-    unsigned long long *bar;   // grid-barrier arrival counter (large routers)
     int *err;
     uint64_t wait_ns;
     // plan: CW consumer warps; phase B (gate/up, in = H) uses KSb warps per
@@ -56,7 +56,7 @@ struct MoeFusedArgs {
 };
 
 // k_moe_decode_g32<JB, JC> for JB / JC groups of 32 per lane in phases B / C
-// (1 or 2 each); cooperative launch with one MoeFusedArgs argument.
+// (1 or 2 each); one CTA per SM, all resident, one MoeFusedArgs argument.
 const void *moe_fused_kernel(int JB, int JC);
 
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine

@@ -1,11 +1,11 @@
 // rb_moe_kernels.cu -- MoE decode on B200: one token through one layer's
 // routed + shared SwiGLU experts (forward_v2.c:280-402).
 //
-// Fused group-32 kernel (k_moe_decode_g32), cooperative launch, one CTA per SM:
+// Fused group-32 kernel (k_moe_decode_g32), one CTA per SM, all resident:
 //   A. every CTA: rmsnorm(h) -> xn in shared memory; router scores: for
 //      routers up to 256 KB every CTA computes all E rows itself (same code
 //      and order everywhere, so the same scores); larger routers are split
-//      over the CTAs and published through a grid barrier.
+//      over the CTAs and published as tagged values (below).
 //      every CTA: top-k + softmax on the scores (identical in all CTAs), the
 //      active slot list (routed in rank order, then shared experts).
 //   B. gate/up: the active slots' GU tiles (TRb rows of gate and of up,
@@ -29,9 +29,8 @@
 //      combine: row tile t is owned by CTA t % grid, which reads its partials
 //      once tagged: down_j = the sum of its chunks in chunk order, h_out =
 //      h + sum_j w_j down_j in slot order (forward_v2.c:356-357, 398-399).
-// There are no grid barriers between the phases (one before top-k for
-// routers too large to stage): CTAs wait only for the data they read.
-// Every wait (mbarrier or grid barrier) is bounded by a %globaltimer limit;
+// There are no grid barriers: CTAs wait only for the data they read.
+// Every wait (mbarrier or tagged value) is bounded by a %globaltimer limit;
 // a timeout records RB_ERR_TIMEOUT and the CTA drains its copies and exits.
 #include "rb_gemv.cuh"
 #include "rb_moe.cuh"
@@ -72,29 +71,6 @@ __device__ uint64_t g_chunk_ns[4 * 64];
     } while (0)
 #endif
 
-// ---------------------------------------------------------- grid barrier --
-// One thread per CTA. *count is a monotonic 64-bit arrival counter (zeroed at
-// pool creation and after any failed wait); every barrier adds exactly
-// gridDim.x, so the round ends at the next multiple of nblocks. One
-// release-atomic to arrive, acquire loads to wait: a single L2 round trip on
-// the critical path.
-__device__ bool grid_barrier(unsigned long long *count, unsigned nblocks, uint64_t wait_ns,
-                             int *err) {
-    unsigned long long old;
-    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(count) : "memory");
-    const unsigned long long target = old - old % nblocks + nblocks;
-    const uint64_t t0 = globaltimer_ns();
-    for (unsigned it = 0;; ++it) {
-        unsigned long long v;
-        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(count) : "memory");
-        if (v >= target) return true;
-        if ((it & 15u) == 15u && globaltimer_ns() - t0 > wait_ns) {
-            set_error(err, RB_ERR_TIMEOUT);
-            return false;
-        }
-    }
-}
-
 // --------------------------------------------------------------- top-k ----
 // Softmax over the k selected scores in place (max-subtracted, expf).
 __device__ __forceinline__ void softmax_k(float *w, int k) {
@@ -132,23 +108,36 @@ __device__ void topk_softmax(const float *scores, int E, int k, int *ids, float 
     softmax_k(w, k);
 }
 
-// forward_v2.c:248-278 by one warp: an expert with a score above the -1e30
-// seed (NaN never qualifies) takes place r = the number of qualifying experts
-// with a larger score, or an equal score and a lower index -- the order the
-// strict-'>' insertion builds. Places past the qualifying count keep (-1,
-// -1e30). ids / w in shared memory; every lane of the warp calls it.
-__device__ void topk_softmax_warp(const float *scores, int E, int k, int *ids, float *w) {
-    const int lane = threadIdx.x & 31;
-    if (lane < k) {
-        ids[lane] = -1;
-        w[lane] = -1e30f;
+// forward_v2.c:248-278 by a whole CTA: an expert with a score above the
+// -1e30 seed (NaN never qualifies) takes place r = the number of qualifying
+// experts with a larger score, or an equal score and a lower index -- the
+// order the strict-'>' insertion builds. Places past the qualifying count
+// keep (-1, -1e30). One thread per expert, the scores read as float4 from
+// shared memory (16-byte aligned); ids / w in shared memory. Every thread
+// calls it; thread 0 softmaxes the list last (no sync after that).
+__device__ void topk_softmax_block(const float *scores, int E, int k, int *ids, float *w) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    if (tid < k) {
+        ids[tid] = -1;
+        w[tid] = -1e30f;
     }
-    __syncwarp();
-    for (int e = lane; e < E; e += 32) {
+    __syncthreads();
+    const float4 *s4 = reinterpret_cast<const float4 *>(scores);
+    const int E4 = E >> 2;
+    for (int e = tid; e < E; e += nthr) {
         const float s = scores[e];
         if (!(s > -1e30f)) continue;
         int r = 0;
-        for (int f = 0; f < E; ++f) {
+#pragma unroll 4
+        for (int f4 = 0; f4 < E4; ++f4) {
+            const float4 t = s4[f4];
+            const int f = 4 * f4;
+            r += (t.x > s || (t.x == s && f < e)) ? 1 : 0;
+            r += (t.y > s || (t.y == s && f + 1 < e)) ? 1 : 0;
+            r += (t.z > s || (t.z == s && f + 2 < e)) ? 1 : 0;
+            r += (t.w > s || (t.w == s && f + 3 < e)) ? 1 : 0;
+        }
+        for (int f = 4 * E4; f < E; ++f) {
             const float t = scores[f];
             r += (t > s || (t == s && f < e)) ? 1 : 0;
         }
@@ -157,9 +146,8 @@ __device__ void topk_softmax_warp(const float *scores, int E, int k, int *ids, f
             w[r] = s;
         }
     }
-    __syncwarp();
-    if (lane == 0) softmax_k(w, k);
-    __syncwarp();
+    __syncthreads();
+    if (tid == 0) softmax_k(w, k);
 }
 
 // Active slot list: routed experts in rank order, then shared experts with
@@ -373,8 +361,16 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
     uint64_t *xfull = pfree + kPartRing;                        // [2] chunk of mid staged
     uint64_t *xfree = xfull + 2;                                // [2] its planes taken
     const uint32_t router_bytes = (uint32_t)a.E * (uint32_t)H * 4u;
-    // the ring is idle until routing is done: [router (route_local)] [h] [rms]
-    float *hs = reinterpret_cast<float *>(ring + (a.route_local ? align_up(router_bytes, 128) : 0));
+    // Split routing: this CTA scores rows r_e0, r_e0 + grid, ... (r_n rows;
+    // r_e0 = CTA % E when E < grid, so every row has several CTAs).
+    const int r_e0 = a.E < (int)gridDim.x ? (int)blockIdx.x % a.E : (int)blockIdx.x;
+    const int r_n = a.route_local || r_e0 >= a.E ? 0 : (a.E - r_e0 + (int)gridDim.x - 1) / (int)gridDim.x;
+    // the ring is idle until routing is done: [router rows] [h] [rms], the
+    // router rows being the whole router (route_local) or this CTA's rows
+    // (route_stage), else none
+    const uint32_t staged =
+        a.route_local ? router_bytes : (a.route_stage ? (uint32_t)r_n * (uint32_t)H * 4u : 0u);
+    float *hs = reinterpret_cast<float *>(ring + align_up(staged, 128));
     float *rs = hs + H;
 
     RB_STAMP(0);
@@ -407,6 +403,17 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
             for (uint32_t o = 0; o < router_bytes; o += 32768u)
                 bulk_g2s(ring + o, reinterpret_cast<const uint8_t *>(a.router) + o,
                          router_bytes - o < 32768u ? router_bytes - o : 32768u, rbar, pol);
+        } else if (staged) {
+            mbar_arrive_expect_tx(rbar, staged);
+            const uint64_t pol = policy_evict_last();  // read again every token
+            const uint32_t rowb = (uint32_t)H * 4u;
+            for (int n = 0; n < r_n; ++n) {
+                const uint8_t *src =
+                    reinterpret_cast<const uint8_t *>(a.router + (size_t)(r_e0 + n * (int)gridDim.x) * H);
+                for (uint32_t o = 0; o < rowb; o += 32768u)
+                    bulk_g2s(ring + (size_t)n * rowb + o, src + o,
+                             rowb - o < 32768u ? rowb - o : 32768u, rbar, pol);
+            }
         }
         wait_prerequisite();
         bulk_g2s(hs, a.h_in, 4u * (uint32_t)H, hbar, pol_h);
@@ -423,7 +430,7 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
         const bool okh = mbar_wait(hbar, 0, a.wait_ns, a.err);
         if (__syncthreads_or(!okh)) {
             if (!okh) mbar_wait(hbar, 0, a.wait_ns, a.err);  // let the copies land first
-            if (a.route_local) mbar_wait(rbar, 0, a.wait_ns, a.err);
+            if (staged) mbar_wait(rbar, 0, a.wait_ns, a.err);
             return;
         }
     }
@@ -491,40 +498,74 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
         __syncthreads();
         RB_STAMP(1);
     } else {
-        // Router rows spread over the CTAs, published through global scratch.
-        for (int e = blockIdx.x; e < a.E; e += gridDim.x) {
-            const float *wr = a.router + (size_t)e * H;
+        // Larger routers: the rows are spread over the CTAs -- rows b, b + G,
+        // ... for CTA b when E >= G, else row b % E, so every row has several
+        // CTAs and the first of them to finish publishes it -- each score
+        // stored tagged with this launch. Every CTA then reads all E scores
+        // once their tags match: no grid barrier, no counter. Each copy of a
+        // row comes from the same code in the same order, so copies agree bit
+        // for bit.
+        const int G = (int)gridDim.x;
+        const int nw = nthr >> 5;
+        if (staged) {
+            const bool okr = mbar_wait(rbar, 0, a.wait_ns, a.err);
+            if (__syncthreads_or(!okr)) {
+                if (!okr) mbar_wait(rbar, 0, a.wait_ns, a.err);  // let the copies land first
+                return;
+            }
+        }
+        for (int n = 0; n < r_n; ++n) {
+            const int e = r_e0 + n * G;
+            const float4 *wr =
+                staged ? reinterpret_cast<const float4 *>(ring + (size_t)n * H * 4)
+                       : reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
             float d = 0.f;
-            for (int i = tid; i < H; i += nthr) d += wr[i] * xn[xpad(i)];
+            for (int i4 = tid; i4 < (H >> 2); i4 += nthr) {
+                const float4 w = wr[i4];
+                const float *xp = xn + xpad(i4 * 4);  // four floats of one group
+                d = fmaf(w.x, xp[0], d);
+                d = fmaf(w.y, xp[1], d);
+                d = fmaf(w.z, xp[2], d);
+                d = fmaf(w.w, xp[3], d);
+            }
             d = warp_sum(d);
             if (lane == 0) red[warp] = d;
             __syncthreads();
             if (tid == 0) {
                 float t = 0.f;
-                for (int w = 0; w < (nthr >> 5); ++w) t += red[w];
-                a.scores[e] = t;
+                for (int w = 0; w < nw; ++w) t += red[w];
+                st_tagged(a.scores + e, t, a.seq);
             }
             __syncthreads();
         }
         RB_STAMP(1);
-        if (tid == 0) {
-            s_misc[1] = grid_barrier(a.bar, gridDim.x, a.wait_ns, a.err) ? 0 : 1;
-            s_misc[2] = 0;
+        bool okr = true;
+        for (int e = tid; okr && e < a.E; e += nthr) {
+            const uint64_t t0 = globaltimer_ns();
+            for (unsigned it = 0;; ++it) {
+                const unsigned long long w = ld_tagged(a.scores + e);
+                if (tag_ok(w, a.seq)) {
+                    s_sc[e] = tag_val(w);
+                    break;
+                }
+                if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                    set_error(a.err, RB_ERR_TIMEOUT);
+                    okr = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
         }
-        __syncthreads();
-        if (s_misc[1]) return;  // nothing in flight yet
-        for (int e = tid; e < a.E; e += nthr) s_sc[e] = __ldcg(a.scores + e);
-        __syncthreads();
+        if (tid == 0) s_misc[2] = 0;
+        if (__syncthreads_or(!okr)) return;  // nothing in flight yet
+        RB_STAMP(6);
     }
     RB_DBG(4);
-    if (warp == 0) {
-        // top-k lists in shared memory (the norm's reduction words are free
-        // by now)
-        int *ids = reinterpret_cast<int *>(red);
-        float *w = red + 8;
-        topk_softmax_warp(s_sc, a.E, a.k, ids, w);
-        RB_DBG(8);
-    }
+    // top-k lists in shared memory (the norm's reduction words are free by
+    // now)
+    topk_softmax_block(s_sc, a.E, a.k, reinterpret_cast<int *>(red), red + 8);
+    RB_STAMP(7);
+    RB_DBG(8);
     if (tid == 0) {
         const int *ids = reinterpret_cast<const int *>(red);
         const float *w = red + 8;
@@ -711,37 +752,61 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
                 flags_seen = true;
             }
             const uint64_t t0 = globaltimer_ns();
-            for (int r = lane; r < TRc; r += 32) {
-                const int row = t * TRc + r;
-                if (row >= H) continue;
-                float delta = 0.f;
-                bool ok = true;
-                for (int j = 0; ok && j < nact; ++j) {
-                    const unsigned long long *dp = a.down + (size_t)j * KC * H + row;
-                    unsigned long long w[16];  // KC <= 16: all loads in flight at once
-                    for (unsigned it = 0;; ++it) {
-                        bool all = true;
+            // The lane's values, rows r = lane + 32 m of the tile, in the order
+            // (m, slot j, chunk c), read 16 at a time with all 16 in flight
+            // and folded in that order: down_j = sum over c, delta += w_j
+            // down_j, h_out = h + delta after the row's last slot.
+            const int r_end = min(TRc, H - t * TRc);
+            const int nr = r_end > lane ? (r_end - lane + 31) >> 5 : 0;
+            const int total = nr * nact * KC;
+            int fm = 0, fj = 0, fc = 0;  // (m, j, c) of the next value to fold
+            float dj = 0.f, delta = 0.f;
+            for (int q0 = 0; q0 < total; q0 += 16) {
+                unsigned long long w[16];
+                for (unsigned it = 0;; ++it) {
+                    int m = fm, j = fj, c = fc;
 #pragma unroll
-                        for (int cc = 0; cc < 16; ++cc) {
-                            w[cc] = cc < KC ? ld_tagged(dp + (size_t)cc * H)
-                                            : (unsigned long long)a.seq << 32;
-                            all = all && tag_ok(w[cc], a.seq);
+                    for (int qq = 0; qq < 16; ++qq) {
+                        w[qq] = (unsigned long long)a.seq << 32;
+                        if (q0 + qq < total) {
+                            const int row = t * TRc + lane + 32 * m;
+                            w[qq] = ld_tagged(a.down + ((size_t)j * KC + c) * H + row);
+                            if (++c == KC) {
+                                c = 0;
+                                if (++j == nact) {
+                                    j = 0;
+                                    ++m;
+                                }
+                            }
                         }
-                        if (all) break;
-                        if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
-                            set_error(a.err, RB_ERR_TIMEOUT);
-                            ok = false;
-                            break;
-                        }
-                        __nanosleep(128);
                     }
-                    float dj = 0.f;
+                    bool all = true;
 #pragma unroll
-                    for (int cc = 0; cc < 16; ++cc)
-                        if (cc < KC) dj += tag_val(w[cc]);
-                    delta += s_w[j] * dj;
+                    for (int qq = 0; qq < 16; ++qq) all = all && tag_ok(w[qq], a.seq);
+                    if (all) break;
+                    if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                        set_error(a.err, RB_ERR_TIMEOUT);
+                        return;
+                    }
+                    __nanosleep(128);
                 }
-                if (ok) a.h_out[row] = a.h_in[row] + delta;
+#pragma unroll
+                for (int qq = 0; qq < 16; ++qq) {
+                    if (q0 + qq >= total) break;
+                    dj += tag_val(w[qq]);
+                    if (++fc == KC) {
+                        fc = 0;
+                        delta += s_w[fj] * dj;
+                        dj = 0.f;
+                        if (++fj == nact) {
+                            fj = 0;
+                            const int row = t * TRc + lane + 32 * fm;
+                            a.h_out[row] = a.h_in[row] + delta;
+                            delta = 0.f;
+                            ++fm;
+                        }
+                    }
+                }
             }
         }
 #ifdef RB_PHASE_TIMERS

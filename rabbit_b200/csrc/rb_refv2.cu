@@ -38,10 +38,15 @@ struct rabbit_cuda_refv2 {
     float *hidden = nullptr, *logits = nullptr, *partial = nullptr, *bval = nullptr;
     int *bbest = nullptr, *ids = nullptr;  // ids[kMaxNew + 1]: argmax chain
     unsigned *done = nullptr;
+    float *apart = nullptr;     // attention split partials [nh][kAttnMaxSplits][hd + 2]
+    unsigned *acount = nullptr; // attention arrivals per head [nh]
     float *pin = nullptr;  // host staging: logits | hidden | argmax
     int nchunk = 0, lm_blocks = 0, am_blocks = 0;
+    const void *gemv_h = nullptr, *gemv_q = nullptr;  // projection kernels, rows of H / q_dim
     int pos = 0, len = 0;
     bool stepped = false;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;  // around the kernels of the last call
+    float last_ms = 0.f;
 
     float *rms_attn(int l) const { return w + off_layers() + (size_t)l * layer_floats; }
     float *w_q(int l) const { return rms_attn(l) + H; }
@@ -53,16 +58,17 @@ struct rabbit_cuda_refv2 {
 
 namespace rb {
 
-static bool g_refv2_attr[kMaxDevices];
 
 static void free_refv2(rabbit_cuda_refv2 *c) {
     if (c->device >= 0) cudaSetDevice(c->device);
     void *bufs[] = {c->w,      c->kc,      c->vc,   c->h,    c->q,     c->k,    c->v,
                     c->att,    c->hidden,  c->logits, c->partial, c->bval, c->bbest, c->ids,
-                    c->done};
+                    c->done,   c->apart,   c->acount};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (c->pin) cudaFreeHost(c->pin);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
     delete c;
 }
 
@@ -80,6 +86,13 @@ static cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, size_t smem, cudaStream
     return cfg;
 }
 
+static cudaError_t launch_pdl_ptr(const void *kern, dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t s, void **args) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(grid, block, smem, s, attr);
+    return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
 template <typename... Args>
 static cudaError_t launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t s, Args... args) {
@@ -89,12 +102,14 @@ static cudaError_t launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size
 }
 
 // Enqueue one token on `s`: its id from *idp (device) when idp != nullptr,
-// else `id`; its argmax to *argmax_out (device).
+// else `id`; its argmax to *argmax_out (device). 4 L + 2 launches: per layer
+// the Q/K/V projections (with the embedding lookup in layer 0), attention,
+// the O projection and the MoE block; then lm_head and the argmax.
 static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argmax_out,
                         bool want_hidden, cudaStream_t s) {
     const int sms = c->ctx->sm_count;
-    RB_CUDA(launch_pdl(k_embed, dim3((c->H + 255) / 256), dim3(256), 0, s,
-                       (const float *)c->embed, c->V, c->H, idp, id, c->h));
+    const int kv_after = c->len < c->max_ctx ? c->len + 1 : c->len;
+    const int splits = attention_splits(kv_after);
     for (int l = 0; l < c->L; ++l) {
         GemvF32Args g = {};
         g.nmat = 3;
@@ -110,7 +125,15 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
         g.in_dim = c->H;
         g.x = c->h;
         g.norm_w = c->rms_attn(l);
-        RB_CUDA(launch_pdl(k_gemv_f32, dim3(2 * sms), dim3(512), sizeof(float) * (size_t)c->H, s, g));
+        if (l == 0) {  // h = embed[id % V] (forward_v2.c:459-461)
+            g.embed = c->embed;
+            g.idp = idp;
+            g.id = id;
+            g.V = c->V;
+            g.h = c->h;
+        }
+        void *ga[] = {&g};
+        RB_CUDA(launch_pdl_ptr(c->gemv_h, dim3(2 * sms), dim3(kGemvF32Threads), 0, s, ga));
         AttnArgs at;
         at.q = c->q;
         at.k = c->k;
@@ -118,14 +141,17 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
         at.kc = c->kc + (size_t)l * c->max_ctx * c->kvd;
         at.vc = c->vc + (size_t)l * c->max_ctx * c->kvd;
         at.out = c->att;
+        at.part = c->apart;
+        at.count = c->acount;
         at.nh = c->nh;
         at.nkv = c->nkv;
         at.hd = c->hd;
         at.pos = c->pos;
         at.len = c->len;
         at.max_len = c->max_ctx;
-        RB_CUDA(launch_pdl(k_attention, dim3(c->nkv), dim3(256),
-                           sizeof(float) * (size_t)(c->hd + c->max_ctx), s, at));
+        at.splits = splits;
+        RB_CUDA(launch_pdl(k_attention, dim3(c->nh, splits), dim3(kAttnThreads),
+                           attention_smem(c->hd, c->max_ctx), s, at));
         GemvF32Args o = {};
         o.nmat = 1;
         o.W[0] = c->w_o(l);
@@ -134,7 +160,8 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
         o.rows[0] = c->H;
         o.in_dim = c->qd;
         o.x = c->att;
-        RB_CUDA(launch_pdl(k_gemv_f32, dim3(2 * sms), dim3(512), sizeof(float) * (size_t)c->qd, s, o));
+        void *oa[] = {&o};
+        RB_CUDA(launch_pdl_ptr(c->gemv_q, dim3(2 * sms), dim3(kGemvF32Threads), 0, s, oa));
         const int st = rabbit_cuda_moe_decode_dev(c->moe, l, c->h, c->h, nullptr, nullptr, s);
         if (st != RABBIT_CUDA_OK) return st;
     }
@@ -163,6 +190,7 @@ static int finish(rabbit_cuda_refv2 *c, cudaStream_t s, float *logits, float *hi
                   int *argmax) {
     float *pl = c->pin, *ph = c->pin + c->V;
     int *pa = reinterpret_cast<int *>(ph + c->H);
+    RB_CUDA(cudaEventRecord(c->ev1, s));
     if (logits)
         RB_CUDA(cudaMemcpyAsync(pl, c->logits, sizeof(float) * c->V, cudaMemcpyDeviceToHost, s));
     if (hidden)
@@ -170,6 +198,7 @@ static int finish(rabbit_cuda_refv2 *c, cudaStream_t s, float *logits, float *hi
     RB_CUDA(cudaMemcpyAsync(pa, c->ids, sizeof(int), cudaMemcpyDeviceToHost, s));
     const int st = check_device_error(c->ctx, s, "refv2");
     if (st != RABBIT_CUDA_OK) return st;
+    RB_CUDA(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
     if (logits) memcpy(logits, pl, sizeof(float) * c->V);
     if (hidden) memcpy(hidden, ph, sizeof(float) * c->H);
     if (argmax) *argmax = *pa;
@@ -198,7 +227,7 @@ int rabbit_cuda_refv2_create(const rabbit_cuda_dense_desc *d, rabbit_cuda_moe *m
     if (mL != d->n_layers || mH != d->hidden)
         return fail(RABBIT_CUDA_ERR_ARGS, "refv2_create: the MoE pool has %d layers of hidden %d",
                     mL, mH);
-    if ((size_t)d->hidden * 4 > 64 * 1024 || (size_t)d->n_heads * d->head_dim * 4 > 64 * 1024)
+    if (!gemv_f32_kernel(d->hidden) || !gemv_f32_kernel(d->n_heads * d->head_dim))
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "refv2_create: hidden / q width above 16384");
     int st;
     DevCtx *ctx = dev_ctx(device, &st);
@@ -241,9 +270,15 @@ int rabbit_cuda_refv2_create(const rabbit_cuda_dense_desc *d, rabbit_cuda_moe *m
          (e = cudaMalloc(&c->ids, sizeof(int) * (kMaxNew + 1))) != cudaSuccess ||
          (e = cudaMalloc(&c->done, sizeof(unsigned))) != cudaSuccess ||
          (e = cudaMemset(c->done, 0, sizeof(unsigned))) != cudaSuccess ||
+         (e = cudaMalloc(&c->apart, sizeof(float) * (size_t)c->nh * kAttnMaxSplits *
+                                        (c->hd + 2))) != cudaSuccess ||
+         (e = cudaMalloc(&c->acount, sizeof(unsigned) * c->nh)) != cudaSuccess ||
+         (e = cudaMemset(c->acount, 0, sizeof(unsigned) * c->nh)) != cudaSuccess ||
          (e = cudaMemset(c->ids, 0, sizeof(int) * (kMaxNew + 1))) != cudaSuccess ||
          (e = cudaMallocHost(&c->pin, sizeof(float) * ((size_t)c->V + c->H + 4))) !=
-             cudaSuccess)) {
+             cudaSuccess ||
+         (e = cudaEventCreate(&c->ev0)) != cudaSuccess ||
+         (e = cudaEventCreate(&c->ev1)) != cudaSuccess)) {
     }
     if (e != cudaSuccess) {
         free_refv2(c);
@@ -252,14 +287,8 @@ int rabbit_cuda_refv2_create(const rabbit_cuda_dense_desc *d, rabbit_cuda_moe *m
     c->embed = c->w;
     c->lm_head = c->w + (size_t)c->V * c->H;
     c->final_norm = c->lm_head + (size_t)c->H * c->V;
-    if (!g_refv2_attr[device]) {
-        if ((e = cudaFuncSetAttribute(k_gemv_f32, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      64 * 1024)) != cudaSuccess) {
-            free_refv2(c);
-            return cuda_fail(e, "refv2_create: smem attribute");
-        }
-        g_refv2_attr[device] = true;
-    }
+    c->gemv_h = gemv_f32_kernel(c->H);
+    c->gemv_q = gemv_f32_kernel(c->qd);
     if (d->embed) {  // host weights -> the device block
         if (!d->lm_head || !d->final_norm || !d->rms_attn || !d->w_q || !d->w_k || !d->w_v ||
             !d->w_o) {
@@ -345,6 +374,7 @@ int rabbit_cuda_refv2_prefill(rabbit_cuda_refv2 *c, const int *token_ids, int n_
     std::lock_guard<std::mutex> g(c->ctx->mu);
     RB_CUDA(cudaSetDevice(c->device));
     cudaStream_t s = c->ctx->stream;
+    RB_CUDA(cudaEventRecord(c->ev0, s));
     for (int t = 0; t < n_tokens; ++t) {
         const int st = enqueue_step(c, nullptr, token_ids[t], c->ids, t == n_tokens - 1 && hidden, s);
         if (st != RABBIT_CUDA_OK) return st;
@@ -361,10 +391,12 @@ int rabbit_cuda_refv2_generate(rabbit_cuda_refv2 *c, int n_new, int *out_ids) {
     RB_CUDA(cudaSetDevice(c->device));
     cudaStream_t s = c->ctx->stream;
     // ids[0] holds the last step's argmax; step i reads ids[i], writes ids[i + 1]
+    RB_CUDA(cudaEventRecord(c->ev0, s));
     for (int i = 0; i < n_new; ++i) {
         const int st = enqueue_step(c, c->ids + i, 0, c->ids + i + 1, false, s);
         if (st != RABBIT_CUDA_OK) return st;
     }
+    RB_CUDA(cudaEventRecord(c->ev1, s));
     RB_CUDA(cudaMemcpyAsync(c->ids, c->ids + n_new, sizeof(int), cudaMemcpyDeviceToDevice, s));
     int *pin_ids = reinterpret_cast<int *>(c->pin);
     const int chunk = std::min(n_new, c->V + c->H);  // staging capacity in ints
@@ -375,7 +407,14 @@ int rabbit_cuda_refv2_generate(rabbit_cuda_refv2 *c, int n_new, int *out_ids) {
         st = check_device_error(c->ctx, s, "refv2_generate");
         if (st == RABBIT_CUDA_OK) memcpy(out_ids + i, pin_ids, sizeof(int) * m);
     }
+    if (st == RABBIT_CUDA_OK) RB_CUDA(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
     return st == RABBIT_CUDA_OK ? ok() : st;
+}
+
+int rabbit_cuda_refv2_device_ms(const rabbit_cuda_refv2 *c, float *ms) {
+    if (!c || !ms) return fail(RABBIT_CUDA_ERR_ARGS, "refv2_device_ms: NULL argument");
+    *ms = c->last_ms;
+    return ok();
 }
 
 }  // extern "C"

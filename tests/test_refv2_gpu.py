@@ -7,7 +7,8 @@ layer attention_step (forward_v2.c:171-246) then moe_step
 Bar: logits and the final-normed hidden within rtol 1e-4 / atol 1e-5 after
 every token, the argmax identical whenever the oracle's top two logits are
 apart by more than 1e-4 of the largest |logit|. Sequences run past max_ctx,
-where the KV cache stops growing (forward_v2.c:198-202). A token whose
+where the KV cache stops growing (forward_v2.c:198-202), and past 32 cached
+positions, where a head's positions are split over several CTAs. A token whose
 router scores hold a near-tie in any layer (adjacent top-k+1 scores within
 1e-5 of the largest) ends the comparison of that sequence: after it the two
 sides may route differently, legitimately.
@@ -27,6 +28,8 @@ CONFIGS = {
     "gqa": (2, 128, 1000, 4, 2, 32, 8, 2, 64, 0, 8),
     "wide_q_shared_odd_vocab": (2, 128, 997, 6, 3, 40, 4, 2, 96, 1, 6),
     "mha_one_layer": (1, 64, 512, 2, 2, 32, 4, 1, 64, 0, 4),
+    # a window past 32 positions: attention split over several CTAs per head
+    "long_window": (2, 128, 1000, 4, 2, 32, 8, 2, 64, 0, 80),
 }
 
 
@@ -74,8 +77,10 @@ class Model:
     def step(self, oracle, tid):
         """One token; returns (logits, hidden, tie) -- tie: a near-tie in the
         router scores of some layer."""
-        t = tid % self.V
-        h = self.w["embed"][t if t >= 0 else 0].copy()
+        # C semantics (forward_v2.c:459-461): id % V truncates toward zero,
+        # a negative result selects row 0
+        t = tid % self.V if tid >= 0 else 0
+        h = self.w["embed"][t].copy()
         tie = False
         for l in range(self.L):
             h, self.kv_len[l] = oracle.attention_step(
