@@ -60,9 +60,11 @@ __device__ __forceinline__ const float4 *gemv_row_ptr(const GemvF32Args &a, int 
 }
 
 template <int XK>
-__global__ void __launch_bounds__(kGemvF32Threads, XK >= 8 ? 1 : 2) k_gemv_f32(GemvF32Args a) {
-    // rows per group: 8 float4 loads per thread in flight whatever XK
-    constexpr int RG = kGemvF32Rows / XK, NW = kGemvF32Threads / 32;
+__global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(GemvF32Args a) {
+    // rows per group: 8 float4 loads per thread in flight (16 for XK = 8),
+    // at least 2 so that a RoPE pair never straddles two groups
+    constexpr int RG = kGemvF32Rows / XK < 2 ? 2 : kGemvF32Rows / XK;
+    constexpr int NW = kGemvF32Threads / 32;
     __shared__ float part[2][NW][kGemvF32Rows];  // per-warp row sums, double-buffered
     __shared__ float red[32];
     launch_dependents();
@@ -70,8 +72,12 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 8 ? 1 : 2) k_gemv_f32(G
     const int in = a.in_dim, in4 = in >> 2;
     int total = 0;
     for (int m = 0; m < a.nmat; ++m) total += a.rows[m];
-    const int r0 = (int)((long long)blockIdx.x * total / gridDim.x);
-    const int r1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    int r0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    int r1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    if (a.rope_nmat > 0) {  // RoPE pairs stay within a CTA (total is even)
+        r0 &= ~1;
+        r1 &= ~1;
+    }
     float4 w[RG][XK];
     auto load_group = [&](int rb) {
 #pragma unroll
@@ -136,13 +142,32 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 8 ? 1 : 2) k_gemv_f32(G
         const float tot = warp_reduce8(v);  // lane 4u holds row u's warp sum
         if ((lane & 3) == 0) part[buf][warp][lane >> 2] = tot;
         __syncthreads();
-        if (tid < RG && rb + tid < r1) {
+        if (warp == 0) {  // lane u < RG finishes row rb + u
             float sum = 0.f;
+            if (lane < RG) {
 #pragma unroll
-            for (int wi = 0; wi < NW; ++wi) sum += part[buf][wi][tid];
-            int m = 0, row = rb + tid;
-            while (row >= a.rows[m]) row -= a.rows[m++];
-            a.y[m][row] = (a.res[m] ? a.res[m][row] : 0.f) + sum;
+                for (int wi = 0; wi < NW; ++wi) sum += part[buf][wi][lane];
+            }
+            const int r = rb + lane;
+            int m = 0, row = r;
+            if (lane < RG && r < r1)
+                while (row >= a.rows[m]) row -= a.rows[m++];
+            float val = (lane < RG && r < r1 && a.res[m]) ? a.res[m][row] + sum : sum;
+            // RoPE (forward_v2.c:92-104): rows 2i, 2i + 1 of a head are lanes
+            // 2i', 2i' + 1 here (even group starts, even matrix sizes)
+            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+            if (lane < RG && r < r1) {
+                if (m < a.rope_nmat) {
+                    const int half = a.rope_hd / 2, i = (row % a.rope_hd) / 2;
+                    const float freq = 1.0f / powf(10000.0f, (float)i / (float)half);
+                    const float angle = (float)a.rope_pos * freq;
+                    const float c = cosf(angle), sn = sinf(angle);
+                    const float x0 = (row & 1) ? other : val, x1 = (row & 1) ? val : other;
+                    val = (row & 1) ? x0 * sn + x1 * c : x0 * c - x1 * sn;
+                }
+                a.y[m][row] = val;
+                if (a.cache[m]) a.cache[m][row] = val;
+            }
         }
     }
 }
@@ -159,19 +184,46 @@ const void *gemv_f32_kernel(int in) {
 }
 
 // ------------------------------------------------------------ attention --
-__device__ __forceinline__ void rope_pairs(float *x, int hd, int pos) {
-    // forward_v2.c:92-104
-    const int half = hd / 2;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float freq = 1.0f / powf(10000.0f, (float)i / (float)half);
-        const float angle = (float)pos * freq;
-        const float c = cosf(angle), s = sinf(angle);
-        const float x0 = x[2 * i], x1 = x[2 * i + 1];
-        x[2 * i] = x0 * c - x1 * s;
-        x[2 * i + 1] = x0 * s + x1 * c;
-    }
+// Positions [p0, p1) of split `split` out of `splits` over len.
+__device__ __forceinline__ void split_range(int len, int split, int splits, int &p0, int &p1) {
+    p0 = (int)((long long)split * len / splits);
+    p1 = (int)((long long)(split + 1) * len / splits);
 }
 
+// The last CTA of a head merges the splits' (max m_s, sum l_s, values o_s):
+// out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s, M = max m_s. Every
+// thread of the CTA calls it after storing its split's values; false for the
+// CTAs that are not last.
+__device__ bool merge_splits(const AttnArgs &a, int head, bool *last) {
+    const int tid = threadIdx.x, nthr = blockDim.x, hd = a.hd;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *last = atomicAdd(a.count + head, 1u) == (unsigned)a.splits - 1;
+    __syncthreads();
+    if (!*last) return false;
+    __threadfence();
+    const float *ph = a.part + (size_t)head * kAttnMaxSplits * (hd + 2);
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < a.splits; ++s2) M = fmaxf(M, __ldcg(ph + (size_t)s2 * (hd + 2) + hd));
+    float L = 0.f;
+    for (int s2 = 0; s2 < a.splits; ++s2) {
+        const float *q2 = ph + (size_t)s2 * (hd + 2);
+        L += __ldcg(q2 + hd + 1) * expf(__ldcg(q2 + hd) - M);
+    }
+    for (int i = tid; i < hd; i += nthr) {
+        float o = 0.f;
+        for (int s2 = 0; s2 < a.splits; ++s2) {
+            const float *q2 = ph + (size_t)s2 * (hd + 2);
+            o = fmaf(__ldcg(q2 + i), expf(__ldcg(q2 + hd) - M), o);
+        }
+        a.out[(size_t)head * hd + i] = L > 0.f ? o / L : o;
+    }
+    if (tid == 0) a.count[head] = 0u;  // ready for the next launch
+    return true;
+}
+
+// Any even head_dim: scores by a warp per position, values by (group,
+// column) threads, two block reductions.
 __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
@@ -181,44 +233,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
     const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int nwarp = nthr >> 5;
     const int head = blockIdx.x, split = blockIdx.y, hd = a.hd, kvd = a.nkv * hd;
-    const int rep = a.nh / a.nkv;  // nh is a multiple of nkv (checked at creation)
-    const int j = head / rep;
+    const int j = head / (a.nh / a.nkv);  // nh is a multiple of nkv (checked at creation)
     const int groups = hd < nthr ? nthr / hd : 1;
-    float *qs = sm;                // [hd]
-    float *ks = qs + hd;           // [hd] this token's k (RoPE applied)
-    float *sc = ks + hd;           // [max_len]
-    float *pv = sc + a.max_len;    // [groups][hd]
-    for (int i = tid; i < hd; i += nthr) {
-        qs[i] = a.q[(size_t)head * hd + i];
-        ks[i] = a.k[(size_t)j * hd + i];
-    }
-    __syncthreads();
-    rope_pairs(qs, hd, a.pos);
-    rope_pairs(ks, hd, a.pos);
-    __syncthreads();
-    const bool append = a.len < a.max_len;
-    const int len = append ? a.len + 1 : a.len;
-    const float *vnew = a.v + (size_t)j * hd;
-    if (append && head % rep == 0 && split == 0)
-        for (int i = tid; i < hd; i += nthr) {
-            a.kc[(size_t)a.len * kvd + (size_t)j * hd + i] = ks[i];
-            a.vc[(size_t)a.len * kvd + (size_t)j * hd + i] = vnew[i];
-        }
-    // this CTA's positions [p0, p1); the appended one reads this CTA's own
-    // k / v (another CTA writes the cache row)
-    const int p0 = (int)((long long)split * len / a.splits);
-    const int p1 = (int)((long long)(split + 1) * len / a.splits);
+    int p0, p1;
+    split_range(a.len, split, a.splits, p0, p1);
     const int n = p1 - p0;
+    float *qs = sm;            // [hd]
+    float *sc = qs + hd;       // [n]
+    float *pv = sc + n;        // [groups][hd]
+    for (int i = tid; i < hd; i += nthr) qs[i] = a.q[(size_t)head * hd + i];
+    __syncthreads();
+    const float *kb = a.kc + (size_t)j * hd, *vb = a.vc + (size_t)j * hd;
     const float scale = 1.0f / sqrtf((float)hd);
-    // scores: a warp per position, lanes across the head, four at a time
     for (int t0 = warp * 4; t0 < n; t0 += nwarp * 4) {
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         const float *kt[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int t = p0 + min(t0 + u, n - 1);
-            kt[u] = append && t == a.len ? ks : a.kc + (size_t)t * kvd + (size_t)j * hd;
-        }
+        for (int u = 0; u < 4; ++u) kt[u] = kb + (size_t)(p0 + min(t0 + u, n - 1)) * kvd;
         for (int i = lane; i < hd; i += 32) {
             const float qi = qs[i];
 #pragma unroll
@@ -241,20 +272,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
         sum += e;
     }
     sum = block_sum(sum, red);  // ends with a barrier: sc is complete
-    // values: thread (g, i) sums positions g, g + groups, ... of column i
     for (int c = tid; c < groups * hd; c += nthr) {
         const int g = c / hd, i = c - g * hd;
         float acc = 0.f;
 #pragma unroll 4
-        for (int t = g; t < n; t += groups) {
-            const int tp = p0 + t;
-            const float vt = append && tp == a.len ? vnew[i]
-                                                  : a.vc[(size_t)tp * kvd + (size_t)j * hd + i];
-            acc = fmaf(sc[t], vt, acc);
-        }
+        for (int t = g; t < n; t += groups) acc = fmaf(sc[t], vb[(size_t)(p0 + t) * kvd + i], acc);
         pv[c] = acc;
     }
     __syncthreads();
+    if (a.splits == 1) {
+        for (int i = tid; i < hd; i += nthr) {
+            float o = 0.f;
+            for (int g = 0; g < groups; ++g) o += pv[g * hd + i];
+            a.out[(size_t)head * hd + i] = sum > 0.f ? o / sum : o;
+        }
+        return;
+    }
     float *mine = a.part + ((size_t)head * kAttnMaxSplits + split) * (hd + 2);
     for (int i = tid; i < hd; i += nthr) {
         float o = 0.f;
@@ -265,31 +298,135 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
         mine[hd] = mx;
         mine[hd + 1] = sum;
     }
-    // the last CTA of this head merges the splits:
-    // out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) last = atomicAdd(a.count + head, 1u) == (unsigned)a.splits - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    const float *ph = a.part + (size_t)head * kAttnMaxSplits * (hd + 2);
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < a.splits; ++s2) M = fmaxf(M, __ldcg(ph + (size_t)s2 * (hd + 2) + hd));
-    float L = 0.f;
-    for (int s2 = 0; s2 < a.splits; ++s2) {
-        const float *q2 = ph + (size_t)s2 * (hd + 2);
-        L += __ldcg(q2 + hd + 1) * expf(__ldcg(q2 + hd) - M);
-    }
-    for (int i = tid; i < hd; i += nthr) {
-        float o = 0.f;
-        for (int s2 = 0; s2 < a.splits; ++s2) {
-            const float *q2 = ph + (size_t)s2 * (hd + 2);
-            o = fmaf(__ldcg(q2 + i), expf(__ldcg(q2 + hd) - M), o);
+    merge_splits(a, head, &last);
+}
+
+// VPL consecutive floats (aligned to min(VPL, 4) floats) as vector loads.
+template <int VPL>
+__device__ __forceinline__ void load_vec(float (&d)[VPL], const float *p) {
+    if constexpr (VPL % 4 == 0) {
+#pragma unroll
+        for (int v = 0; v < VPL; v += 4) {
+            const float4 t = *reinterpret_cast<const float4 *>(p + v);
+            d[v] = t.x;
+            d[v + 1] = t.y;
+            d[v + 2] = t.z;
+            d[v + 3] = t.w;
         }
-        a.out[(size_t)head * hd + i] = L > 0.f ? o / L : o;
+    } else if constexpr (VPL == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(p);
+        d[0] = t.x;
+        d[1] = t.y;
+    } else {
+        d[0] = p[0];
     }
-    if (tid == 0) a.count[head] = 0u;  // ready for the next launch
+}
+
+// head_dim = 32 VPL: lane l holds elements [l VPL, (l + 1) VPL) of q and of
+// every k / v row. Each of the four warps takes batches of PB positions
+// (batch b: positions p0 + b PB ..., warp b % 4), loads their k and v rows
+// at once (2 PB VPL floats per lane in flight), and folds them into its
+// running (max, sum, values); the warps are then merged in shared memory.
+template <int VPL>
+__global__ void __launch_bounds__(kAttnRegThreads) k_attention_reg(AttnArgs a) {
+    constexpr int HD = 32 * VPL, PB = 32 / VPL < 8 ? 32 / VPL : 8, NWA = kAttnRegThreads / 32;
+    __shared__ float wm[NWA], wl[NWA];
+    __shared__ __align__(16) float wo[NWA][HD];
+    __shared__ bool last;
+    launch_dependents();
+    wait_prerequisite();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int head = blockIdx.x, split = blockIdx.y, kvd = a.nkv * HD;
+    const int j = head / (a.nh / a.nkv);
+    int p0, p1;
+    split_range(a.len, split, a.splits, p0, p1);
+    float q[VPL];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) q[v] = a.q[(size_t)head * HD + lane * VPL + v];
+    const float *kb = a.kc + (size_t)j * HD + lane * VPL, *vb = a.vc + (size_t)j * HD + lane * VPL;
+    const float scale = 1.0f / sqrtf((float)HD);
+    float m = -INFINITY, l = 0.f, o[VPL];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) o[v] = 0.f;
+    for (int t0 = p0 + warp * PB; t0 < p1; t0 += NWA * PB) {
+        float kr[PB][VPL], vr[PB][VPL];
+#pragma unroll
+        for (int u = 0; u < PB; ++u) {
+            const int t = min(t0 + u, p1 - 1);
+            load_vec<VPL>(kr[u], kb + (size_t)t * kvd);
+            load_vec<VPL>(vr[u], vb + (size_t)t * kvd);
+        }
+        float s[PB], bm = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < PB; ++u) {
+            float d = 0.f;
+#pragma unroll
+            for (int v = 0; v < VPL; ++v) d = fmaf(q[v], kr[u][v], d);
+            d = warp_sum(d);
+            s[u] = t0 + u < p1 ? d * scale : -INFINITY;
+            bm = fmaxf(bm, s[u]);
+        }
+        const float mn = fmaxf(m, bm);
+        const float corr = expf(m - mn);  // 0 while m is -inf
+        l *= corr;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) o[v] *= corr;
+#pragma unroll
+        for (int u = 0; u < PB; ++u) {
+            const float pu = expf(s[u] - mn);  // 0 past p1
+            l += pu;
+#pragma unroll
+            for (int v = 0; v < VPL; ++v) o[v] = fmaf(pu, vr[u][v], o[v]);
+        }
+        m = mn;
+    }
+    if (lane == 0) {
+        wm[warp] = m;
+        wl[warp] = l;
+    }
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) wo[warp][lane * VPL + v] = o[v];
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w2 = 0; w2 < NWA; ++w2) M = fmaxf(M, wm[w2]);
+    float L = 0.f, f[NWA];
+#pragma unroll
+    for (int w2 = 0; w2 < NWA; ++w2) {
+        f[w2] = wl[w2] > 0.f ? expf(wm[w2] - M) : 0.f;  // warps without positions add 0
+        L += wl[w2] * f[w2];
+    }
+    if (a.splits == 1) {
+        for (int i = tid; i < HD; i += kAttnRegThreads) {
+            float acc = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < NWA; ++w2) acc = fmaf(wo[w2][i], f[w2], acc);
+            a.out[(size_t)head * HD + i] = L > 0.f ? acc / L : acc;
+        }
+        return;
+    }
+    float *mine = a.part + ((size_t)head * kAttnMaxSplits + split) * (HD + 2);
+    for (int i = tid; i < HD; i += kAttnRegThreads) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w2 = 0; w2 < NWA; ++w2) acc = fmaf(wo[w2][i], f[w2], acc);
+        mine[i] = acc;
+    }
+    if (tid == 0) {
+        mine[HD] = M;
+        mine[HD + 1] = L;
+    }
+    merge_splits(a, head, &last);
+}
+
+const void *attention_reg_kernel(int hd) {
+    switch (hd) {
+        case 32: return (const void *)k_attention_reg<1>;
+        case 64: return (const void *)k_attention_reg<2>;
+        case 128: return (const void *)k_attention_reg<4>;
+        case 256: return (const void *)k_attention_reg<8>;
+        default: return nullptr;
+    }
 }
 
 // -------------------------------------------------------------- lm_head --

@@ -14,9 +14,14 @@ constexpr int kMaxGemvMats = 4;
 // embed != nullptr: x is row id % V of embed [V, in] (id from *idp, or `id`
 // when idp is nullptr; negative -> row 0, forward_v2.c:459-461), and the raw
 // row is also written to h (the token's residual stream).
+// rope_nmat > 0: matrices m < rope_nmat are heads of rope_hd rows whose
+// (2i, 2i + 1) row pairs are rotated for position rope_pos
+// (forward_v2.c:92-104) before they are stored. cache[m] != nullptr: y_m is
+// also stored there (the KV-cache row of this position).
 //
-// CTA b owns the stacked rows [b R / G, (b + 1) R / G) (R rows, G CTAs) and
-// walks them in groups of 8 / XK; thread t owns the float4 columns t,
+// CTA b owns the stacked rows [b R / G, (b + 1) R / G) rounded down to even
+// (R rows, G CTAs; R and every matrix even when rope_nmat > 0) and walks
+// them in groups of max(2, 8 / XK); thread t owns the float4 columns t,
 // t + 512, ... (XK of them) of x, held in registers, so each row is one
 // fully coalesced sweep of the CTA. The loads of the first group go out
 // before the wait for the kernel before (weights are not written by it).
@@ -34,6 +39,8 @@ struct GemvF32Args {
     const int *idp;
     int id, V;
     float *h;
+    int rope_nmat, rope_hd, rope_pos;
+    float *cache[kMaxGemvMats];
 };
 
 // The kernel for rows of `in` floats: XK = ceil(in / 4 / 512) float4 columns
@@ -42,36 +49,38 @@ const void *gemv_f32_kernel(int in);
 
 
 // Grid (nh, splits): CTA (h, s) takes query head h and the s-th of `splits`
-// equal ranges of the cached positions. Every CTA applies RoPE to its q and
-// to its KV head's k; the first CTA of each group (h % rep == 0, s == 0)
-// appends the k / v row at position `len` when len < max_len. Each CTA
-// leaves its range's max score, sum of exponentials and unnormalised
-// weighted values in `part`; the last CTA of a head to finish merges them
-// into out (forward_v2.c:171-246: scores scaled by 1/sqrt(hd), softmax,
-// weighted sum of values).
+// equal ranges of the len cached positions -- q already rotated, the cache
+// already holding this token's k / v row (the Q/K/V projection stores them).
+// Each CTA keeps a running max, sum of exponentials and weighted values over
+// its positions (an online softmax); with several splits it leaves them in
+// `part` and the last CTA of the head to finish merges them into out
+// (forward_v2.c:171-246: scores scaled by 1/sqrt(hd), softmax, weighted sum
+// of values). head_dim 32, 64, 128 or 256: k_attention_reg, rows held in
+// registers; any other even head_dim: k_attention.
 constexpr int kAttnMaxSplits = 8;
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 256;     // k_attention
+constexpr int kAttnRegThreads = 128;  // k_attention_reg: four warps
 struct AttnArgs {
-    const float *q;       // [nh * hd] (before RoPE)
-    const float *k;       // [nkv * hd] (before RoPE)
-    const float *v;       // [nkv * hd]
-    float *kc, *vc;       // cache [max_len, nkv * hd]
+    const float *q;       // [nh * hd], RoPE applied
+    const float *kc, *vc; // cache [max_len, nkv * hd], this token's row included
     float *out;           // [nh * hd]
     float *part;          // [nh][kAttnMaxSplits][hd + 2]
     unsigned *count;      // [nh] arrivals, zero between launches
-    int nh, nkv, hd, pos, len, max_len, splits;
+    int nh, nkv, hd, len, splits;
 };
 
-// Splits for a window of n positions (after the append): ranges of >= 32.
+// Splits for n cached positions: ranges of >= 32.
 inline int attention_splits(int n) {
     const int s = (n + 31) / 32;
     return s < 1 ? 1 : (s > kAttnMaxSplits ? kAttnMaxSplits : s);
 }
-// Dynamic shared memory of k_attention.
+// Dynamic shared memory of k_attention (none for k_attention_reg).
 inline size_t attention_smem(int hd, int max_len) {
     const int groups = hd < kAttnThreads ? kAttnThreads / hd : 1;
-    return sizeof(float) * (size_t)(2 * hd + max_len + groups * hd);
+    return sizeof(float) * (size_t)(hd + max_len + groups * hd);
 }
+// k_attention_reg for head_dim hd, nullptr when hd is not 32, 64, 128, 256.
+const void *attention_reg_kernel(int hd);
 
 __global__ void k_attention(AttnArgs a);
 

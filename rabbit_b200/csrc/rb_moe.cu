@@ -143,7 +143,7 @@ static cudaError_t launch_fused(const rabbit_cuda_moe *p, MoeFusedArgs &a, cudaS
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     void *args[] = {&a};
-    return cudaLaunchKernelExC(&cfg, moe_fused_kernel(a.JB, a.JC), args);
+    return cudaLaunchKernelExC(&cfg, moe_fused_kernel(a.JB, a.JC, combine_packed(a.tc.KC)), args);
 }
 
 // Shared-memory bytes in front of the ring, in the order k_moe_decode_g32
@@ -453,8 +453,11 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         }
     }
     if (p->fast && !g_moe_attr[device]) {
-        for (const void *k : {moe_fused_kernel(1, 1), moe_fused_kernel(1, 2), moe_fused_kernel(2, 1),
-                              moe_fused_kernel(2, 2)})
+        for (const void *k :
+             {moe_fused_kernel(1, 1, false), moe_fused_kernel(1, 2, false),
+              moe_fused_kernel(2, 1, false), moe_fused_kernel(2, 2, false),
+              moe_fused_kernel(1, 1, true), moe_fused_kernel(1, 2, true),
+              moe_fused_kernel(2, 1, true), moe_fused_kernel(2, 2, true)})
             if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           kMaxDynSmem)) != cudaSuccess) {
                 free_pool(p);
@@ -465,7 +468,8 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     if (p->fast) {
         int per_sm = 0;
         if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                 &per_sm, moe_fused_kernel(p->plan.JB, p->plan.JC), p->block, p->smem)) !=
+                 &per_sm, moe_fused_kernel(p->plan.JB, p->plan.JC, combine_packed(p->plan.tc.KC)),
+                 p->block, p->smem)) !=
                 cudaSuccess ||
             per_sm < 1) {
             free_pool(p);

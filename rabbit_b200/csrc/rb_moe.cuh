@@ -55,9 +55,12 @@ struct MoeFusedArgs {
     int part_floats;  // floats per partial region
 };
 
-// k_moe_decode_g32<JB, JC> for JB / JC groups of 32 per lane in phases B / C
-// (1 or 2 each); one CTA per SM, all resident, one MoeFusedArgs argument.
-const void *moe_fused_kernel(int JB, int JC);
+// k_moe_decode_g32<JB, JC, PACKED> for JB / JC groups of 32 per lane in
+// phases B / C (1 or 2 each) and the combine's batching (PACKED: fewer than 8
+// column chunks of W2); one CTA per SM, all resident, one MoeFusedArgs
+// argument.
+const void *moe_fused_kernel(int JB, int JC, bool packed);
+inline bool combine_packed(int KC) { return KC < 8; }
 
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine
 struct MoeGenericArgs {

@@ -324,7 +324,7 @@ __device__ __forceinline__ bool moe_down(const MoeFusedArgs &a, const uint8_t *r
     return true;
 }
 
-template <int JB, int JC>
+template <int JB, int JC, bool PACKED>
 __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_g32(MoeFusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nthr = blockDim.x;
@@ -752,61 +752,84 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
                 flags_seen = true;
             }
             const uint64_t t0 = globaltimer_ns();
-            // The lane's values, rows r = lane + 32 m of the tile, in the order
-            // (m, slot j, chunk c), read 16 at a time with all 16 in flight
-            // and folded in that order: down_j = sum over c, delta += w_j
-            // down_j, h_out = h + delta after the row's last slot.
-            const int r_end = min(TRc, H - t * TRc);
-            const int nr = r_end > lane ? (r_end - lane + 31) >> 5 : 0;
-            const int total = nr * nact * KC;
-            int fm = 0, fj = 0, fc = 0;  // (m, j, c) of the next value to fold
-            float dj = 0.f, delta = 0.f;
-            for (int q0 = 0; q0 < total; q0 += 16) {
-                unsigned long long w[16];
-                for (unsigned it = 0;; ++it) {
-                    int m = fm, j = fj, c = fc;
+            // Each of the lane's rows r = lane + 32 m: down_j = the sum of its
+            // chunks in chunk order, delta += w_j down_j in slot order, h_out =
+            // h + delta. PACKED (fewer than 8 chunks per slot): the row's
+            // (slot, chunk) values 16 at a time; else one slot's chunks at a
+            // time. Every load of a batch is in flight at once. (The two are
+            // separate kernels: either form slows the other's shapes.)
+            for (int r = lane; r < TRc; r += 32) {
+                const int row = t * TRc + r;
+                if (row >= H) break;
+                float delta = 0.f;
+                if constexpr (PACKED) {
+                    const int per_row = nact * KC;
+                    float dj = 0.f;
+                    int fj = 0, fc = 0;
+                    for (int q0 = 0; q0 < per_row; q0 += 16) {
+                        unsigned long long w[16];
+                        for (unsigned it = 0;; ++it) {
+                            int j = fj, c = fc;
 #pragma unroll
-                    for (int qq = 0; qq < 16; ++qq) {
-                        w[qq] = (unsigned long long)a.seq << 32;
-                        if (q0 + qq < total) {
-                            const int row = t * TRc + lane + 32 * m;
-                            w[qq] = ld_tagged(a.down + ((size_t)j * KC + c) * H + row);
-                            if (++c == KC) {
-                                c = 0;
-                                if (++j == nact) {
-                                    j = 0;
-                                    ++m;
+                            for (int qq = 0; qq < 16; ++qq) {
+                                w[qq] = (unsigned long long)a.seq << 32;
+                                if (q0 + qq < per_row) {
+                                    w[qq] = ld_tagged(a.down + ((size_t)j * KC + c) * H + row);
+                                    if (++c == KC) {
+                                        c = 0;
+                                        ++j;
+                                    }
                                 }
+                            }
+                            bool all = true;
+#pragma unroll
+                            for (int qq = 0; qq < 16; ++qq) all = all && tag_ok(w[qq], a.seq);
+                            if (all) break;
+                            if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                                set_error(a.err, RB_ERR_TIMEOUT);
+                                return;
+                            }
+                            __nanosleep(128);
+                        }
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) {
+                            if (q0 + qq >= per_row) break;
+                            dj += tag_val(w[qq]);
+                            if (++fc == KC) {
+                                fc = 0;
+                                delta += s_w[fj] * dj;
+                                dj = 0.f;
+                                ++fj;
                             }
                         }
                     }
-                    bool all = true;
+                } else {
+                    for (int j = 0; j < nact; ++j) {
+                        const unsigned long long *dp = a.down + (size_t)j * KC * H + row;
+                        unsigned long long w[16];  // KC <= 16: all loads in flight at once
+                        for (unsigned it = 0;; ++it) {
+                            bool all = true;
 #pragma unroll
-                    for (int qq = 0; qq < 16; ++qq) all = all && tag_ok(w[qq], a.seq);
-                    if (all) break;
-                    if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
-                        set_error(a.err, RB_ERR_TIMEOUT);
-                        return;
-                    }
-                    __nanosleep(128);
-                }
-#pragma unroll
-                for (int qq = 0; qq < 16; ++qq) {
-                    if (q0 + qq >= total) break;
-                    dj += tag_val(w[qq]);
-                    if (++fc == KC) {
-                        fc = 0;
-                        delta += s_w[fj] * dj;
-                        dj = 0.f;
-                        if (++fj == nact) {
-                            fj = 0;
-                            const int row = t * TRc + lane + 32 * fm;
-                            a.h_out[row] = a.h_in[row] + delta;
-                            delta = 0.f;
-                            ++fm;
+                            for (int cc = 0; cc < 16; ++cc) {
+                                w[cc] = cc < KC ? ld_tagged(dp + (size_t)cc * H)
+                                                : (unsigned long long)a.seq << 32;
+                                all = all && tag_ok(w[cc], a.seq);
+                            }
+                            if (all) break;
+                            if ((it & 7u) == 7u && globaltimer_ns() - t0 > a.wait_ns) {
+                                set_error(a.err, RB_ERR_TIMEOUT);
+                                return;
+                            }
+                            __nanosleep(128);
                         }
+                        float dj = 0.f;
+#pragma unroll
+                        for (int cc = 0; cc < 16; ++cc)
+                            if (cc < KC) dj += tag_val(w[cc]);
+                        delta += s_w[j] * dj;
                     }
                 }
+                a.h_out[row] = a.h_in[row] + delta;
             }
         }
 #ifdef RB_PHASE_TIMERS
@@ -864,10 +887,19 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
     RB_STAMP(4);
 }
 
-const void *moe_fused_kernel(int JB, int JC) {
+const void *moe_fused_kernel(int JB, int JC, bool packed) {
+    if (packed) {
+        if (JB == 2)
+            return JC == 2 ? (const void *)k_moe_decode_g32<2, 2, true>
+                           : (const void *)k_moe_decode_g32<2, 1, true>;
+        return JC == 2 ? (const void *)k_moe_decode_g32<1, 2, true>
+                       : (const void *)k_moe_decode_g32<1, 1, true>;
+    }
     if (JB == 2)
-        return JC == 2 ? (const void *)k_moe_decode_g32<2, 2> : (const void *)k_moe_decode_g32<2, 1>;
-    return JC == 2 ? (const void *)k_moe_decode_g32<1, 2> : (const void *)k_moe_decode_g32<1, 1>;
+        return JC == 2 ? (const void *)k_moe_decode_g32<2, 2, false>
+                       : (const void *)k_moe_decode_g32<2, 1, false>;
+    return JC == 2 ? (const void *)k_moe_decode_g32<1, 2, false>
+                   : (const void *)k_moe_decode_g32<1, 1, false>;
 }
 
 #ifdef RB_PHASE_TIMERS

@@ -43,6 +43,7 @@ struct rabbit_cuda_refv2 {
     float *pin = nullptr;  // host staging: logits | hidden | argmax
     int nchunk = 0, lm_blocks = 0, am_blocks = 0;
     const void *gemv_h = nullptr, *gemv_q = nullptr;  // projection kernels, rows of H / q_dim
+    const void *attn_reg = nullptr;  // register attention for this head_dim (or nullptr)
     int pos = 0, len = 0;
     bool stepped = false;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;  // around the kernels of the last call
@@ -132,26 +133,37 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
             g.V = c->V;
             g.h = c->h;
         }
+        // q and k rotated for this position; k / v rows appended to the cache
+        // while it has room (forward_v2.c:190-202)
+        g.rope_nmat = 2;
+        g.rope_hd = c->hd;
+        g.rope_pos = c->pos;
+        float *kc_l = c->kc + (size_t)l * c->max_ctx * c->kvd;
+        float *vc_l = c->vc + (size_t)l * c->max_ctx * c->kvd;
+        if (c->len < c->max_ctx) {
+            g.cache[1] = kc_l + (size_t)c->len * c->kvd;
+            g.cache[2] = vc_l + (size_t)c->len * c->kvd;
+        }
         void *ga[] = {&g};
         RB_CUDA(launch_pdl_ptr(c->gemv_h, dim3(2 * sms), dim3(kGemvF32Threads), 0, s, ga));
         AttnArgs at;
         at.q = c->q;
-        at.k = c->k;
-        at.v = c->v;
-        at.kc = c->kc + (size_t)l * c->max_ctx * c->kvd;
-        at.vc = c->vc + (size_t)l * c->max_ctx * c->kvd;
+        at.kc = kc_l;
+        at.vc = vc_l;
         at.out = c->att;
         at.part = c->apart;
         at.count = c->acount;
         at.nh = c->nh;
         at.nkv = c->nkv;
         at.hd = c->hd;
-        at.pos = c->pos;
-        at.len = c->len;
-        at.max_len = c->max_ctx;
+        at.len = kv_after;
         at.splits = splits;
-        RB_CUDA(launch_pdl(k_attention, dim3(c->nh, splits), dim3(kAttnThreads),
-                           attention_smem(c->hd, c->max_ctx), s, at));
+        void *aa[] = {&at};
+        if (c->attn_reg)
+            RB_CUDA(launch_pdl_ptr(c->attn_reg, dim3(c->nh, splits), dim3(kAttnRegThreads), 0, s, aa));
+        else
+            RB_CUDA(launch_pdl(k_attention, dim3(c->nh, splits), dim3(kAttnThreads),
+                               attention_smem(c->hd, c->max_ctx), s, at));
         GemvF32Args o = {};
         o.nmat = 1;
         o.W[0] = c->w_o(l);
@@ -289,6 +301,7 @@ int rabbit_cuda_refv2_create(const rabbit_cuda_dense_desc *d, rabbit_cuda_moe *m
     c->final_norm = c->lm_head + (size_t)c->H * c->V;
     c->gemv_h = gemv_f32_kernel(c->H);
     c->gemv_q = gemv_f32_kernel(c->qd);
+    c->attn_reg = attention_reg_kernel(c->hd);
     if (d->embed) {  // host weights -> the device block
         if (!d->lm_head || !d->final_norm || !d->rms_attn || !d->w_q || !d->w_k || !d->w_v ||
             !d->w_o) {
