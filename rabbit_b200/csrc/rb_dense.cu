@@ -64,9 +64,11 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(G
     // rows per group: 8 float4 loads per thread in flight (16 for XK = 8),
     // at least 2 so that a RoPE pair never straddles two groups
     constexpr int RG = kGemvF32Rows / XK < 2 ? 2 : kGemvF32Rows / XK;
-    constexpr int NW = kGemvF32Threads / 32;
-    __shared__ float part[2][NW][kGemvF32Rows];  // per-warp row sums, double-buffered
-    __shared__ float red[32];
+    constexpr int NW = kGemvF32Threads / 32, NB = 4;
+    __shared__ float part[NB][NW][kGemvF32Rows];  // per-warp row sums, a ring of NB groups
+    __shared__ __align__(8) uint64_t full[NB], empty[NB];
+    __shared__ float red[NW];
+    __shared__ float2 rope_cs[512];  // (cos, sin) per pair index, head_dim <= 1024
     launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int in = a.in_dim, in4 = in >> 2;
@@ -91,6 +93,18 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(G
         }
     };
     if (r0 < r1) load_group(r0);
+    if (tid == 0) {
+        for (int b = 0; b < NB; ++b) {
+            mbar_init(&full[b], NW);  // every warp posts every group
+            mbar_init(&empty[b], 1);  // warp 0, once the group is stored
+        }
+    }
+    if (a.rope_nmat > 0)  // this position's rotation (forward_v2.c:92-104)
+        for (int i = tid; i < a.rope_hd / 2; i += kGemvF32Threads) {
+            const float freq = 1.0f / powf(10000.0f, (float)i / (float)(a.rope_hd / 2));
+            const float angle = (float)a.rope_pos * freq;
+            rope_cs[i] = make_float2(cosf(angle), sinf(angle));
+        }
     wait_prerequisite();
     if (r0 >= r1 && !(a.embed && blockIdx.x == 0)) return;
     const float *x = a.x;
@@ -110,9 +124,15 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(G
         ss += (xv[k].x * xv[k].x + xv[k].y * xv[k].y) + (xv[k].z * xv[k].z + xv[k].w * xv[k].w);
         if (a.embed && blockIdx.x == 0 && c < in4) reinterpret_cast<float4 *>(a.h)[c] = xv[k];
     }
+    // one barrier: the sum of squares, and the barriers / table above
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
     if (a.norm_w) {
-        ss = block_sum(ss, red);
-        const float inv = 1.0f / sqrtf(ss / (float)in + 1e-5f);
+        float t = 0.f;
+#pragma unroll
+        for (int wi = 0; wi < NW; ++wi) t += red[wi];
+        const float inv = 1.0f / sqrtf(t / (float)in + 1e-5f);
         const float4 *n4 = reinterpret_cast<const float4 *>(a.norm_w);
 #pragma unroll
         for (int k = 0; k < XK; ++k) {
@@ -126,9 +146,41 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(G
             }
         }
     }
-    int buf = 0;
-    for (int rb = r0; rb < r1; rb += RG, buf ^= 1) {
-        if (rb != r0) load_group(rb);
+    // warp 0: sum group g's partials, rotate, store; lane u < RG has row rb + u
+    auto finish = [&](int g) -> bool {
+        const int b = g % NB, rb = r0 + g * RG;
+        if (!mbar_wait(&full[b], (g / NB) & 1, a.wait_ns, a.err)) return false;
+        float sum = 0.f;
+        if (lane < RG) {
+#pragma unroll
+            for (int wi = 0; wi < NW; ++wi) sum += part[b][wi][lane];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[b]);
+        const int r = rb + lane;
+        const bool mine = lane < RG && r < r1;
+        int m = 0, row = r;
+        if (mine)
+            while (row >= a.rows[m]) row -= a.rows[m++];
+        float val = mine && a.res[m] ? a.res[m][row] + sum : sum;
+        // RoPE: rows 2i, 2i + 1 of a head are lanes 2i', 2i' + 1 here (even
+        // group starts, even matrix sizes)
+        const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+        if (mine) {
+            if (m < a.rope_nmat) {
+                const float2 cs = rope_cs[(row % a.rope_hd) / 2];
+                const float x0 = (row & 1) ? other : val, x1 = (row & 1) ? val : other;
+                val = (row & 1) ? x0 * cs.y + x1 * cs.x : x0 * cs.x - x1 * cs.y;
+            }
+            a.y[m][row] = val;
+            if (a.cache[m]) a.cache[m][row] = val;
+        }
+        return true;
+    };
+    const int ng = (r1 - r0 + RG - 1) / RG;
+    for (int g = 0; g < ng; ++g) {
+        if (g > 0) load_group(r0 + g * RG);
+        if (warp == 0 && g > 0 && !finish(g - 1)) return;
         float v[kGemvF32Rows];
 #pragma unroll
         for (int u = 0; u < kGemvF32Rows; ++u) {
@@ -140,36 +192,13 @@ __global__ void __launch_bounds__(kGemvF32Threads, XK >= 4 ? 1 : 2) k_gemv_f32(G
             v[u] = acc;
         }
         const float tot = warp_reduce8(v);  // lane 4u holds row u's warp sum
-        if ((lane & 3) == 0) part[buf][warp][lane >> 2] = tot;
-        __syncthreads();
-        if (warp == 0) {  // lane u < RG finishes row rb + u
-            float sum = 0.f;
-            if (lane < RG) {
-#pragma unroll
-                for (int wi = 0; wi < NW; ++wi) sum += part[buf][wi][lane];
-            }
-            const int r = rb + lane;
-            int m = 0, row = r;
-            if (lane < RG && r < r1)
-                while (row >= a.rows[m]) row -= a.rows[m++];
-            float val = (lane < RG && r < r1 && a.res[m]) ? a.res[m][row] + sum : sum;
-            // RoPE (forward_v2.c:92-104): rows 2i, 2i + 1 of a head are lanes
-            // 2i', 2i' + 1 here (even group starts, even matrix sizes)
-            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-            if (lane < RG && r < r1) {
-                if (m < a.rope_nmat) {
-                    const int half = a.rope_hd / 2, i = (row % a.rope_hd) / 2;
-                    const float freq = 1.0f / powf(10000.0f, (float)i / (float)half);
-                    const float angle = (float)a.rope_pos * freq;
-                    const float c = cosf(angle), sn = sinf(angle);
-                    const float x0 = (row & 1) ? other : val, x1 = (row & 1) ? val : other;
-                    val = (row & 1) ? x0 * sn + x1 * c : x0 * c - x1 * sn;
-                }
-                a.y[m][row] = val;
-                if (a.cache[m]) a.cache[m][row] = val;
-            }
-        }
+        const int b = g % NB;
+        if (g >= NB && !mbar_wait(&empty[b], (g / NB - 1) & 1, a.wait_ns, a.err)) return;
+        if ((lane & 3) == 0) part[b][warp][lane >> 2] = tot;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[b]);
     }
+    if (warp == 0 && ng > 0) finish(ng - 1);
 }
 
 const void *gemv_f32_kernel(int in) {
@@ -327,9 +356,9 @@ __device__ __forceinline__ void load_vec(float (&d)[VPL], const float *p) {
 // (batch b: positions p0 + b PB ..., warp b % 4), loads their k and v rows
 // at once (2 PB VPL floats per lane in flight), and folds them into its
 // running (max, sum, values); the warps are then merged in shared memory.
-template <int VPL>
-__global__ void __launch_bounds__(kAttnRegThreads) k_attention_reg(AttnArgs a) {
-    constexpr int HD = 32 * VPL, PB = 32 / VPL < 8 ? 32 / VPL : 8, NWA = kAttnRegThreads / 32;
+template <int VPL, int NWA>
+__global__ void __launch_bounds__(NWA * 32) k_attention_reg(AttnArgs a) {
+    constexpr int HD = 32 * VPL, PB = 32 / VPL < 8 ? 32 / VPL : 8;
     __shared__ float wm[NWA], wl[NWA];
     __shared__ __align__(16) float wo[NWA][HD];
     __shared__ bool last;
@@ -397,7 +426,7 @@ __global__ void __launch_bounds__(kAttnRegThreads) k_attention_reg(AttnArgs a) {
         L += wl[w2] * f[w2];
     }
     if (a.splits == 1) {
-        for (int i = tid; i < HD; i += kAttnRegThreads) {
+        for (int i = tid; i < HD; i += NWA * 32) {
             float acc = 0.f;
 #pragma unroll
             for (int w2 = 0; w2 < NWA; ++w2) acc = fmaf(wo[w2][i], f[w2], acc);
@@ -406,7 +435,7 @@ __global__ void __launch_bounds__(kAttnRegThreads) k_attention_reg(AttnArgs a) {
         return;
     }
     float *mine = a.part + ((size_t)head * kAttnMaxSplits + split) * (HD + 2);
-    for (int i = tid; i < HD; i += kAttnRegThreads) {
+    for (int i = tid; i < HD; i += NWA * 32) {
         float acc = 0.f;
 #pragma unroll
         for (int w2 = 0; w2 < NWA; ++w2) acc = fmaf(wo[w2][i], f[w2], acc);
@@ -421,10 +450,10 @@ __global__ void __launch_bounds__(kAttnRegThreads) k_attention_reg(AttnArgs a) {
 
 const void *attention_reg_kernel(int hd) {
     switch (hd) {
-        case 32: return (const void *)k_attention_reg<1>;
-        case 64: return (const void *)k_attention_reg<2>;
-        case 128: return (const void *)k_attention_reg<4>;
-        case 256: return (const void *)k_attention_reg<8>;
+        case 32: return (const void *)k_attention_reg<1, kAttnRegThreads / 32>;
+        case 64: return (const void *)k_attention_reg<2, kAttnRegThreads / 32>;
+        case 128: return (const void *)k_attention_reg<4, kAttnRegThreads / 32>;
+        case 256: return (const void *)k_attention_reg<8, kAttnRegThreads / 32>;
         default: return nullptr;
     }
 }

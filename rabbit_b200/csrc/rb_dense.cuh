@@ -25,6 +25,10 @@ constexpr int kMaxGemvMats = 4;
 // t + 512, ... (XK of them) of x, held in registers, so each row is one
 // fully coalesced sweep of the CTA. The loads of the first group go out
 // before the wait for the kernel before (weights are not written by it).
+// Warps do not wait for one another per group: each posts its row partials
+// to a ring of shared buffers (mbarrier arrivals) and streams on; warp 0
+// sums, rotates and stores group g while its own loads of g + 1 are in
+// flight.
 constexpr int kGemvF32Threads = 512;
 constexpr int kGemvF32Rows = 8;  // float4 loads per thread and group
 struct GemvF32Args {
@@ -41,6 +45,8 @@ struct GemvF32Args {
     float *h;
     int rope_nmat, rope_hd, rope_pos;
     float *cache[kMaxGemvMats];
+    int *err;          // device error word (RB_ERR_TIMEOUT when a wait ran out)
+    uint64_t wait_ns;  // bound of every wait
 };
 
 // The kernel for rows of `in` floats: XK = ceil(in / 4 / 512) float4 columns
@@ -59,7 +65,7 @@ const void *gemv_f32_kernel(int in);
 // registers; any other even head_dim: k_attention.
 constexpr int kAttnMaxSplits = 8;
 constexpr int kAttnThreads = 256;     // k_attention
-constexpr int kAttnRegThreads = 128;  // k_attention_reg: four warps
+constexpr int kAttnRegThreads = 256;  // k_attention_reg: eight warps
 struct AttnArgs {
     const float *q;       // [nh * hd], RoPE applied
     const float *kc, *vc; // cache [max_len, nkv * hd], this token's row included

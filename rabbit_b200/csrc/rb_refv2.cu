@@ -109,8 +109,12 @@ static cudaError_t launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size
 static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argmax_out,
                         bool want_hidden, cudaStream_t s) {
     const int sms = c->ctx->sm_count;
+    const uint64_t wait_ns = wait_limit_ns();
     const int kv_after = c->len < c->max_ctx ? c->len + 1 : c->len;
-    const int splits = attention_splits(kv_after);
+    // register attention: one CTA per head covers the whole window (<= 256
+    // positions: a round or four of 64 per CTA); the shared-memory kernel
+    // splits the window over CTAs of 32 positions and more
+    const int splits = c->attn_reg ? 1 : attention_splits(kv_after);
     for (int l = 0; l < c->L; ++l) {
         GemvF32Args g = {};
         g.nmat = 3;
@@ -126,6 +130,8 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
         g.in_dim = c->H;
         g.x = c->h;
         g.norm_w = c->rms_attn(l);
+        g.err = c->ctx->d_err;
+        g.wait_ns = wait_ns;
         if (l == 0) {  // h = embed[id % V] (forward_v2.c:459-461)
             g.embed = c->embed;
             g.idp = idp;
@@ -172,6 +178,8 @@ static int enqueue_step(rabbit_cuda_refv2 *c, const int *idp, int id, int *argma
         o.rows[0] = c->H;
         o.in_dim = c->qd;
         o.x = c->att;
+        o.err = c->ctx->d_err;
+        o.wait_ns = wait_ns;
         void *oa[] = {&o};
         RB_CUDA(launch_pdl_ptr(c->gemv_q, dim3(2 * sms), dim3(kGemvF32Threads), 0, s, oa));
         const int st = rabbit_cuda_moe_decode_dev(c->moe, l, c->h, c->h, nullptr, nullptr, s);

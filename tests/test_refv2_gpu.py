@@ -8,7 +8,8 @@ Bar: logits and the final-normed hidden within rtol 1e-4 / atol 1e-5 after
 every token, the argmax identical whenever the oracle's top two logits are
 apart by more than 1e-4 of the largest |logit|. Sequences run past max_ctx,
 where the KV cache stops growing (forward_v2.c:198-202), and past 32 cached
-positions, where a head's positions are split over several CTAs. A token whose
+positions, where the shared-memory attention splits a head's positions over
+several CTAs. A token whose
 router scores hold a near-tie in any layer (adjacent top-k+1 scores within
 1e-5 of the largest) ends the comparison of that sequence: after it the two
 sides may route differently, legitimately.
@@ -28,8 +29,10 @@ CONFIGS = {
     "gqa": (2, 128, 1000, 4, 2, 32, 8, 2, 64, 0, 8),
     "wide_q_shared_odd_vocab": (2, 128, 997, 6, 3, 40, 4, 2, 96, 1, 6),
     "mha_one_layer": (1, 64, 512, 2, 2, 32, 4, 1, 64, 0, 4),
-    # a window past 32 positions: attention split over several CTAs per head
+    # windows past 32 positions: head_dim 32 (registers, one CTA per head)
+    # and head_dim 40 (shared memory, positions split over CTAs and merged)
     "long_window": (2, 128, 1000, 4, 2, 32, 8, 2, 64, 0, 80),
+    "long_window_split": (1, 128, 1000, 4, 2, 40, 8, 2, 64, 0, 72),
 }
 
 
