@@ -250,11 +250,11 @@ OL = dict(L=16, H=2048, nh=16, nkv=16, hd=128, E=64, k=8, I=1024, V=50304, ctx=2
 OL_PROMPT, OL_NEW = 16, 128
 
 
-def olmoe_dense_bytes(kv_len: int) -> int:
+def olmoe_dense_bytes(kv_len: int, layers: int | None = None) -> int:
     """Algorithmic bytes of one token's dense part at KV length kv_len (after
     the append): per layer rms_attn + W_q/W_k/W_v/W_o + the K/V rows read and
     the row written; the embedding row, final norm and lm_head once."""
-    L, H, V = OL["L"], OL["H"], OL["V"]
+    L, H, V = layers or OL["L"], OL["H"], OL["V"]
     qd, kvd = OL["nh"] * OL["hd"], OL["nkv"] * OL["hd"]
     per_layer = H + qd * H + 2 * kvd * H + H * qd + 2 * kvd * (kv_len + 1)
     return 4 * (L * per_layer + 2 * H + H * V)
@@ -306,11 +306,14 @@ def olmoe_cpu_sample(seconds: float = 6.0) -> dict:
                             "prompt)")}
 
 
-def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True) -> dict:
+def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True,
+                     layers: int | None = None, n_new: int = OL_NEW,
+                     n_prompt: int = OL_PROMPT) -> dict:
     """Device-resident full decode through rabbit_cuda_refv2: prefill a random
     prompt, then generate 128 tokens chained on the device; device time from
-    CUDA events around the generate call's kernels, e2e from the host call."""
-    L, H, V, E, k, I = OL["L"], OL["H"], OL["V"], OL["E"], OL["k"], OL["I"]
+    CUDA events around the generate call's kernels, e2e from the host call.
+    layers / n_new / n_prompt below the workload's: profiling cases."""
+    L, H, V, E, k, I = layers or OL["L"], OL["H"], OL["V"], OL["E"], OL["k"], OL["I"]
     rng = np.random.default_rng(SEED + 5)
     routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
     pool = capi.MoePool(records=None, expert_size=synth.expert_record_size(H, I), n_layers=L,
@@ -320,41 +323,42 @@ def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True) 
     ctx = capi.RefV2(pool, vocab=V, n_heads=OL["nh"], n_kv_heads=OL["nkv"],
                      head_dim=OL["hd"], max_ctx=OL["ctx"])
     ctx.fill_synthetic(SEED * 1000 + 78, 0.02)
-    prompt = rng.integers(0, V, OL_PROMPT)
+    prompt = rng.integers(0, V, n_prompt)
     dev, wall = [], []
     for r in range(runs + 1):  # the first run warms up
         ctx.reset()
         ctx.prefill(prompt, want_logits=False, want_hidden=False)
         t0 = time.perf_counter()
-        out = ctx.generate(OL_NEW)
+        out = ctx.generate(n_new)
         t = time.perf_counter() - t0
         if r:
             dev.append(ctx.device_ms / 1e3)
             wall.append(t)
     assert ((out >= 0) & (out < V)).all()
     moe_bytes = pool.decode_bytes * L
-    gen_bytes = sum(olmoe_dense_bytes(OL_PROMPT + i) for i in range(OL_NEW)) + OL_NEW * moe_bytes
+    gen_bytes = (sum(olmoe_dense_bytes(n_prompt + i, L) for i in range(n_new))
+                 + n_new * moe_bytes)
     dsec, wsec = statistics.median(dev), statistics.median(wall)
     achieved = gen_bytes / dsec / 1e9
     item = {
         "metric": "full decode tokens/s (OLMoE-shaped, batch 1)",
-        "value": round(OL_NEW / dsec, 2), "unit": "tokens/s",
-        "ms_per_token": round(1e3 * dsec / OL_NEW, 4),
+        "value": round(n_new / dsec, 2), "unit": "tokens/s",
+        "ms_per_token": round(1e3 * dsec / n_new, 4),
         "config": {"workload": (f"OLMoE-shaped ref-v2 decode: {L} layers, hidden {H}, "
                                 f"{OL['nh']}x{OL['hd']} heads, {E} experts top-{k}, inter {I}, "
-                                f"vocab {V}, KV window {OL['ctx']}; {OL_PROMPT}-id random "
-                                f"prompt, {OL_NEW} greedy tokens"),
+                                f"vocab {V}, KV window {OL['ctx']}; {n_prompt}-id random "
+                                f"prompt, {n_new} greedy tokens"),
                    "l2": "inputs larger than L2 (1.5 GB fp32 dense + 0.46 GB experts per token)",
                    "runs": runs},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "bytes_per_token": round(gen_bytes / OL_NEW),
+                     "bytes_per_token": round(gen_bytes / n_new),
                      "moe_bytes_per_token": moe_bytes,
                      "what": "every weight byte a token needs read once, over the whole chain"},
-        "e2e": {"value": round(OL_NEW / wsec, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 4 * OL_NEW,
+        "e2e": {"value": round(n_new / wsec, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * n_new,
                 "api": "rabbit_cuda_refv2_generate (host output ids)"},
-        "gpu_launches_per_token": 4 * L + 3,
+        "gpu_launches_per_token": 4 * L + 2,
     }
     ctx.free()
     pool.free()
@@ -419,6 +423,15 @@ def run_rabbit(args) -> None:
                                 device_id=torch.device("cuda", local))
     from rabbit_b200 import capi, synth
 
+    if args.full_decode_only:  # the OLMoE-shaped full decode item alone (profiling)
+        if rank == 0:
+            item = full_decode_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline,
+                                    layers=args.fd_layers, n_new=args.fd_new,
+                                    n_prompt=args.fd_prompt)
+            print(json.dumps({"full_decode": item}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     L = args.layers
 
     capi.check(capi.lib().rabbit_cuda_set_device(local))
@@ -554,6 +567,11 @@ def main(argv=None) -> int:
     ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV line item")
     ap.add_argument("--no-full-decode", action="store_true",
                     help="skip the OLMoE-shaped full decode line item")
+    ap.add_argument("--full-decode-only", action="store_true",
+                    help="run only the full decode item (profiling cases)")
+    ap.add_argument("--fd-layers", type=int, default=None, help="full decode: layers")
+    ap.add_argument("--fd-new", type=int, default=OL_NEW, help="full decode: generated tokens")
+    ap.add_argument("--fd-prompt", type=int, default=OL_PROMPT, help="full decode: prompt ids")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
