@@ -186,6 +186,20 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
 int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                        float *d_h_out, int *d_ids, float *d_weights,
                                        void *stream);
+/* T tokens through one layer's MoE block at once (the multi-token "prefill"
+ * form of moe_step, forward_v2.c:362-402): each token is routed on its own
+ * (rmsnorm, router, top-k, softmax, shared experts with weight 1) and gets the
+ * same result as rabbit_cuda_moe_decode would give it alone, but each expert
+ * the chunk touches is read from HBM once for all the tokens routed to it.
+ * DEVICE buffers, asynchronous on `stream`: h_in / h_out [T][H] (may alias),
+ * ids / weights [T][k] (both or neither may be NULL). 1 <= n_tokens <= 256.
+ * Pools outside the group-32 layout run the per-token decode, token by token. */
+int rabbit_cuda_moe_prefill_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
+                                float *d_h_out, int n_tokens, int *d_ids, float *d_weights,
+                                void *stream);
+/* Same on HOST buffers; synchronous. */
+int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
+                            int n_tokens, int *ids, float *weights);
 /* Check the device error word after work on `stream` finished (TIMEOUT if a
  * bounded wait gave up). Synchronises `stream`. */
 int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);

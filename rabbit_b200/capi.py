@@ -75,6 +75,8 @@ SIGNATURES = {
                                    C.POINTER(C.c_uint64), C.POINTER(_I),
                                    C.POINTER(C.c_uint64)]),
     "rabbit_cuda_moe_decode_bytes": (C.c_uint64, [_P]),
+    "rabbit_cuda_moe_prefill_dev": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
+    "rabbit_cuda_moe_prefill": (_I, [_P, _I, _P, _P, _I, _P, _P]),
     "rabbit_cuda_refv2_create": (_I, [C.POINTER(DenseDesc), _P, C.POINTER(_P)]),
     "rabbit_cuda_refv2_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_refv2_free": (_I, [_P]),
@@ -239,6 +241,22 @@ class MoePool:
         check(lib().rabbit_cuda_moe_decode_dev_noalloc(self.handle, layer, d_h_in, d_h_out,
                                                        d_ids or None, d_w or None,
                                                        stream or None))
+
+    def prefill(self, layer: int, h: np.ndarray):
+        """Host buffers, h [T, H]. Returns (h_out [T, H], ids [T, k], weights [T, k])."""
+        h = np.ascontiguousarray(h, np.float32)
+        T = h.shape[0]
+        out = np.zeros_like(h)
+        ids = np.zeros((T, self.k), np.int32)
+        w = np.zeros((T, self.k), np.float32)
+        check(lib().rabbit_cuda_moe_prefill(self.handle, layer, _ptr(h), _ptr(out), T, _ptr(ids),
+                                            _ptr(w)))
+        return out, ids, w
+
+    def prefill_dev(self, layer: int, d_h_in: int, d_h_out: int, n_tokens: int, d_ids: int = 0,
+                    d_w: int = 0, stream: int = 0) -> None:
+        check(lib().rabbit_cuda_moe_prefill_dev(self.handle, layer, d_h_in, d_h_out, n_tokens,
+                                                d_ids or None, d_w or None, stream or None))
 
     def check(self, stream: int = 0) -> None:
         check(lib().rabbit_cuda_moe_check(self.handle, stream or None))

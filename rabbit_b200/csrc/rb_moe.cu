@@ -75,6 +75,14 @@ struct rabbit_cuda_moe {
     rb::MoeFusedArgs plan{};
     int grid = 0, block = 0;
     size_t smem = 0;
+    // multi-token scratch (rabbit_cuda_moe_prefill*), grown on demand
+    int bt_cap = 0;          // tokens the scratch holds
+    void *bt_block = nullptr;  // one allocation, carved below
+    rb::MoeBatchArgs bt{};   // scratch pointers of the block
+    float *bt_h = nullptr;   // [bt_cap][H] device copy of host tokens
+    int *bt_ids = nullptr;   // [bt_cap][8] routing of host-buffer calls
+    float *bt_w = nullptr;   // [bt_cap][8]
+    float *bt_pin = nullptr; // pinned [bt_cap][H] + ids/weights
     // counters
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
     std::vector<uint8_t> img;  // host image of one record in the tiled layout
@@ -245,6 +253,8 @@ static void free_pool(rabbit_cuda_moe *p) {
         if (p->pin_ev[i]) cudaEventDestroy(p->pin_ev[i]);
     }
     if (p->pin_io) cudaFreeHost(p->pin_io);
+    if (p->bt_block) cudaFree(p->bt_block);
+    if (p->bt_pin) cudaFreeHost(p->bt_pin);
     if (p->up) cudaStreamDestroy(p->up);
     delete p;
 }
@@ -770,6 +780,201 @@ int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, flo
     if (ids) memcpy(ids, pin_o + hb, sizeof(int) * p->k);
     if (weights) memcpy(weights, pin_o + hb + 32, sizeof(float) * p->k);
     if (k_out) *k_out = p->k;
+    return ok();
+}
+
+}  // extern "C"
+
+namespace rb {
+static bool g_batch_attr[kMaxDevices];
+
+// Records a layer can have (the bucket's range).
+static int max_local(const rabbit_cuda_moe *p) { return p->shared_table ? p->n_records : p->epl; }
+
+// Grow the multi-token scratch to T tokens (caller holds no stream work on it).
+static int ensure_batch(rabbit_cuda_moe *p, int T) {
+    if (T <= p->bt_cap) return RABBIT_CUDA_OK;
+    const int cap = std::max(T, std::min(kMaxBatchTokens, 2 * p->bt_cap));
+    const int slots = std::max(1, std::min(kMaxSlots, p->k + p->S));
+    const size_t P = (size_t)cap * slots, R = (size_t)std::max(1, max_local(p));
+    const int KC = p->plan.tc.KC;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off = align_up(off + bytes, 256); return o; };
+    const size_t o_xn = take(sizeof(float) * cap * p->H);
+    const size_t o_srec = take(sizeof(int) * cap * kMaxSlots);
+    const size_t o_sw = take(sizeof(float) * cap * kMaxSlots);
+    const size_t o_ns = take(sizeof(int) * cap);
+    const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
+    const size_t o_pt = take(sizeof(int) * P);
+    const size_t o_act = take(sizeof(int) * R * 3 + sizeof(int));
+    const size_t o_mid = take(sizeof(float) * P * p->I);
+    const size_t o_down = take(sizeof(float) * P * KC * p->H);
+    const size_t o_h = take(sizeof(float) * cap * p->H);
+    const size_t o_ids = take(sizeof(int) * cap * 8);
+    const size_t o_w = take(sizeof(float) * cap * 8);
+    void *blk = nullptr;
+    float *pin = nullptr;
+    cudaError_t e = cudaMalloc(&blk, off);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_prefill: scratch");
+    if ((e = cudaMallocHost(&pin, sizeof(float) * ((size_t)cap * p->H + 2 * (size_t)cap * 8))) !=
+        cudaSuccess) {
+        cudaFree(blk);
+        return cuda_fail(e, "moe_prefill: pinned staging");
+    }
+    if (p->bt_block) cudaFree(p->bt_block);
+    if (p->bt_pin) cudaFreeHost(p->bt_pin);
+    p->bt_block = blk;
+    p->bt_pin = pin;
+    uint8_t *b = static_cast<uint8_t *>(blk);
+    MoeBatchArgs &a = p->bt;
+    a.xn = reinterpret_cast<float *>(b + o_xn);
+    a.srec = reinterpret_cast<int *>(b + o_srec);
+    a.sw = reinterpret_cast<float *>(b + o_sw);
+    a.nslot = reinterpret_cast<int *>(b + o_ns);
+    a.pidx = reinterpret_cast<int *>(b + o_pidx);
+    a.pair_t = reinterpret_cast<int *>(b + o_pt);
+    a.act = reinterpret_cast<int *>(b + o_act);
+    a.act_off = a.act + R;
+    a.act_cnt = a.act_off + R;
+    a.n_act = a.act_cnt + R;
+    a.mid = reinterpret_cast<float *>(b + o_mid);
+    a.down = reinterpret_cast<float *>(b + o_down);
+    p->bt_h = reinterpret_cast<float *>(b + o_h);
+    p->bt_ids = reinterpret_cast<int *>(b + o_ids);
+    p->bt_w = reinterpret_cast<float *>(b + o_w);
+    p->bt_cap = cap;
+    return RABBIT_CUDA_OK;
+}
+
+static cudaError_t launch_batch(int which, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                MoeBatchArgs &a) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&a};
+    return cudaLaunchKernelExC(&cfg, moe_batch_kernel(which), args);
+}
+
+// The body of rabbit_cuda_moe_prefill_dev.
+static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out, int T,
+                        int *d_ids, float *d_w, cudaStream_t s) {
+    int base, n_local;
+    int st = layer_map(p, layer, &base, &n_local);
+    if (st) return st;
+    for (int r = 0; r < n_local; ++r)
+        if (!p->resident[base + r])
+            return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: layer %d not uploaded", layer);
+    RB_CUDA(cudaSetDevice(p->device));
+    if (!p->fast) {  // other record formats: the per-token decode, token by token
+        for (int t = 0; t < T; ++t) {
+            st = decode_impl(p, layer, d_h_in + (size_t)t * p->H, d_h_out + (size_t)t * p->H,
+                             d_ids ? d_ids + (size_t)t * p->k : nullptr,
+                             d_w ? d_w + (size_t)t * p->k : nullptr, s, p->ctx->d_err);
+            if (st) return st;
+        }
+        return ok();
+    }
+    if ((st = ensure_batch(p, T)) != RABBIT_CUDA_OK) return st;
+    const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (T + 31) / 32;
+    const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 2 * sizeof(int) * R;
+    const size_t gu_x = sizeof(float) * (size_t)(p->H / 32) * 33;  // one token's padded xn
+    const size_t gu_tile = align_up(p->plan.tb.tile_bytes, 16);
+    const size_t dn_x = sizeof(float) * (size_t)(p->plan.tc.cols / 32) * 33;
+    const size_t dn_tile = align_up(p->plan.tc.tile_bytes, 16);
+    const size_t cap = kMaxDynSmem / 2 - 1024;  // two CTAs per SM
+    if (bucket_smem > (size_t)kMaxDynSmem || gu_tile + gu_x > (size_t)kMaxDynSmem)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
+    const int gu_chunk = (int)std::min<size_t>(
+        kBatchTokChunk, std::max<size_t>(1, ((gu_tile + kBatchTokChunk * gu_x <= cap ? cap : (size_t)kMaxDynSmem) - gu_tile) / gu_x));
+    if (!g_batch_attr[p->device]) {
+        for (int i = 1; i <= 3; ++i)
+            RB_CUDA(cudaFuncSetAttribute(moe_batch_kernel(i),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
+        g_batch_attr[p->device] = true;
+    }
+    MoeBatchArgs a = p->bt;
+    a.h_in = d_h_in;
+    a.h_out = d_h_out;
+    a.T = T;
+    a.ids_out = d_ids;
+    a.w_out = d_ids ? d_w : nullptr;
+    a.rms = p->rms + (size_t)layer * p->H;
+    a.router = p->router + (size_t)layer * p->H * p->E;
+    a.pool = p->pool;
+    a.rec_stride = p->rec_stride;
+    a.off_d = p->off_d;
+    a.rec_base = base;
+    a.n_local = n_local;
+    a.H = p->H;
+    a.E = p->E;
+    a.k = p->k;
+    a.I = p->I;
+    a.S = p->S;
+    a.usable = p->usable ? 1 : 0;
+    a.tb = p->plan.tb;
+    a.tc = p->plan.tc;
+    a.chunk_gu = gu_chunk;
+    RB_CUDA(launch_batch(0, dim3(T), dim3(256), sizeof(float) * (size_t)p->E, s, a));
+    RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
+    RB_CUDA(launch_batch(2, dim3(2 * sms), dim3(256), gu_tile + (size_t)gu_chunk * gu_x, s, a));
+    RB_CUDA(launch_batch(3, dim3(2 * sms), dim3(256), dn_tile + (size_t)kBatchTokChunk * dn_x, s, a));
+    RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
+    p->hbm_hits += T;
+    return ok();
+}
+}  // namespace rb
+
+extern "C" {
+
+int rabbit_cuda_moe_prefill_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                                int n_tokens, int *d_ids, float *d_weights, void *stream) {
+    if (!p || !d_h_in || !d_h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: NULL argument");
+    if (n_tokens < 1 || n_tokens > kMaxBatchTokens)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: n_tokens must be 1..%d", kMaxBatchTokens);
+    if ((d_ids == nullptr) != (d_weights == nullptr))
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: pass both ids and weights, or neither");
+    return prefill_impl(p, layer, d_h_in, d_h_out, n_tokens, d_ids, d_weights,
+                        as_stream(stream, p->ctx));
+}
+
+int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
+                            int n_tokens, int *ids, float *weights) {
+    if (!p || !h_in || !h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: NULL argument");
+    if (n_tokens < 1 || n_tokens > kMaxBatchTokens)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: n_tokens must be 1..%d", kMaxBatchTokens);
+    std::lock_guard<std::mutex> g(p->ctx->mu);
+    RB_CUDA(cudaSetDevice(p->device));
+    cudaStream_t s = p->ctx->stream;
+    int st = ensure_batch(p, n_tokens);
+    if (st) return st;
+    // pinned staging: [h (cap H)] [ids (cap 8)] [weights (cap 8)]; the device
+    // copy of h is bt_h, ids / weights go to bt_ids / bt_w
+    const size_t hb = sizeof(float) * (size_t)n_tokens * p->H;
+    const size_t kb = sizeof(float) * (size_t)n_tokens * p->k;
+    int *pin_ids = reinterpret_cast<int *>(p->bt_pin + (size_t)p->bt_cap * p->H);
+    float *pin_w = p->bt_pin + (size_t)p->bt_cap * p->H + (size_t)p->bt_cap * 8;
+    memcpy(p->bt_pin, h_in, hb);
+    RB_CUDA(cudaMemcpyAsync(p->bt_h, p->bt_pin, hb, cudaMemcpyHostToDevice, s));
+    const bool want = ids || weights;
+    st = prefill_impl(p, layer, p->bt_h, p->bt_h, n_tokens, want ? p->bt_ids : nullptr,
+                      want ? p->bt_w : nullptr, s);
+    if (st) return st;
+    RB_CUDA(cudaMemcpyAsync(p->bt_pin, p->bt_h, hb, cudaMemcpyDeviceToHost, s));
+    if (want) {
+        RB_CUDA(cudaMemcpyAsync(pin_ids, p->bt_ids, kb, cudaMemcpyDeviceToHost, s));
+        RB_CUDA(cudaMemcpyAsync(pin_w, p->bt_w, kb, cudaMemcpyDeviceToHost, s));
+    }
+    if ((st = check_device_error(p->ctx, s, "moe_prefill")) != RABBIT_CUDA_OK) return st;
+    memcpy(h_out, p->bt_pin, hb);
+    if (ids) memcpy(ids, pin_ids, kb);
+    if (weights) memcpy(weights, pin_w, kb);
     return ok();
 }
 

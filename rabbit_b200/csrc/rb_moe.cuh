@@ -62,6 +62,48 @@ struct MoeFusedArgs {
 const void *moe_fused_kernel(int JB, int JC, bool packed);
 inline bool combine_packed(int KC) { return KC < 8; }
 
+// ------------------------------------------------------- multi-token path --
+// T tokens through one layer's MoE block, each as moe_step (forward_v2.c:
+// 362-402) would take it alone, with every active expert's tiles read once for
+// all the tokens routed to it:
+//   k_batch_route   one CTA per token: rmsnorm -> xn, router, top-k, slots;
+//   k_batch_bucket  one CTA: per local record, the (token, slot) pairs that
+//                   use it, in token order (bitmask ranks: deterministic);
+//   k_batch_gu      (active record, GU tile) items: mid = silu(gate) * up for
+//                   the record's tokens, 8 staged in shared memory at a time;
+//   k_batch_down    (active record, D tile) items: each column chunk's down
+//                   rows per pair;
+//   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
+//                   order (forward_v2.c:356-357, 398-399).
+constexpr int kMaxBatchTokens = 256;
+constexpr int kBatchTokChunk = 8;  // tokens per pass over a staged tile
+struct MoeBatchArgs {
+    const float *h_in;
+    float *h_out;
+    int T;
+    int *ids_out;    // [T][k] or nullptr
+    float *w_out;    // [T][k] or nullptr
+    const float *rms, *router;
+    const uint8_t *pool;
+    uint64_t rec_stride, off_d;
+    int rec_base, n_local, H, E, k, I, S, usable;
+    Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
+    int chunk_gu;    // tokens staged per pass of k_batch_gu (<= kBatchTokChunk)
+    // scratch
+    float *xn;       // [T][H]
+    int *srec;       // [T][kMaxSlots] global record per slot
+    float *sw;       // [T][kMaxSlots] combine weight per slot
+    int *nslot;      // [T]
+    int *pidx;       // [T][kMaxSlots] pair index of (token, slot)
+    int *pair_t;     // [P] token of pair
+    int *act, *act_off, *act_cnt;  // [n_local] active records: global id, first pair, pairs
+    int *n_act;      // [1]
+    float *mid;      // [P][I]
+    float *down;     // [P][tc.KC][H]
+};
+// The five kernels (same translation unit as the fused kernel).
+const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 gu, 3 down, 4 combine
+
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine
 struct MoeGenericArgs {
     const float *h_in;

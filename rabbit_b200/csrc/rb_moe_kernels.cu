@@ -902,6 +902,302 @@ const void *moe_fused_kernel(int JB, int JC, bool packed) {
                    : (const void *)k_moe_decode_g32<1, 1, false>;
 }
 
+// ======================================================= multi-token path ==
+__global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
+    extern __shared__ __align__(16) float s_sc[];  // [E] router scores
+    __shared__ float red[32];
+    __shared__ int s_rec[kMaxSlots];
+    __shared__ float s_w[kMaxSlots];
+    launch_dependents();
+    wait_prerequisite();
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int t = blockIdx.x, H = a.H;
+    const float *h = a.h_in + (size_t)t * H;
+    float *xn = a.xn + (size_t)t * H;
+    // rmsnorm (forward_v2.c:61-69)
+    float ss = 0.f;
+    for (int i = tid; i < H; i += nthr) ss += h[i] * h[i];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < (nthr >> 5) ? red[lane] : 0.f;
+        v = warp_sum(v);
+        if (lane == 0) red[31] = 1.0f / sqrtf(v / (float)H + 1e-5f);
+    }
+    __syncthreads();
+    const float inv = red[31];
+    for (int i = tid; i < H; i += nthr) xn[i] = (h[i] * inv) * a.rms[i];
+    __syncthreads();
+    // router scores (forward_v2.c:71-79, :378): a warp per expert row
+    for (int e = warp; e < a.E; e += nthr >> 5) {
+        const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
+        const float4 *x4 = reinterpret_cast<const float4 *>(xn);
+        float d = 0.f;
+        for (int i4 = lane; i4 < (H >> 2); i4 += 32) {
+            const float4 w = wr[i4], x = x4[i4];
+            d = fmaf(w.x, x.x, d);
+            d = fmaf(w.y, x.y, d);
+            d = fmaf(w.z, x.z, d);
+            d = fmaf(w.w, x.w, d);
+        }
+        d = warp_sum(d);
+        if (lane == 0) s_sc[e] = d;
+    }
+    __syncthreads();
+    int *ids = reinterpret_cast<int *>(red);
+    float *w = red + 8;
+    topk_softmax_block(s_sc, a.E, a.k, ids, w);
+    if (tid == 0) {
+        if (a.ids_out)
+            for (int i = 0; i < a.k; ++i) {
+                a.ids_out[(size_t)t * a.k + i] = ids[i];
+                a.w_out[(size_t)t * a.k + i] = w[i];
+            }
+        const int n = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+        a.nslot[t] = n;
+        for (int j = 0; j < n; ++j) {
+            a.srec[(size_t)t * kMaxSlots + j] = s_rec[j];
+            a.sw[(size_t)t * kMaxSlots + j] = s_w[j];
+        }
+    }
+}
+
+// One CTA. Ranks come from per-record token bitmasks, so the pair order is
+// token order whatever order the atomics land in.
+__global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
+    extern __shared__ __align__(16) uint32_t bm[];  // [R][W] bits, then cnt[R], off[R]
+    launch_dependents();
+    wait_prerequisite();
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int R = a.n_local, W = (a.T + 31) >> 5;
+    int *cnt = reinterpret_cast<int *>(bm + (size_t)R * W), *off = cnt + R;
+    for (int i = tid; i < R * W; i += nthr) bm[i] = 0u;
+    __syncthreads();
+    const int Q = a.T * kMaxSlots;
+    for (int q = tid; q < Q; q += nthr) {
+        const int t = q / kMaxSlots, j = q - t * kMaxSlots;
+        if (j < a.nslot[t]) {
+            const int r = a.srec[q] - a.rec_base;
+            atomicOr(&bm[r * W + (t >> 5)], 1u << (t & 31));
+        }
+    }
+    __syncthreads();
+    for (int r = tid; r < R; r += nthr) {
+        int c = 0;
+        for (int x = 0; x < W; ++x) c += __popc(bm[r * W + x]);
+        cnt[r] = c;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0, na = 0;
+        for (int r = 0; r < R; ++r) {
+            off[r] = o;
+            if (cnt[r]) {
+                a.act[na] = a.rec_base + r;
+                a.act_off[na] = o;
+                a.act_cnt[na] = cnt[r];
+                ++na;
+            }
+            o += cnt[r];
+        }
+        *a.n_act = na;
+    }
+    __syncthreads();
+    for (int q = tid; q < Q; q += nthr) {
+        const int t = q / kMaxSlots, j = q - t * kMaxSlots;
+        if (j < a.nslot[t]) {
+            const int r = a.srec[q] - a.rec_base;
+            int rank = 0;
+            for (int x = 0; x < (t >> 5); ++x) rank += __popc(bm[r * W + x]);
+            rank += __popc(bm[r * W + (t >> 5)] & ((1u << (t & 31)) - 1u));
+            const int pos = off[r] + rank;
+            a.pair_t[pos] = t;
+            a.pidx[q] = pos;
+        }
+    }
+}
+
+// Stage `bytes` (a multiple of 4) from global to shared memory.
+__device__ __forceinline__ void stage_words(uint8_t *dst, const uint8_t *src, uint32_t bytes) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const uint32_t n16 = bytes >> 4;
+    for (uint32_t i = tid; i < n16; i += nthr)
+        reinterpret_cast<uint4 *>(dst)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+    for (uint32_t i = (n16 << 2) + tid; i < (bytes >> 2); i += nthr)
+        reinterpret_cast<uint32_t *>(dst)[i] = __ldg(reinterpret_cast<const uint32_t *>(src) + i);
+}
+
+// 32 weights of one group: nibble n of byte b (low nibble = even element,
+// q = nibble - 8) times the group scale (quant.c:171-185).
+__device__ __forceinline__ void dequant32(const uint8_t *nib, float scale, float (&wq)[32]) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(nib);
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t byte = (words[q] >> (8 * b)) & 0xFFu;
+            wq[8 * q + 2 * b] = (float)((int)(byte & 15u) - 8) * scale;
+            wq[8 * q + 2 * b + 1] = (float)((int)(byte >> 4) - 8) * scale;
+        }
+}
+
+// (active record, GU tile) work items; a warp per gate/up row pair, a lane
+// per group of 32 inputs; the tokens' xn staged 8 at a time in the padded
+// layout (33 floats per group: lane g and element e hit bank (g + e) % 32).
+__global__ void __launch_bounds__(256) k_batch_gu(MoeBatchArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    launch_dependents();
+    wait_prerequisite();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
+    const size_t half = (size_t)H / 2;
+    const int xstride = G * 33;
+    uint8_t *tile = smem;
+    float *xs = reinterpret_cast<float *>(smem + align_up(a.tb.tile_bytes, 16));
+    const int na = *a.n_act;
+    for (int item = blockIdx.x; item < na * ntb; item += gridDim.x) {
+        const int ai = item / ntb, tt = item - ai * ntb;
+        const int off = a.act_off[ai], m = a.act_cnt[ai];
+        __syncthreads();  // the last item's readers are done with the tile
+        stage_words(tile, a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt * a.tb.tile_stride,
+                    a.tb.tile_bytes);
+        const float *gsc = reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half);
+        for (int c0 = 0; c0 < m; c0 += a.chunk_gu) {
+            const int mc = min(a.chunk_gu, m - c0);
+            if (c0 > 0) __syncthreads();
+            for (int i = tid; i < mc * H; i += blockDim.x) {
+                const int ti = i / H, e = i - ti * H;
+                xs[ti * xstride + xpad(e)] = a.xn[(size_t)a.pair_t[off + c0 + ti] * H + e];
+            }
+            __syncthreads();
+            for (int r = warp; r < TR; r += nwarp) {
+                const int row = tt * TR + r;
+                if (row >= I) break;
+                float gs[kBatchTokChunk], us[kBatchTokChunk];
+#pragma unroll
+                for (int q = 0; q < kBatchTokChunk; ++q) gs[q] = us[q] = 0.f;
+                for (int g = lane; g < G; g += 32) {
+                    float gq[32], uq[32];
+                    dequant32(tile + (size_t)r * half + (size_t)g * 16, gsc[(size_t)r * G + g], gq);
+                    dequant32(tile + (size_t)(TR + r) * half + (size_t)g * 16,
+                              gsc[(size_t)(TR + r) * G + g], uq);
+#pragma unroll
+                    for (int q = 0; q < kBatchTokChunk; ++q) {
+                        if (q < mc) {
+                            const float *x = xs + q * xstride + g * 33;
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                gs[q] = fmaf(gq[e], x[e], gs[q]);
+                                us[q] = fmaf(uq[e], x[e], us[q]);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < kBatchTokChunk; ++q) {
+                    if (q < mc) {
+                        const float gv = warp_sum(gs[q]), uv = warp_sum(us[q]);
+                        if (lane == 0) a.mid[(size_t)(off + c0 + q) * I + row] = silu_mul(gv, uv);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// (active record, D tile) work items: tile (chunk c, row tile t) of W2; a
+// warp per row, a lane per group of the chunk; the pairs' mid chunks staged 8
+// at a time.
+__global__ void __launch_bounds__(256) k_batch_down(MoeBatchArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    launch_dependents();
+    wait_prerequisite();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    const int H = a.H, I = a.I, TR = a.tc.TR, ntc = a.tc.ntiles, rt = a.tc.rtiles, KC = a.tc.KC;
+    const int cols = a.tc.cols, Gc = cols / 32;
+    const size_t chalf = (size_t)cols / 2;
+    const int xstride = Gc * 33;
+    uint8_t *tile = smem;
+    float *ms = reinterpret_cast<float *>(smem + align_up(a.tc.tile_bytes, 16));
+    const int na = *a.n_act;
+    for (int item = blockIdx.x; item < na * ntc; item += gridDim.x) {
+        const int ai = item / ntc, d = item - ai * ntc;
+        const int c = d / rt, t = d - c * rt;
+        const int off = a.act_off[ai], m = a.act_cnt[ai];
+        __syncthreads();
+        stage_words(tile, a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d +
+                              (size_t)d * a.tc.tile_stride,
+                    a.tc.tile_bytes);
+        const float *sc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
+        for (int c0 = 0; c0 < m; c0 += kBatchTokChunk) {
+            const int mc = min(kBatchTokChunk, m - c0);
+            if (c0 > 0) __syncthreads();
+            for (int i = tid; i < mc * cols; i += blockDim.x) {
+                const int ti = i / cols, e = i - ti * cols;
+                ms[ti * xstride + xpad(e)] = a.mid[(size_t)(off + c0 + ti) * I + (size_t)c * cols + e];
+            }
+            __syncthreads();
+            for (int r = warp; r < TR; r += nwarp) {
+                const int row = t * TR + r;
+                if (row >= H) break;
+                float acc[kBatchTokChunk];
+#pragma unroll
+                for (int q = 0; q < kBatchTokChunk; ++q) acc[q] = 0.f;
+                if (lane < Gc) {
+                    float wq[32];
+                    dequant32(tile + (size_t)r * chalf + (size_t)lane * 16, sc[(size_t)r * Gc + lane], wq);
+#pragma unroll
+                    for (int q = 0; q < kBatchTokChunk; ++q) {
+                        if (q < mc) {
+                            const float *x = ms + q * xstride + lane * 33;
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) acc[q] = fmaf(wq[e], x[e], acc[q]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < kBatchTokChunk; ++q) {
+                    if (q < mc) {
+                        const float v = warp_sum(acc[q]);
+                        if (lane == 0) a.down[((size_t)(off + c0 + q) * KC + c) * H + row] = v;
+                    }
+                }
+            }
+        }
+    }
+}
+
+// h_out = h + sum_j w_j down_j, down_j = the sum of its chunks in chunk order
+// (forward_v2.c:356-357, 398-399); grid (T, ceil(H / 256)).
+__global__ void __launch_bounds__(256) k_batch_combine(MoeBatchArgs a) {
+    launch_dependents();
+    wait_prerequisite();
+    const int t = blockIdx.x, row = blockIdx.y * blockDim.x + threadIdx.x;
+    if (row >= a.H) return;
+    const int ns = a.nslot[t], KC = a.tc.KC;
+    float delta = 0.f;
+    for (int j = 0; j < ns; ++j) {
+        const int pj = a.pidx[(size_t)t * kMaxSlots + j];
+        float dj = 0.f;
+        for (int c = 0; c < KC; ++c) dj += a.down[((size_t)pj * KC + c) * a.H + row];
+        delta += a.sw[(size_t)t * kMaxSlots + j] * dj;
+    }
+    a.h_out[(size_t)t * a.H + row] = a.h_in[(size_t)t * a.H + row] + delta;
+}
+
+const void *moe_batch_kernel(int i) {
+    switch (i) {
+        case 0: return (const void *)k_batch_route;
+        case 1: return (const void *)k_batch_bucket;
+        case 2: return (const void *)k_batch_gu;
+        case 3: return (const void *)k_batch_down;
+        case 4: return (const void *)k_batch_combine;
+        default: return nullptr;
+    }
+}
+
 #ifdef RB_PHASE_TIMERS
 }  // namespace rb
 extern "C" __attribute__((visibility("default"))) int rabbit_cuda_debug_phase_ns(uint64_t *out,

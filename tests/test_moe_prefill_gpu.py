@@ -1,0 +1,139 @@
+"""GPU parity: the multi-token MoE path (rabbit_cuda_moe_prefill[_dev]) --
+T tokens through one layer's MoE block at once -- against the oracle's
+moe_step (forward_v2.c:362-402) run on each token alone.
+
+Bar: per token, top-k expert ids identical (tokens whose router scores hold a
+near-tie -- adjacent top-k+1 scores within 1e-6 of the largest -- excluded),
+routing weights, the MoE delta and h_out within rtol 1e-4 / atol 1e-5.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import ATOL, RTOL, near_tie, router_scores
+from rabbit_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = {
+    # name: H, E, k, I, S
+    "small_top4": (256, 16, 4, 128, 0),
+    "shared_experts": (256, 16, 3, 96, 2),
+    "w2_two_chunks": (128, 8, 2, 2048, 0),
+    "mixtral_like": (512, 8, 2, 1024, 0),
+}
+
+
+def make_pool(rc, H, E, k, I, S, seed, n_layers=1, quant=4):
+    recs, size, router, rms = synth.moe_layer(seed, H, E, I, S)
+    if quant == 0:
+        rng = np.random.default_rng(seed)
+        recs = np.concatenate([synth.f32_expert_record(rng, H, I) for _ in range(E + S)])
+        size = recs.size // (E + S)
+    pool = rc.MoePool(records=np.concatenate([recs] * n_layers), expert_size=size,
+                      n_layers=n_layers, hidden=H, n_experts=E, top_k=k, inter=I, n_shared=S,
+                      quant=quant, rms_ffn=[rms] * n_layers, w_router=[router] * n_layers)
+    kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=quant, n_records=E + S,
+              expert_size=size, records=recs, rms_ffn=rms, w_router=router)
+    return pool, kw
+
+
+def check_tokens(oracle, h, got_h, got_ids, got_w, kw, min_checked):
+    checked = 0
+    for t in range(h.shape[0]):
+        ref_h, ref_ids, ref_w = oracle.moe_step(h[t], **kw)
+        if near_tie(router_scores(oracle, h[t], kw["rms_ffn"], kw["w_router"]), len(ref_ids)):
+            continue
+        if got_ids is not None:
+            np.testing.assert_array_equal(got_ids[t], ref_ids, err_msg=f"token {t}: ids")
+            np.testing.assert_allclose(got_w[t], ref_w, rtol=RTOL, atol=ATOL,
+                                       err_msg=f"token {t}: weights")
+        np.testing.assert_allclose(got_h[t] - h[t], ref_h - h[t], rtol=RTOL, atol=ATOL,
+                                   err_msg=f"token {t}: MoE delta")
+        np.testing.assert_allclose(got_h[t], ref_h, rtol=RTOL, atol=ATOL,
+                                   err_msg=f"token {t}: h_out")
+        checked += 1
+    assert checked >= min_checked, f"only {checked} tokens free of near-ties"
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+@pytest.mark.parametrize("T", [1, 5, 33])
+def test_prefill_matches_oracle_per_token(rc, oracle, name, T):
+    H, E, k, I, S = SHAPES[name]
+    pool, kw = make_pool(rc, H, E, k, I, S, seed=sum(map(ord, name)) + T)
+    h = np.random.default_rng(T).standard_normal((T, H)).astype(np.float32)
+    got_h, ids, w = pool.prefill(0, h)
+    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=max(1, T - 2))
+    pool.free()
+
+
+def test_prefill_many_tokens_per_expert_and_decode_agree(rc, oracle):
+    """64 tokens over 8 experts top-2: ~16 tokens per expert, more than one
+    staged chunk of 8; the prefill equals the per-token decode on the GPU."""
+    H, E, k, I, S = 256, 8, 2, 256, 1
+    pool, kw = make_pool(rc, H, E, k, I, S, seed=77)
+    h = np.random.default_rng(5).standard_normal((64, H)).astype(np.float32)
+    got_h, ids, w = pool.prefill(0, h)
+    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=60)
+    for t in range(0, 64, 9):
+        dh, dids, dw = pool.decode(0, h[t])
+        np.testing.assert_allclose(got_h[t], dh, rtol=RTOL, atol=ATOL)
+        np.testing.assert_array_equal(ids[t], dids)
+    pool.free()
+
+
+def test_prefill_deepseek_shaped_layer(rc, oracle):
+    """hidden 2048, 64 routed experts top-6 + 2 shared, inter 1408 (W2 in two
+    column chunks of 704 inputs)."""
+    H, E, k, I, S = 2048, 64, 6, 1408, 2
+    pool, kw = make_pool(rc, H, E, k, I, S, seed=4)
+    h = np.random.default_rng(4).standard_normal((8, H)).astype(np.float32)
+    got_h, ids, w = pool.prefill(0, h)
+    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=7)
+    pool.free()
+
+
+def test_prefill_dev_in_place_and_second_layer(rc, oracle):
+    import torch
+
+    H, E, k, I, S = 256, 16, 4, 128, 0
+    recs, size, router, rms = synth.moe_layer(9, H, E, I, S)
+    router2 = np.ascontiguousarray(router[::-1])
+    pool = rc.MoePool(records=np.concatenate([recs, recs]), expert_size=size, n_layers=2,
+                      hidden=H, n_experts=E, top_k=k, inter=I, n_shared=S, quant=4,
+                      rms_ffn=[rms, rms], w_router=[router, router2])
+    h = np.random.default_rng(11).standard_normal((12, H)).astype(np.float32)
+    d = torch.from_numpy(h).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    pool.prefill_dev(1, d.data_ptr(), d.data_ptr(), 12, 0, 0, stream)  # h_out aliases h_in
+    pool.check(stream)
+    kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=4, n_records=E + S,
+              expert_size=size, records=recs, rms_ffn=rms, w_router=router2)
+    check_tokens(oracle, h, d.cpu().numpy(), None, None, kw, min_checked=10)
+    pool.free()
+
+
+def test_prefill_fp32_experts_run_per_token(rc, oracle):
+    """Records outside the group-32 layout take the per-token decode."""
+    H, E, k, I, S = 64, 4, 2, 32, 0
+    pool, kw = make_pool(rc, H, E, k, I, S, seed=3, quant=0)
+    h = np.random.default_rng(2).standard_normal((6, H)).astype(np.float32)
+    got_h, ids, w = pool.prefill(0, h)
+    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=5)
+    pool.free()
+
+
+def test_prefill_rejects_bad_arguments(rc):
+    H, E, k, I, S = 64, 4, 2, 64, 0
+    pool, _ = make_pool(rc, H, E, k, I, S, seed=1)
+    h = np.zeros((1, H), np.float32)
+    with pytest.raises(rc.RabbitCudaError, match="n_tokens"):
+        rc.check(rc.lib().rabbit_cuda_moe_prefill(pool.handle, 0, h.ctypes.data, h.ctypes.data,
+                                                  0, None, None))
+    with pytest.raises(rc.RabbitCudaError, match="n_tokens"):
+        rc.check(rc.lib().rabbit_cuda_moe_prefill(pool.handle, 0, h.ctypes.data, h.ctypes.data,
+                                                  257, None, None))
+    with pytest.raises(rc.RabbitCudaError, match="out of range"):
+        pool.prefill(3, h)
+    pool.free()
