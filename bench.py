@@ -367,6 +367,203 @@ def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True,
     return item
 
 
+# ------------------------------------------------------------ prefill chunk --
+# The DeepSeek-MoE-16B-shaped prefill chunk (MoE blocks): 28 layers, hidden
+# 2048, 64 routed experts top-6 + 2 shared, expert FFN 1408 SwiGLU int4
+# group-32, a 32-token chunk of random hidden states, layer to layer.
+DS = dict(L=28, H=2048, E=64, k=6, S=2, I=1408)
+DS_T = 32
+
+
+def prefill_item(capi, synth, peak: float, runs: int = 5, cpu: bool = True,
+                 layers: int | None = None) -> dict:
+    """rabbit_cuda_moe_prefill_dev over the 28 layers' MoE blocks for one
+    32-token chunk; bytes = the router plus every distinct expert the chunk
+    touches in each layer (counted from this chunk's routing)."""
+    import torch
+
+    L, H, E, k, S, I = layers or DS["L"], DS["H"], DS["E"], DS["k"], DS["S"], DS["I"]
+    rng = np.random.default_rng(SEED + 4)
+    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
+    size = synth.expert_record_size(H, I)
+    pool = capi.MoePool(records=None, expert_size=size, n_layers=L, hidden=H, n_experts=E,
+                        top_k=k, inter=I, n_shared=S, quant=4,
+                        rms_ffn=[np.ones(H, np.float32)] * L, w_router=routers)
+    pool.fill_synthetic(SEED * 1000 + 4)
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+    # each layer gets its own seeded N(0, 1) chunk (chained layers of random
+    # weights crowd the tokens onto a few experts)
+    hin = torch.from_numpy(rng.standard_normal((L, DS_T, H)).astype(np.float32)).cuda()
+    hout = torch.empty_like(hin)
+    ids = torch.zeros((L, DS_T, k), dtype=torch.int32, device="cuda")
+    wts = torch.zeros((L, DS_T, k), dtype=torch.float32, device="cuda")
+
+    def chunk(with_ids: bool):
+        for layer in range(L):
+            pool.prefill_dev(layer, hin[layer].data_ptr(), hout[layer].data_ptr(), DS_T,
+                             ids[layer].data_ptr() if with_ids else 0,
+                             wts[layer].data_ptr() if with_ids else 0, s)
+
+    chunk(True)
+    pool.check(s)
+    routed = ids.cpu().numpy()
+    distinct = [len(np.unique(routed[l])) for l in range(L)]
+    expert_bytes = 2 * synth.int4_nbytes(H * I) + synth.int4_nbytes(H * I)
+    chunk_bytes = sum(E * H * 4 + (d + S) * expert_bytes for d in distinct)
+    for _ in range(2):
+        chunk(False)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(runs):
+        chunk(False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    pool.check(s)
+    sec = ev0.elapsed_time(ev1) / 1e3 / runs
+    achieved = chunk_bytes / sec / 1e9
+    # end to end through the host-buffer entry point (H2D of the chunk, D2H of
+    # the layer outputs and routing, every layer)
+    hh = rng.standard_normal((DS_T, H)).astype(np.float32)
+    pool.prefill(0, hh)
+    t0 = time.perf_counter()
+    x = hh
+    for layer in range(L):
+        x = pool.prefill(layer, x)[0]
+    e2e = time.perf_counter() - t0
+    item = {
+        "metric": "MoE prefill chunk tokens/s (DeepSeek-MoE-16B-shaped, 32 tokens)",
+        "value": round(DS_T / sec, 1), "unit": "tokens/s",
+        "ms_per_chunk": round(sec * 1e3, 4),
+        "config": {"workload": (f"DeepSeek-MoE-16B-shaped MoE blocks: {L} layers, hidden {H}, "
+                                f"{E} routed experts top-{k} + {S} shared, inter {I}, "
+                                f"{DS_T}-token chunk; each layer's chunk seeded N(0, 1)"),
+                   "distinct_experts_per_layer": round(float(np.mean(distinct)), 2),
+                   "l2": f"inputs larger than L2 ({pool.stats()['pool_bytes'] / 1e9:.1f} GB of experts)",
+                   "note": "MoE blocks only (the routed-expert hot path); the chunk's attention "
+                           "is not in this line"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "bytes_per_chunk": chunk_bytes},
+        "e2e": {"value": round(DS_T / e2e, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": L * DS_T * H * 4,
+                "d2h_bytes_per_step": L * DS_T * (H * 4 + 2 * k * 4),
+                "api": "rabbit_cuda_moe_prefill (host buffers)"},
+        "gpu_launches_per_chunk": 5 * L,
+    }
+    pool.free()
+    if cpu:
+        chk, kind = cpu_checker()
+        recs, size2, router, rms = synth.moe_layer(SEED + 14, H, E, I, S)
+        kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=4, n_records=E + S,
+                  expert_size=size2, records=recs, rms_ffn=rms, w_router=router)
+        n, t_cpu = 0, 0.0
+        hs = rng.standard_normal((8, H)).astype(np.float32)
+        while t_cpu < 4.0 or n < 2:
+            t0 = time.perf_counter()
+            chk.moe_step(hs[n % 8], **kw)
+            t_cpu += time.perf_counter() - t0
+            n += 1
+        per_token_layer = t_cpu / n
+        item["cpu_baseline"] = {
+            "value": round(1.0 / (per_token_layer * L), 4), "unit": "tokens/s", "cores": 1,
+            "kind": kind,
+            "sample": f"{n} DeepSeek-shaped token-layers (moe_step, 1 thread), {t_cpu:.1f} s; "
+                      f"a token = {L} layers"}
+    return item
+
+
+# ------------------------------------------------------------ EP decode ------
+# Mixtral-8x22B-shaped decode, expert-parallel: 56 layers, hidden 6144, expert
+# FFN 16384, 8 experts top-2, int4 group-32 (84.5 GB of experts); a batch of
+# 64 decode tokens per step. Rank r of N holds experts e = r (mod N) of every
+# layer; per layer every rank routes all 64 tokens, applies its experts
+# (rabbit_cuda_moe_prefill_dev with rabbit_cuda_moe_set_expert_parallel), and
+# an all-reduce (sum, NCCL) of the shares gives the layer output.
+XL = dict(L=56, H=6144, E=8, k=2, I=16384)
+XL_T = 64
+
+
+def ep_item(capi, synth, peak: float, rank: int, world: int, dist, steps: int = 3,
+            layers: int | None = None) -> dict:
+    import torch
+
+    L, H, E, k, I = layers or XL["L"], XL["H"], XL["E"], XL["k"], XL["I"]
+    if E % world:
+        return {"unavailable": f"{E} experts do not split over {world} ranks"}
+    rng = np.random.default_rng(SEED + 5)  # the same routers and tokens on every rank
+    routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
+    size = synth.expert_record_size(H, I)
+    pool = capi.MoePool(records=None, expert_size=size, n_layers=L, hidden=H, n_experts=E,
+                        top_k=k, inter=I, quant=4, rms_ffn=[np.ones(H, np.float32)] * L,
+                        w_router=routers, experts_per_layer=E // world,
+                        device=torch.cuda.current_device())
+    pool.fill_synthetic(SEED * 1000 + 5 + rank)
+    if world > 1:
+        pool.set_expert_parallel(rank, world)
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+    # each layer gets its own seeded N(0, 1) batch: chained layers of random
+    # weights pull every token onto the same two experts, which real traffic
+    # does not do
+    hin = torch.from_numpy(rng.standard_normal((L, XL_T, H)).astype(np.float32)).cuda()
+    h = torch.empty((L, XL_T, H), dtype=torch.float32, device="cuda")
+    ids = torch.zeros((L, XL_T, k), dtype=torch.int32, device="cuda")
+    wts = torch.zeros((L, XL_T, k), dtype=torch.float32, device="cuda")
+
+    def step(with_ids: bool = False):
+        for layer in range(L):
+            pool.prefill_dev(layer, hin[layer].data_ptr(), h[layer].data_ptr(), XL_T,
+                             ids[layer].data_ptr() if with_ids else 0,
+                             wts[layer].data_ptr() if with_ids else 0, s)
+            if world > 1:
+                dist.all_reduce(h[layer])
+
+    step(True)
+    pool.check(s)
+    routed = ids.cpu().numpy()
+    distinct = [len(np.unique(routed[l])) for l in range(L)]
+    expert_bytes = 3 * synth.int4_nbytes(H * I)
+    step_bytes = sum(E * H * 4 + d * expert_bytes for d in distinct)  # whole job
+    step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    pool.check(s)
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sec = ms / 1e3 / steps
+    per_rank = step_bytes / world
+    pool.free()
+    return {
+        "metric": "EP MoE decode tokens/s (Mixtral-8x22B-shaped, batch 64)",
+        "value": round(XL_T / sec, 1), "unit": "tokens/s", "n_gpus": world,
+        "ms_per_step": round(sec * 1e3, 3), "steps": steps,
+        "config": {"workload": (f"Mixtral-8x22B-shaped MoE blocks: {L} layers, hidden {H}, "
+                                f"inter {I}, {E} experts top-{k}, batch {XL_T} decode tokens, "
+                                f"expert-parallel over {world} GPU(s), NCCL all-reduce of the "
+                                f"shares per layer; each layer's batch seeded N(0, 1)"),
+                   "experts_per_gpu_per_layer": E // world,
+                   "expert_bytes_per_gpu_gb": round(L * (E // world) * size / 1e9, 1),
+                   "distinct_experts_per_layer": round(float(np.mean(distinct)), 2),
+                   "note": "MoE blocks only (the routed-expert hot path); the attention and "
+                           "dense fp32 projections of the step are not in this line"},
+        "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_rank / sec / 1e9, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(per_rank / sec / 1e9 / peak, 4),
+                     "bytes_per_step_whole_job": step_bytes},
+        "scaling": "strong",
+    }
+
+
 # ------------------------------------------------------------ arms ---------
 def run_reference(args) -> None:
     """--impl reference: the reference's C on all host cores."""
@@ -423,6 +620,21 @@ def run_rabbit(args) -> None:
                                 device_id=torch.device("cuda", local))
     from rabbit_b200 import capi, synth
 
+    if args.ep_only:  # the expert-parallel decode item alone
+        item = ep_item(capi, synth, measured_peak()[0], rank, world, dist, layers=args.ep_layers)
+        if rank == 0:
+            print(json.dumps({"ep_decode": item}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
+    if args.prefill_only:  # the DeepSeek-shaped prefill chunk item alone (profiling)
+        if rank == 0:
+            item = prefill_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline,
+                                layers=args.prefill_layers)
+            print(json.dumps({"prefill": item}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     if args.full_decode_only:  # the OLMoE-shaped full decode item alone (profiling)
         if rank == 0:
             item = full_decode_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline,
@@ -510,7 +722,15 @@ def run_rabbit(args) -> None:
         e2e_s = float(t.item())
     e2e_value = world * step_bytes * e2e_steps / e2e_s / 1e9
 
+    pool_stats = pool.stats()
+    pool.free()  # the items below need the room (the EP item holds 84.5 GB at N = 1)
+    ep = None
+    if not args.no_ep:
+        ep = ep_item(capi, synth, measured_peak()[0], rank, world, dist, layers=args.ep_layers)
     gemv = None if args.no_gemv else gemv_item(capi, synth, stream, measured_peak()[0])
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline)
     full = None
     if world == 1 and not args.no_full_decode:
         full = full_decode_item(capi, synth, measured_peak()[0], cpu=not args.no_cpu_baseline)
@@ -527,9 +747,9 @@ def run_rabbit(args) -> None:
             "dtype": "u4 weights, f32 math", "data": "synthetic",
             "config": {"workload": WORKLOAD.format(L), "hidden": H, "inter": I, "experts": E,
                        "top_k": TOPK, "layers_per_step": L, "batch": 1,
-                       "expert_bytes_resident_gb": round(pool.stats()["pool_bytes"] / 1e9, 2),
+                       "expert_bytes_resident_gb": round(pool_stats["pool_bytes"] / 1e9, 2),
                        "l2": (f"inputs larger than L2 ({L} distinct layers, "
-                              f"{pool.stats()['pool_bytes'] / 1e9:.1f} GB of experts)"),
+                              f"{pool_stats['pool_bytes'] / 1e9:.1f} GB of experts)"),
                        "parallelism": f"dp{world} decode replicas" if world > 1 else "single"},
             "tokens_per_s": round(world * args.steps / secs, 2),
             "us_per_token_layer": round(1e6 * secs / launches, 3),
@@ -546,11 +766,12 @@ def run_rabbit(args) -> None:
             "gpu_launches": launches,
             "gemv": gemv,
             "full_decode": full,
+            "prefill": prefill,
+            "ep_decode": ep,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    pool.free()
     if dist:
         dist.destroy_process_group()
 
@@ -567,6 +788,15 @@ def main(argv=None) -> int:
     ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV line item")
     ap.add_argument("--no-full-decode", action="store_true",
                     help="skip the OLMoE-shaped full decode line item")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the DeepSeek-shaped prefill chunk line item")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the prefill chunk item (profiling cases)")
+    ap.add_argument("--prefill-layers", type=int, default=None, help="prefill chunk: layers")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel decode item")
+    ap.add_argument("--ep-only", action="store_true",
+                    help="run only the expert-parallel decode item (profiling cases)")
+    ap.add_argument("--ep-layers", type=int, default=None, help="EP decode: layers")
     ap.add_argument("--full-decode-only", action="store_true",
                     help="run only the full decode item (profiling cases)")
     ap.add_argument("--fd-layers", type=int, default=None, help="full decode: layers")

@@ -200,6 +200,17 @@ int rabbit_cuda_moe_prefill_dev(rabbit_cuda_moe *p, int layer, const float *d_h_
 /* Same on HOST buffers; synchronous. */
 int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
                             int n_tokens, int *ids, float *weights);
+/* Expert parallelism for the multi-token path (no counterpart in the
+ * reference): this pool holds rank `rank`'s share of a layer whose E routed
+ * experts are spread over `size` ranks -- expert e lives on rank e % size as
+ * local record e / size of each layer -- followed by the S shared experts,
+ * so experts_per_layer must be E / size + S. Routing is computed in full on
+ * every rank; rabbit_cuda_moe_prefill[_dev] then writes rank 0: h + its
+ * experts' share (shared experts included), other ranks: their experts'
+ * share only, so the sum of the ranks' outputs (an all-reduce) is the layer
+ * output. ids / weights report the full routing. size 1 (the default) is the
+ * whole layer. Decode calls on a pool with size > 1 are refused. */
+int rabbit_cuda_moe_set_expert_parallel(rabbit_cuda_moe *p, int rank, int size);
 /* Check the device error word after work on `stream` finished (TIMEOUT if a
  * bounded wait gave up). Synchronises `stream`. */
 int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);

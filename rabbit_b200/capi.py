@@ -77,6 +77,7 @@ SIGNATURES = {
     "rabbit_cuda_moe_decode_bytes": (C.c_uint64, [_P]),
     "rabbit_cuda_moe_prefill_dev": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
     "rabbit_cuda_moe_prefill": (_I, [_P, _I, _P, _P, _I, _P, _P]),
+    "rabbit_cuda_moe_set_expert_parallel": (_I, [_P, _I, _I]),
     "rabbit_cuda_refv2_create": (_I, [C.POINTER(DenseDesc), _P, C.POINTER(_P)]),
     "rabbit_cuda_refv2_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_refv2_free": (_I, [_P]),
@@ -252,6 +253,10 @@ class MoePool:
         check(lib().rabbit_cuda_moe_prefill(self.handle, layer, _ptr(h), _ptr(out), T, _ptr(ids),
                                             _ptr(w)))
         return out, ids, w
+
+    def set_expert_parallel(self, rank: int, size: int) -> None:
+        """This pool holds rank `rank`'s experts (e % size == rank) of `size`."""
+        check(lib().rabbit_cuda_moe_set_expert_parallel(self.handle, rank, size))
 
     def prefill_dev(self, layer: int, d_h_in: int, d_h_out: int, n_tokens: int, d_ids: int = 0,
                     d_w: int = 0, stream: int = 0) -> None:

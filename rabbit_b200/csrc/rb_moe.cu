@@ -83,6 +83,7 @@ struct rabbit_cuda_moe {
     int *bt_ids = nullptr;   // [bt_cap][8] routing of host-buffer calls
     float *bt_w = nullptr;   // [bt_cap][8]
     float *bt_pin = nullptr; // pinned [bt_cap][H] + ids/weights
+    int ep_rank = 0, ep_size = 1;  // expert-parallel share of the multi-token path
     // counters
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
     std::vector<uint8_t> img;  // host image of one record in the tiled layout
@@ -554,6 +555,9 @@ namespace rb {
 // kernel records a failed wait in.
 static int decode_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
                        int *d_ids, float *d_weights, cudaStream_t s, int *err) {
+    if (p->ep_size > 1)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_decode: expert-parallel pools run the multi-token path");
     int base, n_local;
     int st = layer_map(p, layer, &base, &n_local);
     if (st) return st;
@@ -681,6 +685,9 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     if (!p->fast)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_decode_noalloc: pool is not in the group-32 fused layout");
+    if (p->ep_size > 1)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_decode_noalloc: expert-parallel pools run the multi-token path");
     if ((reinterpret_cast<uintptr_t>(d_h_in) & 15) || (reinterpret_cast<uintptr_t>(d_h_out) & 15))
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: h must be 16-byte aligned");
     const size_t off_flags = 256;
@@ -806,7 +813,10 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t o_ns = take(sizeof(int) * cap);
     const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
     const size_t o_pt = take(sizeof(int) * P);
-    const size_t o_act = take(sizeof(int) * R * 3 + sizeof(int));
+    const size_t U = P + R;  // work units: at most one per pair, plus one partial per record
+    const size_t o_act = take(sizeof(int) * U * 3 + sizeof(int));
+    const size_t o_sc = take(sizeof(float) * cap * p->E);
+    const size_t o_tc = take(sizeof(unsigned) * cap);
     const size_t o_mid = take(sizeof(float) * P * p->I);
     const size_t o_down = take(sizeof(float) * P * KC * p->H);
     const size_t o_h = take(sizeof(float) * cap * p->H);
@@ -816,6 +826,11 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     float *pin = nullptr;
     cudaError_t e = cudaMalloc(&blk, off);
     if (e != cudaSuccess) return cuda_fail(e, "moe_prefill: scratch");
+    if ((e = cudaMemset(static_cast<uint8_t *>(blk) + o_tc, 0, sizeof(unsigned) * cap)) !=
+        cudaSuccess) {
+        cudaFree(blk);
+        return cuda_fail(e, "moe_prefill: scratch");
+    }
     if ((e = cudaMallocHost(&pin, sizeof(float) * ((size_t)cap * p->H + 2 * (size_t)cap * 8))) !=
         cudaSuccess) {
         cudaFree(blk);
@@ -834,9 +849,11 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     a.pidx = reinterpret_cast<int *>(b + o_pidx);
     a.pair_t = reinterpret_cast<int *>(b + o_pt);
     a.act = reinterpret_cast<int *>(b + o_act);
-    a.act_off = a.act + R;
-    a.act_cnt = a.act_off + R;
-    a.n_act = a.act_cnt + R;
+    a.act_off = a.act + U;
+    a.act_cnt = a.act_off + U;
+    a.n_act = a.act_cnt + U;
+    a.scores = reinterpret_cast<float *>(b + o_sc);
+    a.tcount = reinterpret_cast<unsigned *>(b + o_tc);
     a.mid = reinterpret_cast<float *>(b + o_mid);
     a.down = reinterpret_cast<float *>(b + o_down);
     p->bt_h = reinterpret_cast<float *>(b + o_h);
@@ -872,6 +889,9 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
         if (!p->resident[base + r])
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: layer %d not uploaded", layer);
     RB_CUDA(cudaSetDevice(p->device));
+    if (!p->fast && p->ep_size > 1)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_prefill: expert-parallel pools need the group-32 layout");
     if (!p->fast) {  // other record formats: the per-token decode, token by token
         for (int t = 0; t < T; ++t) {
             st = decode_impl(p, layer, d_h_in + (size_t)t * p->H, d_h_out + (size_t)t * p->H,
@@ -884,19 +904,40 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     if ((st = ensure_batch(p, T)) != RABBIT_CUDA_OK) return st;
     const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (T + 31) / 32;
     const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 2 * sizeof(int) * R;
-    const size_t gu_x = sizeof(float) * (size_t)(p->H / 32) * 33;  // one token's padded xn
-    const size_t gu_tile = align_up(p->plan.tb.tile_bytes, 16);
-    const size_t dn_x = sizeof(float) * (size_t)(p->plan.tc.cols / 32) * 33;
-    const size_t dn_tile = align_up(p->plan.tc.tile_bytes, 16);
-    const size_t cap = kMaxDynSmem / 2 - 1024;  // two CTAs per SM
-    if (bucket_smem > (size_t)kMaxDynSmem || gu_tile + gu_x > (size_t)kMaxDynSmem)
+    // gate/up and down: two tile buffers + the staged tokens; chunk = tokens
+    // per pass, two CTAs per SM when four or more tokens still fit
+    // the batch kernels' static shared memory (mbarriers, reductions) stays
+    // under 1 KB: dynamic sizes leave that room
+    constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
+    auto pick = [](size_t fixed, size_t per, int *chunk, int *per_sm) {
+        const size_t two = (size_t)kMaxDynSmem / 2 - 2048;
+        const int c2 = fixed < two ? (int)std::min<size_t>(kBatchTokChunk, (two - fixed) / per) : 0;
+        if (c2 >= 4) {
+            *chunk = c2;
+            *per_sm = 2;
+            return fixed + (size_t)c2 * per;
+        }
+        const int c1 = fixed < kBatchDynMax
+                           ? (int)std::min<size_t>(kBatchTokChunk, (kBatchDynMax - fixed) / per)
+                           : 0;
+        *chunk = c1;
+        *per_sm = 1;
+        return fixed + (size_t)std::max(c1, 0) * per;
+    };
+    int gu_chunk, gu_per_sm, dn_chunk, dn_per_sm;
+    // one token's activations: 36 floats per group of 32 (see k_batch_gu)
+    const size_t gu_smem = pick(2 * align_up(p->plan.tb.tile_bytes, 128),
+                                sizeof(float) * (size_t)(p->H / 32) * 36, &gu_chunk, &gu_per_sm);
+    const size_t dn_smem = pick(2 * align_up(p->plan.tc.tile_bytes, 128),
+                                sizeof(float) * (size_t)(p->plan.tc.cols / 32) * 36, &dn_chunk,
+                                &dn_per_sm);
+    if (bucket_smem > kBatchDynMax || gu_chunk < 1 || dn_chunk < 1)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
-    const int gu_chunk = (int)std::min<size_t>(
-        kBatchTokChunk, std::max<size_t>(1, ((gu_tile + kBatchTokChunk * gu_x <= cap ? cap : (size_t)kMaxDynSmem) - gu_tile) / gu_x));
     if (!g_batch_attr[p->device]) {
-        for (int i = 1; i <= 3; ++i)
+        for (int i = 0; i <= 3; ++i)
             RB_CUDA(cudaFuncSetAttribute(moe_batch_kernel(i),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kBatchDynMax));
         g_batch_attr[p->device] = true;
     }
     MoeBatchArgs a = p->bt;
@@ -921,10 +962,17 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     a.tb = p->plan.tb;
     a.tc = p->plan.tc;
     a.chunk_gu = gu_chunk;
-    RB_CUDA(launch_batch(0, dim3(T), dim3(256), sizeof(float) * (size_t)p->E, s, a));
+    a.chunk_down = dn_chunk;
+    a.err = p->ctx->d_err;
+    a.wait_ns = wait_limit_ns();
+    a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
+    a.ep_rank = p->ep_rank;
+    a.ep_size = p->ep_size;
+    RB_CUDA(launch_batch(0, dim3(T, (p->E + a.route_split - 1) / a.route_split), dim3(256),
+                         sizeof(float) * (size_t)std::max(p->E, p->H), s, a));
     RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
-    RB_CUDA(launch_batch(2, dim3(2 * sms), dim3(256), gu_tile + (size_t)gu_chunk * gu_x, s, a));
-    RB_CUDA(launch_batch(3, dim3(2 * sms), dim3(256), dn_tile + (size_t)kBatchTokChunk * dn_x, s, a));
+    RB_CUDA(launch_batch(2, dim3(sms), dim3(kBatchThreads), gu_smem, s, a));
+    RB_CUDA(launch_batch(3, dim3(sms), dim3(kBatchThreads), dn_smem, s, a));
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
     p->hbm_hits += T;
     return ok();
@@ -942,6 +990,20 @@ int rabbit_cuda_moe_prefill_dev(rabbit_cuda_moe *p, int layer, const float *d_h_
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: pass both ids and weights, or neither");
     return prefill_impl(p, layer, d_h_in, d_h_out, n_tokens, d_ids, d_weights,
                         as_stream(stream, p->ctx));
+}
+
+int rabbit_cuda_moe_set_expert_parallel(rabbit_cuda_moe *p, int rank, int size) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_expert_parallel: NULL pool");
+    if (size < 1 || rank < 0 || rank >= size)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_expert_parallel: rank %d of %d", rank, size);
+    if (size > 1 && (p->E % size || p->shared_table || p->epl != p->E / size + p->S))
+        return fail(RABBIT_CUDA_ERR_ARGS,
+                    "moe_set_expert_parallel: need E (%d) a multiple of %d and %d records per "
+                    "layer (E / size routed + %d shared)",
+                    p->E, size, p->E / std::max(size, 1) + p->S, p->S);
+    p->ep_rank = rank;
+    p->ep_size = size;
+    return ok();
 }
 
 int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,

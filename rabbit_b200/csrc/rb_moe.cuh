@@ -66,17 +66,20 @@ inline bool combine_packed(int KC) { return KC < 8; }
 // T tokens through one layer's MoE block, each as moe_step (forward_v2.c:
 // 362-402) would take it alone, with every active expert's tiles read once for
 // all the tokens routed to it:
-//   k_batch_route   one CTA per token: rmsnorm -> xn, router, top-k, slots;
+//   k_batch_route   grid (token, router slice): rmsnorm, the slice's router
+//                   rows; the token's last CTA to finish: top-k, slots;
 //   k_batch_bucket  one CTA: per local record, the (token, slot) pairs that
-//                   use it, in token order (bitmask ranks: deterministic);
-//   k_batch_gu      (active record, GU tile) items: mid = silu(gate) * up for
-//                   the record's tokens, 8 staged in shared memory at a time;
-//   k_batch_down    (active record, D tile) items: each column chunk's down
-//                   rows per pair;
+//                   use it, in token order (bitmask ranks: deterministic),
+//                   cut into units of at most kBatchTokChunk pairs;
+//   k_batch_gu      (unit, GU tile) items: mid = silu(gate) * up for the
+//                   unit's tokens;
+//   k_batch_down    (unit, D tile) items: each column chunk's down rows per
+//                   pair;
 //   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
 //                   order (forward_v2.c:356-357, 398-399).
 constexpr int kMaxBatchTokens = 256;
 constexpr int kBatchTokChunk = 8;  // tokens per pass over a staged tile
+constexpr int kBatchThreads = 512;  // threads of k_batch_gu / k_batch_down
 struct MoeBatchArgs {
     const float *h_in;
     float *h_out;
@@ -88,7 +91,9 @@ struct MoeBatchArgs {
     uint64_t rec_stride, off_d;
     int rec_base, n_local, H, E, k, I, S, usable;
     Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
-    int chunk_gu;    // tokens staged per pass of k_batch_gu (<= kBatchTokChunk)
+    int chunk_gu, chunk_down;  // tokens staged per pass of k_batch_gu / _down (<= 8)
+    int *err;                  // device error word (RB_ERR_TIMEOUT)
+    uint64_t wait_ns;          // bound of every wait
     // scratch
     float *xn;       // [T][H]
     int *srec;       // [T][kMaxSlots] global record per slot
@@ -96,8 +101,13 @@ struct MoeBatchArgs {
     int *nslot;      // [T]
     int *pidx;       // [T][kMaxSlots] pair index of (token, slot)
     int *pair_t;     // [P] token of pair
-    int *act, *act_off, *act_cnt;  // [n_local] active records: global id, first pair, pairs
-    int *n_act;      // [1]
+    int *act, *act_off, *act_cnt;  // [units] work units (record, <= kBatchTokChunk of its
+                                   // pairs): global record id, first pair, pairs
+    int *n_act;      // [1] units
+    float *scores;   // [T][E] router scores
+    unsigned *tcount;  // [T] router CTAs done per token (zero between launches)
+    int route_split;   // router rows per CTA of k_batch_route
+    int ep_rank, ep_size;  // expert-parallel share (1 rank: the whole layer)
     float *mid;      // [P][I]
     float *down;     // [P][tc.KC][H]
 };

@@ -903,18 +903,22 @@ const void *moe_fused_kernel(int JB, int JC, bool packed) {
 }
 
 // ======================================================= multi-token path ==
+// Grid (T, ceil(E / route_split)): CTA (t, y) scores router rows
+// [y route_split, (y + 1) route_split) of token t; the token's last CTA to
+// finish ranks all E scores and writes the slot list.
 __global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
-    extern __shared__ __align__(16) float s_sc[];  // [E] router scores
+    extern __shared__ __align__(16) float s_sc[];  // [E] router scores (last CTA)
     __shared__ float red[32];
     __shared__ int s_rec[kMaxSlots];
     __shared__ float s_w[kMaxSlots];
+    __shared__ bool last;
     launch_dependents();
     wait_prerequisite();
     const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int t = blockIdx.x, H = a.H;
     const float *h = a.h_in + (size_t)t * H;
     float *xn = a.xn + (size_t)t * H;
-    // rmsnorm (forward_v2.c:61-69)
+    // rmsnorm (forward_v2.c:61-69), in every CTA of the token; CTA 0 stores xn
     float ss = 0.f;
     for (int i = tid; i < H; i += nthr) ss += h[i] * h[i];
     ss = warp_sum(ss);
@@ -927,23 +931,45 @@ __global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
     }
     __syncthreads();
     const float inv = red[31];
-    for (int i = tid; i < H; i += nthr) xn[i] = (h[i] * inv) * a.rms[i];
+    float *xs = s_sc;  // xn staged here first ([H] fits: the launch gives max(E, H) floats)
+    for (int i = tid; i < H; i += nthr) {
+        const float v = (h[i] * inv) * a.rms[i];
+        xs[i] = v;
+        if (blockIdx.y == 0) xn[i] = v;
+    }
     __syncthreads();
-    // router scores (forward_v2.c:71-79, :378): a warp per expert row
-    for (int e = warp; e < a.E; e += nthr >> 5) {
+    // this CTA's router rows (forward_v2.c:71-79, :378): a warp per row, 16
+    // float4 loads per lane in flight
+    const int e0 = blockIdx.y * a.route_split, e1 = min(a.E, e0 + a.route_split);
+    for (int e = e0 + warp; e < e1; e += nthr >> 5) {
         const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
-        const float4 *x4 = reinterpret_cast<const float4 *>(xn);
+        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
         float d = 0.f;
-        for (int i4 = lane; i4 < (H >> 2); i4 += 32) {
-            const float4 w = wr[i4], x = x4[i4];
-            d = fmaf(w.x, x.x, d);
-            d = fmaf(w.y, x.y, d);
-            d = fmaf(w.z, x.z, d);
-            d = fmaf(w.w, x.w, d);
+        for (int b = lane; b < (H >> 2); b += 32 * 16) {
+            float4 w[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (b + 32 * u < (H >> 2)) w[u] = __ldg(wr + b + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (b + 32 * u < (H >> 2)) {
+                    const float4 x = x4[b + 32 * u];
+                    d = fmaf(w[u].x, x.x, d);
+                    d = fmaf(w[u].y, x.y, d);
+                    d = fmaf(w[u].z, x.z, d);
+                    d = fmaf(w[u].w, x.w, d);
+                }
         }
         d = warp_sum(d);
-        if (lane == 0) s_sc[e] = d;
+        if (lane == 0) a.scores[(size_t)t * a.E + e] = d;
     }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(a.tcount + t, 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int e = tid; e < a.E; e += nthr) s_sc[e] = __ldcg(a.scores + (size_t)t * a.E + e);
     __syncthreads();
     int *ids = reinterpret_cast<int *>(red);
     float *w = red + 8;
@@ -954,12 +980,34 @@ __global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
                 a.ids_out[(size_t)t * a.k + i] = ids[i];
                 a.w_out[(size_t)t * a.k + i] = w[i];
             }
-        const int n = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+        int n = 0;
+        if (a.ep_size <= 1) {
+            n = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+        } else if (a.usable) {
+            // expert-parallel: this rank holds routed experts e = ep_rank (mod
+            // ep_size) as local records e / ep_size, then the shared experts;
+            // rank 0 alone applies the shared ones
+            const int e_loc = a.E / a.ep_size;
+            for (int i = 0; i < a.k; ++i)
+                if (ids[i] >= 0 && ids[i] % a.ep_size == a.ep_rank && ids[i] / a.ep_size < a.n_local) {
+                    s_rec[n] = a.rec_base + ids[i] / a.ep_size;
+                    s_w[n] = w[i];
+                    ++n;
+                }
+            if (a.ep_rank == 0)
+                for (int sh = 0; sh < a.S; ++sh)
+                    if (e_loc + sh < a.n_local) {
+                        s_rec[n] = a.rec_base + e_loc + sh;
+                        s_w[n] = 1.0f;
+                        ++n;
+                    }
+        }
         a.nslot[t] = n;
         for (int j = 0; j < n; ++j) {
             a.srec[(size_t)t * kMaxSlots + j] = s_rec[j];
             a.sw[(size_t)t * kMaxSlots + j] = s_w[j];
         }
+        a.tcount[t] = 0u;  // ready for the next launch
     }
 }
 
@@ -989,19 +1037,19 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
         cnt[r] = c;
     }
     __syncthreads();
-    if (tid == 0) {
-        int o = 0, na = 0;
+    if (tid == 0) {  // units: each record's pairs cut into runs of <= kBatchTokChunk
+        int o = 0, nu = 0;
         for (int r = 0; r < R; ++r) {
             off[r] = o;
-            if (cnt[r]) {
-                a.act[na] = a.rec_base + r;
-                a.act_off[na] = o;
-                a.act_cnt[na] = cnt[r];
-                ++na;
+            for (int c0 = 0; c0 < cnt[r]; c0 += kBatchTokChunk) {
+                a.act[nu] = a.rec_base + r;
+                a.act_off[nu] = o + c0;
+                a.act_cnt[nu] = min(kBatchTokChunk, cnt[r] - c0);
+                ++nu;
             }
             o += cnt[r];
         }
-        *a.n_act = na;
+        *a.n_act = nu;
     }
     __syncthreads();
     for (int q = tid; q < Q; q += nthr) {
@@ -1018,60 +1066,120 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
     }
 }
 
-// Stage `bytes` (a multiple of 4) from global to shared memory.
-__device__ __forceinline__ void stage_words(uint8_t *dst, const uint8_t *src, uint32_t bytes) {
-    const int tid = threadIdx.x, nthr = blockDim.x;
-    const uint32_t n16 = bytes >> 4;
-    for (uint32_t i = tid; i < n16; i += nthr)
-        reinterpret_cast<uint4 *>(dst)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
-    for (uint32_t i = (n16 << 2) + tid; i < (bytes >> 2); i += nthr)
-        reinterpret_cast<uint32_t *>(dst)[i] = __ldg(reinterpret_cast<const uint32_t *>(src) + i);
-}
+// Activations staged for a lane-per-group reader: group g of 32 floats at
+// g * kXP floats, so a warp's float4 reads (lane g, elements 4i..4i+3) fall in
+// distinct banks within each quarter warp.
+constexpr int kXP = 36;
+__device__ __forceinline__ int xpad36(int e) { return (e >> 5) * kXP + (e & 31); }
 
-// 32 weights of one group: nibble n of byte b (low nibble = even element,
-// q = nibble - 8) times the group scale (quant.c:171-185).
-__device__ __forceinline__ void dequant32(const uint8_t *nib, float scale, float (&wq)[32]) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(nib);
-    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+// Stage rows of `n` floats (n a multiple of 4, rows 16-byte aligned) of
+// `nrows` sources into shared memory in that layout: all of a thread's loads
+// are issued before its stores.
+template <typename RowPtr>
+__device__ __forceinline__ void stage_rows_padded(float *dst, int dstride, int nrows, int n,
+                                                  RowPtr row) {
+    const int tid = threadIdx.x, nthr = blockDim.x, n4 = n >> 2;
+    const int total = nrows * n4;
+    for (int base = 0; base < total; base += 8 * nthr) {
+        float4 v[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const uint32_t byte = (words[q] >> (8 * b)) & 0xFFu;
-            wq[8 * q + 2 * b] = (float)((int)(byte & 15u) - 8) * scale;
-            wq[8 * q + 2 * b + 1] = (float)((int)(byte >> 4) - 8) * scale;
+        for (int u = 0; u < 8; ++u) {
+            const int q = base + u * nthr + tid;
+            if (q < total) {
+                const int r = q / n4, c = q - r * n4;
+                v[u] = __ldcg(reinterpret_cast<const float4 *>(row(r)) + c);
+            }
         }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int q = base + u * nthr + tid;
+            if (q < total) {
+                const int r = q / n4, e = (q - r * n4) * 4;
+                *reinterpret_cast<float4 *>(dst + r * dstride + xpad36(e)) = v[u];
+            }
+        }
+    }
 }
 
-// (active record, GU tile) work items; a warp per gate/up row pair, a lane
-// per group of 32 inputs; the tokens' xn staged 8 at a time in the padded
-// layout (33 floats per group: lane g and element e hit bank (g + e) % 32).
-__global__ void __launch_bounds__(256) k_batch_gu(MoeBatchArgs a) {
+// Four weights 4i..4i+3 of a group held as 16 bytes (low nibble = even
+// element, q = nibble - 8) times the group scale (quant.c:171-185).
+__device__ __forceinline__ void nib_weight4(const uint4 &v, int i, float scale, float (&w)[4]) {
+    const uint32_t word = i < 2 ? v.x : i < 4 ? v.y : i < 6 ? v.z : v.w;
+    const uint32_t n = word >> (16 * (i & 1));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = (float)((int)((n >> (4 * j)) & 15u) - 8) * scale;
+}
+
+// The ring of two tile buffers of the batch kernels: thread 0 bulk-copies the
+// tile of item k + 1 while item k is computed. Buffer b's j-th copy completes
+// phase j & 1 of full[b].
+struct TileRing {
+    uint8_t *buf[2];
+    uint64_t *full;
+};
+__device__ __forceinline__ void ring_issue(const TileRing &r, int k, const uint8_t *src,
+                                           uint32_t bytes) {
+    const int b = k & 1;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
+    mbar_arrive_expect_tx(&r.full[b], bytes);
+    bulk_g2s(r.buf[b], src, bytes, &r.full[b], policy_evict_first());
+}
+
+// (active record, GU tile) work items in contiguous ranges per CTA, so that
+// consecutive items mostly share a record and its staged tokens. A warp per
+// gate/up row pair, a lane per group of 32 inputs, tokens chunk_gu at a time.
+__global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    launch_dependents();
-    wait_prerequisite();
+    __shared__ __align__(8) uint64_t full[2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
     const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
-    const size_t half = (size_t)H / 2;
-    const int xstride = G * 33;
-    uint8_t *tile = smem;
-    float *xs = reinterpret_cast<float *>(smem + align_up(a.tb.tile_bytes, 16));
-    const int na = *a.n_act;
-    for (int item = blockIdx.x; item < na * ntb; item += gridDim.x) {
+    const size_t half = (size_t)H / 2, tsz = align_up(a.tb.tile_bytes, 128);
+    const int xstride = G * kXP;
+    TileRing ring{{smem, smem + tsz}, full};
+    float *xs = reinterpret_cast<float *>(smem + 2 * tsz);
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    launch_dependents();
+    wait_prerequisite();
+    const int n = *a.n_act * ntb;
+    const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
+    const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
+    auto src_of = [&](int item) {
+        const int ai = item / ntb, tt = item - ai * ntb;
+        return a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt * a.tb.tile_stride;
+    };
+    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tb.tile_bytes);
+    int st_ai = -1, st_c0 = -1;  // the record / token chunk staged in xs
+    for (int k = 0, item = i0; item < i1; ++k, ++item) {
+        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target)
+        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tb.tile_bytes);
+        const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+        if (__syncthreads_or(!okw)) {  // drain what was issued, then leave
+            if (tid == 0) {  // copies in flight must land before the CTA leaves
+                if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+                if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
+            }
+            return;
+        }
+        const uint8_t *tile = ring.buf[k & 1];
         const int ai = item / ntb, tt = item - ai * ntb;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        __syncthreads();  // the last item's readers are done with the tile
-        stage_words(tile, a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt * a.tb.tile_stride,
-                    a.tb.tile_bytes);
         const float *gsc = reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half);
         for (int c0 = 0; c0 < m; c0 += a.chunk_gu) {
             const int mc = min(a.chunk_gu, m - c0);
-            if (c0 > 0) __syncthreads();
-            for (int i = tid; i < mc * H; i += blockDim.x) {
-                const int ti = i / H, e = i - ti * H;
-                xs[ti * xstride + xpad(e)] = a.xn[(size_t)a.pair_t[off + c0 + ti] * H + e];
+            if (st_ai != ai || st_c0 != c0) {
+                if (st_ai >= 0) __syncthreads();  // every warp is done with the old tokens
+                stage_rows_padded(xs, xstride, mc, H, [&](int r) {
+                    return a.xn + (size_t)a.pair_t[off + c0 + r] * H;
+                });
+                __syncthreads();
+                st_ai = ai;
+                st_c0 = c0;
             }
-            __syncthreads();
             for (int r = warp; r < TR; r += nwarp) {
                 const int row = tt * TR + r;
                 if (row >= I) break;
@@ -1079,18 +1187,28 @@ __global__ void __launch_bounds__(256) k_batch_gu(MoeBatchArgs a) {
 #pragma unroll
                 for (int q = 0; q < kBatchTokChunk; ++q) gs[q] = us[q] = 0.f;
                 for (int g = lane; g < G; g += 32) {
-                    float gq[32], uq[32];
-                    dequant32(tile + (size_t)r * half + (size_t)g * 16, gsc[(size_t)r * G + g], gq);
-                    dequant32(tile + (size_t)(TR + r) * half + (size_t)g * 16,
-                              gsc[(size_t)(TR + r) * G + g], uq);
+                    const uint4 gw = *reinterpret_cast<const uint4 *>(tile + (size_t)r * half + (size_t)g * 16);
+                    const uint4 uw =
+                        *reinterpret_cast<const uint4 *>(tile + (size_t)(TR + r) * half + (size_t)g * 16);
+                    const float gsv = gsc[(size_t)r * G + g], usv = gsc[(size_t)(TR + r) * G + g];
+                    const float *xb = xs + g * kXP;
+#pragma unroll 2
+                    for (int i = 0; i < 8; ++i) {  // elements 4i .. 4i + 3, in order
+                        float wg[4], wu[4];
+                        nib_weight4(gw, i, gsv, wg);
+                        nib_weight4(uw, i, usv, wu);
 #pragma unroll
-                    for (int q = 0; q < kBatchTokChunk; ++q) {
-                        if (q < mc) {
-                            const float *x = xs + q * xstride + g * 33;
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                gs[q] = fmaf(gq[e], x[e], gs[q]);
-                                us[q] = fmaf(uq[e], x[e], us[q]);
+                        for (int q = 0; q < kBatchTokChunk; ++q) {
+                            if (q < mc) {
+                                const float4 x = *reinterpret_cast<const float4 *>(xb + q * xstride + 4 * i);
+                                gs[q] = fmaf(wg[0], x.x, gs[q]);
+                                gs[q] = fmaf(wg[1], x.y, gs[q]);
+                                gs[q] = fmaf(wg[2], x.z, gs[q]);
+                                gs[q] = fmaf(wg[3], x.w, gs[q]);
+                                us[q] = fmaf(wu[0], x.x, us[q]);
+                                us[q] = fmaf(wu[1], x.y, us[q]);
+                                us[q] = fmaf(wu[2], x.z, us[q]);
+                                us[q] = fmaf(wu[3], x.w, us[q]);
                             }
                         }
                     }
@@ -1107,38 +1225,64 @@ __global__ void __launch_bounds__(256) k_batch_gu(MoeBatchArgs a) {
     }
 }
 
-// (active record, D tile) work items: tile (chunk c, row tile t) of W2; a
-// warp per row, a lane per group of the chunk; the pairs' mid chunks staged 8
-// at a time.
-__global__ void __launch_bounds__(256) k_batch_down(MoeBatchArgs a) {
+// (active record, D tile) work items in contiguous ranges per CTA: tile
+// (chunk c, row tile t) of W2; a warp per row, a lane per group of the chunk;
+// the pairs' mid chunks staged chunk_down at a time.
+__global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    launch_dependents();
-    wait_prerequisite();
+    __shared__ __align__(8) uint64_t full[2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
     const int H = a.H, I = a.I, TR = a.tc.TR, ntc = a.tc.ntiles, rt = a.tc.rtiles, KC = a.tc.KC;
     const int cols = a.tc.cols, Gc = cols / 32;
-    const size_t chalf = (size_t)cols / 2;
-    const int xstride = Gc * 33;
-    uint8_t *tile = smem;
-    float *ms = reinterpret_cast<float *>(smem + align_up(a.tc.tile_bytes, 16));
-    const int na = *a.n_act;
-    for (int item = blockIdx.x; item < na * ntc; item += gridDim.x) {
+    const size_t chalf = (size_t)cols / 2, tsz = align_up(a.tc.tile_bytes, 128);
+    const int xstride = Gc * kXP;
+    TileRing ring{{smem, smem + tsz}, full};
+    float *ms = reinterpret_cast<float *>(smem + 2 * tsz);
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    launch_dependents();
+    wait_prerequisite();
+    const int n = *a.n_act * ntc;
+    const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
+    const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
+    auto src_of = [&](int item) {
+        const int ai = item / ntc, d = item - ai * ntc;
+        return a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)d * a.tc.tile_stride;
+    };
+    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tc.tile_bytes);
+    int st_ai = -1, st_c0 = -1, st_c = -1;
+    for (int k = 0, item = i0; item < i1; ++k, ++item) {
+        __syncthreads();
+        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tc.tile_bytes);
+        const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+        if (__syncthreads_or(!okw)) {
+            if (tid == 0) {  // copies in flight must land before the CTA leaves
+                if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+                if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
+            }
+            return;
+        }
+        const uint8_t *tile = ring.buf[k & 1];
         const int ai = item / ntc, d = item - ai * ntc;
         const int c = d / rt, t = d - c * rt;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        __syncthreads();
-        stage_words(tile, a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d +
-                              (size_t)d * a.tc.tile_stride,
-                    a.tc.tile_bytes);
         const float *sc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
-        for (int c0 = 0; c0 < m; c0 += kBatchTokChunk) {
-            const int mc = min(kBatchTokChunk, m - c0);
-            if (c0 > 0) __syncthreads();
-            for (int i = tid; i < mc * cols; i += blockDim.x) {
-                const int ti = i / cols, e = i - ti * cols;
-                ms[ti * xstride + xpad(e)] = a.mid[(size_t)(off + c0 + ti) * I + (size_t)c * cols + e];
+        for (int c0 = 0; c0 < m; c0 += a.chunk_down) {
+            const int mc = min(a.chunk_down, m - c0);
+            if (st_ai != ai || st_c0 != c0 || st_c != c) {
+                if (st_ai >= 0) __syncthreads();
+                stage_rows_padded(ms, xstride, mc, cols, [&](int r) {
+                    return a.mid + (size_t)(off + c0 + r) * I + (size_t)c * cols;
+                });
+                __syncthreads();
+                st_ai = ai;
+                st_c0 = c0;
+                st_c = c;
             }
-            __syncthreads();
             for (int r = warp; r < TR; r += nwarp) {
                 const int row = t * TR + r;
                 if (row >= H) break;
@@ -1146,14 +1290,22 @@ __global__ void __launch_bounds__(256) k_batch_down(MoeBatchArgs a) {
 #pragma unroll
                 for (int q = 0; q < kBatchTokChunk; ++q) acc[q] = 0.f;
                 if (lane < Gc) {
-                    float wq[32];
-                    dequant32(tile + (size_t)r * chalf + (size_t)lane * 16, sc[(size_t)r * Gc + lane], wq);
+                    const uint4 ww = *reinterpret_cast<const uint4 *>(tile + (size_t)r * chalf + (size_t)lane * 16);
+                    const float sv = sc[(size_t)r * Gc + lane];
+                    const float *xb = ms + lane * kXP;
+#pragma unroll 1
+                    for (int i = 0; i < 8; ++i) {
+                        float w[4];
+                        nib_weight4(ww, i, sv, w);
 #pragma unroll
-                    for (int q = 0; q < kBatchTokChunk; ++q) {
-                        if (q < mc) {
-                            const float *x = ms + q * xstride + lane * 33;
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) acc[q] = fmaf(wq[e], x[e], acc[q]);
+                        for (int q = 0; q < kBatchTokChunk; ++q) {
+                            if (q < mc) {
+                                const float4 x = *reinterpret_cast<const float4 *>(xb + q * xstride + 4 * i);
+                                acc[q] = fmaf(w[0], x.x, acc[q]);
+                                acc[q] = fmaf(w[1], x.y, acc[q]);
+                                acc[q] = fmaf(w[2], x.z, acc[q]);
+                                acc[q] = fmaf(w[3], x.w, acc[q]);
+                            }
                         }
                     }
                 }
@@ -1184,7 +1336,10 @@ __global__ void __launch_bounds__(256) k_batch_combine(MoeBatchArgs a) {
         for (int c = 0; c < KC; ++c) dj += a.down[((size_t)pj * KC + c) * a.H + row];
         delta += a.sw[(size_t)t * kMaxSlots + j] * dj;
     }
-    a.h_out[(size_t)t * a.H + row] = a.h_in[(size_t)t * a.H + row] + delta;
+    // expert-parallel ranks other than 0 leave their share only; the ranks'
+    // outputs then sum to h + delta
+    const float base = a.ep_rank == 0 ? a.h_in[(size_t)t * a.H + row] : 0.f;
+    a.h_out[(size_t)t * a.H + row] = base + delta;
 }
 
 const void *moe_batch_kernel(int i) {

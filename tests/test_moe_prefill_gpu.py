@@ -137,3 +137,47 @@ def test_prefill_rejects_bad_arguments(rc):
     with pytest.raises(rc.RabbitCudaError, match="out of range"):
         pool.prefill(3, h)
     pool.free()
+
+
+@pytest.mark.parametrize("G", [2, 4])
+def test_expert_parallel_shares_sum_to_the_layer(rc, oracle, G):
+    """G pools, each holding the routed experts e = r (mod G) of one layer (as
+    local records e / G) plus the shared experts, with
+    rabbit_cuda_moe_set_expert_parallel(r, G): the sum of their outputs is
+    the layer output (what an all-reduce over G ranks computes)."""
+    H, E, k, I, S = 256, 8, 2, 256, 1
+    recs, size, router, rms = synth.moe_layer(21, H, E, I, S)
+    rec_of = lambda e: recs[e * size:(e + 1) * size]  # noqa: E731
+    h = np.random.default_rng(6).standard_normal((40, H)).astype(np.float32)
+    total = np.zeros_like(h)
+    for r in range(G):
+        mine = [rec_of(e) for e in range(r, E, G)] + [rec_of(E + s) for s in range(S)]
+        pool = rc.MoePool(records=np.concatenate(mine), expert_size=size, n_layers=1, hidden=H,
+                          n_experts=E, top_k=k, inter=I, n_shared=S, quant=4, rms_ffn=[rms],
+                          w_router=[router], experts_per_layer=E // G + S)
+        pool.set_expert_parallel(r, G)
+        out, ids, w = pool.prefill(0, h)
+        total += out
+        if r == 0:
+            all_ids, all_w = ids, w
+        else:
+            np.testing.assert_array_equal(ids, all_ids)  # routing is computed in full everywhere
+        with pytest.raises(rc.RabbitCudaError, match="expert-parallel"):
+            pool.decode(0, h[0])
+        pool.free()
+    kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=4, n_records=E + S, expert_size=size,
+              records=recs, rms_ffn=rms, w_router=router)
+    check_tokens(oracle, h, total, all_ids, all_w, kw, min_checked=36)
+
+
+def test_expert_parallel_rejects_bad_shares(rc):
+    H, E, k, I, S = 64, 8, 2, 64, 0
+    pool, _ = make_pool(rc, H, E, k, I, S, seed=2)
+    with pytest.raises(rc.RabbitCudaError):
+        pool.set_expert_parallel(0, 3)  # 8 experts do not split over 3 ranks
+    with pytest.raises(rc.RabbitCudaError):
+        pool.set_expert_parallel(0, 2)  # this pool holds all 8 experts per layer
+    with pytest.raises(rc.RabbitCudaError):
+        pool.set_expert_parallel(2, 2)
+    pool.set_expert_parallel(0, 1)
+    pool.free()
