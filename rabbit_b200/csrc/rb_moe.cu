@@ -814,7 +814,9 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
     const size_t o_pt = take(sizeof(int) * P);
     const size_t U = P + R;  // work units: at most one per pair, plus one partial per record
-    const size_t o_act = take(sizeof(int) * U * 3 + sizeof(int));
+    const size_t o_act = take(sizeof(int) * U * 3 + 2 * sizeof(int));
+    const size_t o_xpl = take(sizeof(GroupPlanes) * cap * (p->H / 32));
+    const size_t o_mpl = take(sizeof(GroupPlanes) * P * (p->I / 32));
     const size_t o_sc = take(sizeof(float) * cap * p->E);
     const size_t o_tc = take(sizeof(unsigned) * cap);
     const size_t o_mid = take(sizeof(float) * P * p->I);
@@ -852,6 +854,8 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     a.act_off = a.act + U;
     a.act_cnt = a.act_off + U;
     a.n_act = a.act_cnt + U;
+    a.xpl = reinterpret_cast<GroupPlanes *>(b + o_xpl);
+    a.mpl = reinterpret_cast<GroupPlanes *>(b + o_mpl);
     a.scores = reinterpret_cast<float *>(b + o_sc);
     a.tcount = reinterpret_cast<unsigned *>(b + o_tc);
     a.mid = reinterpret_cast<float *>(b + o_mid);
@@ -904,34 +908,16 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     if ((st = ensure_batch(p, T)) != RABBIT_CUDA_OK) return st;
     const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (T + 31) / 32;
     const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 2 * sizeof(int) * R;
-    // gate/up and down: two tile buffers + the staged tokens; chunk = tokens
-    // per pass, two CTAs per SM when four or more tokens still fit
     // the batch kernels' static shared memory (mbarriers, reductions) stays
     // under 1 KB: dynamic sizes leave that room
     constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
-    auto pick = [](size_t fixed, size_t per, int *chunk, int *per_sm) {
-        const size_t two = (size_t)kMaxDynSmem / 2 - 2048;
-        const int c2 = fixed < two ? (int)std::min<size_t>(kBatchTokChunk, (two - fixed) / per) : 0;
-        if (c2 >= 4) {
-            *chunk = c2;
-            *per_sm = 2;
-            return fixed + (size_t)c2 * per;
-        }
-        const int c1 = fixed < kBatchDynMax
-                           ? (int)std::min<size_t>(kBatchTokChunk, (kBatchDynMax - fixed) / per)
-                           : 0;
-        *chunk = c1;
-        *per_sm = 1;
-        return fixed + (size_t)std::max(c1, 0) * per;
-    };
-    int gu_chunk, gu_per_sm, dn_chunk, dn_per_sm;
-    // one token's activations: 36 floats per group of 32 (see k_batch_gu)
-    const size_t gu_smem = pick(2 * align_up(p->plan.tb.tile_bytes, 128),
-                                sizeof(float) * (size_t)(p->H / 32) * 36, &gu_chunk, &gu_per_sm);
-    const size_t dn_smem = pick(2 * align_up(p->plan.tc.tile_bytes, 128),
-                                sizeof(float) * (size_t)(p->plan.tc.cols / 32) * 36, &dn_chunk,
-                                &dn_per_sm);
-    if (bucket_smem > kBatchDynMax || gu_chunk < 1 || dn_chunk < 1)
+    // gate/up and down: two tile buffers + the warps' partial sums and the
+    // reduced tile (see k_batch_gu); up to 64 rows per tile
+    const size_t tc_extra = sizeof(float) * (16 * 4 * 2 * 128 + 4 * 16 * kBatchTokChunk);
+    const size_t gu_smem = 2 * align_up(p->plan.tb.tile_bytes, 128) + tc_extra;
+    const size_t dn_smem = 2 * align_up(p->plan.tc.tile_bytes, 128) + tc_extra;
+    if (bucket_smem > kBatchDynMax || gu_smem > kBatchDynMax || dn_smem > kBatchDynMax ||
+        2 * p->plan.tb.TR > 64 || p->plan.tc.TR > 64)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
     if (!g_batch_attr[p->device]) {
         for (int i = 0; i <= 3; ++i)
@@ -961,8 +947,6 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     a.usable = p->usable ? 1 : 0;
     a.tb = p->plan.tb;
     a.tc = p->plan.tc;
-    a.chunk_gu = gu_chunk;
-    a.chunk_down = dn_chunk;
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
     a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
@@ -971,7 +955,9 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     RB_CUDA(launch_batch(0, dim3(T, (p->E + a.route_split - 1) / a.route_split), dim3(256),
                          sizeof(float) * (size_t)std::max(p->E, p->H), s, a));
     RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
+    RB_CUDA(launch_batch(5, dim3(std::min(4 * sms, (T * (p->H / 32) + 255) / 256)), dim3(256), 0, s, a));
     RB_CUDA(launch_batch(2, dim3(sms), dim3(kBatchThreads), gu_smem, s, a));
+    RB_CUDA(launch_batch(6, dim3(4 * sms), dim3(256), 0, s, a));
     RB_CUDA(launch_batch(3, dim3(sms), dim3(kBatchThreads), dn_smem, s, a));
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
     p->hbm_hits += T;

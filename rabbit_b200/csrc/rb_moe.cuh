@@ -71,15 +71,26 @@ inline bool combine_packed(int KC) { return KC < 8; }
 //   k_batch_bucket  one CTA: per local record, the (token, slot) pairs that
 //                   use it, in token order (bitmask ranks: deterministic),
 //                   cut into units of at most kBatchTokChunk pairs;
+//   k_batch_xplanes xn as activation planes (the integer MMA's B operand);
 //   k_batch_gu      (unit, GU tile) items: mid = silu(gate) * up for the
-//                   unit's tokens;
+//                   unit's tokens, integer tensor-core MMAs per group;
+//   k_batch_mplanes mid as activation planes;
 //   k_batch_down    (unit, D tile) items: each column chunk's down rows per
-//                   pair;
+//                   pair, integer tensor-core MMAs per group;
 //   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
 //                   order (forward_v2.c:356-357, 398-399).
 constexpr int kMaxBatchTokens = 256;
-constexpr int kBatchTokChunk = 8;  // tokens per pass over a staged tile
+constexpr int kBatchTokChunk = 16;  // tokens per work unit (two n8 blocks of the MMA)
 constexpr int kBatchThreads = 512;  // threads of k_batch_gu / k_batch_down
+// One group of 32 activations of one token (or pair) as the integer MMA's B
+// operand: planes 0..2 of X = rint(x 2^(22-e)) in the order the nibble
+// operand uses -- bytes of the even elements 0, 2, .., 30 then of the odd
+// ones -- then -8 sum X and the unit 2^(e-22) (see make_xplanes).
+struct GroupPlanes {
+    uint32_t p[3][8];
+    int m8sum;
+    float unit;
+};
 struct MoeBatchArgs {
     const float *h_in;
     float *h_out;
@@ -91,7 +102,6 @@ struct MoeBatchArgs {
     uint64_t rec_stride, off_d;
     int rec_base, n_local, H, E, k, I, S, usable;
     Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
-    int chunk_gu, chunk_down;  // tokens staged per pass of k_batch_gu / _down (<= 8)
     int *err;                  // device error word (RB_ERR_TIMEOUT)
     uint64_t wait_ns;          // bound of every wait
     // scratch
@@ -103,16 +113,18 @@ struct MoeBatchArgs {
     int *pair_t;     // [P] token of pair
     int *act, *act_off, *act_cnt;  // [units] work units (record, <= kBatchTokChunk of its
                                    // pairs): global record id, first pair, pairs
-    int *n_act;      // [1] units
+    int *n_act;      // [2] units, pairs
     float *scores;   // [T][E] router scores
     unsigned *tcount;  // [T] router CTAs done per token (zero between launches)
     int route_split;   // router rows per CTA of k_batch_route
     int ep_rank, ep_size;  // expert-parallel share (1 rank: the whole layer)
     float *mid;      // [P][I]
     float *down;     // [P][tc.KC][H]
+    GroupPlanes *xpl;  // [T][H / 32] planes of xn
+    GroupPlanes *mpl;  // [P][I / 32] planes of mid
 };
 // The five kernels (same translation unit as the fused kernel).
-const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 gu, 3 down, 4 combine
+const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 gu, 3 down, 4 combine, 5 planes
 
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine
 struct MoeGenericArgs {

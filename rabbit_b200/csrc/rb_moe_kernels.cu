@@ -1049,7 +1049,8 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
             }
             o += cnt[r];
         }
-        *a.n_act = nu;
+        a.n_act[0] = nu;
+        a.n_act[1] = o;  // pairs
     }
     __syncthreads();
     for (int q = tid; q < Q; q += nthr) {
@@ -1064,50 +1065,6 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
             a.pidx[q] = pos;
         }
     }
-}
-
-// Activations staged for a lane-per-group reader: group g of 32 floats at
-// g * kXP floats, so a warp's float4 reads (lane g, elements 4i..4i+3) fall in
-// distinct banks within each quarter warp.
-constexpr int kXP = 36;
-__device__ __forceinline__ int xpad36(int e) { return (e >> 5) * kXP + (e & 31); }
-
-// Stage rows of `n` floats (n a multiple of 4, rows 16-byte aligned) of
-// `nrows` sources into shared memory in that layout: all of a thread's loads
-// are issued before its stores.
-template <typename RowPtr>
-__device__ __forceinline__ void stage_rows_padded(float *dst, int dstride, int nrows, int n,
-                                                  RowPtr row) {
-    const int tid = threadIdx.x, nthr = blockDim.x, n4 = n >> 2;
-    const int total = nrows * n4;
-    for (int base = 0; base < total; base += 8 * nthr) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int q = base + u * nthr + tid;
-            if (q < total) {
-                const int r = q / n4, c = q - r * n4;
-                v[u] = __ldcg(reinterpret_cast<const float4 *>(row(r)) + c);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int q = base + u * nthr + tid;
-            if (q < total) {
-                const int r = q / n4, e = (q - r * n4) * 4;
-                *reinterpret_cast<float4 *>(dst + r * dstride + xpad36(e)) = v[u];
-            }
-        }
-    }
-}
-
-// Four weights 4i..4i+3 of a group held as 16 bytes (low nibble = even
-// element, q = nibble - 8) times the group scale (quant.c:171-185).
-__device__ __forceinline__ void nib_weight4(const uint4 &v, int i, float scale, float (&w)[4]) {
-    const uint32_t word = i < 2 ? v.x : i < 4 ? v.y : i < 6 ? v.z : v.w;
-    const uint32_t n = word >> (16 * (i & 1));
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = (float)((int)((n >> (4 * j)) & 15u) - 8) * scale;
 }
 
 // The ring of two tile buffers of the batch kernels: thread 0 bulk-copies the
@@ -1125,18 +1082,208 @@ __device__ __forceinline__ void ring_issue(const TileRing &r, int k, const uint8
     bulk_g2s(r.buf[b], src, bytes, &r.full[b], policy_evict_first());
 }
 
-// (active record, GU tile) work items in contiguous ranges per CTA, so that
-// consecutive items mostly share a record and its staged tokens. A warp per
-// gate/up row pair, a lane per group of 32 inputs, tokens chunk_gu at a time.
+// Planes of every group of 32 of `rows` fp32 rows of `len` floats (row
+// stride `len`) into GroupPlanes records, one thread per group.
+__device__ __forceinline__ void planes_rows(const float *src, int rows, int len, GroupPlanes *dst) {
+    const int G = len / 32;
+    const long long n = (long long)rows * G;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
+         q += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(q / G), g = (int)(q - (long long)r * G);
+        const float4 *x4 = reinterpret_cast<const float4 *>(src + (size_t)r * len + (size_t)g * 32);
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = __ldcg(x4 + i);
+            x[4 * i] = v.x;
+            x[4 * i + 1] = v.y;
+            x[4 * i + 2] = v.z;
+            x[4 * i + 3] = v.w;
+        }
+        XPlanes xp;
+        make_xplanes(xp, x);
+        GroupPlanes &o = dst[q];
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                o.p[pl][j] = xp.lo[pl][j];
+                o.p[pl][4 + j] = xp.hi[pl][j];
+            }
+        o.m8sum = xp.m8sum;
+        o.unit = xp.unit;
+    }
+}
+
+// Planes of xn [T][H] (the gate/up input) and of mid [pairs][I] (the down
+// input).
+__global__ void __launch_bounds__(256) k_batch_xplanes(MoeBatchArgs a) {
+    launch_dependents();
+    wait_prerequisite();
+    planes_rows(a.xn, a.T, a.H, a.xpl);
+}
+__global__ void __launch_bounds__(256) k_batch_mplanes(MoeBatchArgs a) {
+    launch_dependents();
+    wait_prerequisite();
+    planes_rows(a.mid, a.n_act[1], a.I, a.mpl);
+}
+
+// Integer tensor-core products of nibbles (A, u8 0..15) and activation
+// planes (B; u8 for planes 0 and 1, s8 for plane 2): m16n8k32, exact s32.
+__device__ __forceinline__ void mma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+constexpr int kTcMaxMB = 4;                       // 16-row blocks per tile (<= 64 rows)
+constexpr int kTcNB = kBatchTokChunk / 8;         // 8-column blocks per unit
+constexpr int kTcWarps = kBatchThreads / 32;
+
+// One staged tile (rows R < nrows: nibbles at tile + R rowb, scales at
+// sc + R ngrp) against up to 16 columns (col n < m: its group g at
+// col_of(n) + g) as exact integer MMAs per group of 32:
+//   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
+// (the decode path's dot32, on the tensor cores). Warp w takes groups w,
+// w + 16, ...; the warps' sums are added in warp order into out[R * 16 + n]
+// (shared). Every thread of the CTA calls it.
+template <typename ColOf>
+__device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const float *sc, int ngrp,
+                                        int nrows, int m, ColOf col_of, float *red, float *out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int MB = (nrows + 15) >> 4;
+    float acc[kTcMaxMB][kTcNB][4];
+#pragma unroll
+    for (int mb = 0; mb < kTcMaxMB; ++mb)
+#pragma unroll
+        for (int nb = 0; nb < kTcNB; ++nb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[mb][nb][i] = 0.f;
+    const GroupPlanes *cb[kTcNB], *cr[kTcNB][2];  // B column, readout columns
+#pragma unroll
+    for (int nb = 0; nb < kTcNB; ++nb) {
+        const int nB = nb * 8 + g, n0 = nb * 8 + 2 * t;
+        cb[nb] = nB < m ? col_of(nB) : nullptr;
+        cr[nb][0] = n0 < m ? col_of(n0) : nullptr;
+        cr[nb][1] = n0 + 1 < m ? col_of(n0 + 1) : nullptr;
+    }
+    // a group's B operand and readout terms; the next group's are loaded
+    // (from L2) while this group's MMAs run
+    uint32_t b[kTcNB][3][2], bn[kTcNB][3][2];
+    int m8[kTcNB][2], m8n[kTcNB][2];
+    float un[kTcNB][2], unn[kTcNB][2];
+    auto load_b = [&](int grp, uint32_t (&bb)[kTcNB][3][2], int (&mm)[kTcNB][2],
+                      float (&uu)[kTcNB][2]) {
+#pragma unroll
+        for (int nb = 0; nb < kTcNB; ++nb) {
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl) {
+                bb[nb][pl][0] = cb[nb] && grp < ngrp ? __ldcg(&cb[nb][grp].p[pl][t]) : 0u;
+                bb[nb][pl][1] = cb[nb] && grp < ngrp ? __ldcg(&cb[nb][grp].p[pl][4 + t]) : 0u;
+            }
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                mm[nb][c] = cr[nb][c] && grp < ngrp ? __ldcg(&cr[nb][c][grp].m8sum) : 0;
+                uu[nb][c] = cr[nb][c] && grp < ngrp ? __ldcg(&cr[nb][c][grp].unit) : 0.f;
+            }
+        }
+    };
+    load_b(warp, b, m8, un);
+    for (int grp = warp; grp < ngrp; grp += kTcWarps) {
+        load_b(grp + kTcWarps, bn, m8n, unn);
+#pragma unroll
+        for (int mb = 0; mb < kTcMaxMB; ++mb) {
+            if (mb >= MB) break;
+            const int r0 = mb * 16 + g, r1 = r0 + 8;
+            const uint32_t w0 = r0 < nrows ? *reinterpret_cast<const uint32_t *>(
+                                                 tile + (size_t)r0 * rowb + (size_t)grp * 16 + 4 * t)
+                                           : 0u;
+            const uint32_t w1 = r1 < nrows ? *reinterpret_cast<const uint32_t *>(
+                                                 tile + (size_t)r1 * rowb + (size_t)grp * 16 + 4 * t)
+                                           : 0u;
+            const float s0r = r0 < nrows ? sc[(size_t)r0 * ngrp + grp] : 0.f;
+            const float s1r = r1 < nrows ? sc[(size_t)r1 * ngrp + grp] : 0.f;
+            const uint32_t av[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
+                                    (w1 >> 4) & 0x0F0F0F0Fu};
+#pragma unroll
+            for (int nb = 0; nb < kTcNB; ++nb) {
+                int p0[4], p1[4], p2[4];
+                mma_u8u8(p0, av, b[nb][0][0], b[nb][0][1]);
+                mma_u8u8(p1, av, b[nb][1][0], b[nb][1][1]);
+                mma_u8s8(p2, av, b[nb][2][0], b[nb][2][1]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c = i & 1;
+                    const int low = p1[i] * 256 + p0[i] + m8[nb][c];
+                    const float dot = fmaf((float)p2[i], 65536.0f, (float)low) * un[nb][c];
+                    acc[mb][nb][i] = fmaf(i < 2 ? s0r : s1r, dot, acc[mb][nb][i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int nb = 0; nb < kTcNB; ++nb) {
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl) {
+                b[nb][pl][0] = bn[nb][pl][0];
+                b[nb][pl][1] = bn[nb][pl][1];
+            }
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                m8[nb][c] = m8n[nb][c];
+                un[nb][c] = unn[nb][c];
+            }
+        }
+    }
+    // the warps' partial sums, added in warp order
+#pragma unroll
+    for (int mb = 0; mb < kTcMaxMB; ++mb)
+#pragma unroll
+        for (int nb = 0; nb < kTcNB; ++nb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                red[(((size_t)warp * kTcMaxMB + mb) * kTcNB + nb) * 128 + lane * 4 + i] = acc[mb][nb][i];
+    __syncthreads();
+    for (int e = tid; e < MB * kTcNB * 128; e += blockDim.x) {
+        const int mb = e / (kTcNB * 128), rem = e - mb * kTcNB * 128;
+        const int nb = rem >> 7, li = rem & 127, ln = li >> 2, i = li & 3;
+        float v = 0.f;
+        for (int w = 0; w < kTcWarps; ++w)
+            v += red[(((size_t)w * kTcMaxMB + mb) * kTcNB + nb) * 128 + li];
+        const int R = mb * 16 + (ln >> 2) + 8 * (i >> 1);
+        const int n = nb * 8 + 2 * (ln & 3) + (i & 1);
+        out[R * kBatchTokChunk + n] = v;
+    }
+    __syncthreads();
+}
+
+// Dynamic shared memory after the two tile buffers: the warps' partial sums
+// (kTcRedFloats), then the reduced tile result (kTcMaxMB * 16 rows x 16).
+constexpr size_t kTcRedFloats = (size_t)kTcWarps * kTcMaxMB * kTcNB * 128;
+
+// (unit, GU tile) work items in contiguous ranges per CTA: mid = silu(gate)
+// * up for the unit's tokens (forward_v2.c:323-331), gate and up rows of the
+// tile as one block of 2 TR rows.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[2];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    const int tid = threadIdx.x;
     const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
     const size_t half = (size_t)H / 2, tsz = align_up(a.tb.tile_bytes, 128);
-    const int xstride = G * kXP;
     TileRing ring{{smem, smem + tsz}, full};
-    float *xs = reinterpret_cast<float *>(smem + 2 * tsz);
+    float *red = reinterpret_cast<float *>(smem + 2 * tsz);
+    float *out = red + kTcRedFloats;
     if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
@@ -1153,12 +1300,11 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
         return a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt * a.tb.tile_stride;
     };
     if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tb.tile_bytes);
-    int st_ai = -1, st_c0 = -1;  // the record / token chunk staged in xs
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
         __syncthreads();  // item k - 1 is done with its buffer (the next copy's target)
         if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tb.tile_bytes);
         const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-        if (__syncthreads_or(!okw)) {  // drain what was issued, then leave
+        if (__syncthreads_or(!okw)) {
             if (tid == 0) {  // copies in flight must land before the CTA leaves
                 if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
                 if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
@@ -1168,76 +1314,29 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
         const uint8_t *tile = ring.buf[k & 1];
         const int ai = item / ntb, tt = item - ai * ntb;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        const float *gsc = reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half);
-        for (int c0 = 0; c0 < m; c0 += a.chunk_gu) {
-            const int mc = min(a.chunk_gu, m - c0);
-            if (st_ai != ai || st_c0 != c0) {
-                if (st_ai >= 0) __syncthreads();  // every warp is done with the old tokens
-                stage_rows_padded(xs, xstride, mc, H, [&](int r) {
-                    return a.xn + (size_t)a.pair_t[off + c0 + r] * H;
-                });
-                __syncthreads();
-                st_ai = ai;
-                st_c0 = c0;
-            }
-            for (int r = warp; r < TR; r += nwarp) {
-                const int row = tt * TR + r;
-                if (row >= I) break;
-                float gs[kBatchTokChunk], us[kBatchTokChunk];
-#pragma unroll
-                for (int q = 0; q < kBatchTokChunk; ++q) gs[q] = us[q] = 0.f;
-                for (int g = lane; g < G; g += 32) {
-                    const uint4 gw = *reinterpret_cast<const uint4 *>(tile + (size_t)r * half + (size_t)g * 16);
-                    const uint4 uw =
-                        *reinterpret_cast<const uint4 *>(tile + (size_t)(TR + r) * half + (size_t)g * 16);
-                    const float gsv = gsc[(size_t)r * G + g], usv = gsc[(size_t)(TR + r) * G + g];
-                    const float *xb = xs + g * kXP;
-#pragma unroll 2
-                    for (int i = 0; i < 8; ++i) {  // elements 4i .. 4i + 3, in order
-                        float wg[4], wu[4];
-                        nib_weight4(gw, i, gsv, wg);
-                        nib_weight4(uw, i, usv, wu);
-#pragma unroll
-                        for (int q = 0; q < kBatchTokChunk; ++q) {
-                            if (q < mc) {
-                                const float4 x = *reinterpret_cast<const float4 *>(xb + q * xstride + 4 * i);
-                                gs[q] = fmaf(wg[0], x.x, gs[q]);
-                                gs[q] = fmaf(wg[1], x.y, gs[q]);
-                                gs[q] = fmaf(wg[2], x.z, gs[q]);
-                                gs[q] = fmaf(wg[3], x.w, gs[q]);
-                                us[q] = fmaf(wu[0], x.x, us[q]);
-                                us[q] = fmaf(wu[1], x.y, us[q]);
-                                us[q] = fmaf(wu[2], x.z, us[q]);
-                                us[q] = fmaf(wu[3], x.w, us[q]);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < kBatchTokChunk; ++q) {
-                    if (q < mc) {
-                        const float gv = warp_sum(gs[q]), uv = warp_sum(us[q]);
-                        if (lane == 0) a.mid[(size_t)(off + c0 + q) * I + row] = silu_mul(gv, uv);
-                    }
-                }
-            }
+        tc_tile(tile, half, reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half), G, 2 * TR,
+                m, [&](int c) { return a.xpl + (size_t)a.pair_t[off + c] * G; }, red, out);
+        for (int e = tid; e < TR * m; e += blockDim.x) {
+            const int r = e / m, c = e - r * m, row = tt * TR + r;
+            if (row < I)
+                a.mid[(size_t)(off + c) * I + row] =
+                    silu_mul(out[r * kBatchTokChunk + c], out[(TR + r) * kBatchTokChunk + c]);
         }
     }
 }
 
-// (active record, D tile) work items in contiguous ranges per CTA: tile
-// (chunk c, row tile t) of W2; a warp per row, a lane per group of the chunk;
-// the pairs' mid chunks staged chunk_down at a time.
+// (unit, D tile) work items in contiguous ranges per CTA: tile (chunk c, row
+// tile t) of W2 against the unit's pairs' mid planes of that chunk.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[2];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    const int tid = threadIdx.x;
     const int H = a.H, I = a.I, TR = a.tc.TR, ntc = a.tc.ntiles, rt = a.tc.rtiles, KC = a.tc.KC;
-    const int cols = a.tc.cols, Gc = cols / 32;
+    const int cols = a.tc.cols, Gc = cols / 32, GI = I / 32;
     const size_t chalf = (size_t)cols / 2, tsz = align_up(a.tc.tile_bytes, 128);
-    const int xstride = Gc * kXP;
     TileRing ring{{smem, smem + tsz}, full};
-    float *ms = reinterpret_cast<float *>(smem + 2 * tsz);
+    float *red = reinterpret_cast<float *>(smem + 2 * tsz);
+    float *out = red + kTcRedFloats;
     if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
@@ -1254,13 +1353,12 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
         return a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)d * a.tc.tile_stride;
     };
     if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tc.tile_bytes);
-    int st_ai = -1, st_c0 = -1, st_c = -1;
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
         __syncthreads();
         if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tc.tile_bytes);
         const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
         if (__syncthreads_or(!okw)) {
-            if (tid == 0) {  // copies in flight must land before the CTA leaves
+            if (tid == 0) {
                 if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
                 if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
             }
@@ -1270,53 +1368,11 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
         const int ai = item / ntc, d = item - ai * ntc;
         const int c = d / rt, t = d - c * rt;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        const float *sc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
-        for (int c0 = 0; c0 < m; c0 += a.chunk_down) {
-            const int mc = min(a.chunk_down, m - c0);
-            if (st_ai != ai || st_c0 != c0 || st_c != c) {
-                if (st_ai >= 0) __syncthreads();
-                stage_rows_padded(ms, xstride, mc, cols, [&](int r) {
-                    return a.mid + (size_t)(off + c0 + r) * I + (size_t)c * cols;
-                });
-                __syncthreads();
-                st_ai = ai;
-                st_c0 = c0;
-                st_c = c;
-            }
-            for (int r = warp; r < TR; r += nwarp) {
-                const int row = t * TR + r;
-                if (row >= H) break;
-                float acc[kBatchTokChunk];
-#pragma unroll
-                for (int q = 0; q < kBatchTokChunk; ++q) acc[q] = 0.f;
-                if (lane < Gc) {
-                    const uint4 ww = *reinterpret_cast<const uint4 *>(tile + (size_t)r * chalf + (size_t)lane * 16);
-                    const float sv = sc[(size_t)r * Gc + lane];
-                    const float *xb = ms + lane * kXP;
-#pragma unroll 1
-                    for (int i = 0; i < 8; ++i) {
-                        float w[4];
-                        nib_weight4(ww, i, sv, w);
-#pragma unroll
-                        for (int q = 0; q < kBatchTokChunk; ++q) {
-                            if (q < mc) {
-                                const float4 x = *reinterpret_cast<const float4 *>(xb + q * xstride + 4 * i);
-                                acc[q] = fmaf(w[0], x.x, acc[q]);
-                                acc[q] = fmaf(w[1], x.y, acc[q]);
-                                acc[q] = fmaf(w[2], x.z, acc[q]);
-                                acc[q] = fmaf(w[3], x.w, acc[q]);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < kBatchTokChunk; ++q) {
-                    if (q < mc) {
-                        const float v = warp_sum(acc[q]);
-                        if (lane == 0) a.down[((size_t)(off + c0 + q) * KC + c) * H + row] = v;
-                    }
-                }
-            }
+        tc_tile(tile, chalf, reinterpret_cast<const float *>(tile + (size_t)TR * chalf), Gc, TR, m,
+                [&](int q) { return a.mpl + (size_t)(off + q) * GI + (size_t)c * Gc; }, red, out);
+        for (int e = tid; e < TR * m; e += blockDim.x) {
+            const int r = e / m, q = e - r * m, row = t * TR + r;
+            if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = out[r * kBatchTokChunk + q];
         }
     }
 }
@@ -1349,6 +1405,8 @@ const void *moe_batch_kernel(int i) {
         case 2: return (const void *)k_batch_gu;
         case 3: return (const void *)k_batch_down;
         case 4: return (const void *)k_batch_combine;
+        case 5: return (const void *)k_batch_xplanes;
+        case 6: return (const void *)k_batch_mplanes;
         default: return nullptr;
     }
 }
