@@ -1163,7 +1163,7 @@ __device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const 
                                         int nrows, int m, ColOf col_of, float *red, float *out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int MB = (nrows + 15) >> 4;
+    const int MB = (nrows + 15) >> 4, NBu = (m + 7) >> 3;  // row / column blocks in use
     float acc[kTcMaxMB][kTcNB][4];
 #pragma unroll
     for (int mb = 0; mb < kTcMaxMB; ++mb)
@@ -1179,30 +1179,29 @@ __device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const 
         cr[nb][0] = n0 < m ? col_of(n0) : nullptr;
         cr[nb][1] = n0 + 1 < m ? col_of(n0 + 1) : nullptr;
     }
-    // a group's B operand and readout terms; the next group's are loaded
-    // (from L2) while this group's MMAs run
-    uint32_t b[kTcNB][3][2], bn[kTcNB][3][2];
-    int m8[kTcNB][2], m8n[kTcNB][2];
-    float un[kTcNB][2], unn[kTcNB][2];
+    // a group's B operand and readout terms
+    uint32_t b[kTcNB][3][2];
+    int m8[kTcNB][2];
+    float un[kTcNB][2];
     auto load_b = [&](int grp, uint32_t (&bb)[kTcNB][3][2], int (&mm)[kTcNB][2],
                       float (&uu)[kTcNB][2]) {
 #pragma unroll
         for (int nb = 0; nb < kTcNB; ++nb) {
+            if (nb >= NBu) break;
 #pragma unroll
             for (int pl = 0; pl < 3; ++pl) {
-                bb[nb][pl][0] = cb[nb] && grp < ngrp ? __ldcg(&cb[nb][grp].p[pl][t]) : 0u;
-                bb[nb][pl][1] = cb[nb] && grp < ngrp ? __ldcg(&cb[nb][grp].p[pl][4 + t]) : 0u;
+                bb[nb][pl][0] = cb[nb] && grp < ngrp ? cb[nb][grp].p[pl][t] : 0u;
+                bb[nb][pl][1] = cb[nb] && grp < ngrp ? cb[nb][grp].p[pl][4 + t] : 0u;
             }
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                mm[nb][c] = cr[nb][c] && grp < ngrp ? __ldcg(&cr[nb][c][grp].m8sum) : 0;
-                uu[nb][c] = cr[nb][c] && grp < ngrp ? __ldcg(&cr[nb][c][grp].unit) : 0.f;
+                mm[nb][c] = cr[nb][c] && grp < ngrp ? cr[nb][c][grp].m8sum : 0;
+                uu[nb][c] = cr[nb][c] && grp < ngrp ? cr[nb][c][grp].unit : 0.f;
             }
         }
     };
-    load_b(warp, b, m8, un);
     for (int grp = warp; grp < ngrp; grp += kTcWarps) {
-        load_b(grp + kTcWarps, bn, m8n, unn);
+        load_b(grp, b, m8, un);
 #pragma unroll
         for (int mb = 0; mb < kTcMaxMB; ++mb) {
             if (mb >= MB) break;
@@ -1219,6 +1218,7 @@ __device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const 
                                     (w1 >> 4) & 0x0F0F0F0Fu};
 #pragma unroll
             for (int nb = 0; nb < kTcNB; ++nb) {
+                if (nb >= NBu) break;
                 int p0[4], p1[4], p2[4];
                 mma_u8u8(p0, av, b[nb][0][0], b[nb][0][1]);
                 mma_u8u8(p1, av, b[nb][1][0], b[nb][1][1]);
@@ -1232,31 +1232,19 @@ __device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const 
                 }
             }
         }
-#pragma unroll
-        for (int nb = 0; nb < kTcNB; ++nb) {
-#pragma unroll
-            for (int pl = 0; pl < 3; ++pl) {
-                b[nb][pl][0] = bn[nb][pl][0];
-                b[nb][pl][1] = bn[nb][pl][1];
-            }
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                m8[nb][c] = m8n[nb][c];
-                un[nb][c] = unn[nb][c];
-            }
-        }
     }
-    // the warps' partial sums, added in warp order
+    // the warps' partial sums of the blocks in use, added in warp order
 #pragma unroll
     for (int mb = 0; mb < kTcMaxMB; ++mb)
 #pragma unroll
         for (int nb = 0; nb < kTcNB; ++nb)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                red[(((size_t)warp * kTcMaxMB + mb) * kTcNB + nb) * 128 + lane * 4 + i] = acc[mb][nb][i];
+            if (mb < MB && nb < NBu)
+                *reinterpret_cast<float4 *>(
+                    &red[(((size_t)warp * kTcMaxMB + mb) * kTcNB + nb) * 128 + lane * 4]) =
+                    make_float4(acc[mb][nb][0], acc[mb][nb][1], acc[mb][nb][2], acc[mb][nb][3]);
     __syncthreads();
-    for (int e = tid; e < MB * kTcNB * 128; e += blockDim.x) {
-        const int mb = e / (kTcNB * 128), rem = e - mb * kTcNB * 128;
+    for (int e = tid; e < MB * NBu * 128; e += blockDim.x) {
+        const int mb = e / (NBu * 128), rem = e - mb * NBu * 128;
         const int nb = rem >> 7, li = rem & 127, ln = li >> 2, i = li & 3;
         float v = 0.f;
         for (int w = 0; w < kTcWarps; ++w)
@@ -1314,8 +1302,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
         const uint8_t *tile = ring.buf[k & 1];
         const int ai = item / ntb, tt = item - ai * ntb;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        tc_tile(tile, half, reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half), G, 2 * TR,
-                m, [&](int c) { return a.xpl + (size_t)a.pair_t[off + c] * G; }, red, out);
+        auto gcol = [&](int c) -> const GroupPlanes * { return a.xpl + (size_t)a.pair_t[off + c] * G; };
+        const float *gsc = reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half);
+        tc_tile(tile, half, gsc, G, 2 * TR, m, gcol, red, out);
         for (int e = tid; e < TR * m; e += blockDim.x) {
             const int r = e / m, c = e - r * m, row = tt * TR + r;
             if (row < I)
@@ -1368,8 +1357,11 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
         const int ai = item / ntc, d = item - ai * ntc;
         const int c = d / rt, t = d - c * rt;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        tc_tile(tile, chalf, reinterpret_cast<const float *>(tile + (size_t)TR * chalf), Gc, TR, m,
-                [&](int q) { return a.mpl + (size_t)(off + q) * GI + (size_t)c * Gc; }, red, out);
+        auto gcol = [&](int q) -> const GroupPlanes * {
+            return a.mpl + (size_t)(off + q) * GI + (size_t)c * Gc;
+        };
+        const float *dsc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
+        tc_tile(tile, chalf, dsc, Gc, TR, m, gcol, red, out);
         for (int e = tid; e < TR * m; e += blockDim.x) {
             const int r = e / m, q = e - r * m, row = t * TR + r;
             if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = out[r * kBatchTokChunk + q];
