@@ -914,10 +914,15 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     // gate/up and down: two tile buffers + the warps' partial sums and the
     // reduced tile (see k_batch_gu); up to 64 rows per tile
     const size_t tc_extra = sizeof(float) * (16 * 4 * 2 * 128 + 4 * 16 * kBatchTokChunk);
-    const size_t gu_smem = 2 * align_up(p->plan.tb.tile_bytes, 128) + tc_extra;
+    // gate/up: consecutive tiles per item until an item holds 16 rows (two
+    // 4-row tiles of gate and up fill one MMA block)
+    int gu_tpi = 1;
+    while (2 * p->plan.tb.TR * gu_tpi < 16 && gu_tpi < p->plan.tb.ntiles) gu_tpi *= 2;
+    const size_t gu_smem =
+        2 * align_up((size_t)gu_tpi * p->plan.tb.tile_stride, 128) + tc_extra;
     const size_t dn_smem = 2 * align_up(p->plan.tc.tile_bytes, 128) + tc_extra;
     if (bucket_smem > kBatchDynMax || gu_smem > kBatchDynMax || dn_smem > kBatchDynMax ||
-        2 * p->plan.tb.TR > 64 || p->plan.tc.TR > 64)
+        2 * p->plan.tb.TR * gu_tpi > 64 || p->plan.tc.TR > 64)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
     if (!g_batch_attr[p->device]) {
         for (int i = 0; i <= 3; ++i)
@@ -949,6 +954,7 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     a.tc = p->plan.tc;
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
+    a.gu_tpi = gu_tpi;
     a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
     a.ep_rank = p->ep_rank;
     a.ep_size = p->ep_size;

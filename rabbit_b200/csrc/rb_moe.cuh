@@ -102,6 +102,7 @@ struct MoeBatchArgs {
     uint64_t rec_stride, off_d;
     int rec_base, n_local, H, E, k, I, S, usable;
     Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
+    int gu_tpi;                // GU tiles per work item (2 TR gu_tpi <= 64)
     int *err;                  // device error word (RB_ERR_TIMEOUT)
     uint64_t wait_ns;          // bound of every wait
     // scratch

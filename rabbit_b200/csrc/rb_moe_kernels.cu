@@ -1151,16 +1151,16 @@ constexpr int kTcMaxMB = 4;                       // 16-row blocks per tile (<= 
 constexpr int kTcNB = kBatchTokChunk / 8;         // 8-column blocks per unit
 constexpr int kTcWarps = kBatchThreads / 32;
 
-// One staged tile (rows R < nrows: nibbles at tile + R rowb, scales at
-// sc + R ngrp) against up to 16 columns (col n < m: its group g at
+// One staged tile (rows R < nrows: nibbles at row_nib(R), scales at
+// row_sc(R)) against up to 16 columns (col n < m: its group g at
 // col_of(n) + g) as exact integer MMAs per group of 32:
 //   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
 // (the decode path's dot32, on the tensor cores). Warp w takes groups w,
 // w + 16, ...; the warps' sums are added in warp order into out[R * 16 + n]
 // (shared). Every thread of the CTA calls it.
-template <typename ColOf>
-__device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const float *sc, int ngrp,
-                                        int nrows, int m, ColOf col_of, float *red, float *out) {
+template <typename RowNib, typename RowSc, typename ColOf>
+__device__ __forceinline__ void tc_tile(RowNib row_nib, RowSc row_sc, int ngrp, int nrows, int m,
+                                        ColOf col_of, float *red, float *out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int MB = (nrows + 15) >> 4, NBu = (m + 7) >> 3;  // row / column blocks in use
@@ -1207,13 +1207,13 @@ __device__ __forceinline__ void tc_tile(const uint8_t *tile, size_t rowb, const 
             if (mb >= MB) break;
             const int r0 = mb * 16 + g, r1 = r0 + 8;
             const uint32_t w0 = r0 < nrows ? *reinterpret_cast<const uint32_t *>(
-                                                 tile + (size_t)r0 * rowb + (size_t)grp * 16 + 4 * t)
+                                                 row_nib(r0) + (size_t)grp * 16 + 4 * t)
                                            : 0u;
             const uint32_t w1 = r1 < nrows ? *reinterpret_cast<const uint32_t *>(
-                                                 tile + (size_t)r1 * rowb + (size_t)grp * 16 + 4 * t)
+                                                 row_nib(r1) + (size_t)grp * 16 + 4 * t)
                                            : 0u;
-            const float s0r = r0 < nrows ? sc[(size_t)r0 * ngrp + grp] : 0.f;
-            const float s1r = r1 < nrows ? sc[(size_t)r1 * ngrp + grp] : 0.f;
+            const float s0r = r0 < nrows ? row_sc(r0)[grp] : 0.f;
+            const float s1r = r1 < nrows ? row_sc(r1)[grp] : 0.f;
             const uint32_t av[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
                                     (w1 >> 4) & 0x0F0F0F0Fu};
 #pragma unroll
@@ -1268,7 +1268,10 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     __shared__ __align__(8) uint64_t full[2];
     const int tid = threadIdx.x;
     const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
-    const size_t half = (size_t)H / 2, tsz = align_up(a.tb.tile_bytes, 128);
+    // tpi consecutive tiles per item, so that an item fills 16-row MMA blocks
+    const int tpi = a.gu_tpi, nitem_u = (ntb + tpi - 1) / tpi;
+    const size_t half = (size_t)H / 2, tst = a.tb.tile_stride;
+    const size_t tsz = align_up((size_t)tpi * tst, 128);
     TileRing ring{{smem, smem + tsz}, full};
     float *red = reinterpret_cast<float *>(smem + 2 * tsz);
     float *out = red + kTcRedFloats;
@@ -1280,17 +1283,21 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     __syncthreads();
     launch_dependents();
     wait_prerequisite();
-    const int n = *a.n_act * ntb;
+    const int n = *a.n_act * nitem_u;
     const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
     const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
     auto src_of = [&](int item) {
-        const int ai = item / ntb, tt = item - ai * ntb;
-        return a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt * a.tb.tile_stride;
+        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
+        return a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst;
     };
-    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tb.tile_bytes);
+    auto bytes_of = [&](int item) {  // the item's tiles, the last one's tile_bytes
+        const int tt0 = (item % nitem_u) * tpi, nt = min(tpi, ntb - tt0);
+        return (uint32_t)((size_t)(nt - 1) * tst + a.tb.tile_bytes);
+    };
+    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), bytes_of(i0));
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
         __syncthreads();  // item k - 1 is done with its buffer (the next copy's target)
-        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tb.tile_bytes);
+        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), bytes_of(item + 1));
         const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
         if (__syncthreads_or(!okw)) {
             if (tid == 0) {  // copies in flight must land before the CTA leaves
@@ -1299,17 +1306,28 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
             }
             return;
         }
-        const uint8_t *tile = ring.buf[k & 1];
-        const int ai = item / ntb, tt = item - ai * ntb;
+        const uint8_t *tiles = ring.buf[k & 1];
+        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi, nt = min(tpi, ntb - tt0);
         const int off = a.act_off[ai], m = a.act_cnt[ai];
         auto gcol = [&](int c) -> const GroupPlanes * { return a.xpl + (size_t)a.pair_t[off + c] * G; };
-        const float *gsc = reinterpret_cast<const float *>(tile + 2 * (size_t)TR * half);
-        tc_tile(tile, half, gsc, G, 2 * TR, m, gcol, red, out);
-        for (int e = tid; e < TR * m; e += blockDim.x) {
-            const int r = e / m, c = e - r * m, row = tt * TR + r;
+        // block row R: tile R / (2 TR), its gate rows then its up rows
+        auto rnib = [&](int R) {
+            const int j = R / (2 * TR), r = R - j * 2 * TR;
+            return tiles + (size_t)j * tst + (size_t)r * half;
+        };
+        auto rsc = [&](int R) {
+            const int j = R / (2 * TR), r = R - j * 2 * TR;
+            return reinterpret_cast<const float *>(tiles + (size_t)j * tst + 2 * (size_t)TR * half) +
+                   (size_t)r * G;
+        };
+        tc_tile(rnib, rsc, G, nt * 2 * TR, m, gcol, red, out);
+        for (int e = tid; e < nt * TR * m; e += blockDim.x) {
+            const int jr = e / m, c = e - jr * m, j = jr / TR, r = jr - j * TR;
+            const int row = (tt0 + j) * TR + r;
             if (row < I)
                 a.mid[(size_t)(off + c) * I + row] =
-                    silu_mul(out[r * kBatchTokChunk + c], out[(TR + r) * kBatchTokChunk + c]);
+                    silu_mul(out[(j * 2 * TR + r) * kBatchTokChunk + c],
+                             out[(j * 2 * TR + TR + r) * kBatchTokChunk + c]);
         }
     }
 }
@@ -1361,7 +1379,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
             return a.mpl + (size_t)(off + q) * GI + (size_t)c * Gc;
         };
         const float *dsc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
-        tc_tile(tile, chalf, dsc, Gc, TR, m, gcol, red, out);
+        tc_tile([&](int R) { return tile + (size_t)R * chalf; },
+                [&](int R) { return dsc + (size_t)R * Gc; }, Gc, TR, m, gcol, red, out);
         for (int e = tid; e < TR * m; e += blockDim.x) {
             const int r = e / m, q = e - r * m, row = t * TR + r;
             if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = out[r * kBatchTokChunk + q];

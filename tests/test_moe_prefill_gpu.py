@@ -22,6 +22,8 @@ SHAPES = {
     "shared_experts": (256, 16, 3, 96, 2),
     "w2_two_chunks": (128, 8, 2, 2048, 0),
     "mixtral_like": (512, 8, 2, 1024, 0),
+    # hidden 6144: gate/up tiles of 4 rows, two of them per work item
+    "wide_hidden": (6144, 8, 2, 128, 0),
 }
 
 
