@@ -813,10 +813,15 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t o_ns = take(sizeof(int) * cap);
     const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
     const size_t o_pt = take(sizeof(int) * P);
-    const size_t U = P + R;  // work units: at most one per pair, plus one partial per record
+    // work units: each record's pairs in runs of kBatchTokChunk, so at most
+    // one per kBatchTokChunk pairs plus one partial run per record
+    const size_t U = P / kBatchTokChunk + R;
     const size_t o_act = take(sizeof(int) * U * 3 + 2 * sizeof(int));
-    const size_t o_xpl = take(sizeof(GroupPlanes) * cap * (p->H / 32));
-    const size_t o_mpl = take(sizeof(GroupPlanes) * P * (p->I / 32));
+    const size_t o_pu = take(sizeof(int) * P);
+    // activation planes in MMA fragment order, per unit and group (kFragCols)
+    const size_t frag_b = sizeof(uint2) * 2 * 32 * 3, frag_r = sizeof(int2) * kFragCols;
+    const size_t o_xbf = take(frag_b * U * (p->H / 32)), o_xrf = take(frag_r * U * (p->H / 32));
+    const size_t o_mbf = take(frag_b * U * (p->I / 32)), o_mrf = take(frag_r * U * (p->I / 32));
     const size_t o_sc = take(sizeof(float) * cap * p->E);
     const size_t o_tc = take(sizeof(unsigned) * cap);
     const size_t o_mid = take(sizeof(float) * P * p->I);
@@ -854,8 +859,11 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     a.act_off = a.act + U;
     a.act_cnt = a.act_off + U;
     a.n_act = a.act_cnt + U;
-    a.xpl = reinterpret_cast<GroupPlanes *>(b + o_xpl);
-    a.mpl = reinterpret_cast<GroupPlanes *>(b + o_mpl);
+    a.pair_u = reinterpret_cast<int *>(b + o_pu);
+    a.xbf = reinterpret_cast<uint2 *>(b + o_xbf);
+    a.xrf = reinterpret_cast<int2 *>(b + o_xrf);
+    a.mbf = reinterpret_cast<uint2 *>(b + o_mbf);
+    a.mrf = reinterpret_cast<int2 *>(b + o_mrf);
     a.scores = reinterpret_cast<float *>(b + o_sc);
     a.tcount = reinterpret_cast<unsigned *>(b + o_tc);
     a.mid = reinterpret_cast<float *>(b + o_mid);
@@ -883,6 +891,43 @@ static cudaError_t launch_batch(int which, dim3 grid, dim3 block, size_t smem, c
     return cudaLaunchKernelExC(&cfg, moe_batch_kernel(which), args);
 }
 
+// The batch kernels' static shared memory (mbarriers) stays under 1 KB:
+// dynamic sizes leave that room.
+constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
+// Rows of one gate/up or down work item the planner grows to (four 16-row
+// MMA blocks, so four warps share a block's groups).
+constexpr int kTcItemRows = 64;
+
+// Work-item sizes of the multi-token gate/up and down kernels: consecutive
+// tiles per item, doubled up to kTcItemRows rows while two staged items and
+// the warps' partial sums fit in shared memory. False when the layer's tiles
+// cannot be staged (a row wider than shared memory holds, or a tile's scale
+// block that is not a whole number of 16-byte units).
+struct BatchItems {
+    int gu_tpi = 1, dn_tpi = 1;
+    size_t gu_smem = 0, dn_smem = 0;
+};
+static bool batch_items(const rabbit_cuda_moe *p, BatchItems *b) {
+    const Tiling &tb = p->plan.tb, &tc = p->plan.tc;
+    auto smem = [](int rows, int tile_rows, int nib, int sc) -> size_t {
+        const StageGeom g = stage_geom(rows, tile_rows, nib, sc);
+        return g.ok ? 2 * (size_t)g.bytes + sizeof(float) * kTcRedFloats : SIZE_MAX;
+    };
+    auto grow = [&](int tile_rows, int ntiles, int nib, int sc, int *tpi, size_t *bytes) {
+        *tpi = 1;
+        *bytes = smem(tile_rows, tile_rows, nib, sc);
+        while (2 * tile_rows * *tpi <= kTcItemRows && *tpi < ntiles) {
+            const size_t s2 = smem(2 * tile_rows * *tpi, tile_rows, nib, sc);
+            if (s2 > kBatchDynMax) break;
+            *tpi *= 2;
+            *bytes = s2;
+        }
+        return *bytes <= kBatchDynMax && tile_rows * *tpi <= 64;
+    };
+    return grow(2 * tb.TR, tb.rtiles, p->H / 2, p->H / 8, &b->gu_tpi, &b->gu_smem) &&
+           grow(tc.TR, tc.rtiles, tc.cols / 2, tc.cols / 8, &b->dn_tpi, &b->dn_smem);
+}
+
 // The body of rabbit_cuda_moe_prefill_dev.
 static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out, int T,
                         int *d_ids, float *d_w, cudaStream_t s) {
@@ -893,10 +938,12 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
         if (!p->resident[base + r])
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: layer %d not uploaded", layer);
     RB_CUDA(cudaSetDevice(p->device));
-    if (!p->fast && p->ep_size > 1)
+    BatchItems bi;
+    const bool batch = p->fast && batch_items(p, &bi);
+    if (!batch && p->ep_size > 1)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_prefill: expert-parallel pools need the group-32 layout");
-    if (!p->fast) {  // other record formats: the per-token decode, token by token
+    if (!batch) {  // other record formats and shapes: the per-token decode, token by token
         for (int t = 0; t < T; ++t) {
             st = decode_impl(p, layer, d_h_in + (size_t)t * p->H, d_h_out + (size_t)t * p->H,
                              d_ids ? d_ids + (size_t)t * p->k : nullptr,
@@ -907,22 +954,8 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     }
     if ((st = ensure_batch(p, T)) != RABBIT_CUDA_OK) return st;
     const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (T + 31) / 32;
-    const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 2 * sizeof(int) * R;
-    // the batch kernels' static shared memory (mbarriers, reductions) stays
-    // under 1 KB: dynamic sizes leave that room
-    constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
-    // gate/up and down: two tile buffers + the warps' partial sums and the
-    // reduced tile (see k_batch_gu); up to 64 rows per tile
-    const size_t tc_extra = sizeof(float) * (16 * 4 * 2 * 128 + 4 * 16 * kBatchTokChunk);
-    // gate/up: consecutive tiles per item until an item holds 16 rows (two
-    // 4-row tiles of gate and up fill one MMA block)
-    int gu_tpi = 1;
-    while (2 * p->plan.tb.TR * gu_tpi < 16 && gu_tpi < p->plan.tb.ntiles) gu_tpi *= 2;
-    const size_t gu_smem =
-        2 * align_up((size_t)gu_tpi * p->plan.tb.tile_stride, 128) + tc_extra;
-    const size_t dn_smem = 2 * align_up(p->plan.tc.tile_bytes, 128) + tc_extra;
-    if (bucket_smem > kBatchDynMax || gu_smem > kBatchDynMax || dn_smem > kBatchDynMax ||
-        2 * p->plan.tb.TR * gu_tpi > 64 || p->plan.tc.TR > 64)
+    const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 3 * sizeof(int) * R;
+    if (bucket_smem > kBatchDynMax)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
     if (!g_batch_attr[p->device]) {
         for (int i = 0; i <= 3; ++i)
@@ -954,17 +987,23 @@ static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, floa
     a.tc = p->plan.tc;
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
-    a.gu_tpi = gu_tpi;
+    a.gu_tpi = bi.gu_tpi;
+    a.dn_tpi = bi.dn_tpi;
     a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
     a.ep_rank = p->ep_rank;
     a.ep_size = p->ep_size;
     RB_CUDA(launch_batch(0, dim3(T, (p->E + a.route_split - 1) / a.route_split), dim3(256),
                          sizeof(float) * (size_t)std::max(p->E, p->H), s, a));
     RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
-    RB_CUDA(launch_batch(5, dim3(std::min(4 * sms, (T * (p->H / 32) + 255) / 256)), dim3(256), 0, s, a));
-    RB_CUDA(launch_batch(2, dim3(sms), dim3(kBatchThreads), gu_smem, s, a));
-    RB_CUDA(launch_batch(6, dim3(4 * sms), dim3(256), 0, s, a));
-    RB_CUDA(launch_batch(3, dim3(sms), dim3(kBatchThreads), dn_smem, s, a));
+    // planes: one thread per (pair, group), pairs counted on the device
+    const long long pairs_max = (long long)T * std::max(1, std::min(kMaxSlots, p->k + p->S));
+    auto planes_grid = [&](int G) {
+        return dim3((unsigned)std::max(1LL, std::min<long long>(4 * sms, (pairs_max * G + 255) / 256)));
+    };
+    RB_CUDA(launch_batch(5, planes_grid(p->H / 32), dim3(256), 0, s, a));
+    RB_CUDA(launch_batch(2, dim3(sms), dim3(kBatchThreads), bi.gu_smem, s, a));
+    RB_CUDA(launch_batch(6, planes_grid(p->I / 32), dim3(256), 0, s, a));
+    RB_CUDA(launch_batch(3, dim3(sms), dim3(kBatchThreads), bi.dn_smem, s, a));
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
     p->hbm_hits += T;
     return ok();

@@ -82,15 +82,38 @@ inline bool combine_packed(int KC) { return KC < 8; }
 constexpr int kMaxBatchTokens = 256;
 constexpr int kBatchTokChunk = 16;  // tokens per work unit (two n8 blocks of the MMA)
 constexpr int kBatchThreads = 512;  // threads of k_batch_gu / k_batch_down
-// One group of 32 activations of one token (or pair) as the integer MMA's B
-// operand: planes 0..2 of X = rint(x 2^(22-e)) in the order the nibble
-// operand uses -- bytes of the even elements 0, 2, .., 30 then of the odd
-// ones -- then -8 sum X and the unit 2^(e-22) (see make_xplanes).
-struct GroupPlanes {
-    uint32_t p[3][8];
-    int m8sum;
-    float unit;
+// The activation planes of the multi-token kernels, kept in the order the
+// integer MMA (m16n8k32, B operand) reads them. For work unit u, group g of
+// 32 activations and 8-column block nb, lane l = 4 i + t of a warp loads
+// three uint2 at bfrag[((u G + g) 2 + nb) 32 + l]: planes 0..2 of
+// X = rint(x 2^(22-e)) of column 8 nb + i, each as (bytes of the even
+// elements 8t, 8t+2, 8t+4, 8t+6 ; bytes of the odd ones) -- the k order of
+// the nibble operand (see make_xplanes). The readout terms of column c,
+// (-8 sum X, the unit 2^(e-22) as float bits), are at rfrag[(u G + g) 16 + c].
+constexpr int kFragCols = 16;  // columns of one unit (= kBatchTokChunk)
+// One multi-token work item staged in shared memory: its tiles' nibble
+// blocks (tile_rows rows of nib_bytes each) back to back, so `rows` nibble
+// rows at stride nib_bytes, then their scale blocks likewise -- two bulk
+// copies per tile.
+struct StageGeom {
+    uint32_t ns, ss;  // nibble / scale row strides (bytes)
+    uint32_t sc_off;  // scale rows' offset
+    uint32_t bytes;   // the item's buffer, 128-byte aligned
+    bool ok;          // every copy a whole number of 16-byte units
 };
+__host__ __device__ inline StageGeom stage_geom(int rows, int tile_rows, int nib_bytes, int sc_bytes) {
+    StageGeom g;
+    g.ns = (uint32_t)nib_bytes;
+    g.ss = (uint32_t)sc_bytes;
+    g.sc_off = (uint32_t)align_up((size_t)rows * nib_bytes, 16);
+    g.bytes = (uint32_t)align_up((size_t)g.sc_off + (size_t)rows * sc_bytes, 128);
+    g.ok = ((size_t)tile_rows * nib_bytes) % 16 == 0 && ((size_t)tile_rows * sc_bytes) % 16 == 0;
+    return g;
+}
+// Warp partial sums of the multi-token tensor-core tiles: per warp two 16-row
+// blocks x two 8-column blocks of 16x8 fragments.
+constexpr int kTcRedFloats = (kBatchThreads / 32) * 2 * (kBatchTokChunk / 8) * 128;
+
 struct MoeBatchArgs {
     const float *h_in;
     float *h_out;
@@ -103,6 +126,7 @@ struct MoeBatchArgs {
     int rec_base, n_local, H, E, k, I, S, usable;
     Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
     int gu_tpi;                // GU tiles per work item (2 TR gu_tpi <= 64)
+    int dn_tpi;                // D row tiles of one chunk per work item (TR dn_tpi <= 64)
     int *err;                  // device error word (RB_ERR_TIMEOUT)
     uint64_t wait_ns;          // bound of every wait
     // scratch
@@ -121,8 +145,11 @@ struct MoeBatchArgs {
     int ep_rank, ep_size;  // expert-parallel share (1 rank: the whole layer)
     float *mid;      // [P][I]
     float *down;     // [P][tc.KC][H]
-    GroupPlanes *xpl;  // [T][H / 32] planes of xn
-    GroupPlanes *mpl;  // [P][I / 32] planes of mid
+    int *pair_u;     // [P] unit * 16 + column of pair
+    uint2 *xbf;      // [units][H / 32][2][32][3] planes of xn per unit column (see kFragCols)
+    int2 *xrf;       // [units][H / 32][16] their readout terms
+    uint2 *mbf;      // [units][I / 32][2][32][3] planes of mid
+    int2 *mrf;       // [units][I / 32][16]
 };
 // The five kernels (same translation unit as the fused kernel).
 const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 gu, 3 down, 4 combine, 5 planes

@@ -1014,12 +1014,12 @@ __global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
 // One CTA. Ranks come from per-record token bitmasks, so the pair order is
 // token order whatever order the atomics land in.
 __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
-    extern __shared__ __align__(16) uint32_t bm[];  // [R][W] bits, then cnt[R], off[R]
+    extern __shared__ __align__(16) uint32_t bm[];  // [R][W] bits, then cnt[R], off[R], uf[R]
     launch_dependents();
     wait_prerequisite();
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int R = a.n_local, W = (a.T + 31) >> 5;
-    int *cnt = reinterpret_cast<int *>(bm + (size_t)R * W), *off = cnt + R;
+    int *cnt = reinterpret_cast<int *>(bm + (size_t)R * W), *off = cnt + R, *uf = off + R;
     for (int i = tid; i < R * W; i += nthr) bm[i] = 0u;
     __syncthreads();
     const int Q = a.T * kMaxSlots;
@@ -1041,6 +1041,7 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
         int o = 0, nu = 0;
         for (int r = 0; r < R; ++r) {
             off[r] = o;
+            uf[r] = nu;  // the record's first unit
             for (int c0 = 0; c0 < cnt[r]; c0 += kBatchTokChunk) {
                 a.act[nu] = a.rec_base + r;
                 a.act_off[nu] = o + c0;
@@ -1062,35 +1063,24 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
             rank += __popc(bm[r * W + (t >> 5)] & ((1u << (t & 31)) - 1u));
             const int pos = off[r] + rank;
             a.pair_t[pos] = t;
+            a.pair_u[pos] = (uf[r] + rank / kBatchTokChunk) * kFragCols + rank % kBatchTokChunk;
             a.pidx[q] = pos;
         }
     }
 }
 
-// The ring of two tile buffers of the batch kernels: thread 0 bulk-copies the
-// tile of item k + 1 while item k is computed. Buffer b's j-th copy completes
-// phase j & 1 of full[b].
-struct TileRing {
-    uint8_t *buf[2];
-    uint64_t *full;
-};
-__device__ __forceinline__ void ring_issue(const TileRing &r, int k, const uint8_t *src,
-                                           uint32_t bytes) {
-    const int b = k & 1;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
-    mbar_arrive_expect_tx(&r.full[b], bytes);
-    bulk_g2s(r.buf[b], src, bytes, &r.full[b], policy_evict_first());
-}
-
-// Planes of every group of 32 of `rows` fp32 rows of `len` floats (row
-// stride `len`) into GroupPlanes records, one thread per group.
-__device__ __forceinline__ void planes_rows(const float *src, int rows, int len, GroupPlanes *dst) {
-    const int G = len / 32;
-    const long long n = (long long)rows * G;
+// Planes of group g of every pair's activation row (row_of(pair)) in the
+// fragment order of its unit column (see kFragCols), one thread per (pair,
+// group): the column's B words for the four lanes that read it, and its
+// readout terms.
+template <typename RowOf>
+__device__ __forceinline__ void planes_frag(const MoeBatchArgs &a, RowOf row_of, int G, uint2 *bf,
+                                            int2 *rf) {
+    const long long n = (long long)a.n_act[1] * G;
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
          q += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(q / G), g = (int)(q - (long long)r * G);
-        const float4 *x4 = reinterpret_cast<const float4 *>(src + (size_t)r * len + (size_t)g * 32);
+        const int pr = (int)(q / G), g = (int)(q - (long long)pr * G);
+        const float4 *x4 = reinterpret_cast<const float4 *>(row_of(pr) + (size_t)g * 32);
         float x[32];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -1102,30 +1092,28 @@ __device__ __forceinline__ void planes_rows(const float *src, int rows, int len,
         }
         XPlanes xp;
         make_xplanes(xp, x);
-        GroupPlanes &o = dst[q];
+        const int uc = a.pair_u[pr], u = uc / kFragCols, c = uc - u * kFragCols;
+        const size_t ug = (size_t)u * G + g;
+        uint2 *dst = bf + ((ug * 2 + (c >> 3)) * 32 + (size_t)(c & 7) * 4) * 3;
 #pragma unroll
-        for (int pl = 0; pl < 3; ++pl)
+        for (int t = 0; t < 4; ++t)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                o.p[pl][j] = xp.lo[pl][j];
-                o.p[pl][4 + j] = xp.hi[pl][j];
-            }
-        o.m8sum = xp.m8sum;
-        o.unit = xp.unit;
+            for (int pl = 0; pl < 3; ++pl) dst[t * 3 + pl] = make_uint2(xp.lo[pl][t], xp.hi[pl][t]);
+        rf[ug * kFragCols + c] = make_int2(xp.m8sum, __float_as_int(xp.unit));
     }
 }
 
-// Planes of xn [T][H] (the gate/up input) and of mid [pairs][I] (the down
-// input).
+// Planes of xn (the gate/up input, rows by token) and of mid (the down
+// input, rows by pair).
 __global__ void __launch_bounds__(256) k_batch_xplanes(MoeBatchArgs a) {
     launch_dependents();
     wait_prerequisite();
-    planes_rows(a.xn, a.T, a.H, a.xpl);
+    planes_frag(a, [&](int pr) { return a.xn + (size_t)a.pair_t[pr] * a.H; }, a.H / 32, a.xbf, a.xrf);
 }
 __global__ void __launch_bounds__(256) k_batch_mplanes(MoeBatchArgs a) {
     launch_dependents();
     wait_prerequisite();
-    planes_rows(a.mid, a.n_act[1], a.I, a.mpl);
+    planes_frag(a, [&](int pr) { return a.mid + (size_t)pr * a.I; }, a.I / 32, a.mbf, a.mrf);
 }
 
 // Integer tensor-core products of nibbles (A, u8 0..15) and activation
@@ -1147,134 +1135,202 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-constexpr int kTcMaxMB = 4;                       // 16-row blocks per tile (<= 64 rows)
-constexpr int kTcNB = kBatchTokChunk / 8;         // 8-column blocks per unit
+constexpr int kTcNB = kBatchTokChunk / 8;  // 8-column blocks per unit
 constexpr int kTcWarps = kBatchThreads / 32;
 
-// One staged tile (rows R < nrows: nibbles at row_nib(R), scales at
-// row_sc(R)) against up to 16 columns (col n < m: its group g at
-// col_of(n) + g) as exact integer MMAs per group of 32:
-//   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
-// (the decode path's dot32, on the tensor cores). Warp w takes groups w,
-// w + 16, ...; the warps' sums are added in warp order into out[R * 16 + n]
-// (shared). Every thread of the CTA calls it.
-template <typename RowNib, typename RowSc, typename ColOf>
-__device__ __forceinline__ void tc_tile(RowNib row_nib, RowSc row_sc, int ngrp, int nrows, int m,
-                                        ColOf col_of, float *red, float *out) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int MB = (nrows + 15) >> 4, NBu = (m + 7) >> 3;  // row / column blocks in use
-    float acc[kTcMaxMB][kTcNB][4];
-#pragma unroll
-    for (int mb = 0; mb < kTcMaxMB; ++mb)
-#pragma unroll
-        for (int nb = 0; nb < kTcNB; ++nb)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[mb][nb][i] = 0.f;
-    const GroupPlanes *cb[kTcNB], *cr[kTcNB][2];  // B column, readout columns
-#pragma unroll
-    for (int nb = 0; nb < kTcNB; ++nb) {
-        const int nB = nb * 8 + g, n0 = nb * 8 + 2 * t;
-        cb[nb] = nB < m ? col_of(nB) : nullptr;
-        cr[nb][0] = n0 < m ? col_of(n0) : nullptr;
-        cr[nb][1] = n0 + 1 < m ? col_of(n0 + 1) : nullptr;
+// The bulk copies of one work item into its shared-memory buffer, issued by
+// the 32 lanes of warp 0 (copy i by lane i % 32); lane 0 posts the item's
+// bytes first, so the buffer's phase cannot complete before every copy has
+// landed. copy_of(i, dst_offset, src, bytes) describes copy i of n. The
+// kernels keep two buffers: item k goes to buffer k & 1 and completes phase
+// (k >> 1) & 1 of its barrier.
+template <typename CopyOf>
+__device__ __forceinline__ void stage_item(uint8_t *buf, uint64_t *full, uint32_t total, int n,
+                                           CopyOf copy_of) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) mbar_arrive_expect_tx(full, total);
+    __syncwarp();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
+    const uint64_t pol = policy_evict_first();
+    for (int i = lane; i < n; i += 32) {
+        uint32_t off, bytes;
+        const uint8_t *src;
+        copy_of(i, off, src, bytes);
+        bulk_g2s(buf + off, src, bytes, full, pol);
     }
-    // a group's B operand and readout terms
-    uint32_t b[kTcNB][3][2];
-    int m8[kTcNB][2];
-    float un[kTcNB][2];
-    auto load_b = [&](int grp, uint32_t (&bb)[kTcNB][3][2], int (&mm)[kTcNB][2],
-                      float (&uu)[kTcNB][2]) {
+}
+
+// One warp's share of a staged item: the 16-row blocks rs + j RS (j < MBW,
+// block < MB) over the groups ks, ks + KS, ... against NB 8-column blocks,
+// BG groups at a time (the operands of BG groups are loaded before their
+// MMAs). Row R's nibble word t of group g is at nib + R ns + 16 g + 4 t, its
+// scale at sc[R ssw + g]; the B operand and readout terms of group g at
+// bf + (2 g + nb) 96 and rf + 16 g (see kFragCols).
+template <int NB, int BG>
+__device__ __forceinline__ void tc_rows(const uint8_t *nib, uint32_t ns, const float *sc,
+                                        uint32_t ssw, int nrows, int MB, int rs, int RS, int MBW,
+                                        int ks, int KS, int ngrp, int m, const uint2 *bf,
+                                        const int2 *rf, float (&acc)[2][kTcNB][4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint32_t on[2][2], os[2][2];  // byte offset of word t / scale index, rows g and g + 8
+    bool v[2][2];
 #pragma unroll
-        for (int nb = 0; nb < kTcNB; ++nb) {
-            if (nb >= NBu) break;
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int pl = 0; pl < 3; ++pl) {
-                bb[nb][pl][0] = cb[nb] && grp < ngrp ? cb[nb][grp].p[pl][t] : 0u;
-                bb[nb][pl][1] = cb[nb] && grp < ngrp ? cb[nb][grp].p[pl][4 + t] : 0u;
-            }
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                mm[nb][c] = cr[nb][c] && grp < ngrp ? cr[nb][c][grp].m8sum : 0;
-                uu[nb][c] = cr[nb][c] && grp < ngrp ? cr[nb][c][grp].unit : 0.f;
-            }
+        for (int h = 0; h < 2; ++h) {
+            const int R = (rs + j * RS) * 16 + g + 8 * h;
+            v[j][h] = j < MBW && rs + j * RS < MB && R < nrows;
+            on[j][h] = v[j][h] ? (uint32_t)R * ns + 4 * t : 0u;
+            os[j][h] = v[j][h] ? (uint32_t)R * ssw : 0u;
         }
-    };
-    for (int grp = warp; grp < ngrp; grp += kTcWarps) {
-        load_b(grp, b, m8, un);
+    bool cm[NB][2];  // readout columns 8 nb + 2 t (+ 1) in use
 #pragma unroll
-        for (int mb = 0; mb < kTcMaxMB; ++mb) {
-            if (mb >= MB) break;
-            const int r0 = mb * 16 + g, r1 = r0 + 8;
-            const uint32_t w0 = r0 < nrows ? *reinterpret_cast<const uint32_t *>(
-                                                 row_nib(r0) + (size_t)grp * 16 + 4 * t)
-                                           : 0u;
-            const uint32_t w1 = r1 < nrows ? *reinterpret_cast<const uint32_t *>(
-                                                 row_nib(r1) + (size_t)grp * 16 + 4 * t)
-                                           : 0u;
-            const float s0r = r0 < nrows ? row_sc(r0)[grp] : 0.f;
-            const float s1r = r1 < nrows ? row_sc(r1)[grp] : 0.f;
-            const uint32_t av[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
-                                    (w1 >> 4) & 0x0F0F0F0Fu};
+    for (int nb = 0; nb < NB; ++nb) {
+        cm[nb][0] = nb * 8 + 2 * t < m;
+        cm[nb][1] = nb * 8 + 2 * t + 1 < m;
+    }
+    for (int gb = ks; gb < ngrp; gb += KS * BG) {
+        uint2 b[BG][NB][3];
+        int4 r[BG][NB];
+        uint32_t w[BG][2][2];
+        float s[BG][2][2];
 #pragma unroll
-            for (int nb = 0; nb < kTcNB; ++nb) {
-                if (nb >= NBu) break;
-                int p0[4], p1[4], p2[4];
-                mma_u8u8(p0, av, b[nb][0][0], b[nb][0][1]);
-                mma_u8u8(p1, av, b[nb][1][0], b[nb][1][1]);
-                mma_u8s8(p2, av, b[nb][2][0], b[nb][2][1]);
+        for (int q = 0; q < BG; ++q) {
+            const bool in = gb + q * KS < ngrp;
+            const int grp = in ? gb + q * KS : 0;  // addresses stay inside the item
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int c = i & 1;
-                    const int low = p1[i] * 256 + p0[i] + m8[nb][c];
-                    const float dot = fmaf((float)p2[i], 65536.0f, (float)low) * un[nb][c];
-                    acc[mb][nb][i] = fmaf(i < 2 ? s0r : s1r, dot, acc[mb][nb][i]);
+            for (int nb = 0; nb < NB; ++nb) {
+                const uint2 *bp = bf + ((size_t)grp * 2 + nb) * 96 + lane * 3;
+#pragma unroll
+                for (int pl = 0; pl < 3; ++pl) b[q][nb][pl] = in ? bp[pl] : make_uint2(0u, 0u);
+                r[q][nb] = in ? *reinterpret_cast<const int4 *>(rf + (size_t)grp * kFragCols + nb * 8 + 2 * t)
+                              : make_int4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    w[q][j][h] = in && v[j][h]
+                                     ? *reinterpret_cast<const uint32_t *>(nib + on[j][h] + 16 * grp)
+                                     : 0u;
+                    s[q][j][h] = in && v[j][h] ? sc[os[j][h] + grp] : 0.f;
+                }
+        }
+#pragma unroll
+        for (int q = 0; q < BG; ++q) {
+            int m8[NB][2];
+            float un[NB][2];
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                m8[nb][0] = cm[nb][0] ? r[q][nb].x : 0;
+                un[nb][0] = cm[nb][0] ? __int_as_float(r[q][nb].y) : 0.f;
+                m8[nb][1] = cm[nb][1] ? r[q][nb].z : 0;
+                un[nb][1] = cm[nb][1] ? __int_as_float(r[q][nb].w) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if (j >= MBW) break;
+                const uint32_t w0 = w[q][j][0], w1 = w[q][j][1];
+                const uint32_t av[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
+                                        (w1 >> 4) & 0x0F0F0F0Fu};
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    int p0[4], p1[4], p2[4];
+                    mma_u8u8(p0, av, b[q][nb][0].x, b[q][nb][0].y);
+                    mma_u8u8(p1, av, b[q][nb][1].x, b[q][nb][1].y);
+                    mma_u8s8(p2, av, b[q][nb][2].x, b[q][nb][2].y);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int c = i & 1;
+                        const int low = p1[i] * 256 + p0[i] + m8[nb][c];
+                        const float dot = fmaf((float)p2[i], 65536.0f, (float)low) * un[nb][c];
+                        acc[j][nb][i] = fmaf(s[q][j][i >> 1], dot, acc[j][nb][i]);
+                    }
                 }
             }
         }
     }
-    // the warps' partial sums of the blocks in use, added in warp order
+}
+
+// The integer tensor-core products of one staged item (rows R < nrows)
+// against the unit's m <= 16 columns, per group of 32:
+//   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
+// (the decode path's exact per-group dot, on the tensor pipe). With MB =
+// ceil(nrows / 16) row blocks, RS = ceil(MB / 2) warp rows: warp w takes the
+// blocks w % RS and w % RS + RS and the groups w / RS, w / RS + 16 / RS, ...,
+// so each warp loads a group's activation planes once for up to two row
+// blocks. The warps' fragment sums go to red, added up by tc_sum. Every
+// thread of the CTA calls it; it ends with a barrier.
+__device__ __forceinline__ void tc_item(const uint8_t *nib, uint32_t ns, const float *sc,
+                                        uint32_t ssw, int ngrp, int nrows, int m, const uint2 *bf,
+                                        const int2 *rf, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, MBW = MB < 2 ? MB : 2;
+    const int KS = kTcWarps / RS, rs = warp % RS, ks = warp / RS;
+    const int NBu = (m + 7) >> 3;  // column blocks in use
+    float acc[2][kTcNB][4];
 #pragma unroll
-    for (int mb = 0; mb < kTcMaxMB; ++mb)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int nb = 0; nb < kTcNB; ++nb)
-            if (mb < MB && nb < NBu)
-                *reinterpret_cast<float4 *>(
-                    &red[(((size_t)warp * kTcMaxMB + mb) * kTcNB + nb) * 128 + lane * 4]) =
-                    make_float4(acc[mb][nb][0], acc[mb][nb][1], acc[mb][nb][2], acc[mb][nb][3]);
-    __syncthreads();
-    for (int e = tid; e < MB * NBu * 128; e += blockDim.x) {
-        const int mb = e / (NBu * 128), rem = e - mb * NBu * 128;
-        const int nb = rem >> 7, li = rem & 127, ln = li >> 2, i = li & 3;
-        float v = 0.f;
-        for (int w = 0; w < kTcWarps; ++w)
-            v += red[(((size_t)w * kTcMaxMB + mb) * kTcNB + nb) * 128 + li];
-        const int R = mb * 16 + (ln >> 2) + 8 * (i >> 1);
-        const int n = nb * 8 + 2 * (ln & 3) + (i & 1);
-        out[R * kBatchTokChunk + n] = v;
-    }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][nb][i] = 0.f;
+    if (NBu == 1)
+        tc_rows<1, 3>(nib, ns, sc, ssw, nrows, MB, rs, RS, MBW, ks, KS, ngrp, m, bf, rf, acc);
+    else
+        tc_rows<kTcNB, 1>(nib, ns, sc, ssw, nrows, MB, rs, RS, MBW, ks, KS, ngrp, m, bf, rf, acc);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int nb = 0; nb < kTcNB; ++nb)
+            if (j < MBW && rs + j * RS < MB && nb < NBu)
+                *reinterpret_cast<float4 *>(&red[(((size_t)warp * 2 + j) * kTcNB + nb) * 128 + lane * 4]) =
+                    make_float4(acc[j][nb][0], acc[j][nb][1], acc[j][nb][2], acc[j][nb][3]);
     __syncthreads();
 }
 
-// Dynamic shared memory after the two tile buffers: the warps' partial sums
-// (kTcRedFloats), then the reduced tile result (kTcMaxMB * 16 rows x 16).
-constexpr size_t kTcRedFloats = (size_t)kTcWarps * kTcMaxMB * kTcNB * 128;
+// Element (R, n) of the last tc_item over nrows rows: its warps' sums, added
+// in warp order.
+__device__ __forceinline__ float tc_sum(const float *red, int nrows, int R, int n) {
+    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, KS = kTcWarps / RS;
+    const int mb = R >> 4, rs = mb % RS, j = mb / RS, rr = R & 15, nb = n >> 3, nn = n & 7;
+    const int li = ((rr & 7) * 4 + (nn >> 1)) * 4 + ((rr >> 3) << 1) + (nn & 1);
+    float v = 0.f;
+    for (int ks = 0; ks < KS; ++ks)
+        v += red[(((size_t)(ks * RS + rs) * 2 + j) * kTcNB + nb) * 128 + li];
+    return v;
+}
 
-// (unit, GU tile) work items in contiguous ranges per CTA: mid = silu(gate)
-// * up for the unit's tokens (forward_v2.c:323-331), gate and up rows of the
-// tile as one block of 2 TR rows.
+// The wait for item k's buffer; on a timeout every thread learns of it and
+// thread 0 lets the copies in flight (this item's, and the next one's when
+// `next` was issued) land before the CTA leaves. True when the buffer is full.
+__device__ __forceinline__ bool item_wait(uint64_t *full, int k, bool next, const MoeBatchArgs &a) {
+    const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+    if (__syncthreads_or(!okw)) {
+        if (threadIdx.x == 0) {
+            if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+            if (next) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
+        }
+        return false;
+    }
+    return true;
+}
+
+// (unit, gu_tpi consecutive GU tiles) work items in contiguous ranges per
+// CTA: mid = silu(gate) * up for the unit's tokens (forward_v2.c:323-331);
+// the items' gate and up rows staged as one block of rows, two buffers, one
+// item ahead.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[2];
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
-    // tpi consecutive tiles per item, so that an item fills 16-row MMA blocks
+    const int TR2 = 2 * TR, half = H / 2, G4 = G * 4;
     const int tpi = a.gu_tpi, nitem_u = (ntb + tpi - 1) / tpi;
-    const size_t half = (size_t)H / 2, tst = a.tb.tile_stride;
-    const size_t tsz = align_up((size_t)tpi * tst, 128);
-    TileRing ring{{smem, smem + tsz}, full};
-    float *red = reinterpret_cast<float *>(smem + 2 * tsz);
-    float *out = red + kTcRedFloats;
+    const size_t tst = a.tb.tile_stride;
+    const StageGeom sg = stage_geom(tpi * TR2, TR2, half, G4);
+    uint8_t *const buf[2] = {smem, smem + sg.bytes};
+    float *red = reinterpret_cast<float *>(smem + 2 * (size_t)sg.bytes);
     if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
@@ -1286,64 +1342,60 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     const int n = *a.n_act * nitem_u;
     const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
     const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
-    auto src_of = [&](int item) {
+    auto issue = [&](int k, int item) {
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
-        return a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst;
+        const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
+        const uint8_t *rb = a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst;
+        stage_item(buf[k & 1], &full[k & 1], (uint32_t)nrows * (half + G4), 2 * nt,
+                   [&](int i, uint32_t &off, const uint8_t *&src, uint32_t &bytes) {
+                       const int j = i >> 1;  // tile j: its nibble block, then its scale block
+                       if ((i & 1) == 0) {
+                           off = (uint32_t)(j * TR2) * sg.ns;
+                           src = rb + (size_t)j * tst;
+                           bytes = TR2 * half;
+                       } else {
+                           off = sg.sc_off + (uint32_t)(j * TR2) * sg.ss;
+                           src = rb + (size_t)j * tst + (size_t)TR2 * half;
+                           bytes = TR2 * G4;
+                       }
+                   });
     };
-    auto bytes_of = [&](int item) {  // the item's tiles, the last one's tile_bytes
-        const int tt0 = (item % nitem_u) * tpi, nt = min(tpi, ntb - tt0);
-        return (uint32_t)((size_t)(nt - 1) * tst + a.tb.tile_bytes);
-    };
-    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), bytes_of(i0));
+    if (warp == 0 && i0 < i1) issue(0, i0);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target)
-        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), bytes_of(item + 1));
-        const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-        if (__syncthreads_or(!okw)) {
-            if (tid == 0) {  // copies in flight must land before the CTA leaves
-                if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-                if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
-            }
-            return;
-        }
-        const uint8_t *tiles = ring.buf[k & 1];
-        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi, nt = min(tpi, ntb - tt0);
+        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target) and red
+        if (warp == 0 && item + 1 < i1) issue(k + 1, item + 1);
+        if (!item_wait(full, k, item + 1 < i1, a)) return;
+        const uint8_t *st = buf[k & 1];
+        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
+        const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        auto gcol = [&](int c) -> const GroupPlanes * { return a.xpl + (size_t)a.pair_t[off + c] * G; };
-        // block row R: tile R / (2 TR), its gate rows then its up rows
-        auto rnib = [&](int R) {
-            const int j = R / (2 * TR), r = R - j * 2 * TR;
-            return tiles + (size_t)j * tst + (size_t)r * half;
-        };
-        auto rsc = [&](int R) {
-            const int j = R / (2 * TR), r = R - j * 2 * TR;
-            return reinterpret_cast<const float *>(tiles + (size_t)j * tst + 2 * (size_t)TR * half) +
-                   (size_t)r * G;
-        };
-        tc_tile(rnib, rsc, G, nt * 2 * TR, m, gcol, red, out);
+        tc_item(st, sg.ns, reinterpret_cast<const float *>(st + sg.sc_off), sg.ss / 4, G, nrows, m,
+                a.xbf + (size_t)ai * G * 192, a.xrf + (size_t)ai * G * kFragCols, red);
+        // staged row j 2TR + r is gate row r of tile j, j 2TR + TR + r its up row
         for (int e = tid; e < nt * TR * m; e += blockDim.x) {
             const int jr = e / m, c = e - jr * m, j = jr / TR, r = jr - j * TR;
             const int row = (tt0 + j) * TR + r;
             if (row < I)
                 a.mid[(size_t)(off + c) * I + row] =
-                    silu_mul(out[(j * 2 * TR + r) * kBatchTokChunk + c],
-                             out[(j * 2 * TR + TR + r) * kBatchTokChunk + c]);
+                    silu_mul(tc_sum(red, nrows, j * TR2 + r, c), tc_sum(red, nrows, j * TR2 + TR + r, c));
         }
     }
 }
 
-// (unit, D tile) work items in contiguous ranges per CTA: tile (chunk c, row
-// tile t) of W2 against the unit's pairs' mid planes of that chunk.
+// (unit, chunk c, dn_tpi consecutive row tiles of the chunk) work items in
+// contiguous ranges per CTA: those rows of W2's column chunk c against the
+// unit's pairs' mid planes of that chunk.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[2];
-    const int tid = threadIdx.x;
-    const int H = a.H, I = a.I, TR = a.tc.TR, ntc = a.tc.ntiles, rt = a.tc.rtiles, KC = a.tc.KC;
-    const int cols = a.tc.cols, Gc = cols / 32, GI = I / 32;
-    const size_t chalf = (size_t)cols / 2, tsz = align_up(a.tc.tile_bytes, 128);
-    TileRing ring{{smem, smem + tsz}, full};
-    float *red = reinterpret_cast<float *>(smem + 2 * tsz);
-    float *out = red + kTcRedFloats;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int H = a.H, I = a.I, TR = a.tc.TR, rt = a.tc.rtiles, KC = a.tc.KC;
+    const int cols = a.tc.cols, Gc = cols / 32, GI = I / 32, chalf = cols / 2, cG4 = Gc * 4;
+    const int tpi = a.dn_tpi, nic = (rt + tpi - 1) / tpi, nitem_u = KC * nic;
+    const size_t tcs = a.tc.tile_stride;
+    const StageGeom sg = stage_geom(tpi * TR, TR, chalf, cG4);
+    uint8_t *const buf[2] = {smem, smem + sg.bytes};
+    float *red = reinterpret_cast<float *>(smem + 2 * (size_t)sg.bytes);
     if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
@@ -1352,38 +1404,43 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
     __syncthreads();
     launch_dependents();
     wait_prerequisite();
-    const int n = *a.n_act * ntc;
+    const int n = *a.n_act * nitem_u;
     const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
     const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
-    auto src_of = [&](int item) {
-        const int ai = item / ntc, d = item - ai * ntc;
-        return a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)d * a.tc.tile_stride;
+    auto issue = [&](int k, int item) {
+        const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
+        const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
+        const uint8_t *rb = a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d +
+                            (size_t)(c * rt + t0) * tcs;
+        stage_item(buf[k & 1], &full[k & 1], (uint32_t)nrows * (chalf + cG4), 2 * nt,
+                   [&](int i, uint32_t &off, const uint8_t *&src, uint32_t &bytes) {
+                       const int j = i >> 1;
+                       if ((i & 1) == 0) {
+                           off = (uint32_t)(j * TR) * sg.ns;
+                           src = rb + (size_t)j * tcs;
+                           bytes = TR * chalf;
+                       } else {
+                           off = sg.sc_off + (uint32_t)(j * TR) * sg.ss;
+                           src = rb + (size_t)j * tcs + (size_t)TR * chalf;
+                           bytes = TR * cG4;
+                       }
+                   });
     };
-    if (tid == 0 && i0 < i1) ring_issue(ring, 0, src_of(i0), a.tc.tile_bytes);
+    if (warp == 0 && i0 < i1) issue(0, i0);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
         __syncthreads();
-        if (tid == 0 && item + 1 < i1) ring_issue(ring, k + 1, src_of(item + 1), a.tc.tile_bytes);
-        const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-        if (__syncthreads_or(!okw)) {
-            if (tid == 0) {
-                if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-                if (item + 1 < i1) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
-            }
-            return;
-        }
-        const uint8_t *tile = ring.buf[k & 1];
-        const int ai = item / ntc, d = item - ai * ntc;
-        const int c = d / rt, t = d - c * rt;
+        if (warp == 0 && item + 1 < i1) issue(k + 1, item + 1);
+        if (!item_wait(full, k, item + 1 < i1, a)) return;
+        const uint8_t *st = buf[k & 1];
+        const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
+        const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        auto gcol = [&](int q) -> const GroupPlanes * {
-            return a.mpl + (size_t)(off + q) * GI + (size_t)c * Gc;
-        };
-        const float *dsc = reinterpret_cast<const float *>(tile + (size_t)TR * chalf);
-        tc_tile([&](int R) { return tile + (size_t)R * chalf; },
-                [&](int R) { return dsc + (size_t)R * Gc; }, Gc, TR, m, gcol, red, out);
-        for (int e = tid; e < TR * m; e += blockDim.x) {
-            const int r = e / m, q = e - r * m, row = t * TR + r;
-            if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = out[r * kBatchTokChunk + q];
+        const size_t ug = (size_t)ai * GI + (size_t)c * Gc;  // the unit's first group of chunk c
+        tc_item(st, sg.ns, reinterpret_cast<const float *>(st + sg.sc_off), sg.ss / 4, Gc, nrows,
+                m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
+        for (int e = tid; e < nrows * m; e += blockDim.x) {
+            const int R = e / m, q = e - R * m, row = t0 * TR + R;
+            if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = tc_sum(red, nrows, R, q);
         }
     }
 }
