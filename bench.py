@@ -449,7 +449,7 @@ def prefill_item(capi, synth, peak: float, runs: int = 5, cpu: bool = True,
                 "h2d_bytes_per_step": L * DS_T * H * 4,
                 "d2h_bytes_per_step": L * DS_T * (H * 4 + 2 * k * 4),
                 "api": "rabbit_cuda_moe_prefill (host buffers)"},
-        "gpu_launches_per_chunk": 5 * L,
+        "gpu_launches_per_chunk": 7 * L,
     }
     pool.free()
     if cpu:

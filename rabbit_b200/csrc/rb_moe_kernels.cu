@@ -1138,51 +1138,60 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
 constexpr int kTcNB = kBatchTokChunk / 8;  // 8-column blocks per unit
 constexpr int kTcWarps = kBatchThreads / 32;
 
-// The bulk copies of one work item into its shared-memory buffer, issued by
-// the 32 lanes of warp 0 (copy i by lane i % 32); lane 0 posts the item's
-// bytes first, so the buffer's phase cannot complete before every copy has
-// landed. copy_of(i, dst_offset, src, bytes) describes copy i of n. The
-// kernels keep two buffers: item k goes to buffer k & 1 and completes phase
+// The bulk copies of one work item -- nt tiles of tile_rows rows from rb at
+// stride tst, each tile its nibble rows (ns bytes) then its scale rows (ss
+// bytes) -- into the item's banded shared-memory layout (StageGeom), issued
+// by warp 0: lane b < 8 copies band b's nibble rows and lane 8 + b its scale
+// rows (one copy per tile the band touches), or, for unbanded scales, lanes
+// 16.. the tiles' scale blocks. Lane 0 posts the item's bytes first, so the
+// buffer's phase cannot complete before every copy has landed. The kernels
+// keep two buffers: item k goes to buffer k & 1 and completes phase
 // (k >> 1) & 1 of its barrier.
-template <typename CopyOf>
-__device__ __forceinline__ void stage_item(uint8_t *buf, uint64_t *full, uint32_t total, int n,
-                                           CopyOf copy_of) {
+__device__ __forceinline__ void stage_item(uint8_t *buf, uint64_t *full, const StageGeom &sg,
+                                           int nrows, int tile_rows, int nt, const uint8_t *rb,
+                                           size_t tst) {
     const int lane = threadIdx.x & 31;
-    if (lane == 0) mbar_arrive_expect_tx(full, total);
+    if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)nrows * (sg.ns + sg.ss));
     __syncwarp();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
     const uint64_t pol = policy_evict_first();
-    for (int i = lane; i < n; i += 32) {
-        uint32_t off, bytes;
-        const uint8_t *src;
-        copy_of(i, off, src, bytes);
-        bulk_g2s(buf + off, src, bytes, full, pol);
+    const size_t sc_src = (size_t)tile_rows * sg.ns;  // a tile's scale rows
+    if (lane < 8 || (lane < 16 && sg.sc_band)) {
+        const int b = lane & 7;
+        const bool scales = lane >= 8;
+        const int r0 = b * sg.u, r1 = min(r0 + sg.u, nrows);
+        for (int r = r0; r < r1;) {
+            const int j = r / tile_rows, re = min(r1, (j + 1) * tile_rows), rr = r - j * tile_rows;
+            const uint8_t *tile = rb + (size_t)j * tst;
+            if (scales)
+                bulk_g2s(buf + sg.sc_off + (size_t)b * sg.sbs + (size_t)(r - r0) * sg.ss,
+                         tile + sc_src + (size_t)rr * sg.ss, (uint32_t)(re - r) * sg.ss, full, pol);
+            else
+                bulk_g2s(buf + (size_t)b * sg.bs + (size_t)(r - r0) * sg.ns,
+                         tile + (size_t)rr * sg.ns, (uint32_t)(re - r) * sg.ns, full, pol);
+            r = re;
+        }
+    } else if (lane >= 16 && !sg.sc_band) {
+        for (int j = lane - 16; j < nt; j += 16)
+            bulk_g2s(buf + sg.sc_off + (size_t)j * tile_rows * sg.ss, rb + (size_t)j * tst + sc_src,
+                     (uint32_t)tile_rows * sg.ss, full, pol);
     }
 }
 
-// One warp's share of a staged item: the 16-row blocks rs + j RS (j < MBW,
-// block < MB) over the groups ks, ks + KS, ... against NB 8-column blocks,
-// BG groups at a time (the operands of BG groups are loaded before their
-// MMAs). Row R's nibble word t of group g is at nib + R ns + 16 g + 4 t, its
-// scale at sc[R ssw + g]; the B operand and readout terms of group g at
-// bf + (2 g + nb) 96 and rf + 16 g (see kFragCols).
+// One warp's share of a staged item: its (up to) two 16-row blocks j over
+// the groups ks, ks + KS, ... against NB 8-column blocks, BG groups at a time
+// (the operands of BG groups are loaded before their MMAs). Fragment row g
+// (h = 0) or g + 8 (h = 1) of block j has nibble word t of group grp at
+// nib + on[j][h] + 16 grp and its scale at sc[os[j][h] + grp]; v[j][h] is
+// false for rows past the item. The B operand and readout terms of group grp
+// are at bf + (2 grp + nb) 96 and rf + 16 grp (see kFragCols).
 template <int NB, int BG>
-__device__ __forceinline__ void tc_rows(const uint8_t *nib, uint32_t ns, const float *sc,
-                                        uint32_t ssw, int nrows, int MB, int rs, int RS, int MBW,
-                                        int ks, int KS, int ngrp, int m, const uint2 *bf,
-                                        const int2 *rf, float (&acc)[2][kTcNB][4]) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint32_t on[2][2], os[2][2];  // byte offset of word t / scale index, rows g and g + 8
-    bool v[2][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int R = (rs + j * RS) * 16 + g + 8 * h;
-            v[j][h] = j < MBW && rs + j * RS < MB && R < nrows;
-            on[j][h] = v[j][h] ? (uint32_t)R * ns + 4 * t : 0u;
-            os[j][h] = v[j][h] ? (uint32_t)R * ssw : 0u;
-        }
+__device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
+                                        const uint32_t (&on)[2][2], const uint32_t (&os)[2][2],
+                                        const bool (&v)[2][2], int MBW, int ks, int KS, int ngrp,
+                                        int m, const uint2 *bf, const int2 *rf,
+                                        float (&acc)[2][kTcNB][4]) {
+    const int lane = threadIdx.x & 31, t = lane & 3;
     bool cm[NB][2];  // readout columns 8 nb + 2 t (+ 1) in use
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -1252,22 +1261,36 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, uint32_t ns, const f
     }
 }
 
-// The integer tensor-core products of one staged item (rows R < nrows)
-// against the unit's m <= 16 columns, per group of 32:
+// The integer tensor-core products of one staged item (rows R < nrows, laid
+// out as sg) against the unit's m <= 16 columns, per group of 32:
 //   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
-// (the decode path's exact per-group dot, on the tensor pipe). With MB =
-// ceil(nrows / 16) row blocks, RS = ceil(MB / 2) warp rows: warp w takes the
-// blocks w % RS and w % RS + RS and the groups w / RS, w / RS + 16 / RS, ...,
-// so each warp loads a group's activation planes once for up to two row
-// blocks. The warps' fragment sums go to red, added up by tc_sum. Every
-// thread of the CTA calls it; it ends with a barrier.
-__device__ __forceinline__ void tc_item(const uint8_t *nib, uint32_t ns, const float *sc,
-                                        uint32_t ssw, int ngrp, int nrows, int m, const uint2 *bf,
-                                        const int2 *rf, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// (the decode path's exact per-group dot, on the tensor pipe). Block mb of
+// the MB = ceil(nrows / 16) 16-row blocks reads row 2 mb (fragment rows 0..7)
+// and 2 mb + 1 (rows 8..15) of the 8 bands. With RS = ceil(MB / 2) warp
+// rows, warp w takes the blocks w % RS and w % RS + RS and the groups w / RS,
+// w / RS + 16 / RS, ..., so each warp loads a group's activation planes once
+// for up to two blocks. The warps' fragment sums go to red, added up by
+// tc_sum. Every thread of the CTA calls it; it ends with a barrier.
+__device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, int ngrp, int nrows,
+                                        int m, const uint2 *bf, const int2 *rf, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
     const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, MBW = MB < 2 ? MB : 2;
     const int KS = kTcWarps / RS, rs = warp % RS, ks = warp / RS;
     const int NBu = (m + 7) >> 3;  // column blocks in use
+    uint32_t on[2][2], os[2][2];
+    bool v[2][2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int mb = rs + j * RS, w = 2 * mb + h, R = g * sg.u + w;
+            v[j][h] = j < MBW && mb < MB && R < nrows;
+            on[j][h] = v[j][h] ? g * sg.bs + (uint32_t)w * sg.ns + 4 * t : 0u;
+            os[j][h] = !v[j][h] ? 0u
+                       : sg.sc_band ? (g * sg.sbs + (uint32_t)w * sg.ss) / 4
+                                    : (uint32_t)R * (sg.ss / 4);
+        }
+    const float *sc = reinterpret_cast<const float *>(st + sg.sc_off);
     float acc[2][kTcNB][4];
 #pragma unroll
     for (int j = 0; j < 2; ++j)
@@ -1276,9 +1299,9 @@ __device__ __forceinline__ void tc_item(const uint8_t *nib, uint32_t ns, const f
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[j][nb][i] = 0.f;
     if (NBu == 1)
-        tc_rows<1, 3>(nib, ns, sc, ssw, nrows, MB, rs, RS, MBW, ks, KS, ngrp, m, bf, rf, acc);
+        tc_rows<1, 3>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
     else
-        tc_rows<kTcNB, 1>(nib, ns, sc, ssw, nrows, MB, rs, RS, MBW, ks, KS, ngrp, m, bf, rf, acc);
+        tc_rows<kTcNB, 1>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -1289,12 +1312,13 @@ __device__ __forceinline__ void tc_item(const uint8_t *nib, uint32_t ns, const f
     __syncthreads();
 }
 
-// Element (R, n) of the last tc_item over nrows rows: its warps' sums, added
-// in warp order.
+// Element (R, n) of the last tc_item over nrows rows (row R = band b, row w
+// of the band): its warps' sums, added in warp order.
 __device__ __forceinline__ float tc_sum(const float *red, int nrows, int R, int n) {
-    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, KS = kTcWarps / RS;
-    const int mb = R >> 4, rs = mb % RS, j = mb / RS, rr = R & 15, nb = n >> 3, nn = n & 7;
-    const int li = ((rr & 7) * 4 + (nn >> 1)) * 4 + ((rr >> 3) << 1) + (nn & 1);
+    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, KS = kTcWarps / RS, u = 2 * MB;
+    const int b = R / u, w = R - b * u, mb = w >> 1, h = w & 1, rs = mb % RS, j = mb / RS;
+    const int nb = n >> 3, nn = n & 7;
+    const int li = (b * 4 + (nn >> 1)) * 4 + (h << 1) + (nn & 1);
     float v = 0.f;
     for (int ks = 0; ks < KS; ++ks)
         v += red[(((size_t)(ks * RS + rs) * 2 + j) * kTcNB + nb) * 128 + li];
@@ -1345,20 +1369,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     auto issue = [&](int k, int item) {
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
-        const uint8_t *rb = a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst;
-        stage_item(buf[k & 1], &full[k & 1], (uint32_t)nrows * (half + G4), 2 * nt,
-                   [&](int i, uint32_t &off, const uint8_t *&src, uint32_t &bytes) {
-                       const int j = i >> 1;  // tile j: its nibble block, then its scale block
-                       if ((i & 1) == 0) {
-                           off = (uint32_t)(j * TR2) * sg.ns;
-                           src = rb + (size_t)j * tst;
-                           bytes = TR2 * half;
-                       } else {
-                           off = sg.sc_off + (uint32_t)(j * TR2) * sg.ss;
-                           src = rb + (size_t)j * tst + (size_t)TR2 * half;
-                           bytes = TR2 * G4;
-                       }
-                   });
+        stage_item(buf[k & 1], &full[k & 1], stage_geom(nrows, TR2, half, G4), nrows, TR2, nt,
+                   a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst, tst);
     };
     if (warp == 0 && i0 < i1) issue(0, i0);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
@@ -1369,8 +1381,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        tc_item(st, sg.ns, reinterpret_cast<const float *>(st + sg.sc_off), sg.ss / 4, G, nrows, m,
-                a.xbf + (size_t)ai * G * 192, a.xrf + (size_t)ai * G * kFragCols, red);
+        tc_item(st, stage_geom(nrows, TR2, half, G4), G, nrows, m, a.xbf + (size_t)ai * G * 192,
+                a.xrf + (size_t)ai * G * kFragCols, red);
         // staged row j 2TR + r is gate row r of tile j, j 2TR + TR + r its up row
         for (int e = tid; e < nt * TR * m; e += blockDim.x) {
             const int jr = e / m, c = e - jr * m, j = jr / TR, r = jr - j * TR;
@@ -1410,21 +1422,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
     auto issue = [&](int k, int item) {
         const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
-        const uint8_t *rb = a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d +
-                            (size_t)(c * rt + t0) * tcs;
-        stage_item(buf[k & 1], &full[k & 1], (uint32_t)nrows * (chalf + cG4), 2 * nt,
-                   [&](int i, uint32_t &off, const uint8_t *&src, uint32_t &bytes) {
-                       const int j = i >> 1;
-                       if ((i & 1) == 0) {
-                           off = (uint32_t)(j * TR) * sg.ns;
-                           src = rb + (size_t)j * tcs;
-                           bytes = TR * chalf;
-                       } else {
-                           off = sg.sc_off + (uint32_t)(j * TR) * sg.ss;
-                           src = rb + (size_t)j * tcs + (size_t)TR * chalf;
-                           bytes = TR * cG4;
-                       }
-                   });
+        stage_item(buf[k & 1], &full[k & 1], stage_geom(nrows, TR, chalf, cG4), nrows, TR, nt,
+                   a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)(c * rt + t0) * tcs,
+                   tcs);
     };
     if (warp == 0 && i0 < i1) issue(0, i0);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
@@ -1436,8 +1436,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
         const size_t ug = (size_t)ai * GI + (size_t)c * Gc;  // the unit's first group of chunk c
-        tc_item(st, sg.ns, reinterpret_cast<const float *>(st + sg.sc_off), sg.ss / 4, Gc, nrows,
-                m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
+        tc_item(st, stage_geom(nrows, TR, chalf, cG4), Gc, nrows, m, a.mbf + ug * 192,
+                a.mrf + ug * kFragCols, red);
         for (int e = tid; e < nrows * m; e += blockDim.x) {
             const int R = e / m, q = e - R * m, row = t0 * TR + R;
             if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = tc_sum(red, nrows, R, q);
