@@ -1325,16 +1325,17 @@ __device__ __forceinline__ float tc_sum(const float *red, int nrows, int R, int 
     return v;
 }
 
-// The wait for item k's buffer; on a timeout every thread learns of it and
-// thread 0 lets the copies in flight (this item's, and the next one's when
-// `next` was issued) land before the CTA leaves. True when the buffer is full.
-__device__ __forceinline__ bool item_wait(uint64_t *full, int k, bool next, const MoeBatchArgs &a) {
-    const bool okw = mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
+// The wait for item k's buffer (k % nbuf; its (k / nbuf)-th use completes
+// phase (k / nbuf) & 1); on a timeout every thread learns of it and thread 0
+// lets the copies still in flight (items up to `last`, the newest issued)
+// land before the CTA leaves. True when the buffer is full.
+__device__ __forceinline__ bool item_wait(uint64_t *full, int nbuf, int k, int last,
+                                          const MoeBatchArgs &a) {
+    const bool okw = mbar_wait(&full[k % nbuf], (k / nbuf) & 1, a.wait_ns, a.err);
     if (__syncthreads_or(!okw)) {
-        if (threadIdx.x == 0) {
-            if (!okw) mbar_wait(&full[k & 1], (k >> 1) & 1, a.wait_ns, a.err);
-            if (next) mbar_wait(&full[(k + 1) & 1], ((k + 1) >> 1) & 1, a.wait_ns, a.err);
-        }
+        if (threadIdx.x == 0)
+            for (int q = okw ? k + 1 : k; q <= last; ++q)
+                mbar_wait(&full[q % nbuf], (q / nbuf) & 1, a.wait_ns, a.err);
         return false;
     }
     return true;
@@ -1342,22 +1343,21 @@ __device__ __forceinline__ bool item_wait(uint64_t *full, int k, bool next, cons
 
 // (unit, gu_tpi consecutive GU tiles) work items in contiguous ranges per
 // CTA: mid = silu(gate) * up for the unit's tokens (forward_v2.c:323-331);
-// the items' gate and up rows staged as one block of rows, two buffers, one
-// item ahead.
+// the items' gate and up rows staged as one block of rows in a ring of
+// gu_nbuf buffers, gu_nbuf - 1 items ahead.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[2];
+    __shared__ __align__(8) uint64_t full[kTcMaxBuf];
     const int tid = threadIdx.x, warp = tid >> 5;
     const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
     const int TR2 = 2 * TR, half = H / 2, G4 = G * 4;
     const int tpi = a.gu_tpi, nitem_u = (ntb + tpi - 1) / tpi;
     const size_t tst = a.tb.tile_stride;
     const StageGeom sg = stage_geom(tpi * TR2, TR2, half, G4);
-    uint8_t *const buf[2] = {smem, smem + sg.bytes};
-    float *red = reinterpret_cast<float *>(smem + 2 * (size_t)sg.bytes);
+    const int nbuf = a.gu_nbuf;
+    float *red = reinterpret_cast<float *>(smem + (size_t)nbuf * sg.bytes);
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int b = 0; b < nbuf; ++b) mbar_init(&full[b], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -1369,15 +1369,18 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     auto issue = [&](int k, int item) {
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
-        stage_item(buf[k & 1], &full[k & 1], stage_geom(nrows, TR2, half, G4), nrows, TR2, nt,
+        stage_item(smem + (size_t)(k % nbuf) * sg.bytes, &full[k % nbuf],
+                   stage_geom(nrows, TR2, half, G4), nrows, TR2, nt,
                    a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst, tst);
     };
-    if (warp == 0 && i0 < i1) issue(0, i0);
+    if (warp == 0)
+        for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
         __syncthreads();  // item k - 1 is done with its buffer (the next copy's target) and red
-        if (warp == 0 && item + 1 < i1) issue(k + 1, item + 1);
-        if (!item_wait(full, k, item + 1 < i1, a)) return;
-        const uint8_t *st = buf[k & 1];
+        const int nk = k + nbuf - 1;  // takes item k - 1's buffer
+        if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
+        if (!item_wait(full, nbuf, k, min(nk, i1 - 1 - i0), a)) return;
+        const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
@@ -1399,18 +1402,17 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
 // unit's pairs' mid planes of that chunk.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[2];
+    __shared__ __align__(8) uint64_t full[kTcMaxBuf];
     const int tid = threadIdx.x, warp = tid >> 5;
     const int H = a.H, I = a.I, TR = a.tc.TR, rt = a.tc.rtiles, KC = a.tc.KC;
     const int cols = a.tc.cols, Gc = cols / 32, GI = I / 32, chalf = cols / 2, cG4 = Gc * 4;
     const int tpi = a.dn_tpi, nic = (rt + tpi - 1) / tpi, nitem_u = KC * nic;
     const size_t tcs = a.tc.tile_stride;
     const StageGeom sg = stage_geom(tpi * TR, TR, chalf, cG4);
-    uint8_t *const buf[2] = {smem, smem + sg.bytes};
-    float *red = reinterpret_cast<float *>(smem + 2 * (size_t)sg.bytes);
+    const int nbuf = a.dn_nbuf;
+    float *red = reinterpret_cast<float *>(smem + (size_t)nbuf * sg.bytes);
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int b = 0; b < nbuf; ++b) mbar_init(&full[b], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -1422,16 +1424,19 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
     auto issue = [&](int k, int item) {
         const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
-        stage_item(buf[k & 1], &full[k & 1], stage_geom(nrows, TR, chalf, cG4), nrows, TR, nt,
+        stage_item(smem + (size_t)(k % nbuf) * sg.bytes, &full[k % nbuf],
+                   stage_geom(nrows, TR, chalf, cG4), nrows, TR, nt,
                    a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)(c * rt + t0) * tcs,
                    tcs);
     };
-    if (warp == 0 && i0 < i1) issue(0, i0);
+    if (warp == 0)
+        for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        __syncthreads();
-        if (warp == 0 && item + 1 < i1) issue(k + 1, item + 1);
-        if (!item_wait(full, k, item + 1 < i1, a)) return;
-        const uint8_t *st = buf[k & 1];
+        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target) and red
+        const int nk = k + nbuf - 1;  // takes item k - 1's buffer
+        if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
+        if (!item_wait(full, nbuf, k, min(nk, i1 - 1 - i0), a)) return;
+        const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
         const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
