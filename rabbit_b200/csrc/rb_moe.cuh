@@ -91,32 +91,38 @@ constexpr int kBatchThreads = 512;  // threads of k_batch_gu / k_batch_down
 // the nibble operand (see make_xplanes). The readout terms of column c,
 // (-8 sum X, the unit 2^(e-22) as float bits), are at rfrag[(u G + g) 16 + c].
 constexpr int kFragCols = 16;  // columns of one unit (= kBatchTokChunk)
-// One multi-token work item of `rows` weight rows staged in shared memory as
-// 8 bands of u = 2 ceil(rows / 16) consecutive rows: nibble rows at stride
-// ns within a band, bands at stride bs = 16 (mod 128) bytes, so the 8 rows a
-// tensor-core fragment reads (one per band) start in distinct banks; then
-// the scale rows, banded the same way when a scale row is a whole number of
-// 16-byte units (sc_band), else as the tiles' scale blocks back to back.
+// One multi-token work item of `rows` weight rows staged in shared memory.
+// Banded (when a band's nibble rows fill at least 4 KB, so its copies stay
+// large): 8 bands of u = 2 ceil(rows / 16) consecutive rows, nibble rows at
+// stride ns within a band and bands at a stride bs = 16 (mod 128) bytes, so
+// the 8 rows a tensor-core fragment reads (one per band) start in distinct
+// banks; the scale rows banded the same way when every band's (and tile's)
+// scale rows are a whole number of 16-byte units (sc_band), else the tiles'
+// scale blocks back to back. Otherwise the rows in order (fragment rows g and
+// g + 8 of block mb are rows 16 mb + g and + 8), two copies per tile.
 struct StageGeom {
     int u;             // rows per band
     uint32_t ns, bs;   // nibble row stride, band stride (bytes)
     uint32_t ss, sbs;  // scale row stride, band stride (sc_band)
     uint32_t sc_off;   // scales' offset
     uint32_t bytes;    // the item's buffer, 128-byte aligned
-    bool sc_band, ok;  // ok: every copy a whole number of 16-byte units
+    bool banded, sc_band, ok;  // ok: every copy a whole number of 16-byte units
 };
 __host__ __device__ inline StageGeom stage_geom(int rows, int tile_rows, int nib_bytes, int sc_bytes) {
     StageGeom g;
     g.u = 2 * ((rows + 15) / 16);
+    g.banded = (size_t)g.u * nib_bytes >= 4096;
     g.ns = (uint32_t)nib_bytes;
-    g.bs = (uint32_t)align_up((size_t)g.u * nib_bytes, 128) + 16;
-    g.sc_band = sc_bytes % 16 == 0;
+    g.bs = g.banded ? (uint32_t)align_up((size_t)g.u * nib_bytes, 128) + 16 : 0u;
+    g.sc_band = g.banded && ((size_t)g.u * sc_bytes) % 16 == 0 &&
+                ((size_t)tile_rows * sc_bytes) % 16 == 0;
     g.ss = (uint32_t)sc_bytes;
     g.sbs = g.sc_band ? (uint32_t)align_up((size_t)g.u * sc_bytes, 128) + 16 : 0u;
-    g.sc_off = 8 * g.bs;
+    g.sc_off = g.banded ? 8 * g.bs : (uint32_t)align_up((size_t)rows * nib_bytes, 16);
     g.bytes = (uint32_t)align_up(
         (size_t)g.sc_off + (g.sc_band ? 8 * (size_t)g.sbs : (size_t)rows * sc_bytes), 128);
-    g.ok = nib_bytes % 16 == 0 && (g.sc_band || ((size_t)tile_rows * sc_bytes) % 16 == 0);
+    g.ok = nib_bytes % 16 == 0 && (g.sc_band || ((size_t)tile_rows * sc_bytes) % 16 == 0) &&
+           (g.banded || ((size_t)tile_rows * nib_bytes) % 16 == 0);
     return g;
 }
 // Most work-item buffers of a multi-token GEMM kernel. Measured on the

@@ -1143,7 +1143,8 @@ constexpr int kTcWarps = kBatchThreads / 32;
 // bytes) -- into the item's banded shared-memory layout (StageGeom), issued
 // by warp 0: lane b < 8 copies band b's nibble rows and lane 8 + b its scale
 // rows (one copy per tile the band touches), or, for unbanded scales, lanes
-// 16.. the tiles' scale blocks. Lane 0 posts the item's bytes first, so the
+// 16.. the tiles' scale blocks; for an unbanded item lane j copies tile j's
+// nibble and scale blocks. Lane 0 posts the item's bytes first, so the
 // buffer's phase cannot complete before every copy has landed. The kernels
 // keep two buffers: item k goes to buffer k & 1 and completes phase
 // (k >> 1) & 1 of its barrier.
@@ -1156,6 +1157,15 @@ __device__ __forceinline__ void stage_item(uint8_t *buf, uint64_t *full, const S
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
     const uint64_t pol = policy_evict_first();
     const size_t sc_src = (size_t)tile_rows * sg.ns;  // a tile's scale rows
+    if (!sg.banded) {  // rows in order: each tile's nibble block, then its scale block
+        for (int j = lane; j < nt; j += 32) {
+            const uint8_t *tile = rb + (size_t)j * tst;
+            bulk_g2s(buf + (size_t)j * tile_rows * sg.ns, tile, (uint32_t)tile_rows * sg.ns, full, pol);
+            bulk_g2s(buf + sg.sc_off + (size_t)j * tile_rows * sg.ss, tile + sc_src,
+                     (uint32_t)tile_rows * sg.ss, full, pol);
+        }
+        return;
+    }
     if (lane < 8 || (lane < 16 && sg.sc_band)) {
         const int b = lane & 7;
         const bool scales = lane >= 8;
@@ -1266,11 +1276,13 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
 //   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
 // (the decode path's exact per-group dot, on the tensor pipe). Block mb of
 // the MB = ceil(nrows / 16) 16-row blocks reads row 2 mb (fragment rows 0..7)
-// and 2 mb + 1 (rows 8..15) of the 8 bands. With RS = ceil(MB / 2) warp
+// and 2 mb + 1 (rows 8..15) of the 8 bands, or, unbanded, rows 16 mb ..
+// 16 mb + 15. With RS = ceil(MB / 2) warp
 // rows, warp w takes the blocks w % RS and w % RS + RS and the groups w / RS,
 // w / RS + 16 / RS, ..., so each warp loads a group's activation planes once
 // for up to two blocks. The warps' fragment sums go to red, added up by
 // tc_sum. Every thread of the CTA calls it; it ends with a barrier.
+template <bool BANDED>
 __device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, int ngrp, int nrows,
                                         int m, const uint2 *bf, const int2 *rf, float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
@@ -1283,9 +1295,12 @@ __device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, 
     for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int mb = rs + j * RS, w = 2 * mb + h, R = g * sg.u + w;
+            const int mb = rs + j * RS, w = 2 * mb + h;
+            const int R = BANDED ? g * sg.u + w : mb * 16 + g + 8 * h;
             v[j][h] = j < MBW && mb < MB && R < nrows;
-            on[j][h] = v[j][h] ? g * sg.bs + (uint32_t)w * sg.ns + 4 * t : 0u;
+            on[j][h] = !v[j][h] ? 0u
+                       : BANDED ? g * sg.bs + (uint32_t)w * sg.ns + 4 * t
+                                : (uint32_t)R * sg.ns + 4 * t;
             os[j][h] = !v[j][h] ? 0u
                        : sg.sc_band ? (g * sg.sbs + (uint32_t)w * sg.ss) / 4
                                     : (uint32_t)R * (sg.ss / 4);
@@ -1312,11 +1327,22 @@ __device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, 
     __syncthreads();
 }
 
-// Element (R, n) of the last tc_item over nrows rows (row R = band b, row w
-// of the band): its warps' sums, added in warp order.
-__device__ __forceinline__ float tc_sum(const float *red, int nrows, int R, int n) {
+// Element (R, n) of the last tc_item over nrows rows (banded: row R = band
+// b, row w of the band): its warps' sums, added in warp order.
+__device__ __forceinline__ float tc_sum(const float *red, bool banded, int nrows, int R, int n) {
     const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, KS = kTcWarps / RS, u = 2 * MB;
-    const int b = R / u, w = R - b * u, mb = w >> 1, h = w & 1, rs = mb % RS, j = mb / RS;
+    int b, mb, h;
+    if (banded) {
+        b = R / u;
+        const int w = R - b * u;
+        mb = w >> 1;
+        h = w & 1;
+    } else {
+        mb = R >> 4;
+        b = R & 7;
+        h = (R >> 3) & 1;
+    }
+    const int rs = mb % RS, j = mb / RS;
     const int nb = n >> 3, nn = n & 7;
     const int li = (b * 4 + (nn >> 1)) * 4 + (h << 1) + (nn & 1);
     float v = 0.f;
@@ -1384,15 +1410,21 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
-        tc_item(st, stage_geom(nrows, TR2, half, G4), G, nrows, m, a.xbf + (size_t)ai * G * 192,
-                a.xrf + (size_t)ai * G * kFragCols, red);
+        const StageGeom ig = stage_geom(nrows, TR2, half, G4);
+        if (ig.banded)
+            tc_item<true>(st, ig, G, nrows, m, a.xbf + (size_t)ai * G * 192,
+                          a.xrf + (size_t)ai * G * kFragCols, red);
+        else
+            tc_item<false>(st, ig, G, nrows, m, a.xbf + (size_t)ai * G * 192,
+                           a.xrf + (size_t)ai * G * kFragCols, red);
         // staged row j 2TR + r is gate row r of tile j, j 2TR + TR + r its up row
         for (int e = tid; e < nt * TR * m; e += blockDim.x) {
             const int jr = e / m, c = e - jr * m, j = jr / TR, r = jr - j * TR;
             const int row = (tt0 + j) * TR + r;
             if (row < I)
                 a.mid[(size_t)(off + c) * I + row] =
-                    silu_mul(tc_sum(red, nrows, j * TR2 + r, c), tc_sum(red, nrows, j * TR2 + TR + r, c));
+                    silu_mul(tc_sum(red, ig.banded, nrows, j * TR2 + r, c),
+                             tc_sum(red, ig.banded, nrows, j * TR2 + TR + r, c));
         }
     }
 }
@@ -1441,11 +1473,15 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
         const int off = a.act_off[ai], m = a.act_cnt[ai];
         const size_t ug = (size_t)ai * GI + (size_t)c * Gc;  // the unit's first group of chunk c
-        tc_item(st, stage_geom(nrows, TR, chalf, cG4), Gc, nrows, m, a.mbf + ug * 192,
-                a.mrf + ug * kFragCols, red);
+        const StageGeom ig = stage_geom(nrows, TR, chalf, cG4);
+        if (ig.banded)
+            tc_item<true>(st, ig, Gc, nrows, m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
+        else
+            tc_item<false>(st, ig, Gc, nrows, m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
         for (int e = tid; e < nrows * m; e += blockDim.x) {
             const int R = e / m, q = e - R * m, row = t0 * TR + R;
-            if (row < H) a.down[((size_t)(off + q) * KC + c) * H + row] = tc_sum(red, nrows, R, q);
+            if (row < H)
+                a.down[((size_t)(off + q) * KC + c) * H + row] = tc_sum(red, ig.banded, nrows, R, q);
         }
     }
 }
