@@ -1402,10 +1402,11 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
     if (warp == 0)
         for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target) and red
+        // item_wait's barrier also means every thread is done with item k - 1:
+        // its buffer (the next copy's target) and red are free
         const int nk = k + nbuf - 1;  // takes item k - 1's buffer
+        if (!item_wait(full, nbuf, k, min(nk - 1, i1 - 1 - i0), a)) return;
         if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
-        if (!item_wait(full, nbuf, k, min(nk, i1 - 1 - i0), a)) return;
         const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
         const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
         const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
@@ -1464,10 +1465,11 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a)
     if (warp == 0)
         for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
     for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        __syncthreads();  // item k - 1 is done with its buffer (the next copy's target) and red
+        // item_wait's barrier also means every thread is done with item k - 1:
+        // its buffer (the next copy's target) and red are free
         const int nk = k + nbuf - 1;  // takes item k - 1's buffer
+        if (!item_wait(full, nbuf, k, min(nk - 1, i1 - 1 - i0), a)) return;
         if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
-        if (!item_wait(full, nbuf, k, min(nk, i1 - 1 - i0), a)) return;
         const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
         const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
         const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
