@@ -143,6 +143,24 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *desc, int device,
 /* Stage records of layers [layer_begin, layer_end) host -> pinned -> HBM on the
  * pool's side stream (asynchronous; returns once queued). */
 int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end);
+/* Stage records of layers [layer_begin, layer_end) straight from the model
+ * file instead of a host map -- the reference's pread fallback
+ * (rabbit_expert_pread, src/memory.c:255-279, record gid at expert_offset +
+ * gid * expert_size). A reader thread preads records (O_DIRECT when the file
+ * system allows it, else buffered) into a ring of pinned buffers while the
+ * caller's thread re-lays group-32 records into tiles and queues their copies
+ * on the pool's side stream, so file reads, host re-layout and PCIe copies
+ * overlap. `expert_offset` is the file offset of record 0 (the .rabbit
+ * header, then the dense block, then the expert table: src/model.c:324-339);
+ * it is an argument because the reference never sets expert_file_offset
+ * (src/model.c:236-348) and its pread path reads from offset 0. Resident
+ * records are skipped. Returns once the copies are queued (see
+ * rabbit_cuda_moe_sync). RABBIT_CUDA_ERR_IO: the file cannot be opened, a
+ * read fails, or the file ends inside a record; RABBIT_CUDA_ERR_FORMAT: a
+ * record of a pool planned for group-32 records carries another group size.
+ * Records read before an error stay resident. */
+int rabbit_cuda_moe_upload_file(rabbit_cuda_moe *p, const char *path, uint64_t expert_offset,
+                                int layer_begin, int layer_end);
 /* Wait until every queued upload has landed. */
 int rabbit_cuda_moe_sync(rabbit_cuda_moe *p);
 /* Fill every record of a group-32 int4 pool on the device with seeded

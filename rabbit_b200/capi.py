@@ -64,6 +64,7 @@ SIGNATURES = {
     "rabbit_cuda_matrix_bytes": (C.c_uint64, [_P]),
     "rabbit_cuda_moe_create": (_I, [C.POINTER(MoeDesc), _I, C.POINTER(_P)]),
     "rabbit_cuda_moe_upload": (_I, [_P, _I, _I]),
+    "rabbit_cuda_moe_upload_file": (_I, [_P, C.c_char_p, C.c_uint64, _I, _I]),
     "rabbit_cuda_moe_sync": (_I, [_P]),
     "rabbit_cuda_moe_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_moe_free": (_I, [_P]),
@@ -184,7 +185,7 @@ class MoePool:
                  n_experts: int, top_k: int, inter: int, n_shared: int = 0, quant: int = 4,
                  experts_per_layer: int | None = None, experts_shared: bool = False,
                  rms_ffn, w_router, device: int = 0, upload: bool = True):
-        if records is None:  # device-filled pool (fill_synthetic)
+        if records is None:  # device-filled (fill_synthetic) or file-backed (upload_file) pool
             self._records = None
             n_records = n_layers * (experts_per_layer or (n_experts + n_shared))
             upload = False
@@ -212,6 +213,12 @@ class MoePool:
 
     def upload(self, lb: int, le: int) -> None:
         check(lib().rabbit_cuda_moe_upload(self.handle, lb, le))
+
+    def upload_file(self, path, expert_offset: int, lb: int, le: int) -> None:
+        """Records of layers [lb, le) read from `path`, record 0 at byte
+        `expert_offset` (rabbit_cuda_moe_upload_file); queued, see sync()."""
+        check(lib().rabbit_cuda_moe_upload_file(self.handle, str(path).encode(), expert_offset,
+                                                lb, le))
 
     def sync(self) -> None:
         check(lib().rabbit_cuda_moe_sync(self.handle))

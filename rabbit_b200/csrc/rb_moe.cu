@@ -12,10 +12,16 @@
 // bulk copy each: [GU tiles: TRb rows of gate nibbles | up nibbles | gate
 // scales | up scales] over the I rows, then [D tiles: TRc rows of down
 // nibbles | scales] over the H rows. Other formats are kept verbatim.
+#include <errno.h>
+#include <fcntl.h>
 #include <string.h>
+#include <unistd.h>
 
 #include <algorithm>
+#include <condition_variable>
+#include <mutex>
 #include <numeric>
+#include <thread>
 #include <vector>
 
 #include "rb_gemv.cuh"
@@ -25,6 +31,8 @@
 namespace {
 
 constexpr size_t kPinChunk = 32ull << 20;  // bytes per pinned staging buffer
+constexpr int kIoSlots = 3;                 // pinned record buffers of the file reader
+constexpr uint64_t kIoAlign = 4096;         // O_DIRECT offset / length / buffer alignment
 
 inline uint64_t nbytes_g32(uint64_t n) { return 4 + 4 * ((n + 31) / 32) + (n + 1) / 2; }
 
@@ -87,6 +95,13 @@ struct rabbit_cuda_moe {
     // counters
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
     std::vector<uint8_t> img;  // host image of one record in the tiled layout
+    // file-backed upload (rabbit_cuda_moe_upload_file): pinned record buffers
+    // the reader thread fills, and pinned tiled images (group-32 pools), each
+    // with the event of the last copy that reads it
+    uint8_t *io_raw[kIoSlots] = {};
+    uint8_t *io_img[2] = {};
+    cudaEvent_t io_raw_ev[kIoSlots] = {}, io_img_ev[2] = {};
+    uint64_t io_raw_cap = 0;
 };
 
 namespace rb {
@@ -254,6 +269,14 @@ static void free_pool(rabbit_cuda_moe *p) {
         if (p->pin_ev[i]) cudaEventDestroy(p->pin_ev[i]);
     }
     if (p->pin_io) cudaFreeHost(p->pin_io);
+    for (int i = 0; i < kIoSlots; ++i) {
+        if (p->io_raw[i]) cudaFreeHost(p->io_raw[i]);
+        if (p->io_raw_ev[i]) cudaEventDestroy(p->io_raw_ev[i]);
+    }
+    for (int i = 0; i < 2; ++i) {
+        if (p->io_img[i]) cudaFreeHost(p->io_img[i]);
+        if (p->io_img_ev[i]) cudaEventDestroy(p->io_img_ev[i]);
+    }
     if (p->bt_block) cudaFree(p->bt_block);
     if (p->bt_pin) cudaFreeHost(p->bt_pin);
     if (p->up) cudaStreamDestroy(p->up);
@@ -508,6 +531,213 @@ int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end) {
                 return st;
     }
     return ok();
+}
+
+}  // extern "C"
+
+namespace rb {
+
+// Pinned buffers of the file reader, allocated on first use and kept with
+// the pool: kIoSlots record buffers (a record plus O_DIRECT alignment slack)
+// and, for group-32 pools, two tiled images.
+static int ensure_io(rabbit_cuda_moe *p) {
+    const uint64_t cap = align_up(p->expert_size, kIoAlign) + 2 * kIoAlign;
+    cudaError_t e;
+    if (p->io_raw_cap < cap) {
+        for (int i = 0; i < kIoSlots; ++i) {
+            if (p->io_raw_ev[i]) RB_CUDA(cudaEventSynchronize(p->io_raw_ev[i]));
+            if (p->io_raw[i]) cudaFreeHost(p->io_raw[i]);
+            p->io_raw[i] = nullptr;
+        }
+        p->io_raw_cap = 0;
+        for (int i = 0; i < kIoSlots; ++i)
+            if ((e = cudaMallocHost(&p->io_raw[i], cap)) != cudaSuccess)
+                return cuda_fail(e, "moe_upload_file: pinned record buffers");
+        p->io_raw_cap = cap;
+    }
+    for (int i = 0; i < kIoSlots; ++i)
+        if (!p->io_raw_ev[i]) {
+            if ((e = cudaEventCreateWithFlags(&p->io_raw_ev[i], cudaEventDisableTiming)) != cudaSuccess ||
+                (e = cudaEventRecord(p->io_raw_ev[i], p->up)) != cudaSuccess)
+                return cuda_fail(e, "moe_upload_file: events");
+        }
+    if (p->fast)
+        for (int i = 0; i < 2; ++i)
+            if (!p->io_img[i]) {
+                if ((e = cudaMallocHost(&p->io_img[i], p->rec_stride)) != cudaSuccess ||
+                    (e = cudaEventCreateWithFlags(&p->io_img_ev[i], cudaEventDisableTiming)) != cudaSuccess ||
+                    (e = cudaEventRecord(p->io_img_ev[i], p->up)) != cudaSuccess)
+                    return cuda_fail(e, "moe_upload_file: pinned images");
+            }
+    return RABBIT_CUDA_OK;
+}
+
+// Read [off, off + n) of fd into buf. With O_DIRECT the read starts at the
+// aligned offset below off and covers whole blocks (the file's end may cut
+// the last one short); *data is where byte `off` landed. False on an I/O
+// error or a file that ends before off + n.
+static bool read_record(int fd, bool direct, uint64_t off, uint64_t n, uint8_t *buf, uint8_t **data,
+                        int *err) {
+    const uint64_t a0 = direct ? off / kIoAlign * kIoAlign : off;
+    const uint64_t len = direct ? align_up(off + n, kIoAlign) - a0 : n;
+    const uint64_t need = off + n - a0;
+    uint64_t got = 0;
+    while (got < len) {
+        const ssize_t r = pread(fd, buf + got, (size_t)(len - got), (off_t)(a0 + got));
+        if (r < 0) {
+            if (errno == EINTR) continue;
+            *err = errno;
+            return false;
+        }
+        if (r == 0) break;  // end of file
+        got += (uint64_t)r;
+        if (direct && got % kIoAlign != 0) break;  // a short direct read ends at the file's end
+    }
+    *data = buf + (off - a0);
+    if (got < need) *err = 0;
+    return got >= need;
+}
+
+// The body of rabbit_cuda_moe_upload_file: the records of `gids`, read by a
+// reader thread into the pinned ring while this thread lays them out and
+// queues their copies.
+static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t expert_offset,
+                            const std::vector<int> &gids) {
+    int st = ensure_io(p);
+    if (st) return st;
+    int fd = open(path, O_RDONLY | O_DIRECT);
+    bool direct = fd >= 0;
+    if (fd < 0) fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(RABBIT_CUDA_ERR_IO, "moe_upload_file: cannot open %s (%s)", path, strerror(errno));
+
+    const int n = (int)gids.size();
+    std::mutex mu;
+    std::condition_variable cv;
+    int produced = 0, consumed = 0, io_err = -1, bad = -1;  // bad: first record that failed
+    bool stop = false;
+    uint8_t *data[kIoSlots] = {};
+    const int device = p->device;
+    std::thread reader([&] {
+        cudaSetDevice(device);
+        for (int i = 0; i < n; ++i) {
+            const int s = i % kIoSlots;
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                cv.wait(lk, [&] { return stop || i - consumed < kIoSlots; });
+                if (stop) return;
+            }
+            cudaEventSynchronize(p->io_raw_ev[s]);  // the last copy out of this buffer is done
+            const uint64_t off = expert_offset + (uint64_t)gids[i] * p->expert_size;
+            int err = 0;
+            uint8_t *d = nullptr;
+            bool ok = read_record(fd, direct, off, p->expert_size, p->io_raw[s], &d, &err);
+            if (!ok && direct && err == EINVAL) {  // this file system refuses O_DIRECT reads
+                direct = false;
+                ok = read_record(fd, false, off, p->expert_size, p->io_raw[s], &d, &err);
+            }
+            std::lock_guard<std::mutex> lk(mu);
+            if (!ok) {
+                io_err = err;
+                bad = i;
+                cv.notify_all();
+                return;
+            }
+            data[s] = d;
+            produced = i + 1;
+            cv.notify_all();
+        }
+    });
+    const uint64_t nb = nbytes_g32((uint64_t)p->H * p->I);
+    for (int i = 0; i < n && st == RABBIT_CUDA_OK; ++i) {
+        const int s = i % kIoSlots, gid = gids[i];
+        uint8_t *rec;
+        {
+            std::unique_lock<std::mutex> lk(mu);
+            cv.wait(lk, [&] { return produced > i || bad >= 0; });
+            if (produced <= i) {
+                st = io_err > 0 ? fail(RABBIT_CUDA_ERR_IO, "moe_upload_file: reading record %d of %s: %s",
+                                       gid, path, strerror(io_err))
+                                : fail(RABBIT_CUDA_ERR_IO,
+                                       "moe_upload_file: %s ends inside record %d (offset %llu)", path,
+                                       gid, (unsigned long long)(expert_offset + (uint64_t)gid * p->expert_size));
+                break;
+            }
+            rec = data[s];
+        }
+        uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
+        cudaError_t e = cudaSuccess;
+        if (p->fast) {
+            for (int m = 0; m < 3 && st == RABBIT_CUDA_OK; ++m) {
+                uint32_t gs;
+                memcpy(&gs, rec + m * nb, 4);
+                if (gs != 32)
+                    st = fail(RABBIT_CUDA_ERR_FORMAT,
+                              "moe_upload_file: record %d blob %d has group size %u; the pool was "
+                              "planned for group-32 records", gid, m, gs);
+            }
+            if (st) break;
+            const int b = i & 1;
+            if ((e = cudaEventSynchronize(p->io_img_ev[b])) != cudaSuccess) {
+                st = cuda_fail(e, "moe_upload_file");
+                break;
+            }
+            tile_pair_host(rec, rec + nb, p->plan.tb, p->io_img[b]);
+            tile_blob_host(rec + 2 * nb, p->plan.tc, p->io_img[b] + p->off_d);
+            if ((e = cudaMemcpyAsync(dst, p->io_img[b], p->rec_stride, cudaMemcpyHostToDevice, p->up)) !=
+                    cudaSuccess ||
+                (e = cudaEventRecord(p->io_img_ev[b], p->up)) != cudaSuccess) {
+                st = cuda_fail(e, "moe_upload_file");
+                break;
+            }
+            p->h2d_bytes += p->rec_stride;
+        } else {
+            if ((e = cudaMemcpyAsync(dst, rec, p->expert_size, cudaMemcpyHostToDevice, p->up)) != cudaSuccess ||
+                (e = cudaEventRecord(p->io_raw_ev[s], p->up)) != cudaSuccess) {
+                st = cuda_fail(e, "moe_upload_file");
+                break;
+            }
+            p->h2d_bytes += p->expert_size;
+        }
+        p->resident[gid] = 1;
+        p->uploads++;
+        std::lock_guard<std::mutex> lk(mu);
+        consumed = i + 1;  // the record buffer may be refilled (after its copy, for verbatim pools)
+        cv.notify_all();
+    }
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        stop = true;
+        cv.notify_all();
+    }
+    reader.join();
+    close(fd);
+    return st;
+}
+
+}  // namespace rb
+
+extern "C" {
+
+int rabbit_cuda_moe_upload_file(rabbit_cuda_moe *p, const char *path, uint64_t expert_offset,
+                                int layer_begin, int layer_end) {
+    if (!p || !path) return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload_file: NULL argument");
+    if (layer_begin < 0 || layer_end > p->L || layer_begin >= layer_end)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload_file: bad layer range [%d, %d)", layer_begin,
+                    layer_end);
+    RB_CUDA(cudaSetDevice(p->device));
+    std::vector<int> gids;
+    for (int l = layer_begin; l < layer_end; ++l) {
+        int base, n;
+        const int st = layer_map(p, l, &base, &n);
+        if (st) return st;
+        for (int r = 0; r < n; ++r)
+            if (!p->resident[base + r] &&
+                std::find(gids.begin(), gids.end(), base + r) == gids.end())
+                gids.push_back(base + r);
+    }
+    if (gids.empty()) return ok();
+    const int st = rb::upload_from_file(p, path, expert_offset, gids);
+    return st == RABBIT_CUDA_OK ? ok() : st;
 }
 
 int rabbit_cuda_moe_sync(rabbit_cuda_moe *p) {
