@@ -136,6 +136,26 @@ typedef struct {
 
 typedef struct rabbit_cuda_moe rabbit_cuda_moe;
 
+/* expert_quant code of records already in this library's tiled group-32
+ * layout, as rabbit_cuda_tile_records writes them (no counterpart in the
+ * reference, whose codes are 0, 4 and 8; a converter that writes such a file
+ * marks it with this code so readers of the group-32 format never see it).
+ * A pool of such records uploads them without re-laying them out. */
+#define RABBIT_CUDA_QUANT_INT4_TILED 36
+
+/* Re-lay n_records group-32 int4 expert records (gate | up | down blobs,
+ * src/forward_v2.c:314-332; desc's shapes, expert_quant 4, records
+ * desc->expert_size apart) into the tiled layout a pool uses on a GPU with
+ * sm_count SMs (148 on a B200), each followed by a 256-byte trailer that names
+ * the tile plan: the converter side of RABBIT_CUDA_QUANT_INT4_TILED
+ * (convert_hf_stream.py:56-73 writes the group-32 blobs). Host only: touches no
+ * GPU. *tiled_size gets the bytes of one tiled record -- the expert_size the
+ * converted file declares; dst (n_records * *tiled_size bytes) may be NULL to
+ * query it. A pool on a GPU whose plan differs refuses the records
+ * (RABBIT_CUDA_ERR_FORMAT). */
+int rabbit_cuda_tile_records(const rabbit_cuda_moe_desc *desc, int sm_count, const void *src,
+                             int n_records, void *dst, uint64_t *tiled_size);
+
 /* Create the pool on `device`: allocates HBM for every record (the pool is the
  * whole expert table, resident), plus router/norm weights and scratch. */
 int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *desc, int device,

@@ -65,6 +65,7 @@ SIGNATURES = {
     "rabbit_cuda_moe_create": (_I, [C.POINTER(MoeDesc), _I, C.POINTER(_P)]),
     "rabbit_cuda_moe_upload": (_I, [_P, _I, _I]),
     "rabbit_cuda_moe_upload_file": (_I, [_P, C.c_char_p, C.c_uint64, _I, _I]),
+    "rabbit_cuda_tile_records": (_I, [_P, _I, _P, _I, _P, C.POINTER(C.c_uint64)]),
     "rabbit_cuda_moe_sync": (_I, [_P]),
     "rabbit_cuda_moe_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_moe_free": (_I, [_P]),
@@ -176,6 +177,26 @@ def gemv_batch_dev(mats, d_xs, d_ys, stream: int = 0) -> None:
     xs = (C.c_void_p * n)(*d_xs)
     ys = (C.c_void_p * n)(*d_ys)
     check(lib().rabbit_cuda_matrix_gemv_batch_dev(hs, n, xs, ys, stream or None))
+
+
+QUANT_INT4_TILED = 36  # RABBIT_CUDA_QUANT_INT4_TILED
+
+
+def tile_records(records: np.ndarray, expert_size: int, *, hidden: int, n_experts: int,
+                 top_k: int, inter: int, n_shared: int = 0, sm_count: int = 148):
+    """Group-32 int4 records re-laid into the pool's tiled layout for a GPU
+    with sm_count SMs, each with its plan trailer (rabbit_cuda_tile_records;
+    host only). Returns (tiled records as one uint8 array, bytes per record)."""
+    records = np.ascontiguousarray(records, np.uint8)
+    n = records.size // expert_size
+    d = MoeDesc(1, hidden, n_experts, top_k, inter, n_shared, 4, expert_size, n, n_experts + n_shared,
+                0, None, None, None)
+    size = C.c_uint64()
+    check(lib().rabbit_cuda_tile_records(C.byref(d), sm_count, None, 0, None, C.byref(size)))
+    out = np.empty(n * size.value, np.uint8)
+    check(lib().rabbit_cuda_tile_records(C.byref(d), sm_count, _ptr(records), n, _ptr(out),
+                                         C.byref(size)))
+    return out, size.value
 
 
 class MoePool:

@@ -36,6 +36,17 @@ constexpr uint64_t kIoAlign = 4096;         // O_DIRECT offset / length / buffer
 
 inline uint64_t nbytes_g32(uint64_t n) { return 4 + 4 * ((n + 31) / 32) + (n + 1) / 2; }
 
+// A pre-tiled record (RABBIT_CUDA_QUANT_INT4_TILED) is the pool's tiled
+// record (rec_stride bytes) followed by kTileTrailer bytes: a magic word and
+// the tile plan it was laid out for, so a pool planned otherwise refuses it.
+constexpr uint64_t kTileTrailer = 256;
+constexpr char kTileMagic[8] = {'R', 'B', '2', 'T', 'I', 'L', 'E', '1'};
+struct TileTrailer {
+    char magic[8];
+    uint32_t trb, trc, kc, h, inter;
+    uint64_t rec_stride;
+};
+
 inline uint64_t mix_host(uint64_t seed, uint64_t r) {
     uint64_t z = seed * 0x100000001B3ull + r * 0x9E3779B97F4A7C15ull;
     z = (z ^ (z >> 33)) * 0xFF51AFD7ED558CCDull;
@@ -53,6 +64,7 @@ struct rabbit_cuda_moe {
     int n_records = 0, epl = 0, shared_table = 0;
     const uint8_t *host_map = nullptr;
     bool usable = false, fast = false;
+    bool pretiled = false;  // records arrive in the tiled layout (RABBIT_CUDA_QUANT_INT4_TILED)
     // pool
     uint8_t *pool = nullptr;
     uint64_t rec_stride = 0, pool_bytes = 0;
@@ -300,11 +312,41 @@ static int stage_h2d(rabbit_cuda_moe *p, uint8_t *dst, const uint8_t *src, uint6
     return RABBIT_CUDA_OK;
 }
 
+static void fill_trailer(const rabbit_cuda_moe *p, uint8_t *rec) {
+    TileTrailer t = {};
+    memcpy(t.magic, kTileMagic, 8);
+    t.trb = (uint32_t)p->plan.tb.TR;
+    t.trc = (uint32_t)p->plan.tc.TR;
+    t.kc = (uint32_t)p->plan.tc.KC;
+    t.h = (uint32_t)p->H;
+    t.inter = (uint32_t)p->I;
+    t.rec_stride = p->rec_stride;
+    memset(rec + p->rec_stride, 0, kTileTrailer);
+    memcpy(rec + p->rec_stride, &t, sizeof(t));
+}
+
+// A pre-tiled record's trailer must name this pool's tile plan.
+static int check_trailer(const rabbit_cuda_moe *p, const uint8_t *rec, int gid) {
+    TileTrailer t;
+    memcpy(&t, rec + p->rec_stride, sizeof(t));
+    if (memcmp(t.magic, kTileMagic, 8) != 0 || t.trb != (uint32_t)p->plan.tb.TR ||
+        t.trc != (uint32_t)p->plan.tc.TR || t.kc != (uint32_t)p->plan.tc.KC ||
+        t.h != (uint32_t)p->H || t.inter != (uint32_t)p->I || t.rec_stride != p->rec_stride)
+        return fail(RABBIT_CUDA_ERR_FORMAT,
+                    "moe_upload: record %d was not tiled for this pool's plan (tiles of %u / %u "
+                    "rows, %u chunks here)", gid, (unsigned)p->plan.tb.TR, (unsigned)p->plan.tc.TR,
+                    (unsigned)p->plan.tc.KC);
+    return RABBIT_CUDA_OK;
+}
+
 static int upload_record(rabbit_cuda_moe *p, int gid) {
     const uint8_t *src = p->host_map + (uint64_t)gid * p->expert_size;
     uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
     int st;
-    if (p->fast) {
+    if (p->pretiled) {
+        if ((st = check_trailer(p, src, gid)) != RABBIT_CUDA_OK) return st;
+        st = stage_h2d(p, dst, src, p->rec_stride);
+    } else if (p->fast) {
         // gate / up / down blobs -> [GU tiles][D tiles] in a host image
         const uint64_t nb = nbytes_g32((uint64_t)p->H * p->I);
         p->img.resize(p->rec_stride);
@@ -394,6 +436,10 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     p->k = k;
     p->S = (d->n_shared > 0 && d->n_shared <= 64) ? d->n_shared : 0;  // forward_v2.c:392
     p->quant = d->expert_quant;
+    if (p->quant == RABBIT_CUDA_QUANT_INT4_TILED) {  // group-32 int4, already tiled
+        p->pretiled = true;
+        p->quant = 4;
+    }
     p->expert_size = d->expert_size;
     p->n_records = d->n_records;
     p->epl = d->experts_per_layer > 0 ? d->experts_per_layer : d->n_experts;
@@ -409,10 +455,11 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     else
         need = 3 * (4 + mat);
     p->usable = p->expert_size >= need;  // forward_v2.c:299,319,335: else experts add nothing
+    if (p->pretiled) p->usable = true;  // checked against the plan below
 
     // Fast layout only when every blob carries group 32.
     p->fast = p->quant == 4 && p->usable && mat <= 0x7fffffffull;
-    if (p->fast && p->host_map) {
+    if (p->fast && p->host_map && !p->pretiled) {
         const uint64_t nb = nbytes_g32(mat);
         for (int r = 0; r < p->n_records && p->fast; ++r) {
             const uint8_t *rec = p->host_map + (uint64_t)r * p->expert_size;
@@ -427,6 +474,13 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
         }
     }
     if (p->fast && !plan_fused(p, c->sm_count)) p->fast = false;
+    if (p->pretiled && (!p->fast || p->expert_size != p->rec_stride + kTileTrailer)) {
+        const unsigned long long want = p->fast ? p->rec_stride + kTileTrailer : 0;
+        delete p;
+        return fail(RABBIT_CUDA_ERR_FORMAT,
+                    "moe_create: pre-tiled records of %llu bytes do not match this device's tile "
+                    "plan (%llu bytes)", (unsigned long long)d->expert_size, want);
+    }
 
     cudaError_t e = cudaSuccess;
     if (!p->fast) p->rec_stride = align_up(p->expert_size, 256);  // verbatim records
@@ -561,7 +615,7 @@ static int ensure_io(rabbit_cuda_moe *p) {
                 (e = cudaEventRecord(p->io_raw_ev[i], p->up)) != cudaSuccess)
                 return cuda_fail(e, "moe_upload_file: events");
         }
-    if (p->fast)
+    if (p->fast && !p->pretiled)
         for (int i = 0; i < 2; ++i)
             if (!p->io_img[i]) {
                 if ((e = cudaMallocHost(&p->io_img[i], p->rec_stride)) != cudaSuccess ||
@@ -666,7 +720,8 @@ static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t exper
         }
         uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
         cudaError_t e = cudaSuccess;
-        if (p->fast) {
+        if (p->pretiled && (st = check_trailer(p, rec, gid)) != RABBIT_CUDA_OK) break;
+        if (p->fast && !p->pretiled) {
             for (int m = 0; m < 3 && st == RABBIT_CUDA_OK; ++m) {
                 uint32_t gs;
                 memcpy(&gs, rec + m * nb, 4);
@@ -690,13 +745,14 @@ static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t exper
                 break;
             }
             p->h2d_bytes += p->rec_stride;
-        } else {
-            if ((e = cudaMemcpyAsync(dst, rec, p->expert_size, cudaMemcpyHostToDevice, p->up)) != cudaSuccess ||
+        } else {  // verbatim (or pre-tiled) records: copied straight from the record buffer
+            const uint64_t bytes = p->pretiled ? p->rec_stride : p->expert_size;
+            if ((e = cudaMemcpyAsync(dst, rec, bytes, cudaMemcpyHostToDevice, p->up)) != cudaSuccess ||
                 (e = cudaEventRecord(p->io_raw_ev[s], p->up)) != cudaSuccess) {
                 st = cuda_fail(e, "moe_upload_file");
                 break;
             }
-            p->h2d_bytes += p->expert_size;
+            p->h2d_bytes += bytes;
         }
         p->resident[gid] = 1;
         p->uploads++;
@@ -1337,3 +1393,44 @@ uint64_t rabbit_cuda_moe_decode_bytes(const rabbit_cuda_moe *p) {
 }
 
 }  // extern "C"
+
+extern "C" int rabbit_cuda_tile_records(const rabbit_cuda_moe_desc *d, int sm_count, const void *src,
+                                        int n_records, void *dst, uint64_t *tiled_size) {
+    if (!d || !tiled_size || sm_count <= 0 || n_records < 0 || (n_records > 0 && !src && dst))
+        return fail(RABBIT_CUDA_ERR_ARGS, "tile_records: bad arguments");
+    if (d->expert_quant != 4 || d->hidden <= 0 || d->inter <= 0 || d->n_experts <= 0)
+        return fail(RABBIT_CUDA_ERR_ARGS, "tile_records: needs a group-int4 (expert_quant 4) model");
+    // the pool's own planning, on the host only (no device is touched)
+    rabbit_cuda_moe q;
+    q.H = d->hidden;
+    q.I = d->inter;
+    q.E = d->n_experts;
+    int k = d->experts_per_token > 0 ? d->experts_per_token : 2;
+    q.k = std::min(std::min(k, q.E), 8);
+    q.S = (d->n_shared > 0 && d->n_shared <= 64) ? d->n_shared : 0;
+    q.expert_size = d->expert_size;
+    const uint64_t mat = (uint64_t)q.H * q.I, nb = nbytes_g32(mat);
+    if (d->expert_size < 3 * nb || mat > 0x7fffffffull || !rb::plan_fused(&q, sm_count))
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "tile_records: no tiled layout for this shape");
+    const uint64_t rec = q.rec_stride + kTileTrailer;
+    *tiled_size = rec;
+    if (!dst) return ok();
+    const uint8_t *in = static_cast<const uint8_t *>(src);
+    uint8_t *out = static_cast<uint8_t *>(dst);
+    for (int r = 0; r < n_records; ++r) {
+        const uint8_t *blob = in + (uint64_t)r * d->expert_size;
+        for (int m = 0; m < 3; ++m) {
+            uint32_t gs;
+            memcpy(&gs, blob + m * nb, 4);
+            if (gs != 32)
+                return fail(RABBIT_CUDA_ERR_FORMAT, "tile_records: record %d blob %d has group size %u",
+                            r, m, gs);
+        }
+        uint8_t *o = out + (uint64_t)r * rec;
+        memset(o, 0, q.rec_stride);
+        rb::tile_pair_host(blob, blob + nb, q.plan.tb, o);
+        rb::tile_blob_host(blob + 2 * nb, q.plan.tc, o + q.off_d);
+        rb::fill_trailer(&q, o);
+    }
+    return ok();
+}
