@@ -160,6 +160,20 @@ int rabbit_cuda_tile_records(const rabbit_cuda_moe_desc *desc, int sm_count, con
  * whole expert table, resident), plus router/norm weights and scratch. */
 int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *desc, int device,
                            rabbit_cuda_moe **out);
+/* A pool for models larger than HBM (no counterpart in the reference, whose
+ * expert LRU cache, src/memory.c:94-193, holds at most 64 single records):
+ * HBM holds the records of `window_layers` layers at a time, one block per
+ * layer. Uploading a layer that has no block (rabbit_cuda_moe_upload or
+ * _upload_file, at most window_layers layers per call) takes the least
+ * recently used block, dropping the layer it held; the copies wait on the
+ * pool's side stream for the last kernel that read the block, and kernels on
+ * any stream wait for the copies into their layer's block, so an engine can
+ * upload layer l + 1 while layer l computes. Decoding a layer without a block
+ * returns RABBIT_CUDA_ERR_ARGS ("not uploaded"). window_layers >= n_layers is
+ * rabbit_cuda_moe_create. Tables shared by every layer (experts_shared) and
+ * rabbit_cuda_moe_fill_synthetic are not supported. */
+int rabbit_cuda_moe_create_window(const rabbit_cuda_moe_desc *desc, int device, int window_layers,
+                                  rabbit_cuda_moe **out);
 /* Stage records of layers [layer_begin, layer_end) host -> pinned -> HBM on the
  * pool's side stream (asynchronous; returns once queued). */
 int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end);

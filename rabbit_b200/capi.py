@@ -66,6 +66,7 @@ SIGNATURES = {
     "rabbit_cuda_moe_upload": (_I, [_P, _I, _I]),
     "rabbit_cuda_moe_upload_file": (_I, [_P, C.c_char_p, C.c_uint64, _I, _I]),
     "rabbit_cuda_tile_records": (_I, [_P, _I, _P, _I, _P, C.POINTER(C.c_uint64)]),
+    "rabbit_cuda_moe_create_window": (_I, [_P, _I, _I, _P]),
     "rabbit_cuda_moe_sync": (_I, [_P]),
     "rabbit_cuda_moe_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_moe_free": (_I, [_P]),
@@ -205,7 +206,10 @@ class MoePool:
     def __init__(self, *, records: np.ndarray, expert_size: int, n_layers: int, hidden: int,
                  n_experts: int, top_k: int, inter: int, n_shared: int = 0, quant: int = 4,
                  experts_per_layer: int | None = None, experts_shared: bool = False,
-                 rms_ffn, w_router, device: int = 0, upload: bool = True):
+                 rms_ffn, w_router, device: int = 0, upload: bool = True,
+                 window: int | None = None):
+        """window: HBM blocks for that many layers (rabbit_cuda_moe_create_window);
+        layers are then uploaded on demand and nothing is uploaded here."""
         if records is None:  # device-filled (fill_synthetic) or file-backed (upload_file) pool
             self._records = None
             n_records = n_layers * (experts_per_layer or (n_experts + n_shared))
@@ -224,7 +228,11 @@ class MoePool:
                     None if self._records is None else self._records.ctypes.data,
                     C.cast(rms_arr, C.POINTER(C.c_void_p)), C.cast(rt_arr, C.POINTER(C.c_void_p)))
         h = C.c_void_p()
-        check(lib().rabbit_cuda_moe_create(C.byref(d), device, C.byref(h)))
+        if window:
+            check(lib().rabbit_cuda_moe_create_window(C.byref(d), device, window, C.byref(h)))
+            upload = False
+        else:
+            check(lib().rabbit_cuda_moe_create(C.byref(d), device, C.byref(h)))
         self.handle = h
         self.hidden, self.n_layers = hidden, n_layers
         self.k = min(top_k if top_k > 0 else 2, n_experts, 8)

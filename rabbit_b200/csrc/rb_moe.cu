@@ -65,6 +65,14 @@ struct rabbit_cuda_moe {
     const uint8_t *host_map = nullptr;
     bool usable = false, fast = false;
     bool pretiled = false;  // records arrive in the tiled layout (RABBIT_CUDA_QUANT_INT4_TILED)
+    // Windowed pools (rabbit_cuda_moe_create_window): HBM blocks of epl records
+    // for `window` layers, reassigned least recently used first; 0: every
+    // layer has its own block. pool_records = the records HBM holds.
+    int window = 0, pool_records = 0;
+    std::vector<int> layer_block, block_layer;
+    std::vector<uint64_t> block_use;
+    uint64_t use_clock = 0;
+    std::vector<cudaEvent_t> block_ev, block_up_ev;  // last kernel reading / last copy into a block
     // pool
     uint8_t *pool = nullptr;
     uint64_t rec_stride = 0, pool_bytes = 0;
@@ -122,6 +130,13 @@ static bool g_moe_attr[kMaxDevices];
 
 static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_local) {
     if (layer < 0 || layer >= p->L) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d out of range", layer);
+    if (p->window) {  // the layer's block, if it holds one
+        const int b = p->layer_block[layer];
+        if (b < 0) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d not uploaded (not in the pool's window)", layer);
+        *base = b * p->epl;
+        *n_local = std::min(p->epl, p->n_records - layer * p->epl);
+        return RABBIT_CUDA_OK;
+    }
     if (p->shared_table) {
         *base = 0;
         *n_local = p->n_records;
@@ -130,6 +145,51 @@ static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_loca
         *n_local = std::min(p->epl, p->n_records - *base);
         if (*n_local < 0) *n_local = 0;
     }
+    return RABBIT_CUDA_OK;
+}
+
+// The pool records of `layer` for an upload: its block in a windowed pool
+// (taking the least recently used block, and dropping the layer it held, when
+// the layer has none: the side stream first waits for the last kernel that
+// read that block), else its place in the table. *src_base is the layer's
+// first record in the model's expert table.
+static int layer_slot(rabbit_cuda_moe *p, int layer, int *base, int *n_local, int *src_base) {
+    if (!p->window) {
+        const int st = layer_map(p, layer, base, n_local);
+        *src_base = *base;
+        return st;
+    }
+    if (layer < 0 || layer >= p->L) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d out of range", layer);
+    int b = p->layer_block[layer];
+    if (b < 0) {
+        b = 0;
+        for (int i = 1; i < p->window; ++i)
+            if (p->block_use[i] < p->block_use[b]) b = i;
+        if (p->block_layer[b] >= 0) p->layer_block[p->block_layer[b]] = -1;
+        std::fill(p->resident.begin() + (size_t)b * p->epl, p->resident.begin() + (size_t)(b + 1) * p->epl, 0);
+        RB_CUDA(cudaStreamWaitEvent(p->up, p->block_ev[b], 0));
+        p->block_layer[b] = layer;
+        p->layer_block[layer] = b;
+    }
+    p->block_use[b] = ++p->use_clock;
+    *base = b * p->epl;
+    *n_local = std::min(p->epl, p->n_records - layer * p->epl);
+    *src_base = layer * p->epl;
+    return RABBIT_CUDA_OK;
+}
+
+// Windowed pools: kernels on `s` that read the layer's block wait for the
+// copies into it, and later copies into the block wait for them.
+static int window_enter(rabbit_cuda_moe *p, int layer, cudaStream_t s) {
+    if (!p->window || layer < 0 || layer >= p->L || p->layer_block[layer] < 0) return RABBIT_CUDA_OK;
+    RB_CUDA(cudaStreamWaitEvent(s, p->block_up_ev[p->layer_block[layer]], 0));
+    return RABBIT_CUDA_OK;
+}
+static int window_leave(rabbit_cuda_moe *p, int layer, cudaStream_t s) {
+    if (!p->window || layer < 0 || layer >= p->L || p->layer_block[layer] < 0) return RABBIT_CUDA_OK;
+    const int b = p->layer_block[layer];
+    RB_CUDA(cudaEventRecord(p->block_ev[b], s));
+    p->block_use[b] = ++p->use_clock;
     return RABBIT_CUDA_OK;
 }
 
@@ -281,6 +341,10 @@ static void free_pool(rabbit_cuda_moe *p) {
         if (p->pin_ev[i]) cudaEventDestroy(p->pin_ev[i]);
     }
     if (p->pin_io) cudaFreeHost(p->pin_io);
+    for (cudaEvent_t ev : p->block_ev)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : p->block_up_ev)
+        if (ev) cudaEventDestroy(ev);
     for (int i = 0; i < kIoSlots; ++i) {
         if (p->io_raw[i]) cudaFreeHost(p->io_raw[i]);
         if (p->io_raw_ev[i]) cudaEventDestroy(p->io_raw_ev[i]);
@@ -339,9 +403,10 @@ static int check_trailer(const rabbit_cuda_moe *p, const uint8_t *rec, int gid) 
     return RABBIT_CUDA_OK;
 }
 
-static int upload_record(rabbit_cuda_moe *p, int gid) {
+// Record gid of the host map into pool record `pos`.
+static int upload_record(rabbit_cuda_moe *p, int gid, int pos) {
     const uint8_t *src = p->host_map + (uint64_t)gid * p->expert_size;
-    uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
+    uint8_t *dst = p->pool + (uint64_t)pos * p->rec_stride;
     int st;
     if (p->pretiled) {
         if ((st = check_trailer(p, src, gid)) != RABBIT_CUDA_OK) return st;
@@ -358,7 +423,7 @@ static int upload_record(rabbit_cuda_moe *p, int gid) {
         st = stage_h2d(p, dst, src, p->expert_size);
     }
     if (st != RABBIT_CUDA_OK) return st;
-    p->resident[gid] = 1;
+    p->resident[pos] = 1;
     p->uploads++;
     return RABBIT_CUDA_OK;
 }
@@ -410,7 +475,9 @@ using namespace rb;
 
 extern "C" {
 
-int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cuda_moe **out) {
+}  // extern "C"
+
+static int create_pool(const rabbit_cuda_moe_desc *d, int device, int window, rabbit_cuda_moe **out) {
     if (!d || !out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_create: NULL argument");
     *out = nullptr;
     if (d->n_layers <= 0 || d->hidden <= 0 || d->n_experts <= 0 || d->inter <= 0 ||
@@ -445,6 +512,14 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     p->epl = d->experts_per_layer > 0 ? d->experts_per_layer : d->n_experts;
     p->shared_table = d->experts_shared ? 1 : 0;
     p->host_map = static_cast<const uint8_t *>(d->expert_map);
+    if (window > 0 && window < p->L) {
+        if (p->shared_table) {
+            delete p;
+            return fail(RABBIT_CUDA_ERR_ARGS,
+                        "moe_create_window: a table shared by every layer has no per-layer blocks");
+        }
+        p->window = window;
+    }
 
     const uint64_t mat = (uint64_t)p->H * p->I;
     uint64_t need;
@@ -484,8 +559,22 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
 
     cudaError_t e = cudaSuccess;
     if (!p->fast) p->rec_stride = align_up(p->expert_size, 256);  // verbatim records
-    p->pool_bytes = p->rec_stride * (uint64_t)p->n_records;
-    p->resident.assign(p->n_records, 0);
+    p->pool_records = p->window ? p->window * p->epl : p->n_records;
+    p->pool_bytes = p->rec_stride * (uint64_t)p->pool_records;
+    p->resident.assign(p->pool_records, 0);
+    if (p->window) {
+        p->layer_block.assign(p->L, -1);
+        p->block_layer.assign(p->window, -1);
+        p->block_use.assign(p->window, 0);
+        p->block_ev.assign(p->window, nullptr);
+        p->block_up_ev.assign(p->window, nullptr);
+        for (int b = 0; b < p->window; ++b)
+            if ((e = cudaEventCreateWithFlags(&p->block_ev[b], cudaEventDisableTiming)) != cudaSuccess ||
+                (e = cudaEventCreateWithFlags(&p->block_up_ev[b], cudaEventDisableTiming)) != cudaSuccess) {
+                free_pool(p);
+                return cuda_fail(e, "moe_create: window events");
+            }
+    }
 
     const size_t HE = (size_t)p->H * p->E;
     if ((e = cudaMalloc(&p->pool, p->pool_bytes)) != cudaSuccess) {
@@ -568,6 +657,18 @@ int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cud
     return ok();
 }
 
+extern "C" {
+
+int rabbit_cuda_moe_create(const rabbit_cuda_moe_desc *d, int device, rabbit_cuda_moe **out) {
+    return create_pool(d, device, 0, out);
+}
+
+int rabbit_cuda_moe_create_window(const rabbit_cuda_moe_desc *d, int device, int window_layers,
+                                  rabbit_cuda_moe **out) {
+    if (window_layers < 1) return fail(RABBIT_CUDA_ERR_ARGS, "moe_create_window: window of %d layers", window_layers);
+    return create_pool(d, device, window_layers, out);
+}
+
 int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end) {
     if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: NULL pool");
     if (layer_begin < 0 || layer_end > p->L || layer_begin >= layer_end)
@@ -575,14 +676,18 @@ int rabbit_cuda_moe_upload(rabbit_cuda_moe *p, int layer_begin, int layer_end) {
                     layer_end);
     if (!p->host_map)
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: pool was created without a host map");
+    if (p->window && layer_end - layer_begin > p->window)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload: %d layers exceed the pool's window of %d",
+                    layer_end - layer_begin, p->window);
     RB_CUDA(cudaSetDevice(p->device));
     for (int l = layer_begin; l < layer_end; ++l) {
-        int base, n;
-        int st = layer_map(p, l, &base, &n);
+        int base, n, src;
+        int st = layer_slot(p, l, &base, &n, &src);
         if (st) return st;
         for (int r = 0; r < n; ++r)
-            if (!p->resident[base + r] && (st = upload_record(p, base + r)) != RABBIT_CUDA_OK)
+            if (!p->resident[base + r] && (st = upload_record(p, src + r, base + r)) != RABBIT_CUDA_OK)
                 return st;
+        if (p->window) RB_CUDA(cudaEventRecord(p->block_up_ev[p->layer_block[l]], p->up));
     }
     return ok();
 }
@@ -656,7 +761,7 @@ static bool read_record(int fd, bool direct, uint64_t off, uint64_t n, uint8_t *
 // reader thread into the pinned ring while this thread lays them out and
 // queues their copies.
 static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t expert_offset,
-                            const std::vector<int> &gids) {
+                            const std::vector<int> &gids, const std::vector<int> &dsts) {
     int st = ensure_io(p);
     if (st) return st;
     int fd = open(path, O_RDONLY | O_DIRECT);
@@ -703,7 +808,7 @@ static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t exper
     });
     const uint64_t nb = nbytes_g32((uint64_t)p->H * p->I);
     for (int i = 0; i < n && st == RABBIT_CUDA_OK; ++i) {
-        const int s = i % kIoSlots, gid = gids[i];
+        const int s = i % kIoSlots, gid = gids[i], pos = dsts[i];
         uint8_t *rec;
         {
             std::unique_lock<std::mutex> lk(mu);
@@ -718,7 +823,7 @@ static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t exper
             }
             rec = data[s];
         }
-        uint8_t *dst = p->pool + (uint64_t)gid * p->rec_stride;
+        uint8_t *dst = p->pool + (uint64_t)pos * p->rec_stride;
         cudaError_t e = cudaSuccess;
         if (p->pretiled && (st = check_trailer(p, rec, gid)) != RABBIT_CUDA_OK) break;
         if (p->fast && !p->pretiled) {
@@ -754,7 +859,7 @@ static int upload_from_file(rabbit_cuda_moe *p, const char *path, uint64_t exper
             }
             p->h2d_bytes += bytes;
         }
-        p->resident[gid] = 1;
+        p->resident[pos] = 1;
         p->uploads++;
         std::lock_guard<std::mutex> lk(mu);
         consumed = i + 1;  // the record buffer may be refilled (after its copy, for verbatim pools)
@@ -780,19 +885,26 @@ int rabbit_cuda_moe_upload_file(rabbit_cuda_moe *p, const char *path, uint64_t e
     if (layer_begin < 0 || layer_end > p->L || layer_begin >= layer_end)
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload_file: bad layer range [%d, %d)", layer_begin,
                     layer_end);
+    if (p->window && layer_end - layer_begin > p->window)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_upload_file: %d layers exceed the pool's window of %d",
+                    layer_end - layer_begin, p->window);
     RB_CUDA(cudaSetDevice(p->device));
-    std::vector<int> gids;
+    std::vector<int> gids, dsts;  // model record -> pool record
     for (int l = layer_begin; l < layer_end; ++l) {
-        int base, n;
-        const int st = layer_map(p, l, &base, &n);
+        int base, n, src;
+        const int st = layer_slot(p, l, &base, &n, &src);
         if (st) return st;
         for (int r = 0; r < n; ++r)
             if (!p->resident[base + r] &&
-                std::find(gids.begin(), gids.end(), base + r) == gids.end())
-                gids.push_back(base + r);
+                std::find(dsts.begin(), dsts.end(), base + r) == dsts.end()) {
+                gids.push_back(src + r);
+                dsts.push_back(base + r);
+            }
     }
-    if (gids.empty()) return ok();
-    const int st = rb::upload_from_file(p, path, expert_offset, gids);
+    int st = gids.empty() ? RABBIT_CUDA_OK : rb::upload_from_file(p, path, expert_offset, gids, dsts);
+    if (p->window)
+        for (int l = layer_begin; l < layer_end; ++l)
+            if (p->layer_block[l] >= 0) RB_CUDA(cudaEventRecord(p->block_up_ev[p->layer_block[l]], p->up));
     return st == RABBIT_CUDA_OK ? ok() : st;
 }
 
@@ -808,6 +920,8 @@ int rabbit_cuda_moe_fill_synthetic(rabbit_cuda_moe *p, uint64_t seed, float scal
     if (!p->fast)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_fill_synthetic: pool is not in the group-32 layout");
+    if (p->window)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_fill_synthetic: windowed pools load layers on demand");
     RB_CUDA(cudaSetDevice(p->device));
     const int blocks = p->ctx->sm_count * 8;
     const Tiling &tb = p->plan.tb, &tc = p->plan.tc;
@@ -839,8 +953,17 @@ int rabbit_cuda_moe_free(rabbit_cuda_moe *p) {
 namespace rb {
 // The body of rabbit_cuda_moe_decode_dev; `err` is the device word the fused
 // kernel records a failed wait in.
+static int decode_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                         int *d_ids, float *d_weights, cudaStream_t s, int *err);
 static int decode_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
                        int *d_ids, float *d_weights, cudaStream_t s, int *err) {
+    int st = window_enter(p, layer, s);
+    if (st == RABBIT_CUDA_OK) st = decode_launch(p, layer, d_h_in, d_h_out, d_ids, d_weights, s, err);
+    const int st2 = window_leave(p, layer, s);
+    return st ? st : st2;
+}
+static int decode_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                         int *d_ids, float *d_weights, cudaStream_t s, int *err) {
     if (p->ep_size > 1)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_decode: expert-parallel pools run the multi-token path");
@@ -1029,7 +1152,9 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     }
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
+    if ((st = window_enter(p, layer, s)) != RABBIT_CUDA_OK) return st;
     RB_CUDA(launch_fused(p, a, s));
+    if ((st = window_leave(p, layer, s)) != RABBIT_CUDA_OK) return st;
     p->hbm_hits++;
     return ok();
 }
@@ -1220,8 +1345,17 @@ static bool batch_items(const rabbit_cuda_moe *p, BatchItems *b) {
 }
 
 // The body of rabbit_cuda_moe_prefill_dev.
+static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                          int T, int *d_ids, float *d_w, cudaStream_t s);
 static int prefill_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out, int T,
                         int *d_ids, float *d_w, cudaStream_t s) {
+    int st = window_enter(p, layer, s);
+    if (st == RABBIT_CUDA_OK) st = prefill_launch(p, layer, d_h_in, d_h_out, T, d_ids, d_w, s);
+    const int st2 = window_leave(p, layer, s);
+    return st ? st : st2;
+}
+static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
+                          int T, int *d_ids, float *d_w, cudaStream_t s) {
     int base, n_local;
     int st = layer_map(p, layer, &base, &n_local);
     if (st) return st;
