@@ -1261,9 +1261,10 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int c = i & 1;
-                        const int low = p1[i] * 256 + p0[i] + m8[nb][c];
-                        const float dot = fmaf((float)p2[i], 65536.0f, (float)low) * un[nb][c];
-                        acc[j][nb][i] = fmaf(s[q][j][i >> 1], dot, acc[j][nb][i]);
+                        // sum (nib - 8) X exactly: |.| <= 2^30, and the plane
+                        // sums before the -8 sum X term stay below 2^31
+                        const int dot = p2[i] * 65536 + p1[i] * 256 + p0[i] + m8[nb][c];
+                        acc[j][nb][i] = fmaf(s[q][j][i >> 1], (float)dot * un[nb][c], acc[j][nb][i]);
                     }
                 }
             }
