@@ -1244,8 +1244,12 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     float *pin = nullptr;
     cudaError_t e = cudaMalloc(&blk, off);
     if (e != cudaSuccess) return cuda_fail(e, "moe_prefill: scratch");
+    // the router arrival counts start at zero; the fragment arrays too, so the
+    // unused columns of a unit always hold finite planes
+    const size_t frag_end = o_mrf + frag_r * U * (p->I / 32);
     if ((e = cudaMemset(static_cast<uint8_t *>(blk) + o_tc, 0, sizeof(unsigned) * cap)) !=
-        cudaSuccess) {
+            cudaSuccess ||
+        (e = cudaMemset(static_cast<uint8_t *>(blk) + o_xbf, 0, frag_end - o_xbf)) != cudaSuccess) {
         cudaFree(blk);
         return cuda_fail(e, "moe_prefill: scratch");
     }

@@ -1202,12 +1202,10 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
                                         int m, const uint2 *bf, const int2 *rf,
                                         float (&acc)[2][kTcNB][4]) {
     const int lane = threadIdx.x & 31, t = lane & 3;
-    bool cm[NB][2];  // readout columns 8 nb + 2 t (+ 1) in use
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-        cm[nb][0] = nb * 8 + 2 * t < m;
-        cm[nb][1] = nb * 8 + 2 * t + 1 < m;
-    }
+    // Columns past the unit's m read planes some earlier unit left in the
+    // fragment arrays (zeroed when they were allocated): finite, and their
+    // sums are never read out, so they need no masking.
+    (void)m;
     for (int gb = ks; gb < ngrp; gb += KS * BG) {
         uint2 b[BG][NB][3];
         int4 r[BG][NB];
@@ -1241,10 +1239,10 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
             float un[NB][2];
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb) {
-                m8[nb][0] = cm[nb][0] ? r[q][nb].x : 0;
-                un[nb][0] = cm[nb][0] ? __int_as_float(r[q][nb].y) : 0.f;
-                m8[nb][1] = cm[nb][1] ? r[q][nb].z : 0;
-                un[nb][1] = cm[nb][1] ? __int_as_float(r[q][nb].w) : 0.f;
+                m8[nb][0] = r[q][nb].x;
+                un[nb][0] = __int_as_float(r[q][nb].y);
+                m8[nb][1] = r[q][nb].z;
+                un[nb][1] = __int_as_float(r[q][nb].w);
             }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
