@@ -1219,17 +1219,16 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
             for (int nb = 0; nb < NB; ++nb) {
                 const uint2 *bp = bf + ((size_t)grp * 2 + nb) * 96 + lane * 3;
 #pragma unroll
-                for (int pl = 0; pl < 3; ++pl) b[q][nb][pl] = in ? bp[pl] : make_uint2(0u, 0u);
-                r[q][nb] = in ? *reinterpret_cast<const int4 *>(rf + (size_t)grp * kFragCols + nb * 8 + 2 * t)
-                              : make_int4(0, 0, 0, 0);
+                for (int pl = 0; pl < 3; ++pl) b[q][nb][pl] = bp[pl];
+                r[q][nb] = *reinterpret_cast<const int4 *>(rf + (size_t)grp * kFragCols + nb * 8 + 2 * t);
             }
+            // rows past the item and groups past the last read staged data
+            // (offset 0, group 0) and get scale 0: they add exactly nothing
 #pragma unroll
             for (int j = 0; j < 2; ++j)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    w[q][j][h] = in && v[j][h]
-                                     ? *reinterpret_cast<const uint32_t *>(nib + on[j][h] + 16 * grp)
-                                     : 0u;
+                    w[q][j][h] = *reinterpret_cast<const uint32_t *>(nib + on[j][h] + 16 * grp);
                     s[q][j][h] = in && v[j][h] ? sc[os[j][h] + grp] : 0.f;
                 }
         }
