@@ -1200,7 +1200,7 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
                                         const uint32_t (&on)[2][2], const uint32_t (&os)[2][2],
                                         const bool (&v)[2][2], int MBW, int ks, int KS, int ngrp,
                                         int m, const uint2 *bf, const int2 *rf,
-                                        float (&acc)[2][kTcNB][4]) {
+                                        float (&acc)[2][NB][4]) {
     const int lane = threadIdx.x & 31, t = lane & 3;
     // Columns past the unit's m read planes some earlier unit left in the
     // fragment arrays (zeroed when they were allocated): finite, and their
@@ -1269,6 +1269,33 @@ __device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
     }
 }
 
+// One warp's part of tc_item for NB column blocks: its accumulators (sized
+// for NB, so the one-block case keeps no idle registers), the MMA loop, and
+// the store of its fragment sums to red.
+template <int NB, int BG>
+__device__ __forceinline__ void tc_warp(const uint8_t *st, const float *sc,
+                                        const uint32_t (&on)[2][2], const uint32_t (&os)[2][2],
+                                        const bool (&v)[2][2], int MB, int MBW, int rs, int RS,
+                                        int ks, int KS, int ngrp, int m, const uint2 *bf,
+                                        const int2 *rf, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float acc[2][NB][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][nb][i] = 0.f;
+    tc_rows<NB, BG>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+            if (j < MBW && rs + j * RS < MB)
+                *reinterpret_cast<float4 *>(&red[(((size_t)warp * 2 + j) * kTcNB + nb) * 128 + lane * 4]) =
+                    make_float4(acc[j][nb][0], acc[j][nb][1], acc[j][nb][2], acc[j][nb][3]);
+}
+
 // The integer tensor-core products of one staged item (rows R < nrows, laid
 // out as sg) against the unit's m <= 16 columns, per group of 32:
 //   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
@@ -1304,24 +1331,10 @@ __device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, 
                                     : (uint32_t)R * (sg.ss / 4);
         }
     const float *sc = reinterpret_cast<const float *>(st + sg.sc_off);
-    float acc[2][kTcNB][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int nb = 0; nb < kTcNB; ++nb)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[j][nb][i] = 0.f;
     if (NBu == 1)
-        tc_rows<1, 3>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
+        tc_warp<1, 3>(st, sc, on, os, v, MB, MBW, rs, RS, ks, KS, ngrp, m, bf, rf, red);
     else
-        tc_rows<kTcNB, 1>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int nb = 0; nb < kTcNB; ++nb)
-            if (j < MBW && rs + j * RS < MB && nb < NBu)
-                *reinterpret_cast<float4 *>(&red[(((size_t)warp * 2 + j) * kTcNB + nb) * 128 + lane * 4]) =
-                    make_float4(acc[j][nb][0], acc[j][nb][1], acc[j][nb][2], acc[j][nb][3]);
+        tc_warp<kTcNB, 1>(st, sc, on, os, v, MB, MBW, rs, RS, ks, KS, ngrp, m, bf, rf, red);
     __syncthreads();
 }
 
