@@ -50,3 +50,21 @@ def test_tile_records_refuses_other_formats(rc):
         rc.tile_records(bad, size, **SHAPE)
     with pytest.raises(rc.RabbitCudaError):
         rc.tile_records(recs, size, **SHAPE, sm_count=0)
+
+
+@pytest.mark.parametrize("shape", [
+    dict(hidden=128, n_experts=8, top_k=2, inter=2048, n_shared=0),   # W2 in two column chunks
+    dict(hidden=2048, n_experts=64, top_k=6, inter=1408, n_shared=2),  # DeepSeek-MoE-16B shape
+    dict(hidden=256, n_experts=16, top_k=3, inter=96, n_shared=2),     # inter not a multiple of 128
+])
+def test_tiled_bytes_match_for_other_shapes(rc, shape):
+    H, I = shape["hidden"], shape["inter"]
+    recs, size, _, _ = synth.moe_layer(3, H, 2, I, 0)  # two records of this shape
+    tiled, tsize = rc.tile_records(recs, size, **shape)
+    nb = synth.int4_nbytes(H * I)
+    for r in range(2):
+        rec = recs[r * size:(r + 1) * size]
+        body = tiled[r * tsize:(r + 1) * tsize - 256]
+        payload = sum(int(rec[m * nb + 4:(m + 1) * nb].astype(np.int64).sum()) for m in range(3))
+        assert int(body.astype(np.int64).sum()) == payload
+        assert bytes(tiled[(r + 1) * tsize - 256:(r + 1) * tsize - 248]) == b"RB2TILE1"
