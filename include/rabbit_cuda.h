@@ -212,7 +212,10 @@ int rabbit_cuda_moe_free(rabbit_cuda_moe *p);
  * Returns the k used through *k_out (may be NULL). */
 int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
                            int *ids, float *weights, int *k_out);
-/* Same on DEVICE buffers, asynchronous on `stream` (16-byte aligned h). */
+/* Same on DEVICE buffers, asynchronous on `stream` (16-byte aligned h). The
+ * values the kernel's CTAs share are tagged with a number the host picks for
+ * each call, so a call made while `stream` is capturing a CUDA graph (whose
+ * replays would all reuse one tag) returns RABBIT_CUDA_ERR_UNSUPPORTED. */
 int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                float *d_h_out, int *d_ids, float *d_weights, void *stream);
 /* No counterpart in the reference (its moe_step runs on the CPU). The same
@@ -221,19 +224,23 @@ int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_i
  * device's memory between its own arenas, or a serving loop that cannot take
  * the device-wide synchronisation a cudaMalloc/cudaFree brings. The call
  * allocates nothing and frees nothing; its scratch (router scores, the SwiGLU
- * activations, the down-projection rows and per-CTA flags) is a fixed 2 MiB array inside this library, present on every
- * device that loads it until the process exits. Models whose scratch does not
- * fit -- about 5 KB + E*8 + (k + S) * (I + C * H) * 8 bytes, with C the number
- * of column chunks of W2 (I / 1024 when I is a multiple of 1024) -- are
- * rejected with RABBIT_CUDA_ERR_ARGS, pools not
- * in the group-32 layout with RABBIT_CUDA_ERR_UNSUPPORTED. The first call on
- * each device looks up the array's device address (once, with that device
- * current); make that first call before any stream capture. Every call uses
- * the same array, which keeps what the last call left there: the values its
- * CTAs share carry a tag new to each call, so leftovers are never read. Calls
- * that overlap on the GPU (other streams, other pools on the same device) race
- * on the array and give wrong results. d_ids / d_weights may be NULL. Errors
- * surface through
+ * activations, the down-projection rows and per-CTA flags) is a fixed 2 MiB
+ * array inside this library, present on every device that loads it until the
+ * process exits. A model fits when
+ *   256 + 4096 + A(E * 8) + A((k + S) * I * 8) + (k + S) * C * H * 8
+ * is at most 2 MiB, with A(x) = x rounded up to a multiple of 256 and C the
+ * number of column chunks of W2 (the I / 32 groups of a W2 row split into
+ * chunks of the largest divisor of I / 32 up to 32; C = I / 1024 when I is a
+ * multiple of 1024); larger models are rejected with RABBIT_CUDA_ERR_ARGS,
+ * pools not in the group-32 layout with RABBIT_CUDA_ERR_UNSUPPORTED. The
+ * first call on each device looks up the array's device address (once, with
+ * that device current); make that first call before any stream capture. As
+ * for rabbit_cuda_moe_decode_dev, a call made while `stream` is capturing
+ * returns RABBIT_CUDA_ERR_UNSUPPORTED. Every call uses the same array, which
+ * keeps what the last call left there: the values its CTAs share carry a tag
+ * new to each call, so leftovers are never read. Calls that overlap on the GPU
+ * (other streams, other pools on the same device) race on the array and give
+ * wrong results. d_ids / d_weights may be NULL. Errors surface through
  * rabbit_cuda_moe_check as for rabbit_cuda_moe_decode_dev. */
 int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                        float *d_h_out, int *d_ids, float *d_weights,

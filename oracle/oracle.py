@@ -34,11 +34,13 @@ def build_oracle() -> Path:
 
 
 def build_reference(ref_src: str | None = None) -> Path | None:
-    """Compile _ref/libref.so from the reference sources when they are present."""
-    src = ref_src or os.environ.get("RABBIT_REF_SRC", "/root/reference/src")
+    """Compile _ref/libref.so from the reference sources (`ref_src`, else the
+    RABBIT_REF_SRC environment variable: the reference checkout's src/). Returns
+    None when the library is not built and no sources are given."""
     if REF_SO.exists():
         return REF_SO
-    if not Path(src, "quant.c").exists():
+    src = ref_src or os.environ.get("RABBIT_REF_SRC")
+    if not src or not Path(src, "quant.c").exists():
         return None
     subprocess.check_call(["make", "-s", "-C", str(HERE), "ref", f"REF_SRC={src}"])
     return REF_SO

@@ -1,6 +1,6 @@
 """Build librabbit_cuda.so (sm_100a) in-tree with nvcc.
 
-    python -m rabbit_b200.build [--force] [--debug]
+    python -m rabbit_b200.build [--force]
 
 Each csrc/*.cu is compiled to an object under rabbit_b200/_build/ and linked
 into rabbit_b200/librabbit_cuda.so with the CUDA runtime linked statically,
@@ -32,13 +32,10 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _flags(debug: bool) -> list[str]:
-    f = ARCH + ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-                "-I" + str(ROOT / "include"), "--expt-relaxed-constexpr", "-Xptxas",
-                "-warn-spills"]
-    if debug:
-        f += ["-DRABBIT_CUDA_DEBUG=1"]
-    return f
+def _flags() -> list[str]:
+    return ARCH + ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+                   "-I" + str(ROOT / "include"), "--expt-relaxed-constexpr", "-Xptxas",
+                   "-warn-spills"]
 
 
 def _stale(obj: Path, src: Path, headers: list[Path]) -> bool:
@@ -48,7 +45,7 @@ def _stale(obj: Path, src: Path, headers: list[Path]) -> bool:
     return any(p.stat().st_mtime > t for p in [src, *headers])
 
 
-def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Path:
+def build(force: bool = False, verbose: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(
@@ -59,7 +56,7 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
         obj = BUILD / (src.stem + ".o")
         objs.append(obj)
         if force or _stale(obj, src, headers):
-            cmd = [nvcc(), *_flags(debug), "-dc" if False else "-c", str(src), "-o", str(obj)]
+            cmd = [nvcc(), *_flags(), "-c", str(src), "-o", str(obj)]
             if verbose:
                 print(" ".join(cmd), flush=True)
             subprocess.check_call(cmd)
@@ -78,10 +75,9 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
-    ap.add_argument("--debug", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args(argv)
-    print(build(a.force, a.debug, a.verbose))
+    print(build(a.force, a.verbose))
     return 0
 
 

@@ -217,6 +217,22 @@ static unsigned next_seq(unsigned *seq, void *tagged[], const size_t bytes[], in
     return (*seq)++;
 }
 
+// The fused decode tags what its CTAs share with a number the host picks at
+// call time (next_seq). A launch recorded into a CUDA graph would keep that
+// number on every replay, so a replay could accept values an earlier replay
+// left behind; calls made while their stream is capturing are refused.
+static int refuse_capture(cudaStream_t s, const char *who) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const cudaError_t e = cudaStreamIsCapturing(s, &cs);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "%s: the stream is being captured; each launch needs a tag chosen when it "
+                    "is issued, so this call cannot be recorded into a graph",
+                    who);
+    return RABBIT_CUDA_OK;
+}
+
 // One fused decode launch, programmatic-dependent: it may start while the
 // kernel before it on the stream finishes (it waits for that kernel before it
 // reads h or touches scratch), which hides the launch gap between layers.
@@ -1054,6 +1070,7 @@ extern "C" {
 int rabbit_cuda_moe_decode_dev(rabbit_cuda_moe *p, int layer, const float *d_h_in,
                                float *d_h_out, int *d_ids, float *d_weights, void *stream) {
     if (!p || !d_h_in || !d_h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: NULL argument");
+    if (int st = refuse_capture(as_stream(stream, p->ctx), "moe_decode_dev")) return st;
     return decode_impl(p, layer, d_h_in, d_h_out, d_ids, d_weights, as_stream(stream, p->ctx),
                        p->ctx->d_err);
 }
@@ -1091,6 +1108,7 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
                                        void *stream) {
     if (!p || !d_h_in || !d_h_out)
         return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: NULL argument");
+    if (int st = refuse_capture(as_stream(stream, p->ctx), "moe_decode_noalloc")) return st;
     if (!p->fast)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_decode_noalloc: pool is not in the group-32 fused layout");

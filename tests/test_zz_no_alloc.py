@@ -80,11 +80,12 @@ def test_noalloc_matches_decode_dev(rc, name):
 
 
 def test_noalloc_rejects_scratch_over_limit(rc):
-    """(k + S) * I * 4 bytes of activations past the 1 MiB array: a clear error,
-    nothing launched; the pool still decodes through decode_dev."""
+    """The SwiGLU activations alone, (k + S) * I tagged values of 8 bytes each
+    (24 * 16384 * 8 = 3 MiB), exceed the 2 MiB array: a clear error, nothing
+    launched; the pool still decodes through decode_dev."""
     import torch
 
-    H, E, k, I, S = 64, 8, 8, 16384, 8
+    H, E, k, I, S = 64, 8, 8, 16384, 16
     pool = _pool(rc, H, E, k, I, S, seed=11, n_layers=1)
     h = torch.randn(H, device="cuda:0")
     out = torch.empty_like(h)
@@ -94,4 +95,32 @@ def test_noalloc_rejects_scratch_over_limit(rc):
     pool.decode_dev(0, h.data_ptr(), out.data_ptr(), 0, 0, stream)
     pool.check(stream)
     assert torch.isfinite(out).all()
+    pool.free()
+
+
+def test_noalloc_refuses_a_capturing_stream(rc):
+    """Each call tags the values its CTAs share with a number picked when the
+    call is issued; a graph replay would reuse it, so calls on a stream that
+    is being captured are refused before anything is recorded, and the pool
+    decodes normally afterwards."""
+    import torch
+
+    H, E, k, I, S = SHAPES["tiny_shared"]
+    pool = _pool(rc, H, E, k, I, S, seed=5, n_layers=1)
+    h = torch.randn(H, device="cuda:0")
+    out = torch.empty_like(h)
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        with pytest.raises(rc.RabbitCudaError, match="captured"):
+            pool.decode_dev_noalloc(0, h.data_ptr(), out.data_ptr(), 0, 0, side.cuda_stream)
+        with pytest.raises(rc.RabbitCudaError, match="captured"):
+            pool.decode_dev(0, h.data_ptr(), out.data_ptr(), 0, 0, side.cuda_stream)
+    del graph
+    stream = torch.cuda.current_stream().cuda_stream
+    want = torch.empty_like(h)
+    pool.decode_dev(0, h.data_ptr(), want.data_ptr(), 0, 0, stream)
+    pool.decode_dev_noalloc(0, h.data_ptr(), out.data_ptr(), 0, 0, stream)
+    pool.check(stream)
+    np.testing.assert_allclose(out.cpu().numpy(), want.cpu().numpy(), rtol=RTOL, atol=ATOL)
     pool.free()
