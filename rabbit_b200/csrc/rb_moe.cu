@@ -112,6 +112,10 @@ struct rabbit_cuda_moe {
     float *bt_w = nullptr;   // [bt_cap][8]
     float *bt_pin = nullptr; // pinned [bt_cap][H] + ids/weights
     int ep_rank = 0, ep_size = 1;  // expert-parallel share of the multi-token path
+    // tensor maps of the multi-token GEMMs over the pool's GU and D nibble
+    // rows (tc_ok: built; otherwise the multi-token path runs per token)
+    CUtensorMap tm_gu{}, tm_dn{};
+    bool tc_ok = false;
     // counters
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
     std::vector<uint8_t> img;  // host image of one record in the tiled layout
@@ -618,6 +622,16 @@ static int create_pool(const rabbit_cuda_moe_desc *d, int device, int window, ra
             cudaSuccess) {
         free_pool(p);
         return cuda_fail(e, "moe_create: scratch");
+    }
+    if (p->fast) {
+        const int tm = tc_tensor_maps(p->pool, p->pool_bytes, p->rec_stride, p->off_d, p->plan.tb,
+                                      p->plan.tc, p->H, &p->tm_gu, &p->tm_dn);
+        if (tm == 2) {
+            free_pool(p);
+            return fail(RABBIT_CUDA_ERR_DEVICE,
+                        "moe_create: the driver could not encode the expert pool's tensor maps");
+        }
+        p->tc_ok = tm == 0;
     }
     p->h_out = reinterpret_cast<float *>(p->dio);
     p->ids_int = reinterpret_cast<int *>(p->dio + sizeof(float) * (size_t)p->H);
@@ -1242,15 +1256,15 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t o_ns = take(sizeof(int) * cap);
     const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
     const size_t o_pt = take(sizeof(int) * P);
-    // work units: each record's pairs in runs of kBatchTokChunk, so at most
-    // one per kBatchTokChunk pairs plus one partial run per record
-    const size_t U = P / kBatchTokChunk + R;
-    const size_t o_act = take(sizeof(int) * U * 3 + 2 * sizeof(int));
+    // work units: each record's pairs in runs of kTcUnit, so at most one per
+    // kTcUnit pairs plus one partial run per record
+    const size_t U = P / kTcUnit + R;
+    const size_t o_act = take(sizeof(int) * U * 4 + 2 * sizeof(int));
     const size_t o_pu = take(sizeof(int) * P);
-    // activation planes in MMA fragment order, per unit and group (kFragCols)
-    const size_t frag_b = sizeof(uint2) * 2 * 32 * 3, frag_r = sizeof(int2) * kFragCols;
-    const size_t o_xbf = take(frag_b * U * (p->H / 32)), o_xrf = take(frag_r * U * (p->H / 32));
-    const size_t o_mbf = take(frag_b * U * (p->I / 32)), o_mrf = take(frag_r * U * (p->I / 32));
+    // B rows of the units: three per pair, each unit padded by at most 15
+    const size_t rows = 3 * P + 15 * U;
+    const size_t o_xim = take(rows * (size_t)p->H), o_mim = take(rows * (size_t)p->I);
+    const size_t o_xu = take(sizeof(float) * P), o_mu = take(sizeof(float) * P);
     const size_t o_sc = take(sizeof(float) * cap * p->E);
     const size_t o_tc = take(sizeof(unsigned) * cap);
     const size_t o_mid = take(sizeof(float) * P * p->I);
@@ -1262,12 +1276,11 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     float *pin = nullptr;
     cudaError_t e = cudaMalloc(&blk, off);
     if (e != cudaSuccess) return cuda_fail(e, "moe_prefill: scratch");
-    // the router arrival counts start at zero; the fragment arrays too, so the
-    // unused columns of a unit always hold finite planes
-    const size_t frag_end = o_mrf + frag_r * U * (p->I / 32);
+    // the router arrival counts start at zero; the B rows too (a unit's rows
+    // past its pairs' are multiplied, their results never read)
     if ((e = cudaMemset(static_cast<uint8_t *>(blk) + o_tc, 0, sizeof(unsigned) * cap)) !=
             cudaSuccess ||
-        (e = cudaMemset(static_cast<uint8_t *>(blk) + o_xbf, 0, frag_end - o_xbf)) != cudaSuccess) {
+        (e = cudaMemset(static_cast<uint8_t *>(blk) + o_xim, 0, o_xu - o_xim)) != cudaSuccess) {
         cudaFree(blk);
         return cuda_fail(e, "moe_prefill: scratch");
     }
@@ -1291,12 +1304,13 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     a.act = reinterpret_cast<int *>(b + o_act);
     a.act_off = a.act + U;
     a.act_cnt = a.act_off + U;
-    a.n_act = a.act_cnt + U;
+    a.img_off = a.act_cnt + U;
+    a.n_act = a.img_off + U;
     a.pair_u = reinterpret_cast<int *>(b + o_pu);
-    a.xbf = reinterpret_cast<uint2 *>(b + o_xbf);
-    a.xrf = reinterpret_cast<int2 *>(b + o_xrf);
-    a.mbf = reinterpret_cast<uint2 *>(b + o_mbf);
-    a.mrf = reinterpret_cast<int2 *>(b + o_mrf);
+    a.xim = b + o_xim;
+    a.mim = b + o_mim;
+    a.xunit = reinterpret_cast<float *>(b + o_xu);
+    a.munit = reinterpret_cast<float *>(b + o_mu);
     a.scores = reinterpret_cast<float *>(b + o_sc);
     a.tcount = reinterpret_cast<unsigned *>(b + o_tc);
     a.mid = reinterpret_cast<float *>(b + o_mid);
@@ -1324,46 +1338,24 @@ static cudaError_t launch_batch(int which, dim3 grid, dim3 block, size_t smem, c
     return cudaLaunchKernelExC(&cfg, moe_batch_kernel(which), args);
 }
 
-// The batch kernels' static shared memory (mbarriers) stays under 1 KB:
-// dynamic sizes leave that room.
+// The batch kernels' static shared memory stays under 1 KB: dynamic sizes
+// leave that room.
 constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
-// Largest work item (weight rows) of the multi-token GEMM kernels: four
-// 16-row MMA blocks.
-constexpr int kTcItemRows = 64;
 
-// Work items of the multi-token gate/up and down kernels: consecutive tiles
-// per item, the largest count (up to kTcItemRows rows) for which two item
-// buffers and the warps' partial sums fit in shared memory, then as many item
-// buffers as fit (up to kTcMaxBuf): nbuf - 1 items are in flight while one is
-// computed. (Measured on the DeepSeek-shaped chunk: 64-row items with two
-// buffers beat 32-row items with four by 13%.) False when the layer's tiles cannot
-// be staged (a row wider than shared memory holds, or a tile's scale block
-// that is not a whole number of 16-byte units).
-struct BatchItems {
-    int gu_tpi = 1, dn_tpi = 1, gu_nbuf = 2, dn_nbuf = 2;
-    size_t gu_smem = 0, dn_smem = 0;
-};
-static bool batch_items(const rabbit_cuda_moe *p, BatchItems *b) {
-    const Tiling &tb = p->plan.tb, &tc = p->plan.tc;
-    const size_t red = sizeof(float) * kTcRedFloats;
-    auto plan = [&](int tile_rows, int ntiles, int nib, int sc, int *tpi, int *nbuf,
-                    size_t *smem) {
-        size_t bytes = 0;
-        *tpi = 0;
-        for (int t = 1; tile_rows * t <= 64 && (t == 1 || (tile_rows * t <= kTcItemRows && t <= ntiles));
-             t *= 2) {
-            const StageGeom g = stage_geom(tile_rows * t, tile_rows, nib, sc);
-            if (!g.ok || red + 2 * (size_t)g.bytes > kBatchDynMax) break;
-            *tpi = t;
-            bytes = g.bytes;
-        }
-        if (*tpi == 0) return false;
-        *nbuf = (int)std::min<size_t>(kTcMaxBuf, (kBatchDynMax - red) / bytes);
-        *smem = (size_t)*nbuf * bytes + red;
-        return true;
-    };
-    return plan(2 * tb.TR, tb.rtiles, p->H / 2, p->H / 8, &b->gu_tpi, &b->gu_nbuf, &b->gu_smem) &&
-           plan(tc.TR, tc.rtiles, tc.cols / 2, tc.cols / 8, &b->dn_tpi, &b->dn_nbuf, &b->dn_smem);
+static cudaError_t launch_tc(int which, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             void *arg) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {arg};
+    return cudaLaunchKernelExC(&cfg, moe_tc_kernel(which), args);
 }
 
 // The body of rabbit_cuda_moe_prefill_dev.
@@ -1385,8 +1377,7 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
         if (!p->resident[base + r])
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: layer %d not uploaded", layer);
     RB_CUDA(cudaSetDevice(p->device));
-    BatchItems bi;
-    const bool batch = p->fast && batch_items(p, &bi);
+    const bool batch = p->tc_ok;
     if (!batch && p->ep_size > 1)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
                     "moe_prefill: expert-parallel pools need the group-32 layout");
@@ -1405,10 +1396,14 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     if (bucket_smem > kBatchDynMax)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
     if (!g_batch_attr[p->device]) {
-        for (int i = 0; i <= 3; ++i)
+        for (int i : {0, 1})
             RB_CUDA(cudaFuncSetAttribute(moe_batch_kernel(i),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kBatchDynMax));
+        for (int i : {1, 3})
+            RB_CUDA(cudaFuncSetAttribute(moe_tc_kernel(i),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tc_gemm_smem()));
         g_batch_attr[p->device] = true;
     }
     MoeBatchArgs a = p->bt;
@@ -1434,25 +1429,22 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     a.tc = p->plan.tc;
     a.err = p->ctx->d_err;
     a.wait_ns = wait_limit_ns();
-    a.gu_tpi = bi.gu_tpi;
-    a.dn_tpi = bi.dn_tpi;
-    a.gu_nbuf = bi.gu_nbuf;
-    a.dn_nbuf = bi.dn_nbuf;
     a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
     a.ep_rank = p->ep_rank;
     a.ep_size = p->ep_size;
     RB_CUDA(launch_batch(0, dim3(T, (p->E + a.route_split - 1) / a.route_split), dim3(256),
                          sizeof(float) * (size_t)std::max(p->E, p->H), s, a));
     RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
-    // planes: one thread per (pair, group), pairs counted on the device
-    const long long pairs_max = (long long)T * std::max(1, std::min(kMaxSlots, p->k + p->S));
-    auto planes_grid = [&](int G) {
-        return dim3((unsigned)std::max(1LL, std::min<long long>(4 * sms, (pairs_max * G + 255) / 256)));
-    };
-    RB_CUDA(launch_batch(5, planes_grid(p->H / 32), dim3(256), 0, s, a));
-    RB_CUDA(launch_batch(2, dim3(sms), dim3(kBatchThreads), bi.gu_smem, s, a));
-    RB_CUDA(launch_batch(6, planes_grid(p->I / 32), dim3(256), 0, s, a));
-    RB_CUDA(launch_batch(3, dim3(sms), dim3(kBatchThreads), bi.dn_smem, s, a));
+    // B rows: one CTA per pair (pairs counted on the device; the rest leave)
+    const unsigned pairs_max = (unsigned)T * std::max(1, std::min(kMaxSlots, p->k + p->S));
+    TcGemmArgs ga;
+    ga.b = a;
+    ga.tmap = p->tm_gu;
+    RB_CUDA(launch_tc(0, dim3(pairs_max), dim3(256), 0, s, &a));
+    RB_CUDA(launch_tc(1, dim3(sms), dim3(kTcThreads), tc_gemm_smem(), s, &ga));
+    RB_CUDA(launch_tc(2, dim3(pairs_max), dim3(256), 0, s, &a));
+    ga.tmap = p->tm_dn;
+    RB_CUDA(launch_tc(3, dim3(sms), dim3(kTcThreads), tc_gemm_smem(), s, &ga));
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
     p->hbm_hits += T;
     return ok();

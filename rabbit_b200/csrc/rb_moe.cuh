@@ -2,6 +2,8 @@
 #pragma once
 #include <stdint.h>
 
+#include <cuda.h>
+
 #include "rb_device.cuh"
 #include "rb_gemv.cuh"
 
@@ -64,74 +66,31 @@ inline bool combine_packed(int KC) { return KC < 8; }
 
 // ------------------------------------------------------- multi-token path --
 // T tokens through one layer's MoE block, each as moe_step (forward_v2.c:
-// 362-402) would take it alone, with every active expert's tiles read once for
-// all the tokens routed to it:
+// 362-402) would take it alone, with every active expert's tiles read once
+// per work unit for all the pairs routed to it:
 //   k_batch_route   grid (token, router slice): rmsnorm, the slice's router
 //                   rows; the token's last CTA to finish: top-k, slots;
 //   k_batch_bucket  one CTA: per local record, the (token, slot) pairs that
 //                   use it, in token order (bitmask ranks: deterministic),
-//                   cut into units of at most kBatchTokChunk pairs;
-//   k_batch_xplanes xn as activation planes (the integer MMA's B operand);
-//   k_batch_gu      (unit, GU tile) items: mid = silu(gate) * up for the
-//                   unit's tokens, integer tensor-core MMAs per group;
-//   k_batch_mplanes mid as activation planes;
-//   k_batch_down    (unit, D tile) items: each column chunk's down rows per
-//                   pair, integer tensor-core MMAs per group;
+//                   cut into units of at most kTcUnit pairs;
+//   k_tc_images     xn as the tensor-core MMA's B rows, per unit;
+//   k_tc_gemm<1>    (unit, 128 rows of W1 and of W3) items: mid = silu(gate)
+//                   * up for the unit's pairs (tcgen05, kind::i8);
+//   k_tc_images     mid as B rows;
+//   k_tc_gemm<0>    (unit, W2 column chunk, 256 rows) items: each chunk's
+//                   down rows per pair;
 //   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
 //                   order (forward_v2.c:356-357, 398-399).
 constexpr int kMaxBatchTokens = 256;
-constexpr int kBatchTokChunk = 16;  // tokens per work unit (two n8 blocks of the MMA)
-constexpr int kBatchThreads = 512;  // threads of k_batch_gu / k_batch_down
-// The activation planes of the multi-token kernels, kept in the order the
-// integer MMA (m16n8k32, B operand) reads them. For work unit u, group g of
-// 32 activations and 8-column block nb, lane l = 4 i + t of a warp loads
-// three uint2 at bfrag[((u G + g) 2 + nb) 32 + l]: planes 0..2 of
-// X = rint(x 2^(22-e)) of column 8 nb + i, each as (bytes of the even
-// elements 8t, 8t+2, 8t+4, 8t+6 ; bytes of the odd ones) -- the k order of
-// the nibble operand (see make_xplanes). The readout terms of column c,
-// (-8 sum X, the unit 2^(e-22) as float bits), are at rfrag[(u G + g) 16 + c].
-constexpr int kFragCols = 16;  // columns of one unit (= kBatchTokChunk)
-// One multi-token work item of `rows` weight rows staged in shared memory.
-// Banded (when a band's nibble rows fill at least 4 KB, so its copies stay
-// large): 8 bands of u = 2 ceil(rows / 16) consecutive rows, nibble rows at
-// stride ns within a band and bands at a stride bs = 16 (mod 128) bytes, so
-// the 8 rows a tensor-core fragment reads (one per band) start in distinct
-// banks; the scale rows banded the same way when every band's (and tile's)
-// scale rows are a whole number of 16-byte units (sc_band), else the tiles'
-// scale blocks back to back. Otherwise the rows in order (fragment rows g and
-// g + 8 of block mb are rows 16 mb + g and + 8), two copies per tile.
-struct StageGeom {
-    int u;             // rows per band
-    uint32_t ns, bs;   // nibble row stride, band stride (bytes)
-    uint32_t ss, sbs;  // scale row stride, band stride (sc_band)
-    uint32_t sc_off;   // scales' offset
-    uint32_t bytes;    // the item's buffer, 128-byte aligned
-    bool banded, sc_band, ok;  // ok: every copy a whole number of 16-byte units
-};
-__host__ __device__ inline StageGeom stage_geom(int rows, int tile_rows, int nib_bytes, int sc_bytes) {
-    StageGeom g;
-    g.u = 2 * ((rows + 15) / 16);
-    g.banded = (size_t)g.u * nib_bytes >= 4096;
-    g.ns = (uint32_t)nib_bytes;
-    g.bs = g.banded ? (uint32_t)align_up((size_t)g.u * nib_bytes, 128) + 16 : 0u;
-    g.sc_band = g.banded && ((size_t)g.u * sc_bytes) % 16 == 0 &&
-                ((size_t)tile_rows * sc_bytes) % 16 == 0;
-    g.ss = (uint32_t)sc_bytes;
-    g.sbs = g.sc_band ? (uint32_t)align_up((size_t)g.u * sc_bytes, 128) + 16 : 0u;
-    g.sc_off = g.banded ? 8 * g.bs : (uint32_t)align_up((size_t)rows * nib_bytes, 16);
-    g.bytes = (uint32_t)align_up(
-        (size_t)g.sc_off + (g.sc_band ? 8 * (size_t)g.sbs : (size_t)rows * sc_bytes), 128);
-    g.ok = nib_bytes % 16 == 0 && (g.sc_band || ((size_t)tile_rows * sc_bytes) % 16 == 0) &&
-           (g.banded || ((size_t)tile_rows * nib_bytes) % 16 == 0);
-    return g;
-}
-// Most work-item buffers of a multi-token GEMM kernel. Measured on the
-// DeepSeek- and Mixtral-8x22B-shaped chunks: 2 (one item in flight while one
-// is computed) beat 3, 4 and 8 buffers by 1-3%.
-constexpr int kTcMaxBuf = 2;
-// Warp partial sums of the multi-token tensor-core tiles: per warp two 16-row
-// blocks x two 8-column blocks of 16x8 fragments.
-constexpr int kTcRedFloats = (kBatchThreads / 32) * 2 * (kBatchTokChunk / 8) * 128;
+constexpr int kTcUnit = 32;          // pairs per work unit
+constexpr int kTcMaxN = 3 * kTcUnit; // MMA N of a full unit: three digit rows per pair
+constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 MMAs)
+constexpr int kTcStages = 3;         // staged 8-group chunks per CTA
+constexpr int kTcASlots = 8;         // A operands (one group each) in tensor memory
+constexpr int kTcDBufs = 2;          // accumulator buffers in tensor memory
+constexpr int kTcThreads = 18 * 32;  // TMA, MMA, 8 unpack and 8 readout warps
+// MMA N of a unit of n pairs: three digit rows per pair, rounded up to 16.
+__host__ __device__ inline int tc_n_of(int n) { return (3 * n + 15) / 16 * 16; }
 
 struct MoeBatchArgs {
     const float *h_in;
@@ -144,9 +103,6 @@ struct MoeBatchArgs {
     uint64_t rec_stride, off_d;
     int rec_base, n_local, H, E, k, I, S, usable;
     Tiling tb, tc;   // GU tiles (gate + up pair), D tiles (column chunks)
-    int gu_tpi;                // GU tiles per work item (2 TR gu_tpi <= 64)
-    int dn_tpi;                // D row tiles of one chunk per work item (TR dn_tpi <= 64)
-    int gu_nbuf, dn_nbuf;      // staged items per CTA: one computed, the rest in flight
     int *err;                  // device error word (RB_ERR_TIMEOUT)
     uint64_t wait_ns;          // bound of every wait
     // scratch
@@ -156,8 +112,9 @@ struct MoeBatchArgs {
     int *nslot;      // [T]
     int *pidx;       // [T][kMaxSlots] pair index of (token, slot)
     int *pair_t;     // [P] token of pair
-    int *act, *act_off, *act_cnt;  // [units] work units (record, <= kBatchTokChunk of its
+    int *act, *act_off, *act_cnt;  // [units] work units (record, <= kTcUnit of its
                                    // pairs): global record id, first pair, pairs
+    int *img_off;    // [units] B rows of the units before this one (sum of tc_n_of)
     int *n_act;      // [2] units, pairs
     float *scores;   // [T][E] router scores
     unsigned *tcount;  // [T] router CTAs done per token (zero between launches)
@@ -165,14 +122,35 @@ struct MoeBatchArgs {
     int ep_rank, ep_size;  // expert-parallel share (1 rank: the whole layer)
     float *mid;      // [P][I]
     float *down;     // [P][tc.KC][H]
-    int *pair_u;     // [P] unit * 16 + column of pair
-    uint2 *xbf;      // [units][H / 32][2][32][3] planes of xn per unit column (see kFragCols)
-    int2 *xrf;       // [units][H / 32][16] their readout terms
-    uint2 *mbf;      // [units][I / 32][2][32][3] planes of mid
-    int2 *mrf;       // [units][I / 32][16]
+    int *pair_u;     // [P] unit * kTcUnit + column of pair
+    // B rows of the units: unit u's image holds, per group g of 32 inputs,
+    // tc_n_of(n_u) rows of 32 bytes (row 3c + p = digit p of pair c) as 8-row
+    // x 16-byte core matrices, at (img_off[u] G + g N_u) 32 bytes
+    uint8_t *xim;    // xn rows (G = H / 32)
+    uint8_t *mim;    // mid rows (G = I / 32)
+    float *xunit;    // [P] 2^(e-22) of the pair's xn row
+    float *munit;    // [P] same for its mid row
 };
-// The five kernels (same translation unit as the fused kernel).
-const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 gu, 3 down, 4 combine, 5 planes
+// route, bucket, combine (same translation unit as the fused kernel)
+const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 4 combine
+
+// The tensor-core kernels (rb_moe_tc.cu): one launch argument each, the
+// GEMMs with a tensor map over the pool's nibble rows of their phase.
+struct alignas(64) TcGemmArgs {
+    CUtensorMap tmap;
+    MoeBatchArgs b;
+};
+const void *moe_tc_kernel(int i);  // 0 x images, 1 gate/up GEMM, 2 mid images, 3 down GEMM
+size_t tc_gemm_smem();             // dynamic shared memory of a GEMM launch
+// Tensor maps over a pool's GU and D nibble rows (boxes of 256 rows x 128
+// bytes, 128-byte swizzle): 0 built, 1 the tiling does not fit the kernels'
+// boxes, 2 the driver's tensor-map encoder is missing or refused.
+int tc_tensor_maps(const uint8_t *pool, uint64_t pool_bytes, uint64_t rec_stride, uint64_t off_d,
+                   const Tiling &tb, const Tiling &tc, int H, CUtensorMap *gu, CUtensorMap *dn);
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float sg = 1.0f / (1.0f + expf(-g));  // forward_v2.c:327-331
+    return (g * sg) * u;
+}
 
 // ---- generic path (any quant / shape): route, up (gate+up+silu), down, combine
 struct MoeGenericArgs {

@@ -171,10 +171,6 @@ __device__ int build_slots(const int *ids, const float *w, int k, int E, int S, 
     return n;
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    const float sg = 1.0f / (1.0f + expf(-g));  // forward_v2.c:327-331
-    return (g * sg) * u;
-}
 
 // Release a stage this warp has no rows of (its wait has completed).
 __device__ __forceinline__ void release_stage(uint64_t *empty) {
@@ -1037,15 +1033,18 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
         cnt[r] = c;
     }
     __syncthreads();
-    if (tid == 0) {  // units: each record's pairs cut into runs of <= kBatchTokChunk
-        int o = 0, nu = 0;
+    if (tid == 0) {  // units: each record's pairs cut into runs of <= kTcUnit
+        int o = 0, nu = 0, rows = 0;
         for (int r = 0; r < R; ++r) {
             off[r] = o;
             uf[r] = nu;  // the record's first unit
-            for (int c0 = 0; c0 < cnt[r]; c0 += kBatchTokChunk) {
+            for (int c0 = 0; c0 < cnt[r]; c0 += kTcUnit) {
+                const int n = min(kTcUnit, cnt[r] - c0);
                 a.act[nu] = a.rec_base + r;
                 a.act_off[nu] = o + c0;
-                a.act_cnt[nu] = min(kBatchTokChunk, cnt[r] - c0);
+                a.act_cnt[nu] = n;
+                a.img_off[nu] = rows;  // the unit's B rows follow the earlier units'
+                rows += tc_n_of(n);
                 ++nu;
             }
             o += cnt[r];
@@ -1063,438 +1062,8 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
             rank += __popc(bm[r * W + (t >> 5)] & ((1u << (t & 31)) - 1u));
             const int pos = off[r] + rank;
             a.pair_t[pos] = t;
-            a.pair_u[pos] = (uf[r] + rank / kBatchTokChunk) * kFragCols + rank % kBatchTokChunk;
+            a.pair_u[pos] = (uf[r] + rank / kTcUnit) * kTcUnit + rank % kTcUnit;
             a.pidx[q] = pos;
-        }
-    }
-}
-
-// Planes of group g of every pair's activation row (row_of(pair)) in the
-// fragment order of its unit column (see kFragCols), one thread per (pair,
-// group): the column's B words for the four lanes that read it, and its
-// readout terms.
-template <typename RowOf>
-__device__ __forceinline__ void planes_frag(const MoeBatchArgs &a, RowOf row_of, int G, uint2 *bf,
-                                            int2 *rf) {
-    const long long n = (long long)a.n_act[1] * G;
-    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
-         q += (long long)gridDim.x * blockDim.x) {
-        const int pr = (int)(q / G), g = (int)(q - (long long)pr * G);
-        const float4 *x4 = reinterpret_cast<const float4 *>(row_of(pr) + (size_t)g * 32);
-        float x[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 v = __ldcg(x4 + i);
-            x[4 * i] = v.x;
-            x[4 * i + 1] = v.y;
-            x[4 * i + 2] = v.z;
-            x[4 * i + 3] = v.w;
-        }
-        XPlanes xp;
-        make_xplanes(xp, x);
-        const int uc = a.pair_u[pr], u = uc / kFragCols, c = uc - u * kFragCols;
-        const size_t ug = (size_t)u * G + g;
-        uint2 *dst = bf + ((ug * 2 + (c >> 3)) * 32 + (size_t)(c & 7) * 4) * 3;
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int pl = 0; pl < 3; ++pl) dst[t * 3 + pl] = make_uint2(xp.lo[pl][t], xp.hi[pl][t]);
-        rf[ug * kFragCols + c] = make_int2(xp.m8sum, __float_as_int(xp.unit));
-    }
-}
-
-// Planes of xn (the gate/up input, rows by token) and of mid (the down
-// input, rows by pair).
-__global__ void __launch_bounds__(256) k_batch_xplanes(MoeBatchArgs a) {
-    launch_dependents();
-    wait_prerequisite();
-    planes_frag(a, [&](int pr) { return a.xn + (size_t)a.pair_t[pr] * a.H; }, a.H / 32, a.xbf, a.xrf);
-}
-__global__ void __launch_bounds__(256) k_batch_mplanes(MoeBatchArgs a) {
-    launch_dependents();
-    wait_prerequisite();
-    planes_frag(a, [&](int pr) { return a.mid + (size_t)pr * a.I; }, a.I / 32, a.mbf, a.mrf);
-}
-
-// Integer tensor-core products of nibbles (A, u8 0..15) and activation
-// planes (B; u8 for planes 0 and 1, s8 for plane 2): m16n8k32, exact s32.
-__device__ __forceinline__ void mma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%10,%10,%10,%10};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
-}
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%10,%10,%10,%10};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
-}
-
-constexpr int kTcNB = kBatchTokChunk / 8;  // 8-column blocks per unit
-constexpr int kTcWarps = kBatchThreads / 32;
-
-// The bulk copies of one work item -- nt tiles of tile_rows rows from rb at
-// stride tst, each tile its nibble rows (ns bytes) then its scale rows (ss
-// bytes) -- into the item's banded shared-memory layout (StageGeom), issued
-// by warp 0: lane b < 8 copies band b's nibble rows and lane 8 + b its scale
-// rows (one copy per tile the band touches), or, for unbanded scales, lanes
-// 16.. the tiles' scale blocks; for an unbanded item lane j copies tile j's
-// nibble and scale blocks. Lane 0 posts the item's bytes first, so the
-// buffer's phase cannot complete before every copy has landed. The kernels
-// keep two buffers: item k goes to buffer k & 1 and completes phase
-// (k >> 1) & 1 of its barrier.
-__device__ __forceinline__ void stage_item(uint8_t *buf, uint64_t *full, const StageGeom &sg,
-                                           int nrows, int tile_rows, int nt, const uint8_t *rb,
-                                           size_t tst) {
-    const int lane = threadIdx.x & 31;
-    if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)nrows * (sg.ns + sg.ss));
-    __syncwarp();
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // buffer was read generically
-    const uint64_t pol = policy_evict_first();
-    const size_t sc_src = (size_t)tile_rows * sg.ns;  // a tile's scale rows
-    if (!sg.banded) {  // rows in order: each tile's nibble block, then its scale block
-        for (int j = lane; j < nt; j += 32) {
-            const uint8_t *tile = rb + (size_t)j * tst;
-            bulk_g2s(buf + (size_t)j * tile_rows * sg.ns, tile, (uint32_t)tile_rows * sg.ns, full, pol);
-            bulk_g2s(buf + sg.sc_off + (size_t)j * tile_rows * sg.ss, tile + sc_src,
-                     (uint32_t)tile_rows * sg.ss, full, pol);
-        }
-        return;
-    }
-    if (lane < 8 || (lane < 16 && sg.sc_band)) {
-        const int b = lane & 7;
-        const bool scales = lane >= 8;
-        const int r0 = b * sg.u, r1 = min(r0 + sg.u, nrows);
-        for (int r = r0; r < r1;) {
-            const int j = r / tile_rows, re = min(r1, (j + 1) * tile_rows), rr = r - j * tile_rows;
-            const uint8_t *tile = rb + (size_t)j * tst;
-            if (scales)
-                bulk_g2s(buf + sg.sc_off + (size_t)b * sg.sbs + (size_t)(r - r0) * sg.ss,
-                         tile + sc_src + (size_t)rr * sg.ss, (uint32_t)(re - r) * sg.ss, full, pol);
-            else
-                bulk_g2s(buf + (size_t)b * sg.bs + (size_t)(r - r0) * sg.ns,
-                         tile + (size_t)rr * sg.ns, (uint32_t)(re - r) * sg.ns, full, pol);
-            r = re;
-        }
-    } else if (lane >= 16 && !sg.sc_band) {
-        for (int j = lane - 16; j < nt; j += 16)
-            bulk_g2s(buf + sg.sc_off + (size_t)j * tile_rows * sg.ss, rb + (size_t)j * tst + sc_src,
-                     (uint32_t)tile_rows * sg.ss, full, pol);
-    }
-}
-
-// One warp's share of a staged item: its (up to) two 16-row blocks j over
-// the groups ks, ks + KS, ... against NB 8-column blocks, BG groups at a time
-// (the operands of BG groups are loaded before their MMAs). Fragment row g
-// (h = 0) or g + 8 (h = 1) of block j has nibble word t of group grp at
-// nib + on[j][h] + 16 grp and its scale at sc[os[j][h] + grp]; v[j][h] is
-// false for rows past the item. The B operand and readout terms of group grp
-// are at bf + (2 grp + nb) 96 and rf + 16 grp (see kFragCols).
-template <int NB, int BG>
-__device__ __forceinline__ void tc_rows(const uint8_t *nib, const float *sc,
-                                        const uint32_t (&on)[2][2], const uint32_t (&os)[2][2],
-                                        const bool (&v)[2][2], int MBW, int ks, int KS, int ngrp,
-                                        int m, const uint2 *bf, const int2 *rf,
-                                        float (&acc)[2][NB][4]) {
-    const int lane = threadIdx.x & 31, t = lane & 3;
-    // Columns past the unit's m read planes some earlier unit left in the
-    // fragment arrays (zeroed when they were allocated): finite, and their
-    // sums are never read out, so they need no masking.
-    (void)m;
-    for (int gb = ks; gb < ngrp; gb += KS * BG) {
-        uint2 b[BG][NB][3];
-        int4 r[BG][NB];
-        uint32_t w[BG][2][2];
-        float s[BG][2][2];
-#pragma unroll
-        for (int q = 0; q < BG; ++q) {
-            const bool in = gb + q * KS < ngrp;
-            const int grp = in ? gb + q * KS : 0;  // addresses stay inside the item
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
-                const uint2 *bp = bf + ((size_t)grp * 2 + nb) * 96 + lane * 3;
-#pragma unroll
-                for (int pl = 0; pl < 3; ++pl) b[q][nb][pl] = bp[pl];
-                r[q][nb] = *reinterpret_cast<const int4 *>(rf + (size_t)grp * kFragCols + nb * 8 + 2 * t);
-            }
-            // rows past the item and groups past the last read staged data
-            // (offset 0, group 0) and get scale 0: they add exactly nothing
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    w[q][j][h] = *reinterpret_cast<const uint32_t *>(nib + on[j][h] + 16 * grp);
-                    s[q][j][h] = in && v[j][h] ? sc[os[j][h] + grp] : 0.f;
-                }
-        }
-#pragma unroll
-        for (int q = 0; q < BG; ++q) {
-            int m8[NB][2];
-            float un[NB][2];
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
-                m8[nb][0] = r[q][nb].x;
-                un[nb][0] = __int_as_float(r[q][nb].y);
-                m8[nb][1] = r[q][nb].z;
-                un[nb][1] = __int_as_float(r[q][nb].w);
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (j >= MBW) break;
-                const uint32_t w0 = w[q][j][0], w1 = w[q][j][1];
-                const uint32_t av[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
-                                        (w1 >> 4) & 0x0F0F0F0Fu};
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    int p0[4], p1[4], p2[4];
-                    mma_u8u8(p0, av, b[q][nb][0].x, b[q][nb][0].y);
-                    mma_u8u8(p1, av, b[q][nb][1].x, b[q][nb][1].y);
-                    mma_u8s8(p2, av, b[q][nb][2].x, b[q][nb][2].y);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int c = i & 1;
-                        // sum (nib - 8) X exactly: |.| <= 2^30, and the plane
-                        // sums before the -8 sum X term stay below 2^31
-                        const int dot = p2[i] * 65536 + p1[i] * 256 + p0[i] + m8[nb][c];
-                        acc[j][nb][i] = fmaf(s[q][j][i >> 1], (float)dot * un[nb][c], acc[j][nb][i]);
-                    }
-                }
-            }
-        }
-    }
-}
-
-// One warp's part of tc_item for NB column blocks: its accumulators (sized
-// for NB, so the one-block case keeps no idle registers), the MMA loop, and
-// the store of its fragment sums to red.
-template <int NB, int BG>
-__device__ __forceinline__ void tc_warp(const uint8_t *st, const float *sc,
-                                        const uint32_t (&on)[2][2], const uint32_t (&os)[2][2],
-                                        const bool (&v)[2][2], int MB, int MBW, int rs, int RS,
-                                        int ks, int KS, int ngrp, int m, const uint2 *bf,
-                                        const int2 *rf, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float acc[2][NB][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[j][nb][i] = 0.f;
-    tc_rows<NB, BG>(st, sc, on, os, v, MBW, ks, KS, ngrp, m, bf, rf, acc);
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-            if (j < MBW && rs + j * RS < MB)
-                *reinterpret_cast<float4 *>(&red[(((size_t)warp * 2 + j) * kTcNB + nb) * 128 + lane * 4]) =
-                    make_float4(acc[j][nb][0], acc[j][nb][1], acc[j][nb][2], acc[j][nb][3]);
-}
-
-// The integer tensor-core products of one staged item (rows R < nrows, laid
-// out as sg) against the unit's m <= 16 columns, per group of 32:
-//   acc[R][n] += scale[R][g] * (S2 * 65536 + S1 * 256 + S0 - 8 sum X) * unit
-// (the decode path's exact per-group dot, on the tensor pipe). Block mb of
-// the MB = ceil(nrows / 16) 16-row blocks reads row 2 mb (fragment rows 0..7)
-// and 2 mb + 1 (rows 8..15) of the 8 bands, or, unbanded, rows 16 mb ..
-// 16 mb + 15. With RS = ceil(MB / 2) warp
-// rows, warp w takes the blocks w % RS and w % RS + RS and the groups w / RS,
-// w / RS + 16 / RS, ..., so each warp loads a group's activation planes once
-// for up to two blocks. The warps' fragment sums go to red, added up by
-// tc_sum. Every thread of the CTA calls it; it ends with a barrier.
-template <bool BANDED>
-__device__ __forceinline__ void tc_item(const uint8_t *st, const StageGeom &sg, int ngrp, int nrows,
-                                        int m, const uint2 *bf, const int2 *rf, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, MBW = MB < 2 ? MB : 2;
-    const int KS = kTcWarps / RS, rs = warp % RS, ks = warp / RS;
-    const int NBu = (m + 7) >> 3;  // column blocks in use
-    uint32_t on[2][2], os[2][2];
-    bool v[2][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int mb = rs + j * RS, w = 2 * mb + h;
-            const int R = BANDED ? g * sg.u + w : mb * 16 + g + 8 * h;
-            v[j][h] = j < MBW && mb < MB && R < nrows;
-            on[j][h] = !v[j][h] ? 0u
-                       : BANDED ? g * sg.bs + (uint32_t)w * sg.ns + 4 * t
-                                : (uint32_t)R * sg.ns + 4 * t;
-            os[j][h] = !v[j][h] ? 0u
-                       : sg.sc_band ? (g * sg.sbs + (uint32_t)w * sg.ss) / 4
-                                    : (uint32_t)R * (sg.ss / 4);
-        }
-    const float *sc = reinterpret_cast<const float *>(st + sg.sc_off);
-    if (NBu == 1)
-        tc_warp<1, 3>(st, sc, on, os, v, MB, MBW, rs, RS, ks, KS, ngrp, m, bf, rf, red);
-    else
-        tc_warp<kTcNB, 1>(st, sc, on, os, v, MB, MBW, rs, RS, ks, KS, ngrp, m, bf, rf, red);
-    __syncthreads();
-}
-
-// Element (R, n) of the last tc_item over nrows rows (banded: row R = band
-// b, row w of the band): its warps' sums, added in warp order.
-__device__ __forceinline__ float tc_sum(const float *red, bool banded, int nrows, int R, int n) {
-    const int MB = (nrows + 15) >> 4, RS = (MB + 1) >> 1, KS = kTcWarps / RS, u = 2 * MB;
-    int b, mb, h;
-    if (banded) {
-        b = R / u;
-        const int w = R - b * u;
-        mb = w >> 1;
-        h = w & 1;
-    } else {
-        mb = R >> 4;
-        b = R & 7;
-        h = (R >> 3) & 1;
-    }
-    const int rs = mb % RS, j = mb / RS;
-    const int nb = n >> 3, nn = n & 7;
-    const int li = (b * 4 + (nn >> 1)) * 4 + (h << 1) + (nn & 1);
-    float v = 0.f;
-    for (int ks = 0; ks < KS; ++ks)
-        v += red[(((size_t)(ks * RS + rs) * 2 + j) * kTcNB + nb) * 128 + li];
-    return v;
-}
-
-// The wait for item k's buffer (k % nbuf; its (k / nbuf)-th use completes
-// phase (k / nbuf) & 1); on a timeout every thread learns of it and thread 0
-// lets the copies still in flight (items up to `last`, the newest issued)
-// land before the CTA leaves. True when the buffer is full.
-__device__ __forceinline__ bool item_wait(uint64_t *full, int nbuf, int k, int last,
-                                          const MoeBatchArgs &a) {
-    const bool okw = mbar_wait(&full[k % nbuf], (k / nbuf) & 1, a.wait_ns, a.err);
-    if (__syncthreads_or(!okw)) {
-        if (threadIdx.x == 0)
-            for (int q = okw ? k + 1 : k; q <= last; ++q)
-                mbar_wait(&full[q % nbuf], (q / nbuf) & 1, a.wait_ns, a.err);
-        return false;
-    }
-    return true;
-}
-
-// (unit, gu_tpi consecutive GU tiles) work items in contiguous ranges per
-// CTA: mid = silu(gate) * up for the unit's tokens (forward_v2.c:323-331);
-// the items' gate and up rows staged as one block of rows in a ring of
-// gu_nbuf buffers, gu_nbuf - 1 items ahead.
-__global__ void __launch_bounds__(kBatchThreads, 1) k_batch_gu(MoeBatchArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kTcMaxBuf];
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int H = a.H, G = H / 32, I = a.I, TR = a.tb.TR, ntb = a.tb.ntiles;
-    const int TR2 = 2 * TR, half = H / 2, G4 = G * 4;
-    const int tpi = a.gu_tpi, nitem_u = (ntb + tpi - 1) / tpi;
-    const size_t tst = a.tb.tile_stride;
-    const StageGeom sg = stage_geom(tpi * TR2, TR2, half, G4);
-    const int nbuf = a.gu_nbuf;
-    float *red = reinterpret_cast<float *>(smem + (size_t)nbuf * sg.bytes);
-    if (tid == 0) {
-        for (int b = 0; b < nbuf; ++b) mbar_init(&full[b], 1);
-        mbar_init_fence();
-    }
-    __syncthreads();
-    launch_dependents();
-    wait_prerequisite();
-    const int n = *a.n_act * nitem_u;
-    const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
-    const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
-    auto issue = [&](int k, int item) {
-        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
-        const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
-        stage_item(smem + (size_t)(k % nbuf) * sg.bytes, &full[k % nbuf],
-                   stage_geom(nrows, TR2, half, G4), nrows, TR2, nt,
-                   a.pool + (size_t)a.act[ai] * a.rec_stride + (size_t)tt0 * tst, tst);
-    };
-    if (warp == 0)
-        for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
-    for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        // item_wait's barrier also means every thread is done with item k - 1:
-        // its buffer (the next copy's target) and red are free
-        const int nk = k + nbuf - 1;  // takes item k - 1's buffer
-        if (!item_wait(full, nbuf, k, min(nk - 1, i1 - 1 - i0), a)) return;
-        if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
-        const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
-        const int ai = item / nitem_u, tt0 = (item - ai * nitem_u) * tpi;
-        const int nt = min(tpi, ntb - tt0), nrows = nt * TR2;
-        const int off = a.act_off[ai], m = a.act_cnt[ai];
-        const StageGeom ig = stage_geom(nrows, TR2, half, G4);
-        if (ig.banded)
-            tc_item<true>(st, ig, G, nrows, m, a.xbf + (size_t)ai * G * 192,
-                          a.xrf + (size_t)ai * G * kFragCols, red);
-        else
-            tc_item<false>(st, ig, G, nrows, m, a.xbf + (size_t)ai * G * 192,
-                           a.xrf + (size_t)ai * G * kFragCols, red);
-        // staged row j 2TR + r is gate row r of tile j, j 2TR + TR + r its up row
-        for (int e = tid; e < nt * TR * m; e += blockDim.x) {
-            const int jr = e / m, c = e - jr * m, j = jr / TR, r = jr - j * TR;
-            const int row = (tt0 + j) * TR + r;
-            if (row < I)
-                a.mid[(size_t)(off + c) * I + row] =
-                    silu_mul(tc_sum(red, ig.banded, nrows, j * TR2 + r, c),
-                             tc_sum(red, ig.banded, nrows, j * TR2 + TR + r, c));
-        }
-    }
-}
-
-// (unit, chunk c, dn_tpi consecutive row tiles of the chunk) work items in
-// contiguous ranges per CTA: those rows of W2's column chunk c against the
-// unit's pairs' mid planes of that chunk.
-__global__ void __launch_bounds__(kBatchThreads, 1) k_batch_down(MoeBatchArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kTcMaxBuf];
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int H = a.H, I = a.I, TR = a.tc.TR, rt = a.tc.rtiles, KC = a.tc.KC;
-    const int cols = a.tc.cols, Gc = cols / 32, GI = I / 32, chalf = cols / 2, cG4 = Gc * 4;
-    const int tpi = a.dn_tpi, nic = (rt + tpi - 1) / tpi, nitem_u = KC * nic;
-    const size_t tcs = a.tc.tile_stride;
-    const StageGeom sg = stage_geom(tpi * TR, TR, chalf, cG4);
-    const int nbuf = a.dn_nbuf;
-    float *red = reinterpret_cast<float *>(smem + (size_t)nbuf * sg.bytes);
-    if (tid == 0) {
-        for (int b = 0; b < nbuf; ++b) mbar_init(&full[b], 1);
-        mbar_init_fence();
-    }
-    __syncthreads();
-    launch_dependents();
-    wait_prerequisite();
-    const int n = *a.n_act * nitem_u;
-    const int i0 = (int)((long long)blockIdx.x * n / gridDim.x);
-    const int i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x);
-    auto issue = [&](int k, int item) {
-        const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
-        const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
-        stage_item(smem + (size_t)(k % nbuf) * sg.bytes, &full[k % nbuf],
-                   stage_geom(nrows, TR, chalf, cG4), nrows, TR, nt,
-                   a.pool + (size_t)a.act[ai] * a.rec_stride + a.off_d + (size_t)(c * rt + t0) * tcs,
-                   tcs);
-    };
-    if (warp == 0)
-        for (int q = 0; q < nbuf - 1 && i0 + q < i1; ++q) issue(q, i0 + q);
-    for (int k = 0, item = i0; item < i1; ++k, ++item) {
-        // item_wait's barrier also means every thread is done with item k - 1:
-        // its buffer (the next copy's target) and red are free
-        const int nk = k + nbuf - 1;  // takes item k - 1's buffer
-        if (!item_wait(full, nbuf, k, min(nk - 1, i1 - 1 - i0), a)) return;
-        if (warp == 0 && i0 + nk < i1) issue(nk, i0 + nk);
-        const uint8_t *st = smem + (size_t)(k % nbuf) * sg.bytes;
-        const int ai = item / nitem_u, d = item - ai * nitem_u, c = d / nic;
-        const int t0 = (d - c * nic) * tpi, nt = min(tpi, rt - t0), nrows = nt * TR;
-        const int off = a.act_off[ai], m = a.act_cnt[ai];
-        const size_t ug = (size_t)ai * GI + (size_t)c * Gc;  // the unit's first group of chunk c
-        const StageGeom ig = stage_geom(nrows, TR, chalf, cG4);
-        if (ig.banded)
-            tc_item<true>(st, ig, Gc, nrows, m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
-        else
-            tc_item<false>(st, ig, Gc, nrows, m, a.mbf + ug * 192, a.mrf + ug * kFragCols, red);
-        for (int e = tid; e < nrows * m; e += blockDim.x) {
-            const int R = e / m, q = e - R * m, row = t0 * TR + R;
-            if (row < H)
-                a.down[((size_t)(off + q) * KC + c) * H + row] = tc_sum(red, ig.banded, nrows, R, q);
         }
     }
 }
@@ -1524,11 +1093,7 @@ const void *moe_batch_kernel(int i) {
     switch (i) {
         case 0: return (const void *)k_batch_route;
         case 1: return (const void *)k_batch_bucket;
-        case 2: return (const void *)k_batch_gu;
-        case 3: return (const void *)k_batch_down;
         case 4: return (const void *)k_batch_combine;
-        case 5: return (const void *)k_batch_xplanes;
-        case 6: return (const void *)k_batch_mplanes;
         default: return nullptr;
     }
 }

@@ -11,7 +11,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import ATOL, RTOL, near_tie, router_scores
+from conftest import ATOL, RTOL, check_tokens, check_tokens_long, exact_moe_layer, oracle_many
 from rabbit_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -41,24 +41,6 @@ def make_pool(rc, H, E, k, I, S, seed, n_layers=1, quant=4):
     return pool, kw
 
 
-def check_tokens(oracle, h, got_h, got_ids, got_w, kw, min_checked):
-    checked = 0
-    for t in range(h.shape[0]):
-        ref_h, ref_ids, ref_w = oracle.moe_step(h[t], **kw)
-        if near_tie(router_scores(oracle, h[t], kw["rms_ffn"], kw["w_router"]), len(ref_ids)):
-            continue
-        if got_ids is not None:
-            np.testing.assert_array_equal(got_ids[t], ref_ids, err_msg=f"token {t}: ids")
-            np.testing.assert_allclose(got_w[t], ref_w, rtol=RTOL, atol=ATOL,
-                                       err_msg=f"token {t}: weights")
-        np.testing.assert_allclose(got_h[t] - h[t], ref_h - h[t], rtol=RTOL, atol=ATOL,
-                                   err_msg=f"token {t}: MoE delta")
-        np.testing.assert_allclose(got_h[t], ref_h, rtol=RTOL, atol=ATOL,
-                                   err_msg=f"token {t}: h_out")
-        checked += 1
-    assert checked >= min_checked, f"only {checked} tokens free of near-ties"
-
-
 @pytest.mark.parametrize("name", list(SHAPES))
 @pytest.mark.parametrize("T", [1, 5, 33])
 def test_prefill_matches_oracle_per_token(rc, oracle, name, T):
@@ -85,15 +67,57 @@ def test_prefill_many_tokens_per_expert_and_decode_agree(rc, oracle):
     pool.free()
 
 
-def test_prefill_deepseek_shaped_layer(rc, oracle):
+@pytest.mark.parametrize("T", [8, 32])
+def test_prefill_deepseek_shaped_layer(rc, oracle, T):
     """hidden 2048, 64 routed experts top-6 + 2 shared, inter 1408 (W2 in two
-    column chunks of 704 inputs)."""
+    column chunks of 704 inputs); T = 32 is the DeepSeek-MoE-16B-shaped
+    prefill chunk, where the two shared experts see every token (two work
+    units each)."""
     H, E, k, I, S = 2048, 64, 6, 1408, 2
     pool, kw = make_pool(rc, H, E, k, I, S, seed=4)
-    h = np.random.default_rng(4).standard_normal((8, H)).astype(np.float32)
+    h = np.random.default_rng(4 + T).standard_normal((T, H)).astype(np.float32)
     got_h, ids, w = pool.prefill(0, h)
-    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=7)
+    check_tokens(oracle, h, got_h, ids, w, kw, min_checked=T - 2,
+                 ref=oracle_many(oracle, h, kw))
     pool.free()
+
+
+def test_prefill_mixtral_8x22b_shaped_layer_and_expert_parallel_shares(rc, oracle):
+    """One Mixtral-8x22B-shaped layer (hidden 6144, 8 experts top-2, inter
+    16384: W2 in 16 column chunks of 1024 inputs) with a batch of 64 decode
+    tokens through the multi-token path, then the same layer split
+    expert-parallel over 2, 4 and 8 ranks, emulated as pools on this GPU
+    (rank r holds experts e = r mod G): the whole layer and each sum of
+    shares against the oracle's moe_step per token. Rows of W2 sum 16384
+    products, and the oracle's serial fp32 sum is itself up to ~2e-5 from the
+    exact value there, so each element may also differ by the oracle's own
+    deviation from the float64 value of the same quantised layer."""
+    H, E, k, I, S, T = 6144, 8, 2, 16384, 0, 64
+    recs, size, router, rms = synth.moe_layer(5, H, E, I, S)
+    kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=4, n_records=E + S,
+              expert_size=size, records=recs, rms_ffn=rms, w_router=router)
+    h = np.random.default_rng(55).standard_normal((T, H)).astype(np.float32)
+    ref = oracle_many(oracle, h, kw)
+    exact = exact_moe_layer(oracle, h, kw, ref)
+    pool = rc.MoePool(records=recs, expert_size=size, n_layers=1, hidden=H, n_experts=E,
+                      top_k=k, inter=I, n_shared=S, quant=4, rms_ffn=[rms], w_router=[router])
+    got_h, ids, w = pool.prefill(0, h)
+    pool.free()
+    check_tokens_long(oracle, h, got_h, ids, w, kw, ref, exact, min_checked=T - 2)
+    rec_of = lambda e: recs[e * size:(e + 1) * size]  # noqa: E731
+    for G in (2, 4, 8):
+        total = np.zeros_like(h)
+        for r in range(G):
+            share = rc.MoePool(records=np.concatenate([rec_of(e) for e in range(r, E, G)]),
+                               expert_size=size, n_layers=1, hidden=H, n_experts=E, top_k=k,
+                               inter=I, n_shared=S, quant=4, rms_ffn=[rms], w_router=[router],
+                               experts_per_layer=E // G)
+            share.set_expert_parallel(r, G)
+            out, sids, _ = share.prefill(0, h)
+            np.testing.assert_array_equal(sids, ids)
+            total += out
+            share.free()
+        check_tokens_long(oracle, h, total, ids, w, kw, ref, exact, min_checked=T - 2)
 
 
 def test_prefill_dev_in_place_and_second_layer(rc, oracle):

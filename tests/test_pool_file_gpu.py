@@ -15,6 +15,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+from conftest import check_tokens, oracle_kw
 from rabbit_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -36,10 +37,13 @@ def model(name, seed, n_layers=2):
         size = recs.size // (E + S)
     # layer l's records differ: layer 1 reverses the expert order
     per = recs.reshape(E + S, size)
-    table = np.concatenate([per.reshape(-1), per[::-1].reshape(-1)][:n_layers])
+    layers = [per.reshape(-1), np.ascontiguousarray(per[::-1]).reshape(-1)][:n_layers]
+    table = np.concatenate(layers)
     kw = dict(expert_size=size, n_layers=n_layers, hidden=H, n_experts=E, top_k=k, inter=I,
               n_shared=S, quant=quant, rms_ffn=[rms] * n_layers, w_router=[router] * n_layers)
-    return table, kw
+    okw = [oracle_kw(H=H, E=E, k=k, I=I, S=S, records=layer, expert_size=size, rms_ffn=rms,
+                     w_router=router, quant=quant) for layer in layers]
+    return table, kw, okw
 
 
 def write_model(path, table, tail=0):
@@ -50,8 +54,8 @@ def write_model(path, table, tail=0):
 
 
 @pytest.mark.parametrize("name", list(SHAPES))
-def test_file_pool_decodes_like_the_mapped_pool(rc, tmp_path, name):
-    table, kw = model(name, seed=31)
+def test_file_pool_decodes_like_the_mapped_pool(rc, oracle, tmp_path, name):
+    table, kw, okw = model(name, seed=31)
     path = tmp_path / "model.rabbit"
     write_model(path, table)
     ref = rc.MoePool(records=table, **kw)
@@ -65,18 +69,24 @@ def test_file_pool_decodes_like_the_mapped_pool(rc, tmp_path, name):
     assert st["uploads"] == st["resident_records"]
     h = np.random.default_rng(3).standard_normal((4, kw["hidden"])).astype(np.float32)
     for layer in range(kw["n_layers"]):
+        outs = []
         for t in range(h.shape[0]):
             a, ia, wa = ref.decode(layer, h[t])
             b, ib, wb = pool.decode(layer, h[t])
             np.testing.assert_array_equal(b, a)
             np.testing.assert_array_equal(ib, ia)
             np.testing.assert_array_equal(wb, wa)
+            outs.append((b, ib, wb))
+        check_tokens(oracle, h, np.stack([o[0] for o in outs]), np.stack([o[1] for o in outs]),
+                     np.stack([o[2] for o in outs]), okw[layer], min_checked=3)
+        pf, pids, pw = pool.prefill(layer, h)
+        check_tokens(oracle, h, pf, pids, pw, okw[layer], min_checked=3)
     ref.free()
     pool.free()
 
 
 def test_file_read_failures_are_statuses(rc, tmp_path):
-    table, kw = model("group32_tiled", seed=5)
+    table, kw, _ = model("group32_tiled", seed=5)
     size = kw["expert_size"]
     pool = rc.MoePool(records=None, **kw)
     with pytest.raises(rc.RabbitCudaError, match="cannot open"):

@@ -2,13 +2,15 @@
 rabbit_cuda_tile_records for this GPU's SM count) against a pool that tiles
 the same group-32 records at upload. Bar: bit-identical decode and prefill
 outputs, from a host map and from the model file; records tiled for another
-plan are refused with a status.
+plan are refused with a status; the pre-tiled pool's outputs are also held to
+the oracle's moe_step (rtol 1e-4 / atol 1e-5, ids identical).
 """
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
+from conftest import check_tokens, oracle_kw
 from rabbit_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -30,7 +32,7 @@ def pools(rc, recs, size, router, rms, tiled, tsize, **extra):
     return ref, pre
 
 
-def test_pretiled_pool_matches_tiling_at_upload(rc, tmp_path):
+def test_pretiled_pool_matches_tiling_at_upload(rc, oracle, tmp_path):
     recs, size, router, rms = synth.moe_layer(11, H, E, I, S)
     tiled, tsize = rc.tile_records(recs, size, hidden=H, n_experts=E, top_k=K, inter=I,
                                    n_shared=S, sm_count=sm_count())
@@ -43,8 +45,14 @@ def test_pretiled_pool_matches_tiling_at_upload(rc, tmp_path):
         np.testing.assert_array_equal(ib, ia)
         np.testing.assert_array_equal(wb, wa)
     pa, _, _ = ref.prefill(0, h)
-    pb, _, _ = pre.prefill(0, h)
+    pb, pids, pw = pre.prefill(0, h)
     np.testing.assert_array_equal(pb, pa)
+    okw = oracle_kw(H=H, E=E, k=K, I=I, S=S, records=recs, expert_size=size, rms_ffn=rms,
+                    w_router=router)
+    check_tokens(oracle, h, pb, pids, pw, okw, min_checked=5)
+    dec = [pre.decode(0, h[t]) for t in range(h.shape[0])]
+    check_tokens(oracle, h, np.stack([d[0] for d in dec]), np.stack([d[1] for d in dec]),
+                 np.stack([d[2] for d in dec]), okw, min_checked=5)
     # the same tiled records straight from a file, after a 300-byte header
     path = tmp_path / "tiled.rabbit"
     with open(path, "wb") as f:

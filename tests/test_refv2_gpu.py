@@ -33,7 +33,17 @@ CONFIGS = {
     # and head_dim 40 (shared memory, positions split over CTAs and merged)
     "long_window": (2, 128, 1000, 4, 2, 32, 8, 2, 64, 0, 80),
     "long_window_split": (1, 128, 1000, 4, 2, 40, 8, 2, 64, 0, 72),
+    # the OLMoE-1B-7B shape of the full-decode workload (hidden 2048, 16 heads
+    # of 128: the register attention with 4 values per lane, 64 experts top-8,
+    # inter 1024) with 2 layers and a 4096-id vocabulary so the oracle stays
+    # fast; the window passes 32 cached positions
+    "olmoe_dims": (2, 2048, 4096, 16, 16, 128, 64, 8, 1024, 0, 48),
 }
+
+# Standard deviations of the dense weights: (embed, lm_head, norm spread,
+# w_q, w_k, w_v, w_o). The OLMoE-shaped model uses the workload's N(0, 0.02).
+SIGMAS = {"olmoe_dims": (1.0, 0.02, 0.1, 0.02, 0.02, 0.02, 0.02)}
+DEFAULT_SIGMAS = (1.0, 0.05, 0.1, 0.15, 0.15, 0.1, 0.1)
 
 
 class Model:
@@ -46,15 +56,16 @@ class Model:
         rng = np.random.default_rng(seed)
         qd, kvd = nh * hd, nkv * hd
         f = lambda *s, sg: (rng.standard_normal(s) * sg).astype(np.float32)  # noqa: E731
+        s_emb, s_lm, s_nrm, s_q, s_k, s_v, s_o = SIGMAS.get(name, DEFAULT_SIGMAS)
         self.w = {
-            "embed": f(V, H, sg=1.0),
-            "lm_head": f(H, V, sg=0.05),
-            "final_norm": (1.0 + f(H, sg=0.1)),
-            "rms_attn": [1.0 + f(H, sg=0.1) for _ in range(L)],
-            "w_q": [f(qd, H, sg=0.15) for _ in range(L)],
-            "w_k": [f(kvd, H, sg=0.15) for _ in range(L)],
-            "w_v": [f(kvd, H, sg=0.1) for _ in range(L)],
-            "w_o": [f(H, qd, sg=0.1) for _ in range(L)],
+            "embed": f(V, H, sg=s_emb),
+            "lm_head": f(H, V, sg=s_lm),
+            "final_norm": (1.0 + f(H, sg=s_nrm)),
+            "rms_attn": [1.0 + f(H, sg=s_nrm) for _ in range(L)],
+            "w_q": [f(qd, H, sg=s_q) for _ in range(L)],
+            "w_k": [f(kvd, H, sg=s_k) for _ in range(L)],
+            "w_v": [f(kvd, H, sg=s_v) for _ in range(L)],
+            "w_o": [f(H, qd, sg=s_o) for _ in range(L)],
         }
         self.moe = [synth.moe_layer(seed * 31 + l, H, E, I, S) for l in range(L)]
         self.size = self.moe[0][1]
