@@ -15,6 +15,7 @@
  *   moe_step / expert_swiglu /
  *     select_top_k (static)         src/forward_v2.c:248-402
  *   expert cache + mmap fetch       src/memory.c:94-253, src/moe.c:73-117
+ *   rabbit_cache_* (HBM slots)      src/rabbit.h:123-134, src/memory.c:12-193
  *   rabbit_cache_stats_ex           src/rabbit.h:132-134
  */
 #ifndef RABBIT_CUDA_H
@@ -279,8 +280,47 @@ int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);
  * records resident, pool bytes. */
 int rabbit_cuda_moe_stats(const rabbit_cuda_moe *p, uint64_t *hbm_hits, uint64_t *uploads,
                           uint64_t *h2d_bytes, int *resident_records, uint64_t *pool_bytes);
+/* The counters of rabbit_cache_stats_ex (src/rabbit.h:132-134,
+ * src/memory.c:74-92) for the pool: hits = kernel calls served from HBM,
+ * misses = calls refused because their layer was not resident, inserts =
+ * records uploaded, evictions = resident records dropped when a window block
+ * was taken for another layer, bytes_copied = bytes moved host -> device,
+ * n_slots = records HBM holds, n_pinned = records that cannot be dropped
+ * (every resident record of a pool without a window; 0 with one). Any
+ * pointer may be NULL. */
+int rabbit_cuda_moe_stats_ex(const rabbit_cuda_moe *p, uint64_t *hits, uint64_t *misses,
+                             uint64_t *inserts, uint64_t *evictions, uint64_t *bytes_copied,
+                             int *n_slots, int *n_pinned);
 /* Algorithmic bytes of one decode (router + selected + shared experts). */
 uint64_t rabbit_cuda_moe_decode_bytes(const rabbit_cuda_moe *p);
+
+/* ------------------------------------------------- HBM expert cache -- */
+
+/* The reference's expert cache (src/rabbit.h:123-134, src/memory.c:12-193)
+ * with its slots in HBM: the same signatures, argument meaning, return
+ * conventions (NULL / -1; rabbit_cuda_last_error() says why where a CUDA call
+ * failed), replacement rule (a resident id is bumped; else the first empty
+ * slot, else the least recently used unpinned one) and counters. get / put /
+ * pin return DEVICE pointers to the record's slot (256-byte aligned); put /
+ * pin copy the caller's HOST record in and return once it is in HBM. The
+ * cache lives on the calling thread's device (rabbit_cuda_set_device). Not
+ * thread safe, as in the reference. */
+typedef struct rabbit_cuda_cache rabbit_cuda_cache;
+/* n_slots <= 0 means 4; at most 64 (RABBIT_MAX_CACHE_SLOTS). NULL on failure. */
+rabbit_cuda_cache *rabbit_cuda_cache_create(int n_slots);
+void rabbit_cuda_cache_free(rabbit_cuda_cache *c);
+/* Allocates every slot in HBM (n_slots x size); a new size empties the cache. */
+void rabbit_cuda_cache_set_expert_size(rabbit_cuda_cache *c, size_t size);
+void *rabbit_cuda_cache_get(rabbit_cuda_cache *c, int expert_id);
+void *rabbit_cuda_cache_put(rabbit_cuda_cache *c, int expert_id, const void *src);
+/* Pin an already-cached or about-to-be-cached expert so LRU will not evict
+ * it; 0 on success, -1 otherwise. */
+int rabbit_cuda_cache_pin(rabbit_cuda_cache *c, int expert_id, const void *src_or_null);
+void rabbit_cuda_cache_stats(const rabbit_cuda_cache *c, uint64_t *hits, uint64_t *misses,
+                             uint64_t *inserts);
+void rabbit_cuda_cache_stats_ex(const rabbit_cuda_cache *c, uint64_t *hits, uint64_t *misses,
+                                uint64_t *inserts, uint64_t *evictions, uint64_t *bytes_copied,
+                                int *n_slots, int *n_pinned);
 
 /* ------------------------------------- incremental ref-v2 decode context -- */
 

@@ -77,7 +77,21 @@ SIGNATURES = {
     "rabbit_cuda_moe_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
                                    C.POINTER(C.c_uint64), C.POINTER(_I),
                                    C.POINTER(C.c_uint64)]),
+    "rabbit_cuda_moe_stats_ex": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                      C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                      C.POINTER(C.c_uint64), C.POINTER(_I), C.POINTER(_I)]),
     "rabbit_cuda_moe_decode_bytes": (C.c_uint64, [_P]),
+    "rabbit_cuda_cache_create": (_P, [_I]),
+    "rabbit_cuda_cache_free": (None, [_P]),
+    "rabbit_cuda_cache_set_expert_size": (None, [_P, C.c_size_t]),
+    "rabbit_cuda_cache_get": (_P, [_P, _I]),
+    "rabbit_cuda_cache_put": (_P, [_P, _I, _P]),
+    "rabbit_cuda_cache_pin": (_I, [_P, _I, _P]),
+    "rabbit_cuda_cache_stats": (None, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                       C.POINTER(C.c_uint64)]),
+    "rabbit_cuda_cache_stats_ex": (None, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                          C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                          C.POINTER(C.c_uint64), C.POINTER(_I), C.POINTER(_I)]),
     "rabbit_cuda_moe_prefill_dev": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
     "rabbit_cuda_moe_prefill": (_I, [_P, _I, _P, _P, _I, _P, _P]),
     "rabbit_cuda_moe_set_expert_parallel": (_I, [_P, _I, _I]),
@@ -310,6 +324,16 @@ class MoePool:
         return {"hbm_hits": a.value, "uploads": b.value, "h2d_bytes": c.value,
                 "resident_records": r.value, "pool_bytes": e.value}
 
+    def stats_ex(self) -> dict:
+        """The rabbit_cache_stats_ex counters of the pool."""
+        v = [C.c_uint64() for _ in range(5)]
+        n = [C.c_int(), C.c_int()]
+        check(lib().rabbit_cuda_moe_stats_ex(self.handle, *[C.byref(x) for x in v],
+                                             *[C.byref(x) for x in n]))
+        keys = ("hits", "misses", "inserts", "evictions", "bytes_copied")
+        return {**{k: x.value for k, x in zip(keys, v)}, "n_slots": n[0].value,
+                "n_pinned": n[1].value}
+
     @property
     def decode_bytes(self) -> int:
         return int(lib().rabbit_cuda_moe_decode_bytes(self.handle))
@@ -408,3 +432,39 @@ class RefV2:
             self.free()
         except Exception:
             pass
+
+
+class Cache:
+    """The reference's expert cache API (rabbit_cache_*, src/rabbit.h:123-134)
+    with HBM slots: get / put / pin return device addresses (0 for NULL)."""
+
+    def __init__(self, n_slots: int):
+        self.handle = lib().rabbit_cuda_cache_create(n_slots)
+        if not self.handle:
+            raise RabbitCudaError(ERR_DEVICE, lib().rabbit_cuda_last_error().decode())
+
+    def set_expert_size(self, size: int) -> None:
+        lib().rabbit_cuda_cache_set_expert_size(self.handle, size)
+
+    def get(self, expert_id: int) -> int:
+        return lib().rabbit_cuda_cache_get(self.handle, expert_id) or 0
+
+    def put(self, expert_id: int, record) -> int:
+        src = None if record is None else _ptr(record)
+        return lib().rabbit_cuda_cache_put(self.handle, expert_id, src) or 0
+
+    def pin(self, expert_id: int, record=None) -> int:
+        src = None if record is None else _ptr(record)
+        return int(lib().rabbit_cuda_cache_pin(self.handle, expert_id, src))
+
+    def stats_ex(self) -> tuple:
+        v = [C.c_uint64() for _ in range(5)]
+        n = [C.c_int(), C.c_int()]
+        lib().rabbit_cuda_cache_stats_ex(self.handle, *[C.byref(x) for x in v],
+                                         *[C.byref(x) for x in n])
+        return tuple(x.value for x in v) + (n[0].value, n[1].value)
+
+    def free(self) -> None:
+        if self.handle:
+            lib().rabbit_cuda_cache_free(self.handle)
+            self.handle = None

@@ -116,8 +116,12 @@ struct rabbit_cuda_moe {
     // rows (tc_ok: built; otherwise the multi-token path runs per token)
     CUtensorMap tm_gu{}, tm_dn{};
     bool tc_ok = false;
-    // counters
+    // counters (rabbit_cuda_moe_stats[_ex]): kernel calls served from HBM,
+    // calls refused because their layer was not resident, records uploaded,
+    // records dropped from a window block taken for another layer, bytes moved
     uint64_t hbm_hits = 0, uploads = 0, h2d_bytes = 0;
+    mutable uint64_t misses = 0;
+    uint64_t evictions = 0;
     std::vector<uint8_t> img;  // host image of one record in the tiled layout
     // file-backed upload (rabbit_cuda_moe_upload_file): pinned record buffers
     // the reader thread fills, and pinned tiled images (group-32 pools), each
@@ -136,7 +140,10 @@ static int layer_map(const rabbit_cuda_moe *p, int layer, int *base, int *n_loca
     if (layer < 0 || layer >= p->L) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d out of range", layer);
     if (p->window) {  // the layer's block, if it holds one
         const int b = p->layer_block[layer];
-        if (b < 0) return fail(RABBIT_CUDA_ERR_ARGS, "layer %d not uploaded (not in the pool's window)", layer);
+        if (b < 0) {
+            p->misses++;
+            return fail(RABBIT_CUDA_ERR_ARGS, "layer %d not uploaded (not in the pool's window)", layer);
+        }
         *base = b * p->epl;
         *n_local = std::min(p->epl, p->n_records - layer * p->epl);
         return RABBIT_CUDA_OK;
@@ -170,6 +177,7 @@ static int layer_slot(rabbit_cuda_moe *p, int layer, int *base, int *n_local, in
         for (int i = 1; i < p->window; ++i)
             if (p->block_use[i] < p->block_use[b]) b = i;
         if (p->block_layer[b] >= 0) p->layer_block[p->block_layer[b]] = -1;
+        for (int r = 0; r < p->epl; ++r) p->evictions += p->resident[(size_t)b * p->epl + r];
         std::fill(p->resident.begin() + (size_t)b * p->epl, p->resident.begin() + (size_t)(b + 1) * p->epl, 0);
         RB_CUDA(cudaStreamWaitEvent(p->up, p->block_ev[b], 0));
         p->block_layer[b] = layer;
@@ -1002,7 +1010,10 @@ static int decode_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, flo
     if (st) return st;
     for (int r = 0; r < n_local; ++r)
         if (!p->resident[base + r])
+        {
+            p->misses++;
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode: layer %d not uploaded", layer);
+        }
     RB_CUDA(cudaSetDevice(p->device));
     int *ids = d_ids ? d_ids : p->ids_int;
     float *w = d_weights ? d_weights : p->w_int;
@@ -1146,7 +1157,10 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     if (st) return st;
     for (int r = 0; r < n_local; ++r)
         if (!p->resident[base + r])
+        {
+            p->misses++;
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_decode_noalloc: layer %d not uploaded", layer);
+        }
     RB_CUDA(cudaSetDevice(p->device));
     uint8_t *scratch = nullptr;
     if ((st = noalloc_scratch(p->device, &scratch)) != RABBIT_CUDA_OK) return st;
@@ -1261,7 +1275,8 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t U = P / kTcUnit + R;
     const size_t o_act = take(sizeof(int) * U * 4 + 2 * sizeof(int));
     const size_t o_pu = take(sizeof(int) * P);
-    // B rows of the units: three per pair, each unit padded by at most 15
+    // B rows of the units: three per pair, each unit padded by at most 15; a
+    // row holds one byte per input
     const size_t rows = 3 * P + 15 * U;
     const size_t o_xim = take(rows * (size_t)p->H), o_mim = take(rows * (size_t)p->I);
     const size_t o_xu = take(sizeof(float) * P), o_mu = take(sizeof(float) * P);
@@ -1375,7 +1390,10 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     if (st) return st;
     for (int r = 0; r < n_local; ++r)
         if (!p->resident[base + r])
+        {
+            p->misses++;
             return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: layer %d not uploaded", layer);
+        }
     RB_CUDA(cudaSetDevice(p->device));
     const bool batch = p->tc_ok;
     if (!batch && p->ep_size > 1)
@@ -1524,6 +1542,25 @@ int rabbit_cuda_moe_stats(const rabbit_cuda_moe *p, uint64_t *hbm_hits, uint64_t
         *resident_records = n;
     }
     if (pool_bytes) *pool_bytes = p->pool_bytes;
+    return ok();
+}
+
+int rabbit_cuda_moe_stats_ex(const rabbit_cuda_moe *p, uint64_t *hits, uint64_t *misses,
+                             uint64_t *inserts, uint64_t *evictions, uint64_t *bytes_copied,
+                             int *n_slots, int *n_pinned) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_stats_ex: NULL pool");
+    if (hits) *hits = p->hbm_hits;
+    if (misses) *misses = p->misses;
+    if (inserts) *inserts = p->uploads;
+    if (evictions) *evictions = p->evictions;
+    if (bytes_copied) *bytes_copied = p->h2d_bytes;
+    if (n_slots) *n_slots = p->pool_records;
+    if (n_pinned) {  // a pool without a window never drops a record it holds
+        int n = 0;
+        if (!p->window)
+            for (uint8_t r : p->resident) n += r;
+        *n_pinned = n;
+    }
     return ok();
 }
 

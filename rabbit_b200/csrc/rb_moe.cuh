@@ -124,8 +124,8 @@ struct MoeBatchArgs {
     float *down;     // [P][tc.KC][H]
     int *pair_u;     // [P] unit * kTcUnit + column of pair
     // B rows of the units: unit u's image holds, per group g of 32 inputs,
-    // tc_n_of(n_u) rows of 32 bytes (row 3c + p = digit p of pair c) as 8-row
-    // x 16-byte core matrices, at (img_off[u] G + g N_u) 32 bytes
+    // N_u = tc_n_of(n_u) rows of 32 bytes (row 3c + p = digit p of pair c) as
+    // 8-row x 16-byte core matrices, at (img_off[u] G + g N_u) 32 bytes
     uint8_t *xim;    // xn rows (G = H / 32)
     uint8_t *mim;    // mid rows (G = I / 32)
     float *xunit;    // [P] 2^(e-22) of the pair's xn row

@@ -67,3 +67,21 @@ def test_moe_desc_layout_matches_header(rc):
     body = re.search(r"typedef struct \{(.*?)\} rabbit_cuda_moe_desc;", text, re.S).group(1)
     fields = re.findall(r"(\w+)\s*;", body)
     assert fields == [f for f, _ in rc.MoeDesc._fields_]
+
+
+def test_cache_api_without_a_device_follows_null_conventions(rc):
+    """The cache keeps the reference's conventions for a NULL cache
+    (src/memory.c:68-92): stats read as zeros, get / put return NULL, pin -1;
+    creating one on a host without a GPU returns NULL with the reason set."""
+    so = rc.lib()
+    v = [C.c_uint64(7) for _ in range(5)]
+    n = [C.c_int(7), C.c_int(7)]
+    so.rabbit_cuda_cache_stats_ex(None, *[C.byref(x) for x in v], *[C.byref(x) for x in n])
+    assert [x.value for x in v] == [0] * 5 and [x.value for x in n] == [0, 0]
+    assert not so.rabbit_cuda_cache_get(None, 1)
+    assert not so.rabbit_cuda_cache_put(None, 1, None)
+    assert so.rabbit_cuda_cache_pin(None, 1, None) == -1
+    so.rabbit_cuda_cache_free(None)
+    if rc.device_count() == 0:
+        assert not so.rabbit_cuda_cache_create(4)
+        assert so.rabbit_cuda_last_error()
