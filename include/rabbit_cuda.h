@@ -60,6 +60,8 @@ int rabbit_cuda_set_device(int device);
 /* Device-side wait limit in milliseconds for mbarrier / inter-CTA spins
  * (default 2000). A wait that runs out sets RABBIT_CUDA_ERR_TIMEOUT. */
 int rabbit_cuda_set_wait_limit_ms(int ms);
+/* The same limit in microseconds (for tests of the timeout path). */
+int rabbit_cuda_set_wait_limit_us(int us);
 
 /* --------------------------------------------- stateless quant drop-ins -- */
 
@@ -271,6 +273,13 @@ int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, fl
  * output. ids / weights report the full routing. size 1 (the default) is the
  * whole layer. Decode calls on a pool with size > 1 are refused. */
 int rabbit_cuda_moe_set_expert_parallel(rabbit_cuda_moe *p, int rank, int size);
+/* Test hook (no counterpart in the reference): in the next fused decode of
+ * this pool, no CTA publishes router row `expert`, so every CTA's bounded
+ * wait for that score runs out (RABBIT_CUDA_ERR_TIMEOUT through
+ * rabbit_cuda_moe_check) with no copy in flight; the launch after it is
+ * normal. UNSUPPORTED for pools whose decode scores every router row in
+ * every CTA (routers up to 256 KB). */
+int rabbit_cuda_moe_debug_withhold_score(rabbit_cuda_moe *p, int expert);
 /* Check the device error word after work on `stream` finished (TIMEOUT if a
  * bounded wait gave up). Synchronises `stream`. */
 int rabbit_cuda_moe_check(rabbit_cuda_moe *p, void *stream);

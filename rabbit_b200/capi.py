@@ -53,6 +53,7 @@ SIGNATURES = {
     "rabbit_cuda_device_count": (_I, [C.POINTER(_I)]),
     "rabbit_cuda_set_device": (_I, [_I]),
     "rabbit_cuda_set_wait_limit_ms": (_I, [_I]),
+    "rabbit_cuda_set_wait_limit_us": (_I, [_I]),
     "rabbit_cuda_gemv_int4_grouped": (_I, [_P, _P, _P, _I, _I]),
     "rabbit_cuda_dequant_int4_grouped_dev": (_I, [_P, _P, _I, _P]),
     "rabbit_cuda_gemv_int4_grouped_dev": (_I, [_P, _P, _P, _I, _I, _P]),
@@ -74,6 +75,7 @@ SIGNATURES = {
     "rabbit_cuda_moe_decode_dev": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "rabbit_cuda_moe_decode_dev_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "rabbit_cuda_moe_check": (_I, [_P, _P]),
+    "rabbit_cuda_moe_debug_withhold_score": (_I, [_P, _I]),
     "rabbit_cuda_moe_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
                                    C.POINTER(C.c_uint64), C.POINTER(_I),
                                    C.POINTER(C.c_uint64)]),

@@ -112,6 +112,7 @@ struct rabbit_cuda_moe {
     float *bt_w = nullptr;   // [bt_cap][8]
     float *bt_pin = nullptr; // pinned [bt_cap][H] + ids/weights
     int ep_rank = 0, ep_size = 1;  // expert-parallel share of the multi-token path
+    int withhold_row = -1;  // test hook for the next fused launch (see rabbit_cuda_moe_debug_*)
     // tensor maps of the multi-token GEMMs over the pool's GU and D nibble
     // rows (tc_ok: built; otherwise the multi-token path runs per token)
     CUtensorMap tm_gu{}, tm_dn{};
@@ -352,6 +353,7 @@ static bool plan_fused(rabbit_cuda_moe *p, int sm_count) {
     p->block = (CW + 3) * 32;  // consumers, producer, epilogue, scout
     if (G > kMaxGrid) return false;
     p->grid = G;
+    a.withhold_row = -1;
     p->off_d = align_up((size_t)a.tb.ntiles * a.tb.tile_stride, 256);
     p->rec_stride = p->off_d + align_up((size_t)a.tc.ntiles * a.tc.tile_stride, 256);
     return true;
@@ -1052,6 +1054,8 @@ static int decode_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, flo
             a.seq = next_seq(&p->seq, tagged, bytes, 4, s);
         }
         a.wait_ns = wait_limit_ns();
+        a.withhold_row = p->withhold_row;
+        p->withhold_row = -1;
         RB_CUDA(launch_fused(p, a, s));
     } else {
         MoeGenericArgs a;
@@ -1202,6 +1206,19 @@ int rabbit_cuda_moe_decode_dev_noalloc(rabbit_cuda_moe *p, int layer, const floa
     RB_CUDA(launch_fused(p, a, s));
     if ((st = window_leave(p, layer, s)) != RABBIT_CUDA_OK) return st;
     p->hbm_hits++;
+    return ok();
+}
+
+int rabbit_cuda_moe_debug_withhold_score(rabbit_cuda_moe *p, int expert) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_debug_withhold_score: NULL pool");
+    if (!p->fast || p->plan.route_local)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_debug_withhold_score: this pool's fused decode scores every router row "
+                    "in every CTA (no scores are published)");
+    if (expert < 0 || expert >= p->E)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_debug_withhold_score: expert %d of %d", expert,
+                    p->E);
+    p->withhold_row = expert;
     return ok();
 }
 

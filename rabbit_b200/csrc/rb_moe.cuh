@@ -47,6 +47,7 @@ struct MoeFusedArgs {
     unsigned long long *down;  // [k+S][tc.KC][H]: down rows per slot and column chunk
     unsigned *flags;           // [grid]: seq once the CTA has read h
     unsigned seq;              // this launch's tag (never 0)
+    int withhold_row;          // test hook: router row no CTA publishes (-1: none)
     int *err;
     uint64_t wait_ns;
     // plan: CW consumer warps; phase B (gate/up, in = H) uses KSb warps per

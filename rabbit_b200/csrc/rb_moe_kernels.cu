@@ -527,7 +527,7 @@ __global__ void __launch_bounds__((kMoeConsumerWarps + 3) * 32, 1) k_moe_decode_
             d = warp_sum(d);
             if (lane == 0) red[warp] = d;
             __syncthreads();
-            if (tid == 0) {
+            if (tid == 0 && e != a.withhold_row) {
                 float t = 0.f;
                 for (int w = 0; w < nw; ++w) t += red[w];
                 st_tagged(a.scores + e, t, a.seq);

@@ -154,4 +154,10 @@ int rabbit_cuda_set_wait_limit_ms(int ms) {
     return rb::ok();
 }
 
+int rabbit_cuda_set_wait_limit_us(int us) {
+    if (us <= 0) return rb::fail(RABBIT_CUDA_ERR_ARGS, "wait limit must be positive");
+    rb::g_wait_ns.store(static_cast<uint64_t>(us) * 1000ull);
+    return rb::ok();
+}
+
 }  // extern "C"
