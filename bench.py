@@ -477,9 +477,13 @@ def prefill_item(capi, synth, peak: float, runs: int = 5, cpu: bool = True,
 # Mixtral-8x22B-shaped decode, expert-parallel: 56 layers, hidden 6144, expert
 # FFN 16384, 8 experts top-2, int4 group-32 (84.5 GB of experts); a batch of
 # 64 decode tokens per step. Rank r of N holds experts e = r (mod N) of every
-# layer; per layer every rank routes all 64 tokens, applies its experts
-# (rabbit_cuda_moe_prefill_dev with rabbit_cuda_moe_set_expert_parallel), and
-# an all-reduce (sum, NCCL) of the shares gives the layer output.
+# layer. The exchange is the library's own (rabbit_cuda_ep_* over NCCL,
+# rabbit_cuda_moe_set_ep), inside each rabbit_cuda_moe_prefill_dev call:
+#   all-to-all  each rank owns 64 / N of the tokens, routes them, sends the
+#               pairs routed to other ranks' experts there (grouped
+#               ncclSend / ncclRecv) and combines the rows that come back;
+#   all-reduce  every rank routes all 64 tokens, applies its experts, and the
+#               shares are summed (ncclAllReduce).
 XL = dict(L=56, H=6144, E=8, k=2, I=16384)
 XL_T = 64
 
@@ -489,77 +493,121 @@ def ep_item(capi, synth, peak: float, rank: int, world: int, dist, steps: int = 
     import torch
 
     L, H, E, k, I = layers or XL["L"], XL["H"], XL["E"], XL["k"], XL["I"]
-    if E % world:
-        return {"unavailable": f"{E} experts do not split over {world} ranks"}
+    if E % world or XL_T % world:
+        return {"unavailable": f"{E} experts / {XL_T} tokens do not split over {world} ranks"}
     rng = np.random.default_rng(SEED + 5)  # the same routers and tokens on every rank
     routers = [rng.normal(0, 0.02, (E, H)).astype(np.float32) for _ in range(L)]
     size = synth.expert_record_size(H, I)
+    dev = torch.cuda.current_device()
     pool = capi.MoePool(records=None, expert_size=size, n_layers=L, hidden=H, n_experts=E,
                         top_k=k, inter=I, quant=4, rms_ffn=[np.ones(H, np.float32)] * L,
-                        w_router=routers, experts_per_layer=E // world,
-                        device=torch.cuda.current_device())
+                        w_router=routers, experts_per_layer=E // world, device=dev)
     pool.fill_synthetic(SEED * 1000 + 5 + rank)
+    ep = None
     if world > 1:
-        pool.set_expert_parallel(rank, world)
+        box = [capi.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ep = capi.Ep(box[0], rank, world, dev)
     stream = torch.cuda.current_stream()
     s = stream.cuda_stream
     # each layer gets its own seeded N(0, 1) batch: chained layers of random
     # weights pull every token onto the same two experts, which real traffic
     # does not do
     hin = torch.from_numpy(rng.standard_normal((L, XL_T, H)).astype(np.float32)).cuda()
-    h = torch.empty((L, XL_T, H), dtype=torch.float32, device="cuda")
-    ids = torch.zeros((L, XL_T, k), dtype=torch.int32, device="cuda")
-    wts = torch.zeros((L, XL_T, k), dtype=torch.float32, device="cuda")
-
-    def step(with_ids: bool = False):
-        for layer in range(L):
-            pool.prefill_dev(layer, hin[layer].data_ptr(), h[layer].data_ptr(), XL_T,
-                             ids[layer].data_ptr() if with_ids else 0,
-                             wts[layer].data_ptr() if with_ids else 0, s)
-            if world > 1:
-                dist.all_reduce(h[layer])
-
-    step(True)
-    pool.check(s)
-    routed = ids.cpu().numpy()
-    distinct = [len(np.unique(routed[l])) for l in range(L)]
     expert_bytes = 3 * synth.int4_nbytes(H * I)
-    step_bytes = sum(E * H * 4 + d * expert_bytes for d in distinct)  # whole job
-    step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    pool.check(s)
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    sec = ms / 1e3 / steps
-    per_rank = step_bytes / world
+
+    def measure(mode: int) -> dict:
+        a2a = mode == capi.EP_ALLTOALL
+        Tm = XL_T // world if a2a else XL_T
+        src = hin[:, rank * Tm:(rank + 1) * Tm].contiguous() if a2a else hin
+        h = torch.empty((L, Tm, H), dtype=torch.float32, device="cuda")
+        ids = torch.zeros((L, Tm, k), dtype=torch.int32, device="cuda")
+        wts = torch.zeros((L, Tm, k), dtype=torch.float32, device="cuda")
+        if ep:
+            pool.set_ep(ep, mode)
+
+        def step(with_ids: bool = False):
+            for layer in range(L):
+                pool.prefill_dev(layer, src[layer].data_ptr(), h[layer].data_ptr(), Tm,
+                                 ids[layer].data_ptr() if with_ids else 0,
+                                 wts[layer].data_ptr() if with_ids else 0, s)
+
+        step(True)
+        pool.check(s)
+        if a2a and world > 1:  # every rank's routing, for the bytes the step reads
+            parts = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(parts, ids)
+            routed = torch.cat(parts, dim=1).cpu().numpy()
+        else:
+            routed = ids.cpu().numpy()
+        distinct = [len(np.unique(routed[l])) for l in range(L)]
+        step_bytes = sum(E * H * 4 + d * expert_bytes for d in distinct)  # whole job
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        pool.check(s)
+        ms = ev0.elapsed_time(ev1)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        sec = ms / 1e3 / steps
+        out = {"tokens_per_s": round(XL_T / sec, 1), "ms_per_step": round(sec * 1e3, 3),
+               "distinct_experts_per_layer": round(float(np.mean(distinct)), 2),
+               "achieved_per_gpu": round(step_bytes / world / sec / 1e9, 1),
+               "bytes_per_step_whole_job": step_bytes}
+        if ep:  # one more step with per-call events: kernels vs exchange, per rank
+            ep.set_timing(True)
+            ep.stats(reset=True)
+            step()
+            st = ep.stats(reset=True)
+            ep.set_timing(False)
+            mine = [st["total_ms"] / max(1, st["calls"]), st["exchange_ms"] / max(1, st["calls"])]
+            allr = [None] * world
+            dist.all_gather_object(allr, mine)
+            out["per_layer_ms_by_rank"] = [
+                {"rank": r, "layer_ms": round(v[0], 4), "exchange_ms": round(v[1], 4),
+                 "kernels_ms": round(v[0] - v[1], 4)} for r, v in enumerate(allr)]
+        return out
+
+    if world > 1:
+        res = {"all_to_all": measure(capi.EP_ALLTOALL), "all_reduce": measure(capi.EP_ALLREDUCE)}
+        best = res["all_to_all"]
+        pool.set_ep(None)
+    else:
+        res = {"single_gpu": measure(0)}
+        best = res["single_gpu"]
     pool.free()
+    if ep:
+        ep.free()
+    sec = best["ms_per_step"] / 1e3
     return {
         "metric": "EP MoE decode tokens/s (Mixtral-8x22B-shaped, batch 64)",
-        "value": round(XL_T / sec, 1), "unit": "tokens/s", "n_gpus": world,
-        "ms_per_step": round(sec * 1e3, 3), "steps": steps,
+        "value": best["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "ms_per_step": best["ms_per_step"], "steps": steps,
         "config": {"workload": (f"Mixtral-8x22B-shaped MoE blocks: {L} layers, hidden {H}, "
                                 f"inter {I}, {E} experts top-{k}, batch {XL_T} decode tokens, "
-                                f"expert-parallel over {world} GPU(s), NCCL all-reduce of the "
-                                f"shares per layer; each layer's batch seeded N(0, 1)"),
+                                f"expert-parallel over {world} GPU(s); the exchange is the "
+                                f"library's own NCCL all-to-all (value) or all-reduce (beside "
+                                f"it) inside rabbit_cuda_moe_prefill_dev; each layer's batch "
+                                f"seeded N(0, 1)"),
                    "experts_per_gpu_per_layer": E // world,
                    "expert_bytes_per_gpu_gb": round(L * (E // world) * size / 1e9, 1),
-                   "distinct_experts_per_layer": round(float(np.mean(distinct)), 2),
                    "note": "MoE blocks only (the routed-expert hot path); the attention and "
                            "dense fp32 projections of the step are not in this line"},
-        "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_rank / sec / 1e9, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(per_rank / sec / 1e9 / peak, 4),
-                     "bytes_per_step_whole_job": step_bytes},
+        "modes": res,
+        "roofline": {"bound": "hbm", "achieved_per_gpu": best["achieved_per_gpu"],
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(best["achieved_per_gpu"] / peak, 4),
+                     "bytes_per_step_whole_job": best["bytes_per_step_whole_job"]},
         "scaling": "strong",
     }
 

@@ -273,6 +273,54 @@ int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, fl
  * output. ids / weights report the full routing. size 1 (the default) is the
  * whole layer. Decode calls on a pool with size > 1 are refused. */
 int rabbit_cuda_moe_set_expert_parallel(rabbit_cuda_moe *p, int rank, int size);
+
+/* ------------------------------------- expert-parallel exchange (NCCL) --
+ * No counterpart in the reference (a single-process engine): the exchange
+ * between expert-parallel ranks done inside the library, over an NCCL
+ * communicator (libnccl.so.2, loaded when the first exchange object is made;
+ * RABBIT_NCCL_LIB names another file), so a C engine gets expert
+ * parallelism without torch. One process per GPU; every rank makes the same
+ * calls in the same order. */
+#define RABBIT_CUDA_EP_ID_BYTES 128
+typedef struct rabbit_cuda_ep rabbit_cuda_ep;
+/* A new communicator id (one rank makes it and hands the bytes to the others
+ * out of band: a file, a socket, MPI). */
+int rabbit_cuda_ep_unique_id(unsigned char id[RABBIT_CUDA_EP_ID_BYTES]);
+/* Join the communicator `id` as `rank` of `size` on `device`; collective (all
+ * ranks call it, each blocks until all have). NULL on failure. */
+rabbit_cuda_ep *rabbit_cuda_ep_create(const unsigned char id[RABBIT_CUDA_EP_ID_BYTES], int rank,
+                                      int size, int device);
+/* Destroy (ep_abort first if a peer is gone: it ends the communicator's
+ * pending work instead of waiting for it). Pools that use it must be freed,
+ * or given another exchange, first. */
+void rabbit_cuda_ep_free(rabbit_cuda_ep *ep);
+int rabbit_cuda_ep_abort(rabbit_cuda_ep *ep);
+/* Per-call timing (CUDA events on the call's stream, off by default):
+ * rabbit_cuda_ep_stats then synchronises them and reports the exchanged
+ * calls timed, their total time on the stream and the part spent in the
+ * exchange steps (collective wait included), in ms. Any pointer may be NULL;
+ * reset != 0 zeroes the sums afterwards. */
+int rabbit_cuda_ep_set_timing(rabbit_cuda_ep *ep, int on);
+int rabbit_cuda_ep_stats(rabbit_cuda_ep *ep, uint64_t *calls, double *total_ms,
+                         double *exchange_ms, int reset);
+
+/* Exchange modes of rabbit_cuda_moe_set_ep. */
+#define RABBIT_CUDA_EP_ALLREDUCE 1 /* every rank passes the same tokens; the ranks'
+                                      shares are summed (ncclAllReduce) so every
+                                      rank gets the layer output */
+#define RABBIT_CUDA_EP_ALLTOALL 2  /* every rank passes its OWN n_tokens tokens (the
+                                      same n_tokens on every rank) and gets their
+                                      layer output; pairs routed to another rank's
+                                      experts go there and come back (grouped
+                                      ncclSend / ncclRecv) */
+/* Give the pool's multi-token path (rabbit_cuda_moe_prefill[_dev]) an
+ * exchange: the pool holds rank ep.rank's share as in
+ * rabbit_cuda_moe_set_expert_parallel(p, ep.rank, ep.size) (same record rule),
+ * and each call also does the exchange of `mode` on its stream, so its output
+ * is the whole layer's. ALLTOALL outputs equal the single-pool outputs bit for
+ * bit (each token's slots combine in the same order). ep NULL (or mode 0)
+ * goes back to no exchange. The pool's device must be ep's. */
+int rabbit_cuda_moe_set_ep(rabbit_cuda_moe *p, rabbit_cuda_ep *ep, int mode);
 /* Test hook (no counterpart in the reference): in the next fused decode of
  * this pool, no CTA publishes router row `expert`, so every CTA's bounded
  * wait for that score runs out (RABBIT_CUDA_ERR_TIMEOUT through

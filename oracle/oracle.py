@@ -46,6 +46,18 @@ def build_reference(ref_src: str | None = None) -> Path | None:
     return REF_SO
 
 
+def build_engine(ref_src: str | None = None) -> Path | None:
+    """Build the reference engine twice from its sources (engine/Makefile):
+    _ref/engine/rabbit as it is and _ref/engine/rabbit_cuda with moe_step and
+    rabbit_ref_v2_greedy hooked into librabbit_cuda.so (build that first).
+    None when no sources are given."""
+    src = ref_src or os.environ.get("RABBIT_REF_SRC")
+    if not src or not Path(src, "forward_v2.c").exists():
+        return None
+    subprocess.check_call(["make", "-s", "-C", str(HERE / "engine"), f"REF_SRC={src}"])
+    return HERE / "_ref" / "engine"
+
+
 def _c(a, dtype):
     return np.ascontiguousarray(a, dtype=dtype)
 

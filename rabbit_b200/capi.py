@@ -97,6 +97,14 @@ SIGNATURES = {
     "rabbit_cuda_moe_prefill_dev": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
     "rabbit_cuda_moe_prefill": (_I, [_P, _I, _P, _P, _I, _P, _P]),
     "rabbit_cuda_moe_set_expert_parallel": (_I, [_P, _I, _I]),
+    "rabbit_cuda_ep_unique_id": (_I, [_P]),
+    "rabbit_cuda_ep_create": (_P, [_P, _I, _I, _I]),
+    "rabbit_cuda_ep_free": (None, [_P]),
+    "rabbit_cuda_ep_abort": (_I, [_P]),
+    "rabbit_cuda_ep_set_timing": (_I, [_P, _I]),
+    "rabbit_cuda_ep_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_double),
+                                  C.POINTER(C.c_double), _I]),
+    "rabbit_cuda_moe_set_ep": (_I, [_P, _P, _I]),
     "rabbit_cuda_refv2_create": (_I, [C.POINTER(DenseDesc), _P, C.POINTER(_P)]),
     "rabbit_cuda_refv2_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_refv2_free": (_I, [_P]),
@@ -310,6 +318,11 @@ class MoePool:
         """This pool holds rank `rank`'s experts (e % size == rank) of `size`."""
         check(lib().rabbit_cuda_moe_set_expert_parallel(self.handle, rank, size))
 
+    def set_ep(self, ep: "Ep | None", mode: int = 0) -> None:
+        """Exchange the pool's expert-parallel share through `ep` in `mode`
+        (EP_ALLREDUCE / EP_ALLTOALL) inside every prefill call; None: none."""
+        check(lib().rabbit_cuda_moe_set_ep(self.handle, ep.handle if ep else None, mode))
+
     def prefill_dev(self, layer: int, d_h_in: int, d_h_out: int, n_tokens: int, d_ids: int = 0,
                     d_w: int = 0, stream: int = 0) -> None:
         check(lib().rabbit_cuda_moe_prefill_dev(self.handle, layer, d_h_in, d_h_out, n_tokens,
@@ -434,6 +447,48 @@ class RefV2:
             self.free()
         except Exception:
             pass
+
+
+EP_ID_BYTES = 128
+EP_ALLREDUCE = 1
+EP_ALLTOALL = 2
+
+
+def ep_unique_id() -> bytes:
+    """A new communicator id for Ep (made by one rank, handed to the others)."""
+    buf = C.create_string_buffer(EP_ID_BYTES)
+    check(lib().rabbit_cuda_ep_unique_id(buf))
+    return buf.raw
+
+
+class Ep:
+    """The library's expert-parallel exchange (rabbit_cuda_ep_*): an NCCL
+    communicator joined collectively by every rank."""
+
+    def __init__(self, uid: bytes, rank: int, size: int, device: int):
+        assert len(uid) == EP_ID_BYTES
+        buf = C.create_string_buffer(uid, EP_ID_BYTES)
+        self.handle = lib().rabbit_cuda_ep_create(buf, rank, size, device)
+        if not self.handle:
+            raise RabbitCudaError(ERR_DEVICE, lib().rabbit_cuda_last_error().decode())
+        self.rank, self.size, self.device = rank, size, device
+
+    def set_timing(self, on: bool) -> None:
+        check(lib().rabbit_cuda_ep_set_timing(self.handle, 1 if on else 0))
+
+    def stats(self, reset: bool = False) -> dict:
+        n, t, x = C.c_uint64(), C.c_double(), C.c_double()
+        check(lib().rabbit_cuda_ep_stats(self.handle, C.byref(n), C.byref(t), C.byref(x),
+                                         1 if reset else 0))
+        return {"calls": n.value, "total_ms": t.value, "exchange_ms": x.value}
+
+    def abort(self) -> None:
+        check(lib().rabbit_cuda_ep_abort(self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            lib().rabbit_cuda_ep_free(self.handle)
+            self.handle = None
 
 
 class Cache:

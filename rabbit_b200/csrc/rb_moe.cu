@@ -24,6 +24,7 @@
 #include <thread>
 #include <vector>
 
+#include "rb_ep.h"
 #include "rb_gemv.cuh"
 #include "rb_moe.cuh"
 #include "rb_runtime.h"
@@ -112,6 +113,12 @@ struct rabbit_cuda_moe {
     float *bt_w = nullptr;   // [bt_cap][8]
     float *bt_pin = nullptr; // pinned [bt_cap][H] + ids/weights
     int ep_rank = 0, ep_size = 1;  // expert-parallel share of the multi-token path
+    // exchange of that share (rabbit_cuda_moe_set_ep): the communicator, the
+    // mode, and the all-to-all buffers for ep_tcap own tokens
+    rabbit_cuda_ep *ep = nullptr;
+    int ep_mode = 0;
+    void *ep_block = nullptr;
+    int ep_tcap = 0;
     int withhold_row = -1;  // test hook for the next fused launch (see rabbit_cuda_moe_debug_*)
     // tensor maps of the multi-token GEMMs over the pool's GU and D nibble
     // rows (tc_ok: built; otherwise the multi-token path runs per token)
@@ -385,6 +392,7 @@ static void free_pool(rabbit_cuda_moe *p) {
     }
     if (p->bt_block) cudaFree(p->bt_block);
     if (p->bt_pin) cudaFreeHost(p->bt_pin);
+    if (p->ep_block) cudaFree(p->ep_block);
     if (p->up) cudaStreamDestroy(p->up);
     delete p;
 }
@@ -1354,6 +1362,71 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     return RABBIT_CUDA_OK;
 }
 
+// All-to-all rows per peer for T own tokens: a token sends a peer at most
+// one pair per expert that peer holds, and at most k.
+static int ep_rows(const rabbit_cuda_moe *p, int T) {
+    return T * std::max(1, std::min(p->k, p->E / std::max(1, p->ep_size)));
+}
+// Tokens the batch scratch must hold for T own tokens: T, plus the rows the
+// peers may send in all-to-all mode.
+// All-to-all exchange in force (one rank alone has nothing to exchange).
+static bool ep_a2a(const rabbit_cuda_moe *p) {
+    return p->ep && p->ep_mode == RABBIT_CUDA_EP_ALLTOALL && p->ep_size > 1;
+}
+static int batch_tokens(const rabbit_cuda_moe *p, int T) {
+    return ep_a2a(p) ? T + (p->ep_size - 1) * ep_rows(p, T) : T;
+}
+
+// All-to-all buffers for T own tokens (after ensure_batch, whose block they
+// join in p->bt).
+static int ensure_ep(rabbit_cuda_moe *p, int T) {
+    if (T <= p->ep_tcap) return RABBIT_CUDA_OK;
+    const size_t peers = (size_t)p->ep_size - 1, cap = (size_t)ep_rows(p, T);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off = align_up(off + bytes, 256); return o; };
+    const size_t o_ids = take(sizeof(int) * T * p->k), o_w = take(sizeof(float) * T * p->k);
+    const size_t o_pos = take(sizeof(int) * T * p->k);
+    const size_t o_sm = take(sizeof(int4) * peers * cap), o_rm = take(sizeof(int4) * peers * cap);
+    const size_t rows = sizeof(float) * peers * cap * p->H;
+    const size_t o_sx = take(rows), o_rs = take(rows), o_rr = take(rows);
+    void *blk = nullptr;
+    cudaError_t e = cudaMalloc(&blk, off);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_prefill: exchange buffers");
+    if (p->ep_block) cudaFree(p->ep_block);
+    p->ep_block = blk;
+    uint8_t *b = static_cast<uint8_t *>(blk);
+    MoeBatchArgs &a = p->bt;
+    a.rt_ids = reinterpret_cast<int *>(b + o_ids);
+    a.rt_w = reinterpret_cast<float *>(b + o_w);
+    a.pos_tab = reinterpret_cast<int *>(b + o_pos);
+    a.send_meta = reinterpret_cast<int4 *>(b + o_sm);
+    a.recv_meta = reinterpret_cast<int4 *>(b + o_rm);
+    a.send_x = reinterpret_cast<float *>(b + o_sx);
+    a.ret_send = reinterpret_cast<float *>(b + o_rs);
+    a.ret_recv = reinterpret_cast<float *>(b + o_rr);
+    p->ep_tcap = T;
+    return RABBIT_CUDA_OK;
+}
+
+// Grouped send / receive of one float list (n_per_peer floats per peer) to
+// and from every other rank: peer index qi is rank qi, or qi + 1 from this
+// rank on.
+static int ep_swap(rabbit_cuda_moe *p, const Nccl *n, const void *send, void *recv,
+                   size_t n_per_peer, int dtype, size_t elem_bytes, cudaStream_t s) {
+    int r = n->group_start();
+    for (int qi = 0; r == 0 && qi < p->ep_size - 1; ++qi) {
+        const int q = qi < p->ep_rank ? qi : qi + 1;
+        const size_t o = (size_t)qi * n_per_peer * elem_bytes;
+        r = n->send(static_cast<const uint8_t *>(send) + o, n_per_peer, dtype, q, p->ep->comm, s);
+        if (r == 0)
+            r = n->recv(static_cast<uint8_t *>(recv) + o, n_per_peer, dtype, q, p->ep->comm, s);
+    }
+    const int r2 = n->group_end();
+    if (r) return nccl_fail(r, "moe_prefill: exchange");
+    if (r2) return nccl_fail(r2, "moe_prefill: exchange (group end)");
+    return RABBIT_CUDA_OK;
+}
+
 static cudaError_t launch_batch(int which, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                                 MoeBatchArgs &a) {
     cudaLaunchAttribute attr[1];
@@ -1425,8 +1498,14 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
         }
         return ok();
     }
-    if ((st = ensure_batch(p, T)) != RABBIT_CUDA_OK) return st;
-    const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (T + 31) / 32;
+    // all-to-all: V tokens = the T own ones and the rows the peers may send
+    const bool a2a = ep_a2a(p);
+    const int V = batch_tokens(p, T);
+    if ((st = ensure_batch(p, V)) != RABBIT_CUDA_OK) return st;
+    if (a2a && (st = ensure_ep(p, T)) != RABBIT_CUDA_OK) return st;
+    const Nccl *nc = nullptr;
+    if (p->ep && p->ep_mode && !(nc = nccl_lib())) return RABBIT_CUDA_ERR_UNSUPPORTED;
+    const int sms = p->ctx->sm_count, R = std::max(1, n_local), W = (V + 31) / 32;
     const size_t bucket_smem = sizeof(uint32_t) * (size_t)R * W + 3 * sizeof(int) * R;
     if (bucket_smem > kBatchDynMax)
         return fail(RABBIT_CUDA_ERR_UNSUPPORTED, "moe_prefill: layer too wide for the batch kernels");
@@ -1467,11 +1546,32 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     a.route_split = 8;  // router rows per CTA: E / 8 CTAs per token
     a.ep_rank = p->ep_rank;
     a.ep_size = p->ep_size;
+    a.ep_mode = a2a ? RABBIT_CUDA_EP_ALLTOALL : 0;
+    a.T_own = T;
+    a.ep_cap = a2a ? ep_rows(p, T) : 0;
+    const size_t cap = (size_t)a.ep_cap, H = (size_t)p->H;
+    // per-call timing marks of the exchange (nullptr: timing off); a mode
+    // without a first or second exchange records that pair back to back
+    EpMarks *mk = p->ep && p->ep_mode ? ep_begin(p->ep, s) : nullptr;
+    auto mark = [&](int i) {
+        if (mk) cudaEventRecord(mk->ev[i], s);
+    };
     RB_CUDA(launch_batch(0, dim3(T, (p->E + a.route_split - 1) / a.route_split), dim3(256),
                          sizeof(float) * (size_t)std::max(p->E, p->H), s, a));
+    if (a2a) {  // dispatch: the pairs routed to the peers' experts, with their xn rows
+        RB_CUDA(launch_batch(2, dim3(T, p->k), dim3(256), 0, s, a));
+        mark(1);
+        if ((st = ep_swap(p, nc, a.send_meta, a.recv_meta, 4 * cap, kNcclInt32, 4, s)) ||
+            (st = ep_swap(p, nc, a.send_x, a.xn + (size_t)T * H, cap * H, kNcclFloat32, 4, s)))
+            return st;
+        a.T = V;
+    } else {
+        mark(1);
+    }
+    mark(2);
     RB_CUDA(launch_batch(1, dim3(1), dim3(1024), bucket_smem, s, a));
     // B rows: one CTA per pair (pairs counted on the device; the rest leave)
-    const unsigned pairs_max = (unsigned)T * std::max(1, std::min(kMaxSlots, p->k + p->S));
+    const unsigned pairs_max = (unsigned)V * std::max(1, std::min(kMaxSlots, p->k + p->S));
     TcGemmArgs ga;
     ga.b = a;
     ga.tmap = p->tm_gu;
@@ -1480,7 +1580,21 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     RB_CUDA(launch_tc(2, dim3(pairs_max), dim3(256), 0, s, &a));
     ga.tmap = p->tm_dn;
     RB_CUDA(launch_tc(3, dim3(sms), dim3(kTcThreads), tc_gemm_smem(), s, &ga));
+    if (a2a) {  // combine, first half: the received pairs' outputs go back to their senders
+        if (V > T) RB_CUDA(launch_batch(3, dim3(V - T, (p->H + 255) / 256), dim3(256), 0, s, a));
+        mark(3);
+        if ((st = ep_swap(p, nc, a.ret_send, a.ret_recv, cap * H, kNcclFloat32, 4, s))) return st;
+        mark(4);
+    }
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
+    if (p->ep && p->ep_mode == RABBIT_CUDA_EP_ALLREDUCE) {  // the ranks' shares summed
+        mark(3);
+        const int r = nc->all_reduce(d_h_out, d_h_out, (size_t)T * H, kNcclFloat32, kNcclSum,
+                                     p->ep->comm, s);
+        if (r) return nccl_fail(r, "moe_prefill: all-reduce");
+        mark(4);
+    }
+    mark(5);
     p->hbm_hits += T;
     return ok();
 }
@@ -1513,6 +1627,37 @@ int rabbit_cuda_moe_set_expert_parallel(rabbit_cuda_moe *p, int rank, int size) 
     return ok();
 }
 
+int rabbit_cuda_moe_set_ep(rabbit_cuda_moe *p, rabbit_cuda_ep *ep, int mode) {
+    if (!p) return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_ep: NULL pool");
+    if (!ep || mode == 0) {
+        p->ep = nullptr;
+        p->ep_mode = 0;
+        return ok();
+    }
+    if (mode != RABBIT_CUDA_EP_ALLREDUCE && mode != RABBIT_CUDA_EP_ALLTOALL)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_ep: unknown mode %d", mode);
+    if (!ep->comm) return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_ep: the exchange was aborted");
+    if (ep->device != p->device)
+        return fail(RABBIT_CUDA_ERR_ARGS, "moe_set_ep: pool on device %d, exchange on %d", p->device,
+                    ep->device);
+    if (!p->tc_ok)
+        return fail(RABBIT_CUDA_ERR_UNSUPPORTED,
+                    "moe_set_ep: expert-parallel pools need the group-32 layout");
+    const int st = rabbit_cuda_moe_set_expert_parallel(p, ep->rank, ep->size);
+    if (st) return st;
+    std::lock_guard<std::mutex> g(p->ctx->mu);
+    if (p->ep_block) {  // sized for another rank count
+        RB_CUDA(cudaSetDevice(p->device));
+        RB_CUDA(cudaDeviceSynchronize());
+        cudaFree(p->ep_block);
+        p->ep_block = nullptr;
+    }
+    p->ep_tcap = 0;
+    p->ep = ep;
+    p->ep_mode = mode;
+    return ok();
+}
+
 int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, float *h_out,
                             int n_tokens, int *ids, float *weights) {
     if (!p || !h_in || !h_out) return fail(RABBIT_CUDA_ERR_ARGS, "moe_prefill: NULL argument");
@@ -1521,7 +1666,8 @@ int rabbit_cuda_moe_prefill(rabbit_cuda_moe *p, int layer, const float *h_in, fl
     std::lock_guard<std::mutex> g(p->ctx->mu);
     RB_CUDA(cudaSetDevice(p->device));
     cudaStream_t s = p->ctx->stream;
-    int st = ensure_batch(p, n_tokens);
+    // sized for the whole call up front: the staging below lives in the block
+    int st = ensure_batch(p, batch_tokens(p, n_tokens));
     if (st) return st;
     // pinned staging: [h (cap H)] [ids (cap 8)] [weights (cap 8)]; the device
     // copy of h is bt_h, ids / weights go to bt_ids / bt_w

@@ -131,9 +131,25 @@ struct MoeBatchArgs {
     uint8_t *mim;    // mid rows (G = I / 32)
     float *xunit;    // [P] 2^(e-22) of the pair's xn row
     float *munit;    // [P] same for its mid row
+    // expert-parallel exchange (rabbit_cuda_moe_set_ep): ep_mode 0 none or
+    // all-reduce (the kernels then see a plain share), 2 all-to-all. In
+    // all-to-all mode the first T_own tokens are this rank's own; tokens
+    // T_own .. T - 1 are the rows received from the peers, peer index
+    // qi (ranks other than this one, in rank order) at rows qi * ep_cap ..,
+    // each one pair (token, slot) of a peer's token routed to an expert here
+    int ep_mode, T_own, ep_cap;
+    int *rt_ids;      // [T_own][k] full routing of the own tokens (-1: none)
+    float *rt_w;      // [T_own][k]
+    int *pos_tab;     // [T_own][k] the pair's row in the owner peer's list (-1: local)
+    int4 *send_meta;  // [size-1][cap] {token, slot, local record, valid} sent to peer qi
+    int4 *recv_meta;  // [size-1][cap] the same, received from peer qi
+    float *send_x;    // [size-1][cap][H] xn rows sent (received ones land in xn)
+    float *ret_send;  // [size-1][cap][H] expert outputs of the received rows
+    float *ret_recv;  // [size-1][cap][H] expert outputs of the rows sent
 };
-// route, bucket, combine (same translation unit as the fused kernel)
-const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 4 combine
+// route, bucket, combine (same translation unit as the fused kernel); with
+// all-to-all exchange 2 pack, 3 return
+const void *moe_batch_kernel(int i);  // 0 route, 1 bucket, 2 pack, 3 return, 4 combine
 
 // The tensor-core kernels (rb_moe_tc.cu): one launch argument each, the
 // GEMMs with a tensor map over the pool's nibble rows of their phase.

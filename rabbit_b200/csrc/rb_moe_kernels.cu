@@ -979,6 +979,29 @@ __global__ void __launch_bounds__(256) k_batch_route(MoeBatchArgs a) {
         int n = 0;
         if (a.ep_size <= 1) {
             n = build_slots(ids, w, a.k, a.E, a.S, a.rec_base, a.n_local, a.usable, s_rec, s_w);
+        } else if (a.ep_mode == 2) {
+            // all-to-all: the token's full routing is kept for the dispatch
+            // and the combine; local slots are its experts on this rank
+            // (local record e / ep_size), then every shared expert
+            for (int i = 0; i < a.k; ++i) {
+                a.rt_ids[(size_t)t * a.k + i] = a.usable ? ids[i] : -1;
+                a.rt_w[(size_t)t * a.k + i] = w[i];
+            }
+            if (a.usable) {
+                for (int i = 0; i < a.k; ++i)
+                    if (ids[i] >= 0 && ids[i] % a.ep_size == a.ep_rank) {
+                        s_rec[n] = a.rec_base + ids[i] / a.ep_size;
+                        s_w[n] = w[i];
+                        ++n;
+                    }
+                const int e_loc = a.E / a.ep_size;
+                for (int sh = 0; sh < a.S; ++sh)
+                    if (e_loc + sh < a.n_local) {
+                        s_rec[n] = a.rec_base + e_loc + sh;
+                        s_w[n] = 1.0f;
+                        ++n;
+                    }
+            }
         } else if (a.usable) {
             // expert-parallel: this rank holds routed experts e = ep_rank (mod
             // ep_size) as local records e / ep_size, then the shared experts;
@@ -1017,6 +1040,19 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
     const int R = a.n_local, W = (a.T + 31) >> 5;
     int *cnt = reinterpret_cast<int *>(bm + (size_t)R * W), *off = cnt + R, *uf = off + R;
     for (int i = tid; i < R * W; i += nthr) bm[i] = 0u;
+    if (a.ep_mode == 2) {
+        // all-to-all: each received row is a token of one slot, the local
+        // record its sender named (padding rows: no slot)
+        for (int v = a.T_own + tid; v < a.T; v += nthr) {
+            const int4 m = a.recv_meta[v - a.T_own];
+            const bool used = m.w != 0 && m.z >= 0 && m.z < R;
+            a.nslot[v] = used ? 1 : 0;
+            if (used) {
+                a.srec[(size_t)v * kMaxSlots] = a.rec_base + m.z;
+                a.sw[(size_t)v * kMaxSlots] = 1.0f;
+            }
+        }
+    }
     __syncthreads();
     const int Q = a.T * kMaxSlots;
     for (int q = tid; q < Q; q += nthr) {
@@ -1077,6 +1113,35 @@ __global__ void __launch_bounds__(256) k_batch_combine(MoeBatchArgs a) {
     if (row >= a.H) return;
     const int ns = a.nslot[t], KC = a.tc.KC;
     float delta = 0.f;
+    if (a.ep_mode == 2) {
+        // all-to-all: the token's routed slots in order, each from its local
+        // pair or from the row its owner sent back, then the shared experts
+        // (local): the same terms in the same order as one pool's combine
+        int jl = 0;
+        for (int i = 0; i < a.k; ++i) {
+            const int e = a.rt_ids[(size_t)t * a.k + i];
+            if (e < 0) continue;
+            float dj = 0.f;
+            const int q = e % a.ep_size;
+            if (q == a.ep_rank) {
+                const int pj = a.pidx[(size_t)t * kMaxSlots + jl++];
+                for (int c = 0; c < KC; ++c) dj += a.down[((size_t)pj * KC + c) * a.H + row];
+            } else {
+                const int qi = q < a.ep_rank ? q : q - 1;
+                const int r = a.pos_tab[(size_t)t * a.k + i];
+                dj = a.ret_recv[((size_t)qi * a.ep_cap + r) * a.H + row];
+            }
+            delta += a.rt_w[(size_t)t * a.k + i] * dj;
+        }
+        for (; jl < ns; ++jl) {
+            const int pj = a.pidx[(size_t)t * kMaxSlots + jl];
+            float dj = 0.f;
+            for (int c = 0; c < KC; ++c) dj += a.down[((size_t)pj * KC + c) * a.H + row];
+            delta += a.sw[(size_t)t * kMaxSlots + jl] * dj;
+        }
+        a.h_out[(size_t)t * a.H + row] = a.h_in[(size_t)t * a.H + row] + delta;
+        return;
+    }
     for (int j = 0; j < ns; ++j) {
         const int pj = a.pidx[(size_t)t * kMaxSlots + j];
         float dj = 0.f;
@@ -1089,10 +1154,76 @@ __global__ void __launch_bounds__(256) k_batch_combine(MoeBatchArgs a) {
     a.h_out[(size_t)t * a.H + row] = base + delta;
 }
 
+// All-to-all dispatch, grid (T_own, k): CTA (t, i) places pair (token t,
+// slot i) in the list of the rank that owns its expert (e % ep_size), when
+// that is another rank: its row there is the number of earlier pairs (token
+// major, slot minor) with the same owner, so every list is in token order
+// whatever order the CTAs run in. The row gets the token's xn row and
+// {t, i, local record e / ep_size, 1}; CTA (0, 0) marks each list's rows
+// past its count unused.
+__global__ void __launch_bounds__(256) k_ep_pack(MoeBatchArgs a) {
+    __shared__ int s_pos;
+    launch_dependents();
+    wait_prerequisite();
+    const int t = blockIdx.x, i = blockIdx.y, tid = threadIdx.x, nthr = blockDim.x;
+    const int K = a.k, size = a.ep_size, rank = a.ep_rank, cap = a.ep_cap;
+    const int n = a.T_own * K;
+    if (t == 0 && i == 0) {
+        for (int qi = 0; qi < size - 1; ++qi) {
+            const int q = qi < rank ? qi : qi + 1;
+            int c = 0;
+            for (int x0 = 0; x0 < n; x0 += nthr) {
+                const int x = x0 + tid;
+                const int e = x < n ? a.rt_ids[x] : -1;
+                c += __syncthreads_count(e >= 0 && e % size == q);
+            }
+            for (int r = c + tid; r < cap; r += nthr)
+                a.send_meta[(size_t)qi * cap + r] = make_int4(0, 0, 0, 0);
+        }
+    }
+    const int me = t * K + i, e = a.rt_ids[me];
+    if (e < 0 || e % size == rank) {
+        if (tid == 0) a.pos_tab[me] = -1;
+        return;
+    }
+    const int q = e % size, qi = q < rank ? q : q - 1;
+    int c = 0;
+    for (int x0 = 0; x0 < me; x0 += nthr) {
+        const int x = x0 + tid;
+        const int ex = x < me ? a.rt_ids[x] : -1;
+        c += __syncthreads_count(ex >= 0 && ex % size == q);
+    }
+    if (tid == 0) {
+        s_pos = c;
+        a.pos_tab[me] = c;
+        a.send_meta[(size_t)qi * cap + c] = make_int4(t, i, e / size, 1);
+    }
+    __syncthreads();
+    const float4 *src = reinterpret_cast<const float4 *>(a.xn + (size_t)t * a.H);
+    float4 *dst = reinterpret_cast<float4 *>(a.send_x + ((size_t)qi * cap + s_pos) * a.H);
+    for (int j = tid; j < (a.H >> 2); j += nthr) dst[j] = src[j];
+}
+
+// All-to-all return, grid (T - T_own, ceil(H / 256)): each received pair's
+// expert output (its down row: the column chunks summed in order) into the
+// list that goes back to its sender, at the row it came in.
+__global__ void __launch_bounds__(256) k_ep_return(MoeBatchArgs a) {
+    launch_dependents();
+    wait_prerequisite();
+    const int v = a.T_own + blockIdx.x, row = blockIdx.y * blockDim.x + threadIdx.x;
+    if (row >= a.H || a.nslot[v] == 0) return;
+    const int KC = a.tc.KC, pj = a.pidx[(size_t)v * kMaxSlots];
+    float dj = 0.f;
+    for (int c = 0; c < KC; ++c) dj += a.down[((size_t)pj * KC + c) * a.H + row];
+    a.ret_send[(size_t)blockIdx.x * a.H + row] = dj;
+}
+
 const void *moe_batch_kernel(int i) {
     switch (i) {
         case 0: return (const void *)k_batch_route;
         case 1: return (const void *)k_batch_bucket;
+        case 2: return (const void *)k_ep_pack;
+        case 3: return (const void *)k_ep_return;
         case 4: return (const void *)k_batch_combine;
         default: return nullptr;
     }
