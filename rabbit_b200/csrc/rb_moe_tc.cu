@@ -350,26 +350,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 #pragma unroll
             for (int c = 0; c < kTcUnit; ++c) acc[c] = 0.f;
             const int nblk = (it.n + 7) >> 3;
-            float sc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sc[i] = valid && i < it.G ? __ldg(srow + i) : 0.f;
+            // the group's scale, fetched one group ahead
+            float s_next = valid ? __ldg(srow) : 0.f;
             for (int ch = 0; ch < it.nchunks && ok; ++ch) {
                 const int ng = min(8, it.G - ch * 8);
-                float scn[8];  // the next chunk's scales, loaded while this one is read out
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int gn = (ch + 1) * 8 + i;
-                    scn[i] = valid && gn < it.G ? __ldg(srow + gn) : 0.f;
-                }
-#pragma unroll
-                for (int gi = 0; gi < 8; ++gi) {
-                    if (gi >= ng) break;
+#pragma unroll 1
+                for (int gi = 0; gi < ng; ++gi) {
+                    const float s = s_next;
+                    {
+                        const int gn = ch * 8 + gi + 1;
+                        s_next = valid && gn < it.G ? __ldg(srow + gn) : 0.f;
+                    }
                     const int d = g % kTcDBufs;
                     if (!(ok = tc_wait_warp(&ss.dfull[d], (g / kTcDBufs) & 1, a, abort))) break;
                     tc_fence_after();
                     const uint32_t dt = tmem + lane_base + kColD +
                                         (uint32_t)(d * 2 * kTcMaxN + t * kTcMaxN);
-                    const float s = sc[gi];
 #pragma unroll
                     for (int blk = 0; blk < kTcUnit / 8; ++blk) {
                         if (blk < nblk) {
@@ -395,8 +391,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                     if (lane == 0) mbar_arrive(&ss.dempty[d]);
                     ++g;
                 }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) sc[i] = scn[i];
             }
             if (!ok) break;
             // the item's outputs: acc * 2^(e-22) / 16 per pair
