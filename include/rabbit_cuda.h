@@ -379,6 +379,27 @@ void rabbit_cuda_cache_stats_ex(const rabbit_cuda_cache *c, uint64_t *hits, uint
                                 uint64_t *inserts, uint64_t *evictions, uint64_t *bytes_copied,
                                 int *n_slots, int *n_pinned);
 
+/* ----------------------------------------- legacy per-tensor experts -- */
+
+/* The legacy expert of src/moe.c:119-224 (apply_expert), for records in the
+ * older per-tensor format (expert_quant 4: int4, any other value: int8; one
+ * fp32 scale per matrix): hidden[hidden_dim] += the expert's output times
+ * `weight`, the record read exactly as apply_expert reads it -- three
+ * [scale | payload] matrices (gate, up, down; I = expert_dim, 2 H when 0 or
+ * above 4 H; scales that are not positive finite numbers read as 1/127) with
+ * SwiGLU between them, or, for a record too small for three, its square-matrix
+ * and raw-byte fallbacks (moe.c:183-220). HOST record and hidden; synchronous.
+ * Sums are reordered across lanes: outputs match the reference within fp32
+ * rounding. A record whose odd-width int4 rows would run past its end (the
+ * reference reads beyond the buffer there) returns RABBIT_CUDA_ERR_FORMAT. */
+int rabbit_cuda_legacy_apply_expert(const void *record, uint64_t expert_size, int expert_quant,
+                                    int hidden_dim, int expert_dim, float *hidden, float weight);
+/* Same on DEVICE record and hidden (e.g. a slot of rabbit_cuda_cache_put),
+ * asynchronous on `stream`. */
+int rabbit_cuda_legacy_apply_expert_dev(const void *d_record, uint64_t expert_size,
+                                        int expert_quant, int hidden_dim, int expert_dim,
+                                        float *d_hidden, float weight, void *stream);
+
 /* ------------------------------------- incremental ref-v2 decode context -- */
 
 /* The dense (fp32) weights of a ref-v2 model, in the layout parse_weights

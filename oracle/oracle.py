@@ -93,6 +93,9 @@ class _Checker:
         self._swiglu = getattr(lib, p + "expert_swiglu")
         self._logits = getattr(lib, p + "logits")
         self._logits.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        self._legacy = getattr(lib, p + "legacy_apply_expert")
+        self._legacy.argtypes = [_u8p, C.c_size_t, C.c_int, C.c_int, C.c_int, _f32p, C.c_float]
+        self._legacy.restype = None
 
     # -- quant ---------------------------------------------------------------
     def int4_grouped_nbytes(self, n: int, group_size: int = 32) -> int:
@@ -143,6 +146,14 @@ class _Checker:
         x = _c(x, np.float32).copy()
         self._rope(x, x.size, pos)
         return x
+
+    def legacy_apply_expert(self, record, quant: int, hidden, expert_dim: int,
+                            weight: float) -> np.ndarray:
+        """moe.c:119-224: hidden + the legacy per-tensor expert's output."""
+        record = _c(record, np.uint8)
+        h = _c(hidden, np.float32).copy()
+        self._legacy(record, record.size, quant, h.size, expert_dim, h, float(weight))
+        return h
 
     def logits(self, lm_head, h) -> np.ndarray:
         lm_head = _c(lm_head, np.float32)

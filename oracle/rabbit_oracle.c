@@ -374,3 +374,115 @@ int orc_argmax(const float *x, int n) {
         if (x[i] > x[best]) best = i;
     return best;
 }
+
+/* ------------------------------------------------ legacy per-tensor experts -- */
+
+/* moe.c:7-16: y[o] += weight * (sum_i row[i] x[i]) * scale */
+static void orc_legacy_gemv_int8(const int8_t *W, float scale, const float *x, float *y,
+                                 int out_dim, int in_dim, float weight) {
+    for (int o = 0; o < out_dim; o++) {
+        const int8_t *row = W + (size_t)o * in_dim;
+        float sum = 0.0f;
+        for (int i = 0; i < in_dim; i++) sum += (float)row[i] * x[i];
+        y[o] += weight * sum * scale;
+    }
+}
+
+/* moe.c:18-35: rows of (in_dim + 1) / 2 bytes, element 2j = low nibble of
+ * byte j, 2j + 1 = its high nibble, value nibble - 8 */
+static void orc_legacy_gemv_int4(const uint8_t *W, float scale, const float *x, float *y,
+                                 int out_dim, int in_dim, float weight) {
+    const int in_bytes = (in_dim + 1) / 2;
+    for (int o = 0; o < out_dim; o++) {
+        const uint8_t *row = W + (size_t)o * in_bytes;
+        float sum = 0.0f;
+        for (int i = 0; i < in_dim; i += 2) {
+            const uint8_t b = row[i / 2];
+            sum += (float)((int)(b & 0x0F) - 8) * x[i];
+            if (i + 1 < in_dim) sum += (float)((int)((b >> 4) & 0x0F) - 8) * x[i + 1];
+        }
+        y[o] += weight * sum * scale;
+    }
+}
+
+/* moe.c:137-143: a stored scale that is not a positive finite number reads as 1/127 */
+static float orc_legacy_scale(const uint8_t *p) {
+    float s;
+    memcpy(&s, p, 4);
+    return (s > 0.0f && isfinite(s)) ? s : 1.0f / 127.0f;
+}
+
+/* moe.c:119-224 */
+void orc_legacy_apply_expert(const uint8_t *bytes, size_t size, int quant, int hidden_dim,
+                             int expert_dim, float *hidden, float weight) {
+    if (!bytes || !hidden || hidden_dim <= 0) return;
+    const int H = hidden_dim;
+    float *delta = (float *)calloc((size_t)H, sizeof(float));
+    if (!delta) return;
+    int inter = expert_dim > 0 ? expert_dim : H * 2;       /* moe.c:126-128 */
+    if (inter > H * 4) inter = H * 2;
+    if (inter < 1) inter = H;
+    const size_t mat = (size_t)inter * (size_t)H;
+    const size_t payload3 = quant == 4 ? (mat + 1) / 2 : mat;
+    if (size >= 3 * (4 + payload3) && inter > 0) {          /* moe.c:135-181 */
+        float *gate = (float *)calloc((size_t)inter, sizeof(float));
+        float *up = (float *)calloc((size_t)inter, sizeof(float));
+        float *mid = (float *)calloc((size_t)inter, sizeof(float));
+        const uint8_t *p = bytes;
+        if (gate && up && mid) {
+            for (int part = 0; part < 3; part++) {
+                float scale = 1.0f / 127.0f;
+                if (size - (size_t)(p - bytes) >= 4) {
+                    scale = orc_legacy_scale(p);
+                    p += 4;
+                }
+                const uint8_t *W = p;
+                p += payload3;
+                if (part < 2) {
+                    float *y = part == 0 ? gate : up;
+                    if (quant == 4) orc_legacy_gemv_int4(W, scale, hidden, y, inter, H, 1.0f);
+                    else orc_legacy_gemv_int8((const int8_t *)W, scale, hidden, y, inter, H, 1.0f);
+                } else {
+                    orc_silu_mul(gate, up, mid, inter);
+                    if (quant == 4) orc_legacy_gemv_int4(W, scale, mid, delta, H, inter, weight);
+                    else orc_legacy_gemv_int8((const int8_t *)W, scale, mid, delta, H, inter, weight);
+                }
+            }
+            for (int i = 0; i < H; i++) hidden[i] += delta[i];
+        }
+        free(gate);
+        free(up);
+        free(mid);
+        free(delta);
+        return;
+    }
+    /* moe.c:183-220: one square matrix, or the raw bytes */
+    float scale = 1.0f / 127.0f;
+    const uint8_t *W = bytes;
+    size_t payload = size;
+    if (size >= 4 + (size_t)H) {
+        scale = orc_legacy_scale(bytes);
+        W = bytes + 4;
+        payload = size - 4;
+    }
+    const float w = weight * 0.05f;
+    if (quant == 4) {
+        if (payload >= (size_t)H * (size_t)((H + 1) / 2))
+            orc_legacy_gemv_int4(W, scale, hidden, delta, H, H, w);
+    } else {
+        const size_t need = (size_t)H * (size_t)H;
+        if (payload >= need) {
+            orc_legacy_gemv_int8((const int8_t *)W, scale, hidden, delta, H, H, w);
+        } else if (size >= need) {
+            orc_legacy_gemv_int8((const int8_t *)bytes, 1.0f / 127.0f, hidden, delta, H, H, w);
+        } else {
+            const int usable = (int)(size < (size_t)H ? size : (size_t)H);
+            for (int i = 0; i < usable; i++) {
+                const float v = ((float)bytes[i] - 128.0f) / 128.0f;
+                delta[i] = weight * v * 0.1f;
+            }
+        }
+    }
+    for (int i = 0; i < H; i++) hidden[i] += delta[i];
+    free(delta);
+}

@@ -93,6 +93,15 @@ void orc_logits(const float *lm_head, const float *h, float *logits, int H, int 
 /* forward_v2.c:415-421 */
 int  orc_argmax(const float *x, int n);
 
+/* The legacy per-tensor expert of moe.c:119-224 (apply_expert): a record of
+ * three [f32 scale | int4 or int8 payload] matrices (gate, up, down; quant 4
+ * is int4 with rows of (in + 1) / 2 bytes, any other value int8), or, for a
+ * record too small for that, the square fallback (moe.c:183-220). Adds the
+ * expert's output times `weight` into hidden[hidden_dim]. expert_dim is the
+ * header's expert_dim (0: 2 * hidden_dim, moe.c:126-128). */
+void orc_legacy_apply_expert(const uint8_t *record, size_t expert_size, int quant, int hidden_dim,
+                             int expert_dim, float *hidden, float weight);
+
 #ifdef __cplusplus
 }
 #endif

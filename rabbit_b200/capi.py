@@ -105,6 +105,9 @@ SIGNATURES = {
     "rabbit_cuda_ep_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_double),
                                   C.POINTER(C.c_double), _I]),
     "rabbit_cuda_moe_set_ep": (_I, [_P, _P, _I]),
+    "rabbit_cuda_legacy_apply_expert": (_I, [_P, C.c_uint64, _I, _I, _I, _P, C.c_float]),
+    "rabbit_cuda_legacy_apply_expert_dev": (_I, [_P, C.c_uint64, _I, _I, _I, _P, C.c_float,
+                                                 _P]),
     "rabbit_cuda_refv2_create": (_I, [C.POINTER(DenseDesc), _P, C.POINTER(_P)]),
     "rabbit_cuda_refv2_fill_synthetic": (_I, [_P, C.c_uint64, C.c_float]),
     "rabbit_cuda_refv2_free": (_I, [_P]),
@@ -447,6 +450,17 @@ class RefV2:
             self.free()
         except Exception:
             pass
+
+
+def legacy_apply_expert(record: np.ndarray, quant: int, hidden: np.ndarray, expert_dim: int,
+                        weight: float) -> np.ndarray:
+    """src/moe.c:119-224 on the GPU: hidden + the legacy per-tensor expert's
+    output (host arrays; returns a new array)."""
+    record = np.ascontiguousarray(record, np.uint8)
+    h = np.ascontiguousarray(hidden, np.float32).copy()
+    check(lib().rabbit_cuda_legacy_apply_expert(_ptr(record), record.size, quant, h.size,
+                                                expert_dim, _ptr(h), float(weight)))
+    return h
 
 
 EP_ID_BYTES = 128

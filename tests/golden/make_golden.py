@@ -1,13 +1,14 @@
 """Generate the golden fixtures in this directory from the reference's own C.
 
     make -C oracle ref            # builds oracle/_ref/libref.so from the reference sources
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [name ...]   # all files, or only those named
 
 The reference publishes no int4 golden vectors (its tests/test_quant.c only
 bounds round-trip error), so these fixtures pin the reference's behaviour by
 running its compiled routines (rabbit_gemv_int4_grouped, rabbit_dequant_
 int4_grouped, rabbit_pack_int4_grouped, and forward_v2.c's select_top_k,
-expert_swiglu, moe_step, attention_step, logits_from_hidden) on small seeded
+expert_swiglu, moe_step, attention_step, logits_from_hidden; moe.c's legacy
+apply_expert) on small seeded
 inputs. Every array is stored with its inputs, so the oracle and the CUDA
 path can be checked against them on machines without the reference.
 """
@@ -178,10 +179,28 @@ def attn_cases(ref: Reference, out: dict) -> None:
     out["rope_y"] = np.stack([ref.apply_rope_head(x, p) for p in (0, 1, 7, 200)])
 
 
+def legacy_cases(ref: Reference, out: dict) -> None:
+    """moe.c:119-224 (apply_expert) on the cases of tests/legacy_cases.py."""
+    sys.path.insert(0, str(HERE.parent))
+    from legacy_cases import legacy_cases as cases
+
+    for i, (name, q, H, ed, rec, h, w) in enumerate(cases()):
+        out[f"legacy{i}_meta"] = np.array([q, H, ed], np.int64)
+        out[f"legacy{i}_rec"] = rec
+        out[f"legacy{i}_h"] = h
+        out[f"legacy{i}_w"] = np.array(w, np.float32)
+        out[f"legacy{i}_hout"] = ref.legacy_apply_expert(rec, q, h, ed, float(w))
+    out["legacy_count"] = np.array(i + 1)
+
+
 def main() -> None:
     ref = Reference()
+    only = set(sys.argv[1:])  # e.g. `legacy`: write only those files
     for name, fn in [("gemv", gemv_cases), ("pack", pack_cases), ("topk", topk_cases),
-                     ("swiglu", swiglu_cases), ("moe", moe_cases), ("attn", attn_cases)]:
+                     ("swiglu", swiglu_cases), ("moe", moe_cases), ("attn", attn_cases),
+                     ("legacy", legacy_cases)]:
+        if only and name not in only:
+            continue
         out: dict = {}
         fn(ref, out)
         np.savez_compressed(HERE / f"{name}.npz", **out)

@@ -149,3 +149,22 @@ def test_live_moe_matches_reference(oracle, reference, spec):
         kw = dict(H=H, E=E, top_k=k, inter=I, n_shared=S, quant=4, n_records=E + S,
                   expert_size=size, records=recs, rms_ffn=rms, w_router=w_router)
         _same(oracle.moe_step(h, **kw)[0], reference.moe_step(h, **kw))
+
+
+def test_golden_legacy_expert(oracle):
+    """moe.c:119-224: the oracle's legacy per-tensor expert equals the
+    reference's on every committed case, bit for bit."""
+    g = _load("legacy")
+    for i in range(int(g["legacy_count"])):
+        q, H, ed = (int(v) for v in g[f"legacy{i}_meta"])
+        got = oracle.legacy_apply_expert(g[f"legacy{i}_rec"], q, g[f"legacy{i}_h"], ed,
+                                         float(g[f"legacy{i}_w"]))
+        _same(got, g[f"legacy{i}_hout"])
+
+
+def test_live_legacy_expert_matches_reference(oracle, reference):
+    from legacy_cases import legacy_cases
+
+    for name, q, H, ed, rec, h, w in legacy_cases():
+        _same(oracle.legacy_apply_expert(rec, q, h, ed, w),
+              reference.legacy_apply_expert(rec, q, h, ed, w))
