@@ -89,7 +89,7 @@ constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 M
 constexpr int kTcStages = 3;         // staged 8-group chunks per CTA
 constexpr int kTcASlots = 8;         // A operands (one group each) in tensor memory
 constexpr int kTcDBufs = 2;          // accumulator buffers in tensor memory
-constexpr int kTcThreads = 18 * 32;  // TMA, MMA, 8 unpack and 8 readout warps
+constexpr int kTcThreads = 14 * 32;  // TMA, MMA, 4 unpack and 8 readout warps
 // MMA N of a unit of n pairs: three digit rows per pair, rounded up to 16.
 __host__ __device__ inline int tc_n_of(int n) { return (3 * n + 15) / 16 * 16; }
 

@@ -53,7 +53,7 @@ namespace rb {
 namespace {
 
 constexpr int kWarpUnpack = 2;   // first unpack warp
-constexpr int kWarpReadout = 10; // first readout warp
+constexpr int kWarpReadout = 6;  // first readout warp
 constexpr uint32_t kNibBytes = kTcRows * 128;                // one stage's nibble box
 constexpr uint32_t kBBytes = 8 * kTcMaxN * 32;               // one stage's B rows
 constexpr uint32_t kStageBytes = kNibBytes + kBBytes;
@@ -179,10 +179,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             mbar_init(&ss.full[s], 1);
-            mbar_init(&ss.empty[s], 8 + 1);  // the unpack warps + the MMA commit
+            mbar_init(&ss.empty[s], 4 + 1);  // the unpack warps + the MMA commit
         }
         for (int j = 0; j < kTcASlots; ++j) {
-            mbar_init(&ss.afull[j], 8);
+            mbar_init(&ss.afull[j], 4);
             mbar_init(&ss.aempty[j], 1);
         }
         for (int d = 0; d < kTcDBufs; ++d) {
@@ -273,12 +273,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         __syncwarp();
     } else if (warp < kWarpReadout) {
         // ------------------------------------------------------- unpack --
-        const int w = warp - kWarpUnpack, t = w >> 2, q = warp & 3;
-        const int m = t * 128 + q * 32 + lane;  // the TMEM row this thread fills
-        int srow_m = m;                          // the staged row it takes
+        const int q = warp & 3;
+        // the TMEM rows this thread fills: lane q * 32 + lane of both halves
+        const int m0 = q * 32 + lane, m1 = 128 + q * 32 + lane;
+        int sr0 = m0, sr1 = m1;  // the staged rows they take
         if (GU) {
             int p, h;
-            srow_m = gu_row(m, b.tb.TR, &p, &h);
+            sr0 = gu_row(m0, b.tb.TR, &p, &h);
+            sr1 = gu_row(m1, b.tb.TR, &p, &h);
         }
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         int kc = 0, g = 0;
@@ -288,7 +290,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
             for (int ch = 0; ch < it.nchunks && ok; ++ch, ++kc) {
                 const int s = kc % kTcStages;
                 if (!(ok = tc_wait_warp(&ss.full[s], (kc / kTcStages) & 1, a, abort))) break;
-                const uint8_t *row = stages + (size_t)s * kStageBytes + (size_t)srow_m * 128;
+                const uint8_t *row0 = stages + (size_t)s * kStageBytes + (size_t)sr0 * 128;
+                const uint8_t *row1 = stages + (size_t)s * kStageBytes + (size_t)sr1 * 128;
                 const int ng = min(8, it.G - ch * 8);
                 for (int gi = 0; gi < ng; ++gi, ++g) {
                     const int j = g % kTcASlots;
@@ -296,11 +299,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                         !(ok = tc_wait_warp(&ss.aempty[j], ((g / kTcASlots) - 1) & 1, a, abort)))
                         break;
                     // 128-byte swizzle: 16-byte unit gi of row m sits at unit gi ^ (m % 8)
-                    const uint4 wv =
-                        *reinterpret_cast<const uint4 *>(row + ((gi ^ (srow_m & 7)) << 4));
+                    const uint4 w0 = *reinterpret_cast<const uint4 *>(row0 + ((gi ^ (sr0 & 7)) << 4));
+                    const uint4 w1 = *reinterpret_cast<const uint4 *>(row1 + ((gi ^ (sr1 & 7)) << 4));
                     uint32_t av[8];
-                    nibbles_to_a(wv, av);
-                    tmem_st8(tmem + lane_base + kColA + (uint32_t)(j * 16 + t * 8), av);
+                    nibbles_to_a(w0, av);
+                    tmem_st8(tmem + lane_base + kColA + (uint32_t)(j * 16), av);
+                    nibbles_to_a(w1, av);
+                    tmem_st8(tmem + lane_base + kColA + (uint32_t)(j * 16 + 8), av);
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
