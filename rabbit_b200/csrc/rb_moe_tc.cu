@@ -158,9 +158,43 @@ __device__ __forceinline__ int gu_row(int m, int TRb, int *p_out, int *h_out) {
 }
 
 template <bool GU>
-__device__ __forceinline__ int items_total(const MoeBatchArgs &b) {
-    return GU ? b.n_act[0] * ((b.I + 127) / 128)
-              : b.n_act[0] * b.tc.KC * ((b.H + kTcRows - 1) / kTcRows);
+__device__ __forceinline__ int items_per_unit(const MoeBatchArgs &b) {
+    return GU ? (b.I + 127) / 128 : b.tc.KC * ((b.H + kTcRows - 1) / kTcRows);
+}
+
+// Relative cost of one item of a unit of n pairs: a fixed part per group
+// (staging, unpack, MMA, hand-offs) and the readout's 8-pair blocks.
+__device__ __forceinline__ long long item_cost(int n) { return 2 + ((n + 7) >> 3); }
+
+// The first item (units in order, items_per_unit each) whose cost-weighted
+// start s satisfies s * grid >= T; n_items if none.
+template <bool GU>
+__device__ int first_item_from(const MoeBatchArgs &b, long long T, int grid) {
+    const int U = b.n_act[0], ipu = items_per_unit<GU>(b);
+    long long pre = 0;
+    for (int u = 0; u < U; ++u) {
+        const long long c = item_cost(b.act_cnt[u]);
+        const long long end = pre + (long long)ipu * c;
+        if (end * grid > T) {  // some item of this unit starts at or past T / grid
+            const long long num = T - pre * grid, den = c * grid;
+            const long long k = num <= 0 ? 0 : (num + den - 1) / den;
+            if (k < ipu) return u * ipu + (int)k;
+        }
+        pre = end;
+    }
+    return U * ipu;
+}
+
+// This CTA's items: a contiguous run whose summed cost is about 1 / grid of
+// the launch's, so CTAs that draw the wide units (e.g. the shared experts,
+// routed every token) take fewer of them.
+template <bool GU>
+__device__ void cta_items(const MoeBatchArgs &b, int bx, int grid, int *i0, int *i1) {
+    const int U = b.n_act[0], ipu = items_per_unit<GU>(b);
+    long long total = 0;
+    for (int u = 0; u < U; ++u) total += (long long)ipu * item_cost(b.act_cnt[u]);
+    *i0 = first_item_from<GU>(b, total * bx, grid);
+    *i1 = first_item_from<GU>(b, total * (bx + 1), grid);
 }
 
 }  // namespace
@@ -202,9 +236,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     launch_dependents();
     wait_prerequisite();
 
-    const int n_items = items_total<GU>(b);
-    const int i0 = (int)((long long)blockIdx.x * n_items / gridDim.x);
-    const int i1 = (int)((long long)(blockIdx.x + 1) * n_items / gridDim.x);
+    int i0, i1;
+    cta_items<GU>(b, (int)blockIdx.x, (int)gridDim.x, &i0, &i1);
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA --
