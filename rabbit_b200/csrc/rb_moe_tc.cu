@@ -28,18 +28,27 @@
 //
 // Work items are (unit, 256 weight rows): for gate/up 128 rows of W1 and the
 // same 128 rows of W3 (the pool's GU tiles interleave TRb rows of each), for
-// down 256 rows of one column chunk of W2. A CTA (one per SM) runs its items
-// through a warp-specialised pipeline:
+// down 256 rows of one column chunk of W2. A CTA (one per SM) takes a
+// contiguous run of items whose summed cost (a fixed part per group plus the
+// readout's 8-pair blocks) is 1 / grid of the launch's, and runs it through a
+// warp-specialised pipeline:
 //   warp 0       TMA: each 8-group chunk of the item's 256 nibble rows (one
 //                cp.async.bulk.tensor box, 128-byte swizzle) and the unit's
 //                B rows of those 8 groups (one bulk copy) into a stage ring;
 //   warp 1       allocates tensor memory; one lane issues the MMAs (two per
-//                group: rows 0..127 and 128..255) and commits them;
-//   warps 2..9   unpack: one weight row per thread, nibbles -> A in TMEM;
-//   warps 10..17 readout: one weight row per thread, accumulators in
+//                group: rows 0..127 and 128..255) and commits them once per
+//                group (gdone[g % kTcASlots]: the group's A slot is free and
+//                its D buffer full);
+//   warps 2..5   unpack: two weight rows per thread (one of each 128-row
+//                half), nibbles -> A in TMEM;
+//   warps 6..13  readout: one weight row per thread, accumulators in
 //                registers; the item's outputs at its end (gate/up: mid =
 //                silu(gate) * up, the partner row in the same warp, taken
 //                by a shuffle; down: the chunk's rows of each pair).
+// A group's gdone phase cannot be overtaken before both its readers have
+// seen it: the MMA of group g + kTcASlots needs that group's A, which its
+// unpack writes only after seeing group g done, and the readout of group g
+// frees the D buffer that group g + kTcDBufs needs.
 // Every wait is bounded; on a timeout the CTA drains its copies and MMAs,
 // frees its tensor memory and leaves with RB_ERR_TIMEOUT in the error word.
 #include <cuda.h>
@@ -65,8 +74,8 @@ static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned (128-byte 
 
 struct TcSmem {
     uint64_t full[kTcStages], empty[kTcStages];
-    uint64_t afull[kTcASlots], aempty[kTcASlots];
-    uint64_t dfull[kTcDBufs], dempty[kTcDBufs];
+    uint64_t afull[kTcASlots], gdone[kTcASlots];
+    uint64_t dempty[kTcDBufs];
     uint64_t mdone;
     uint32_t tmem;
     int abort;
@@ -217,10 +226,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         }
         for (int j = 0; j < kTcASlots; ++j) {
             mbar_init(&ss.afull[j], 4);
-            mbar_init(&ss.aempty[j], 1);
+            mbar_init(&ss.gdone[j], 1);
         }
         for (int d = 0; d < kTcDBufs; ++d) {
-            mbar_init(&ss.dfull[d], 1);
             mbar_init(&ss.dempty[d], 8);
         }
         mbar_init(&ss.mdone, 1);
@@ -293,8 +301,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                         for (int t = 0; t < 2; ++t)
                             mma_i8_ts(tmem + kColD + (uint32_t)(d * 2 * kTcMaxN + t * kTcMaxN),
                                       tmem + kColA + (uint32_t)(j * 16 + t * 8), bd, idesc, 0u);
-                        mma_commit(&ss.aempty[j]);
-                        mma_commit(&ss.dfull[d]);
+                        mma_commit(&ss.gdone[j]);
                     }
                     if (ok) mma_commit(&ss.empty[s]);
                 }
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                 for (int gi = 0; gi < ng; ++gi, ++g) {
                     const int j = g % kTcASlots;
                     if (g >= kTcASlots &&
-                        !(ok = tc_wait_warp(&ss.aempty[j], ((g / kTcASlots) - 1) & 1, a, abort)))
+                        !(ok = tc_wait_warp(&ss.gdone[j], ((g / kTcASlots) - 1) & 1, a, abort)))
                         break;
                     // 128-byte swizzle: 16-byte unit gi of row m sits at unit gi ^ (m % 8)
                     const uint4 w0 = *reinterpret_cast<const uint4 *>(row0 + ((gi ^ (sr0 & 7)) << 4));
@@ -400,7 +407,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                         s_next = valid && gn < it.G ? __ldg(srow + gn) : 0.f;
                     }
                     const int d = g % kTcDBufs;
-                    if (!(ok = tc_wait_warp(&ss.dfull[d], (g / kTcDBufs) & 1, a, abort))) break;
+                    if (!(ok = tc_wait_warp(&ss.gdone[g % kTcASlots], (g / kTcASlots) & 1, a, abort)))
+                        break;
                     tc_fence_after();
                     const uint32_t dt = tmem + lane_base + kColD +
                                         (uint32_t)(d * 2 * kTcMaxN + t * kTcMaxN);
