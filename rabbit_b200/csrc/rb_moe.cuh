@@ -88,7 +88,9 @@ constexpr int kTcMaxN = 3 * kTcUnit; // MMA N of a full unit: three digit rows p
 constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 MMAs)
 constexpr int kTcStages = 3;         // staged 8-group chunks per CTA
 constexpr int kTcASlots = 8;         // A operands (one group each) in tensor memory
-constexpr int kTcDBufs = 2;          // accumulator buffers in tensor memory
+constexpr int kTcMaxDBufs = 8;       // accumulator buffers in tensor memory, at most: as
+                                     // many of 2 x N columns as fit (2 for N = 96), never
+                                     // more than the A slots (see k_tc_gemm)
 constexpr int kTcThreads = 14 * 32;  // TMA, MMA, 4 unpack and 8 readout warps
 // MMA N of a unit of n pairs: three digit rows per pair, rounded up to 16.
 __host__ __device__ inline int tc_n_of(int n) { return (3 * n + 15) / 16 * 16; }

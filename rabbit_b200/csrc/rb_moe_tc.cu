@@ -45,10 +45,13 @@
 //                registers; the item's outputs at its end (gate/up: mid =
 //                silu(gate) * up, the partner row in the same warp, taken
 //                by a shuffle; down: the chunk's rows of each pair).
-// A group's gdone phase cannot be overtaken before both its readers have
-// seen it: the MMA of group g + kTcASlots needs that group's A, which its
-// unpack writes only after seeing group g done, and the readout of group g
-// frees the D buffer that group g + kTcDBufs needs.
+// The D buffers form a ring of nD <= kTcASlots buffers of 2 x NW columns
+// (NW: the widest MMA N among the CTA's items), as many as tensor memory holds
+// past the A slots, so small units keep more groups in flight. A group's
+// gdone phase cannot be overtaken before both its readers have seen it: the
+// MMA of group g + kTcASlots needs that group's A, which its unpack writes
+// only after seeing group g done, and a D buffer that only the readout of
+// group g or a later one frees (nD <= kTcASlots).
 // Every wait is bounded; on a timeout the CTA drains its copies and MMAs,
 // frees its tensor memory and leaves with RB_ERR_TIMEOUT in the error word.
 #include <cuda.h>
@@ -69,13 +72,14 @@ constexpr uint32_t kStageBytes = kNibBytes + kBBytes;
 constexpr uint32_t kColA = 0;                               // A slots: 16 columns each
 constexpr uint32_t kColD = kTcASlots * 16;                  // D buffers: 2 x kTcMaxN each
 constexpr uint32_t kTmemCols = 512;
-static_assert(kColD + kTcDBufs * 2 * kTcMaxN <= kTmemCols, "tensor memory plan");
+static_assert(kColD + 2 * 2 * kTcMaxN <= kTmemCols, "tensor memory plan: two full buffers");
+static_assert(kTcMaxDBufs <= kTcASlots, "a group's gdone phase is read before it can recur");
 static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
 
 struct TcSmem {
     uint64_t full[kTcStages], empty[kTcStages];
     uint64_t afull[kTcASlots], gdone[kTcASlots];
-    uint64_t dempty[kTcDBufs];
+    uint64_t dempty[kTcMaxDBufs];
     uint64_t mdone;
     uint32_t tmem;
     int abort;
@@ -228,7 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
             mbar_init(&ss.afull[j], 4);
             mbar_init(&ss.gdone[j], 1);
         }
-        for (int d = 0; d < kTcDBufs; ++d) {
+        for (int d = 0; d < kTcMaxDBufs; ++d) {
             mbar_init(&ss.dempty[d], 8);
         }
         mbar_init(&ss.mdone, 1);
@@ -246,6 +250,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 
     int i0, i1;
     cta_items<GU>(b, (int)blockIdx.x, (int)gridDim.x, &i0, &i1);
+    int nmax = 1;
+    {
+        const int ipu = items_per_unit<GU>(b);
+        for (int item = i0; item < i1; ++item) nmax = max(nmax, b.act_cnt[item / ipu]);
+    }
+    // the readout loads 24 columns per 8 pairs, up to OV columns past an
+    // item's NW-column half (garbage for pairs past n, never used): the ring
+    // leaves that much room at its end
+    const int NW = tc_n_of(nmax), OV = max(0, 24 * ((nmax + 7) / 8) - NW);
+    const int nD = min(kTcMaxDBufs, (int)(kTmemCols - kColD - OV) / (2 * NW));
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA --
@@ -278,6 +292,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         // ---------------------------------------------------------- MMA --
         if (lane == 0) {
             int kc = 0, g = 0;
+            int d = 0;
+            uint32_t dph = 0;
+            bool wrapped = false;
             bool ok = true;
             for (int item = i0; item < i1 && ok; ++item) {
                 const Item it = item_of<GU>(a, item);
@@ -288,20 +305,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                     const uint32_t bsm = smem_u32(stages + (size_t)s * kStageBytes + kNibBytes);
                     const int ng = min(8, it.G - ch * 8);
                     for (int gi = 0; gi < ng; ++gi, ++g) {
-                        const int j = g % kTcASlots, d = g % kTcDBufs;
+                        const int j = g % kTcASlots;
                         if (!(ok = tc_wait(&ss.afull[j], (g / kTcASlots) & 1, a, abort, false)))
                             break;
-                        if (g >= kTcDBufs &&
-                            !(ok = tc_wait(&ss.dempty[d], ((g / kTcDBufs) - 1) & 1, a, abort,
-                                           false)))
+                        if (wrapped && !(ok = tc_wait(&ss.dempty[d], dph ^ 1u, a, abort, false)))
                             break;
                         tc_fence_after();
                         const uint64_t bd = kmajor_desc(bsm + (uint32_t)(gi * it.N * 32));
 #pragma unroll
                         for (int t = 0; t < 2; ++t)
-                            mma_i8_ts(tmem + kColD + (uint32_t)(d * 2 * kTcMaxN + t * kTcMaxN),
+                            mma_i8_ts(tmem + kColD + (uint32_t)((2 * d + t) * NW),
                                       tmem + kColA + (uint32_t)(j * 16 + t * 8), bd, idesc, 0u);
                         mma_commit(&ss.gdone[j]);
+                        if (++d == nD) {
+                            d = 0;
+                            dph ^= 1u;
+                            wrapped = true;
+                        }
                     }
                     if (ok) mma_commit(&ss.empty[s]);
                 }
@@ -361,6 +381,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         const int m = t * 128 + q * 32 + lane;  // the item row this thread reads out
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         int g = 0;
+        int d = 0;
+        uint32_t dph = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; ++item) {
             const Item it = item_of<GU>(a, item);
@@ -406,12 +428,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                         const int gn = ch * 8 + gi + 1;
                         s_next = valid && gn < it.G ? __ldg(srow + gn) : 0.f;
                     }
-                    const int d = g % kTcDBufs;
                     if (!(ok = tc_wait_warp(&ss.gdone[g % kTcASlots], (g / kTcASlots) & 1, a, abort)))
                         break;
                     tc_fence_after();
-                    const uint32_t dt = tmem + lane_base + kColD +
-                                        (uint32_t)(d * 2 * kTcMaxN + t * kTcMaxN);
+                    const uint32_t dt = tmem + lane_base + kColD + (uint32_t)((2 * d + t) * NW);
 #pragma unroll
                     for (int blk = 0; blk < kTcUnit / 8; ++blk) {
                         if (blk < nblk) {
@@ -436,6 +456,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&ss.dempty[d]);
                     ++g;
+                    if (++d == nD) {
+                        d = 0;
+                        dph ^= 1u;
+                    }
                 }
             }
             if (!ok) break;
