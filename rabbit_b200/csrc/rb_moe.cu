@@ -1408,18 +1408,30 @@ static int ensure_ep(rabbit_cuda_moe *p, int T) {
     return RABBIT_CUDA_OK;
 }
 
-// Grouped send / receive of one float list (n_per_peer floats per peer) to
-// and from every other rank: peer index qi is rank qi, or qi + 1 from this
-// rank on.
-static int ep_swap(rabbit_cuda_moe *p, const Nccl *n, const void *send, void *recv,
-                   size_t n_per_peer, int dtype, size_t elem_bytes, cudaStream_t s) {
+// One list exchanged with every other rank: n_per_peer elements of dtype per
+// peer, peer index qi (rank qi, or qi + 1 from this rank on) at qi * n_per_peer.
+struct EpList {
+    const void *send;
+    void *recv;
+    size_t n_per_peer;
+    int dtype;
+    size_t elem_bytes;
+};
+// Every list of one exchange step in one NCCL group (a single launch on s).
+static int ep_swap(rabbit_cuda_moe *p, const Nccl *n, const EpList *lists, int n_lists,
+                   cudaStream_t s) {
     int r = n->group_start();
     for (int qi = 0; r == 0 && qi < p->ep_size - 1; ++qi) {
         const int q = qi < p->ep_rank ? qi : qi + 1;
-        const size_t o = (size_t)qi * n_per_peer * elem_bytes;
-        r = n->send(static_cast<const uint8_t *>(send) + o, n_per_peer, dtype, q, p->ep->comm, s);
-        if (r == 0)
-            r = n->recv(static_cast<uint8_t *>(recv) + o, n_per_peer, dtype, q, p->ep->comm, s);
+        for (int l = 0; r == 0 && l < n_lists; ++l) {
+            const EpList &L = lists[l];
+            const size_t o = (size_t)qi * L.n_per_peer * L.elem_bytes;
+            r = n->send(static_cast<const uint8_t *>(L.send) + o, L.n_per_peer, L.dtype, q,
+                        p->ep->comm, s);
+            if (r == 0)
+                r = n->recv(static_cast<uint8_t *>(L.recv) + o, L.n_per_peer, L.dtype, q,
+                            p->ep->comm, s);
+        }
     }
     const int r2 = n->group_end();
     if (r) return nccl_fail(r, "moe_prefill: exchange");
@@ -1561,9 +1573,9 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     if (a2a) {  // dispatch: the pairs routed to the peers' experts, with their xn rows
         RB_CUDA(launch_batch(2, dim3(T, p->k), dim3(256), 0, s, a));
         mark(1);
-        if ((st = ep_swap(p, nc, a.send_meta, a.recv_meta, 4 * cap, kNcclInt32, 4, s)) ||
-            (st = ep_swap(p, nc, a.send_x, a.xn + (size_t)T * H, cap * H, kNcclFloat32, 4, s)))
-            return st;
+        const EpList lists[2] = {{a.send_meta, a.recv_meta, 4 * cap, kNcclInt32, 4},
+                                 {a.send_x, a.xn + (size_t)T * H, cap * H, kNcclFloat32, 4}};
+        if ((st = ep_swap(p, nc, lists, 2, s))) return st;
         a.T = V;
     } else {
         mark(1);
@@ -1583,7 +1595,8 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     if (a2a) {  // combine, first half: the received pairs' outputs go back to their senders
         if (V > T) RB_CUDA(launch_batch(3, dim3(V - T, (p->H + 255) / 256), dim3(256), 0, s, a));
         mark(3);
-        if ((st = ep_swap(p, nc, a.ret_send, a.ret_recv, cap * H, kNcclFloat32, 4, s))) return st;
+        const EpList back = {a.ret_send, a.ret_recv, cap * H, kNcclFloat32, 4};
+        if ((st = ep_swap(p, nc, &back, 1, s))) return st;
         mark(4);
     }
     RB_CUDA(launch_batch(4, dim3(T, (p->H + 255) / 256), dim3(256), 0, s, a));
