@@ -756,18 +756,20 @@ def run_rabbit(args) -> None:
     achieved = per_layer / kernel_s / 1e9
     peak, peak_kind = measured_peak()
 
-    # end to end through the host-buffer C ABI (H2D of h, D2H of h + routing, per layer)
+    # end to end through the host-buffer C ABI, h updated in place in a host
+    # array as an engine's token loop does (per layer: h from host memory into
+    # HBM, h_out and the routing back into host memory, one synchronisation)
     h_host = rng.standard_normal(H).astype(np.float32)
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(2):
         for layer in range(L):
-            h_host = pool.decode(layer, h_host)[0]
+            pool.decode_into(layer, h_host, h_host)
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         for layer in range(L):
-            h_host = pool.decode(layer, h_host)[0]
+            pool.decode_into(layer, h_host, h_host)
     e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], device="cuda")

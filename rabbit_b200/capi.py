@@ -261,6 +261,7 @@ class MoePool:
         else:
             check(lib().rabbit_cuda_moe_create(C.byref(d), device, C.byref(h)))
         self.handle = h
+        self._decode = lib().rabbit_cuda_moe_decode
         self.hidden, self.n_layers = hidden, n_layers
         self.k = min(top_k if top_k > 0 else 2, n_experts, 8)
         if upload:
@@ -292,6 +293,11 @@ class MoePool:
         check(lib().rabbit_cuda_moe_decode(self.handle, layer, _ptr(h), _ptr(out), _ptr(ids),
                                            _ptr(w), C.byref(k)))
         return out, ids[:k.value].copy(), w[:k.value].copy()
+
+    def decode_into(self, layer: int, h: np.ndarray, out: np.ndarray) -> None:
+        """decode on caller-owned host buffers (C-contiguous float32 [H]; out may
+        be h), allocating nothing per call: the form an engine's token loop uses."""
+        check(self._decode(self.handle, layer, h.ctypes.data, out.ctypes.data, None, None, None))
 
     def decode_dev(self, layer: int, d_h_in: int, d_h_out: int, d_ids: int = 0,
                    d_w: int = 0, stream: int = 0) -> None:

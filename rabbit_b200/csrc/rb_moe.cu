@@ -100,6 +100,7 @@ struct rabbit_cuda_moe {
     int pin_next = 0;
     // host-buffer decode staging
     float *pin_io = nullptr;
+    float *pin_io_dev = nullptr;  // the same pinned block as the device addresses it
     // fused plan
     rb::MoeFusedArgs plan{};
     int grid = 0, block = 0;
@@ -637,6 +638,8 @@ static int create_pool(const rabbit_cuda_moe_desc *d, int device, int window, ra
         (e = cudaMalloc(&p->route, sizeof(Route))) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMallocHost(&p->pin_io, sizeof(float) * (2 * (size_t)p->H + 32))) !=
+            cudaSuccess ||
+        (e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&p->pin_io_dev), p->pin_io, 0)) !=
             cudaSuccess) {
         free_pool(p);
         return cuda_fail(e, "moe_create: scratch");
@@ -1003,6 +1006,23 @@ namespace rb {
 // kernel records a failed wait in.
 static int decode_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
                          int *d_ids, float *d_weights, cudaStream_t s, int *err);
+// Host-buffer decode helpers: h from pinned host memory into HBM (one CTA,
+// float4 over PCIe), and the device error word into the pinned block (then
+// cleared for the next call).
+__global__ void __launch_bounds__(256) k_h_in(const float *src, float *dst, int n) {
+    const int n4 = n >> 2;  // both 16-byte aligned: a page of pinned memory, cudaMalloc
+    for (int i = threadIdx.x; i < n4; i += blockDim.x)
+        reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(src)[i];
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+__global__ void k_err_out(int *d_err, int *h_err) {
+    if (threadIdx.x == 0) {
+        const int e = *reinterpret_cast<volatile int *>(d_err);
+        *reinterpret_cast<volatile int *>(h_err) = e;
+        if (e) *d_err = 0;
+    }
+}
+
 static int decode_impl(rabbit_cuda_moe *p, int layer, const float *d_h_in, float *d_h_out,
                        int *d_ids, float *d_weights, cudaStream_t s, int *err) {
     int st = window_enter(p, layer, s);
@@ -1247,20 +1267,27 @@ int rabbit_cuda_moe_decode(rabbit_cuda_moe *p, int layer, const float *h_in, flo
     RB_CUDA(cudaSetDevice(p->device));
     cudaStream_t s = p->ctx->stream;
     const size_t hb = sizeof(float) * p->H;
-    // pinned: [h_in (H)] [h_out (H) | ids (8) | weights (8) | error word], the
-    // second part a mirror of the device block p->dio
+    // pinned, mapped: [h_in (H)] [h_out (H) | ids (8) | weights (8) | error word].
+    // One small kernel brings h into HBM over PCIe, the decode writes h_out,
+    // ids and weights straight into the pinned block, and a last one-thread
+    // kernel moves the error word there (and clears it): no copy engine
+    // transfers, one synchronisation.
     float *pin_h = p->pin_io;
     uint8_t *pin_o = reinterpret_cast<uint8_t *>(p->pin_io + p->H);
+    uint8_t *dev_o = reinterpret_cast<uint8_t *>(p->pin_io_dev + p->H);
+    int *dev_err = reinterpret_cast<int *>(dev_o + (p->dio_bytes - 16));
     memcpy(pin_h, h_in, hb);
-    RB_CUDA(cudaMemcpyAsync(p->h_in, pin_h, hb, cudaMemcpyHostToDevice, s));
-    int st = decode_impl(p, layer, p->h_in, p->h_out, p->ids_int, p->w_int, s, p->err_io);
+    k_h_in<<<1, 256, 0, s>>>(p->pin_io_dev, p->h_in, p->H);
+    RB_CUDA(cudaGetLastError());
+    int st = decode_impl(p, layer, p->h_in, reinterpret_cast<float *>(dev_o),
+                         reinterpret_cast<int *>(dev_o + hb),
+                         reinterpret_cast<float *>(dev_o + hb + 32), s, p->err_io);
     if (st) return st;
-    RB_CUDA(cudaMemcpyAsync(pin_o, p->dio, p->dio_bytes, cudaMemcpyDeviceToHost, s));
+    k_err_out<<<1, 32, 0, s>>>(p->err_io, dev_err);
+    RB_CUDA(cudaGetLastError());
     RB_CUDA(cudaStreamSynchronize(s));
-    const int err = *reinterpret_cast<const int *>(pin_o + (p->dio_bytes - 16));
+    const int err = *reinterpret_cast<const volatile int *>(pin_o + (p->dio_bytes - 16));
     if (err != 0) {
-        cudaMemsetAsync(p->err_io, 0, sizeof(int), s);
-        cudaStreamSynchronize(s);
         if (err == RB_ERR_TIMEOUT)
             return fail(RABBIT_CUDA_ERR_TIMEOUT, "moe_decode: a bounded device wait ran out");
         return fail(RABBIT_CUDA_ERR_DEVICE, "moe_decode: device error code %d", err);
