@@ -371,6 +371,58 @@ def full_decode_item(capi, synth, peak: float, runs: int = 3, cpu: bool = True,
 # The DeepSeek-MoE-16B-shaped prefill chunk (MoE blocks): 28 layers, hidden
 # 2048, 64 routed experts top-6 + 2 shared, expert FFN 1408 SwiGLU int4
 # group-32, a 32-token chunk of random hidden states, layer to layer.
+def dense_share(L: int, H: int, q_dim: int, kv_dim: int, V: int, T: int, moe_ms: float,
+                runs: int = 3) -> dict:
+    """The dense part of a full step beside an MoE-block line: every layer's
+    Q, K, V and O projections for T tokens plus the lm_head, fp32 (TF32 off),
+    as torch matmuls (cuBLAS) over seeded weights resident in HBM. Context for
+    the MoE line, not this library's work: the attention core over the KV
+    window, the norms and the embedding are left out."""
+    import torch
+
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        mats = []
+        for _ in range(L):
+            mats.append([torch.randn(o, i, device="cuda", generator=g) * 0.02
+                         for o, i in ((q_dim, H), (kv_dim, H), (kv_dim, H), (H, q_dim))])
+        lm = torch.randn(V, H, device="cuda", generator=g) * 0.02
+        x = torch.randn(T, H, device="cuda", generator=g)
+
+        def step():
+            h = x
+            for wq, wk, wv, wo in mats:
+                q = h @ wq.t()
+                h.matmul(wk.t())
+                h.matmul(wv.t())
+                h = h + q @ wo.t()
+            return h @ lm.t()
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(runs):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / runs
+        nbytes = 4 * (L * (q_dim * H * 2 + kv_dim * H * 2) + V * H)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        del mats
+        torch.cuda.empty_cache()
+    return {"what": (f"Q/K/V/O projections of every layer and the lm_head for {T} tokens, "
+                     f"fp32, torch matmul (cuBLAS) on seeded resident weights; attention core, "
+                     f"norms and embedding not included"),
+            "dense_bytes": nbytes, "dense_ms": round(ms, 3), "moe_ms": round(moe_ms, 3),
+            "dense_share": round(ms / (ms + moe_ms), 3),
+            "full_step_tokens_per_s": round(T / ((ms + moe_ms) / 1e3), 1)}
+
+
 DS = dict(L=28, H=2048, E=64, k=6, S=2, I=1408)
 DS_T = 32
 
@@ -452,6 +504,9 @@ def prefill_item(capi, synth, peak: float, runs: int = 5, cpu: bool = True,
         "gpu_launches_per_chunk": 7 * L,
     }
     pool.free()
+    # the chunk's dense projections beside it (DeepSeek-MoE-16B: 16 heads x 128,
+    # vocab 102400)
+    item["dense"] = dense_share(L, H, 2048, 2048, 102400, DS_T, sec * 1e3)
     if cpu:
         chk, kind = cpu_checker()
         recs, size2, router, rms = synth.moe_layer(SEED + 14, H, E, I, S)
@@ -592,6 +647,11 @@ def ep_item(capi, synth, peak: float, rank: int, world: int, dist, steps: int = 
     if ep:
         ep.free()
     sec = best["ms_per_step"] / 1e3
+    # the step's dense projections, which every rank runs for its own 64 / N
+    # tokens (attention data-parallel over the ranks, as in the all-to-all
+    # mode; Mixtral-8x22B: 48 heads x 128, 8 KV heads, vocab 32768)
+    dense = dense_share(L, H, 6144, 1024, 32768, XL_T // world if world > 1 else XL_T,
+                        best["ms_per_step"])
     return {
         "metric": "EP MoE decode tokens/s (Mixtral-8x22B-shaped, batch 64)",
         "value": best["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
@@ -609,6 +669,7 @@ def ep_item(capi, synth, peak: float, rank: int, world: int, dist, steps: int = 
                    "note": "MoE blocks only (the routed-expert hot path); the attention and "
                            "dense fp32 projections of the step are not in this line"},
         "modes": res,
+        "dense": dense,
         "roofline": {"bound": "hbm", "achieved_per_gpu": best["achieved_per_gpu"],
                      "peak": peak, "unit": "GB/s",
                      "frac": round(best["achieved_per_gpu"] / peak, 4),
