@@ -21,8 +21,8 @@
 static rabbit_cuda_moe *rc_pool;
 static const RabbitModel *rc_pool_model;
 
-/* One pool per model: every layer's records uploaded once (INTEGRATION.md,
- * section 2). */
+/* One pool per model: every layer's records uploaded once, from the model's
+ * host map of the expert table. */
 static rabbit_cuda_moe *rabbit_cuda_pool_for(const RabbitModel *m, const RefV2Weights *w) {
     if (rc_pool && rc_pool_model == m) return rc_pool;
     if (rc_pool) {
