@@ -83,12 +83,12 @@ inline bool combine_packed(int KC) { return KC < 8; }
 //   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
 //                   order (forward_v2.c:356-357, 398-399).
 constexpr int kMaxBatchTokens = 256;
-constexpr int kTcUnit = 32;          // pairs per work unit
+constexpr int kTcUnit = 16;          // pairs per work unit
 constexpr int kTcMaxN = 3 * kTcUnit; // MMA N of a full unit: three digit rows per pair
 constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 MMAs)
-constexpr int kTcStages = 3;         // staged 8-group chunks per CTA
-constexpr int kTcASlots = 8;         // A operands (one group each) in tensor memory
-constexpr int kTcMaxDBufs = 8;       // accumulator buffers in tensor memory, at most: as
+constexpr int kTcStages = 2;         // staged 8-group chunks per CTA
+constexpr int kTcASlots = 4;         // A operands (one group each) in tensor memory
+constexpr int kTcMaxDBufs = 4;       // accumulator buffers in tensor memory, at most: as
                                      // many of 2 x N columns as fit (2 for N = 96), never
                                      // more than the A slots (see k_tc_gemm)
 constexpr int kTcThreads = 14 * 32;  // TMA, MMA, 4 unpack and 8 readout warps

@@ -2,8 +2,8 @@
 // (tcgen05.mma, kind::i8, accumulators in tensor memory).
 //
 // T tokens through one layer (rabbit_cuda_moe_prefill[_dev]): every expert
-// the chunk touches is streamed from HBM once per work unit (up to 32 of the
-// (token, slot) pairs routed to it), and each 32-input group of a weight row
+// the chunk touches is streamed from HBM once per work unit (up to kTcUnit of
+// the (token, slot) pairs routed to it), and each 32-input group of a weight row
 // is multiplied exactly, in integers, as the decode path does it:
 //
 //   * the weights stay group-32 int4: the warps that unpack a staged tile
@@ -28,13 +28,16 @@
 //
 // Work items are (unit, 256 weight rows): for gate/up 128 rows of W1 and the
 // same 128 rows of W3 (the pool's GU tiles interleave TRb rows of each), for
-// down 256 rows of one column chunk of W2. A CTA (one per SM) takes a
-// contiguous run of items whose summed cost (a fixed part per group plus the
+// down 256 rows of one column chunk of W2. Two CTAs share an SM (each half
+// the SM's tensor memory, 91 KB of shared memory, at most 72 registers a
+// thread), so one CTA's hand-off latencies overlap the other's work; a CTA
+// takes a contiguous run of items whose summed cost (a fixed part per group plus the
 // readout's 8-pair blocks) is 1 / grid of the launch's, and runs it through a
 // warp-specialised pipeline:
 //   warp 0       TMA: each 8-group chunk of the item's 256 nibble rows (one
 //                cp.async.bulk.tensor box, 128-byte swizzle) and the unit's
-//                B rows of those 8 groups (one bulk copy) into a stage ring;
+//                B rows of those 8 groups (one bulk copy) into a ring of
+//                kTcStages stages;
 //   warp 1       allocates tensor memory; one lane issues the MMAs (two per
 //                group: rows 0..127 and 128..255) and commits them once per
 //                group (gdone[g % kTcASlots]: the group's A slot is free and
@@ -45,7 +48,8 @@
 //                registers; the item's outputs at its end (gate/up: mid =
 //                silu(gate) * up, the partner row in the same warp, taken
 //                by a shuffle; down: the chunk's rows of each pair).
-// The D buffers form a ring of nD <= kTcASlots buffers of 2 x NW columns
+// A takes kTcASlots slots of 16 columns; the D buffers form a ring of
+// nD <= kTcASlots buffers of 2 x NW columns
 // (NW: the widest MMA N among the CTA's items), as many as tensor memory holds
 // past the A slots, so small units keep more groups in flight. A group's
 // gdone phase cannot be overtaken before both its readers have seen it: the
@@ -71,7 +75,7 @@ constexpr uint32_t kBBytes = 8 * kTcMaxN * 32;               // one stage's B ro
 constexpr uint32_t kStageBytes = kNibBytes + kBBytes;
 constexpr uint32_t kColA = 0;                               // A slots: 16 columns each
 constexpr uint32_t kColD = kTcASlots * 16;                  // D buffers: 2 x kTcMaxN each
-constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemCols = 256;
 static_assert(kColD + 2 * 2 * kTcMaxN <= kTmemCols, "tensor memory plan: two full buffers");
 static_assert(kTcMaxDBufs <= kTcASlots, "a group's gdone phase is read before it can recur");
 static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
@@ -213,7 +217,7 @@ __device__ void cta_items(const MoeBatchArgs &b, int bx, int grid, int *i0, int 
 }  // namespace
 
 template <bool GU>
-__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ TcGemmArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant__ TcGemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ TcSmem ss;
     // stages at the first 1024-byte boundary of the dynamic block
