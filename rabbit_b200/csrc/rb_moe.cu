@@ -1322,9 +1322,10 @@ static int ensure_batch(rabbit_cuda_moe *p, int T) {
     const size_t o_ns = take(sizeof(int) * cap);
     const size_t o_pidx = take(sizeof(int) * cap * kMaxSlots);
     const size_t o_pt = take(sizeof(int) * P);
-    // work units: each record's pairs in runs of kTcUnit, so at most one per
-    // kTcUnit pairs plus one partial run per record
-    const size_t U = P / kTcUnit + R;
+    // work units: each record's pairs in runs of at most the unit cap (the
+    // narrowest is kTcMinUnit), so at most one per kTcMinUnit pairs plus one
+    // partial run per record
+    const size_t U = P / kTcMinUnit + R;
     const size_t o_act = take(sizeof(int) * U * 4 + 2 * sizeof(int));
     const size_t o_pu = take(sizeof(int) * P);
     // B rows of the units: three per pair, each unit padded by at most 15; a
@@ -1486,8 +1487,8 @@ static cudaError_t launch_batch(int which, dim3 grid, dim3 block, size_t smem, c
 // leave that room.
 constexpr size_t kBatchDynMax = (size_t)kMaxDynSmem - 1024;
 
-static cudaError_t launch_tc(int which, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                             void *arg) {
+static cudaError_t launch_tc(int which, bool wide, dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t s, void *arg) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1499,7 +1500,7 @@ static cudaError_t launch_tc(int which, dim3 grid, dim3 block, size_t smem, cuda
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     void *args[] = {arg};
-    return cudaLaunchKernelExC(&cfg, moe_tc_kernel(which), args);
+    return cudaLaunchKernelExC(&cfg, moe_tc_kernel(which, wide), args);
 }
 
 // The body of rabbit_cuda_moe_prefill_dev.
@@ -1554,9 +1555,10 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kBatchDynMax));
         for (int i : {1, 3})
-            RB_CUDA(cudaFuncSetAttribute(moe_tc_kernel(i),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)tc_gemm_smem()));
+            for (bool wide : {true, false})
+                RB_CUDA(cudaFuncSetAttribute(moe_tc_kernel(i, wide),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)tc_gemm_smem(wide)));
         g_batch_attr[p->device] = true;
     }
     MoeBatchArgs a = p->bt;
@@ -1586,6 +1588,20 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     a.ep_rank = p->ep_rank;
     a.ep_size = p->ep_size;
     a.ep_mode = a2a ? RABBIT_CUDA_EP_ALLTOALL : 0;
+    // GEMM configuration: the narrow one (two CTAs per SM, 16-pair units) when
+    // the layer's gate/up work can fill two CTAs per SM -- the experts the
+    // batch can touch here (this rank's routed records, at most the batch's
+    // routed pairs, plus the shared ones) times the 128-row items of each --
+    // else the wide one (one CTA per SM, an expert read once for up to 32
+    // pairs), whose single CTA per SM does not share the SM when work is
+    // scarce (one expert per rank in 8-way expert parallelism)
+    const int tokens_all = a2a ? T * p->ep_size : T;
+    const long long routed_local = std::max(0, n_local - p->S);
+    const long long touched =
+        std::min(routed_local, (long long)tokens_all * p->k) + std::min(p->S, n_local);
+    const bool wide = touched * ((p->I + 127) / 128) < 2ll * sms;
+    a.unit_cap = wide ? TcWide::kUnit : TcNarrow::kUnit;
+    const int gemm_ctas = (wide ? TcWide::kCtasPerSm : TcNarrow::kCtasPerSm) * sms;
     a.T_own = T;
     a.ep_cap = a2a ? ep_rows(p, T) : 0;
     const size_t cap = (size_t)a.ep_cap, H = (size_t)p->H;
@@ -1614,11 +1630,11 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     TcGemmArgs ga;
     ga.b = a;
     ga.tmap = p->tm_gu;
-    RB_CUDA(launch_tc(0, dim3(pairs_max), dim3(256), 0, s, &a));
-    RB_CUDA(launch_tc(1, dim3(2 * sms), dim3(kTcThreads), tc_gemm_smem(), s, &ga));
-    RB_CUDA(launch_tc(2, dim3(pairs_max), dim3(256), 0, s, &a));
+    RB_CUDA(launch_tc(0, wide, dim3(pairs_max), dim3(256), 0, s, &a));
+    RB_CUDA(launch_tc(1, wide, dim3(gemm_ctas), dim3(kTcThreads), tc_gemm_smem(wide), s, &ga));
+    RB_CUDA(launch_tc(2, wide, dim3(pairs_max), dim3(256), 0, s, &a));
     ga.tmap = p->tm_dn;
-    RB_CUDA(launch_tc(3, dim3(2 * sms), dim3(kTcThreads), tc_gemm_smem(), s, &ga));
+    RB_CUDA(launch_tc(3, wide, dim3(gemm_ctas), dim3(kTcThreads), tc_gemm_smem(wide), s, &ga));
     if (a2a) {  // combine, first half: the received pairs' outputs go back to their senders
         if (V > T) RB_CUDA(launch_batch(3, dim3(V - T, (p->H + 255) / 256), dim3(256), 0, s, a));
         mark(3);

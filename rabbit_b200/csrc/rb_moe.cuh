@@ -73,7 +73,7 @@ inline bool combine_packed(int KC) { return KC < 8; }
 //                   rows; the token's last CTA to finish: top-k, slots;
 //   k_batch_bucket  one CTA: per local record, the (token, slot) pairs that
 //                   use it, in token order (bitmask ranks: deterministic),
-//                   cut into units of at most kTcUnit pairs;
+//                   cut into units of at most unit_cap pairs;
 //   k_tc_images     xn as the tensor-core MMA's B rows, per unit;
 //   k_tc_gemm<1>    (unit, 128 rows of W1 and of W3) items: mid = silu(gate)
 //                   * up for the unit's pairs (tcgen05, kind::i8);
@@ -83,15 +83,27 @@ inline bool combine_packed(int KC) { return KC < 8; }
 //   k_batch_combine h_out = h + sum_j w_j sum_c down_jc, slots and chunks in
 //                   order (forward_v2.c:356-357, 398-399).
 constexpr int kMaxBatchTokens = 256;
-constexpr int kTcUnit = 16;          // pairs per work unit
-constexpr int kTcMaxN = 3 * kTcUnit; // MMA N of a full unit: three digit rows per pair
+constexpr int kTcMaxUnit = 32;       // widest work unit (pairs); pair_u = unit * kTcMaxUnit + column
+constexpr int kTcMinUnit = 16;       // narrowest (bounds the number of units)
 constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 MMAs)
-constexpr int kTcStages = 2;         // staged 8-group chunks per CTA
-constexpr int kTcASlots = 4;         // A operands (one group each) in tensor memory
-constexpr int kTcMaxDBufs = 4;       // accumulator buffers in tensor memory, at most: as
-                                     // many of 2 x N columns as fit (2 for N = 96), never
-                                     // more than the A slots (see k_tc_gemm)
 constexpr int kTcThreads = 14 * 32;  // TMA, MMA, 4 unpack and 8 readout warps
+// The tensor-core GEMMs in two configurations, picked per launch by how many
+// pairs an expert can expect:
+//   wide    one CTA per SM: units of up to 32 pairs, 3 staged chunks, 8 A
+//           slots, up to 8 D buffers, 512 tensor-memory columns;
+//   narrow  two CTAs per SM (each 256 columns, 89 KB of shared memory, at
+//           most 72 registers a thread), so one CTA's hand-off latencies
+//           overlap the other's work: units of up to 16 pairs, 2 stages, 4 A
+//           slots, up to 4 D buffers. Experts drawing more pairs than that
+//           are read once per unit.
+struct TcWide {
+    static constexpr int kUnit = 32, kStages = 3, kASlots = 8, kMaxDBufs = 8, kTmemCols = 512,
+                         kCtasPerSm = 1;
+};
+struct TcNarrow {
+    static constexpr int kUnit = 16, kStages = 2, kASlots = 4, kMaxDBufs = 4, kTmemCols = 256,
+                         kCtasPerSm = 2;
+};
 // MMA N of a unit of n pairs: three digit rows per pair, rounded up to 16.
 __host__ __device__ inline int tc_n_of(int n) { return (3 * n + 15) / 16 * 16; }
 
@@ -115,7 +127,8 @@ struct MoeBatchArgs {
     int *nslot;      // [T]
     int *pidx;       // [T][kMaxSlots] pair index of (token, slot)
     int *pair_t;     // [P] token of pair
-    int *act, *act_off, *act_cnt;  // [units] work units (record, <= kTcUnit of its
+    int unit_cap;    // pairs per work unit of this launch (the GEMMs' configuration)
+    int *act, *act_off, *act_cnt;  // [units] work units (record, <= unit_cap of its
                                    // pairs): global record id, first pair, pairs
     int *img_off;    // [units] B rows of the units before this one (sum of tc_n_of)
     int *n_act;      // [2] units, pairs
@@ -125,7 +138,7 @@ struct MoeBatchArgs {
     int ep_rank, ep_size;  // expert-parallel share (1 rank: the whole layer)
     float *mid;      // [P][I]
     float *down;     // [P][tc.KC][H]
-    int *pair_u;     // [P] unit * kTcUnit + column of pair
+    int *pair_u;     // [P] unit * kTcMaxUnit + column of pair
     // B rows of the units: unit u's image holds, per group g of 32 inputs,
     // N_u = tc_n_of(n_u) rows of 32 bytes (row 3c + p = digit p of pair c) as
     // 8-row x 16-byte core matrices, at (img_off[u] G + g N_u) 32 bytes
@@ -159,8 +172,9 @@ struct alignas(64) TcGemmArgs {
     CUtensorMap tmap;
     MoeBatchArgs b;
 };
-const void *moe_tc_kernel(int i);  // 0 x images, 1 gate/up GEMM, 2 mid images, 3 down GEMM
-size_t tc_gemm_smem();             // dynamic shared memory of a GEMM launch
+// 0 x images, 1 gate/up GEMM, 2 mid images, 3 down GEMM; wide: TcWide, else TcNarrow
+const void *moe_tc_kernel(int i, bool wide);
+size_t tc_gemm_smem(bool wide);  // dynamic shared memory of a GEMM launch
 // Tensor maps over a pool's GU and D nibble rows (boxes of 256 rows x 128
 // bytes, 128-byte swizzle): 0 built, 1 the tiling does not fit the kernels'
 // boxes, 2 the driver's tensor-map encoder is missing or refused.

@@ -1069,13 +1069,14 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
         cnt[r] = c;
     }
     __syncthreads();
-    if (tid == 0) {  // units: each record's pairs cut into runs of <= kTcUnit
+    const int cap = a.unit_cap;
+    if (tid == 0) {  // units: each record's pairs cut into runs of <= unit_cap
         int o = 0, nu = 0, rows = 0;
         for (int r = 0; r < R; ++r) {
             off[r] = o;
             uf[r] = nu;  // the record's first unit
-            for (int c0 = 0; c0 < cnt[r]; c0 += kTcUnit) {
-                const int n = min(kTcUnit, cnt[r] - c0);
+            for (int c0 = 0; c0 < cnt[r]; c0 += cap) {
+                const int n = min(cap, cnt[r] - c0);
                 a.act[nu] = a.rec_base + r;
                 a.act_off[nu] = o + c0;
                 a.act_cnt[nu] = n;
@@ -1098,7 +1099,7 @@ __global__ void __launch_bounds__(1024) k_batch_bucket(MoeBatchArgs a) {
             rank += __popc(bm[r * W + (t >> 5)] & ((1u << (t & 31)) - 1u));
             const int pos = off[r] + rank;
             a.pair_t[pos] = t;
-            a.pair_u[pos] = (uf[r] + rank / kTcUnit) * kTcUnit + rank % kTcUnit;
+            a.pair_u[pos] = (uf[r] + rank / cap) * kTcMaxUnit + rank % cap;
             a.pidx[q] = pos;
         }
     }

@@ -68,22 +68,29 @@ namespace rb {
 
 namespace {
 
-constexpr int kWarpUnpack = 2;   // first unpack warp
 constexpr int kWarpReadout = 6;  // first readout warp
-constexpr uint32_t kNibBytes = kTcRows * 128;                // one stage's nibble box
-constexpr uint32_t kBBytes = 8 * kTcMaxN * 32;               // one stage's B rows
-constexpr uint32_t kStageBytes = kNibBytes + kBBytes;
-constexpr uint32_t kColA = 0;                               // A slots: 16 columns each
-constexpr uint32_t kColD = kTcASlots * 16;                  // D buffers: 2 x kTcMaxN each
-constexpr uint32_t kTmemCols = 256;
-static_assert(kColD + 2 * 2 * kTcMaxN <= kTmemCols, "tensor memory plan: two full buffers");
-static_assert(kTcMaxDBufs <= kTcASlots, "a group's gdone phase is read before it can recur");
-static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
+constexpr uint32_t kNibBytes = kTcRows * 128;  // one stage's nibble box
+constexpr uint32_t kColA = 0;                  // A slots: 16 columns each
 
+// The layout a configuration C (TcWide / TcNarrow) implies.
+template <class C>
+struct TcPlan {
+    static constexpr int kMaxN = 3 * C::kUnit;               // MMA N of a full unit
+    static constexpr uint32_t kBBytes = 8 * kMaxN * 32;      // one stage's B rows
+    static constexpr uint32_t kStageBytes = kNibBytes + kBBytes;
+    static constexpr uint32_t kColD = C::kASlots * 16;       // the D ring after the A slots
+    static_assert(kColD + 2 * 2 * kMaxN <= (uint32_t)C::kTmemCols,
+                  "tensor memory plan: two full buffers");
+    static_assert(C::kMaxDBufs <= C::kASlots,
+                  "a group's gdone phase is read before it can recur");
+    static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
+};
+
+template <class C>
 struct TcSmem {
-    uint64_t full[kTcStages], empty[kTcStages];
-    uint64_t afull[kTcASlots], gdone[kTcASlots];
-    uint64_t dempty[kTcMaxDBufs];
+    uint64_t full[C::kStages], empty[C::kStages];
+    uint64_t afull[C::kASlots], gdone[C::kASlots];
+    uint64_t dempty[C::kMaxDBufs];
     uint64_t mdone;
     uint32_t tmem;
     int abort;
@@ -216,10 +223,15 @@ __device__ void cta_items(const MoeBatchArgs &b, int bx, int grid, int *i0, int 
 
 }  // namespace
 
-template <bool GU>
-__global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant__ TcGemmArgs a) {
+template <bool GU, class C>
+__global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
+    k_tc_gemm(const __grid_constant__ TcGemmArgs a) {
+    using P = TcPlan<C>;
+    constexpr int kTcUnit = C::kUnit, kTcStages = C::kStages, kTcASlots = C::kASlots;
+    constexpr int kTcMaxDBufs = C::kMaxDBufs;
+    constexpr uint32_t kTmemCols = C::kTmemCols, kStageBytes = P::kStageBytes, kColD = P::kColD;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ TcSmem ss;
+    __shared__ TcSmem<C> ss;
     // stages at the first 1024-byte boundary of the dynamic block
     uint8_t *stages = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -524,7 +536,7 @@ __global__ void __launch_bounds__(256) k_tc_images(MoeBatchArgs a) {
     if (e < -100) e = -100;
     const float scale = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e)
     if (tid == 0) (MID ? a.munit : a.xunit)[pr] = __int_as_float((127 - 22 + e) << 23);
-    const int uc = a.pair_u[pr], u = uc / kTcUnit, c = uc - u * kTcUnit;
+    const int uc = a.pair_u[pr], u = uc / kTcMaxUnit, c = uc - u * kTcMaxUnit;
     const int N = tc_n_of(a.act_cnt[u]);
     uint8_t *img = (MID ? a.mim : a.xim) + (size_t)a.img_off[u] * G * 32;
     for (int g = tid; g < G; g += 256) {
@@ -571,17 +583,22 @@ __global__ void __launch_bounds__(256) k_tc_images(MoeBatchArgs a) {
     }
 }
 
-const void *moe_tc_kernel(int i) {
+const void *moe_tc_kernel(int i, bool wide) {
     switch (i) {
         case 0: return (const void *)k_tc_images<false>;
-        case 1: return (const void *)k_tc_gemm<true>;
+        case 1: return wide ? (const void *)k_tc_gemm<true, TcWide>
+                            : (const void *)k_tc_gemm<true, TcNarrow>;
         case 2: return (const void *)k_tc_images<true>;
-        case 3: return (const void *)k_tc_gemm<false>;
+        case 3: return wide ? (const void *)k_tc_gemm<false, TcWide>
+                            : (const void *)k_tc_gemm<false, TcNarrow>;
         default: return nullptr;
     }
 }
 
-size_t tc_gemm_smem() { return 1024 + (size_t)kTcStages * kStageBytes; }
+size_t tc_gemm_smem(bool wide) {
+    return wide ? 1024 + (size_t)TcWide::kStages * TcPlan<TcWide>::kStageBytes
+                : 1024 + (size_t)TcNarrow::kStages * TcPlan<TcNarrow>::kStageBytes;
+}
 
 // ----------------------------------------------------------- tensor maps --
 namespace {
