@@ -670,6 +670,11 @@ def ep_item(capi, synth, peak: float, rank: int, world: int, dist, steps: int = 
                            "dense fp32 projections of the step are not in this line"},
         "modes": res,
         "dense": dense,
+        # this library's kernels per step (NCCL's own not counted): route,
+        # bucket, two B-row images, two GEMMs, combine per layer, plus the
+        # all-to-all pack and return
+        "gpu_launches_per_step": {"single_gpu": 7 * L} if world == 1 else
+                                 {"all_to_all": 9 * L, "all_reduce": 7 * L},
         "roofline": {"bound": "hbm", "achieved_per_gpu": best["achieved_per_gpu"],
                      "peak": peak, "unit": "GB/s",
                      "frac": round(best["achieved_per_gpu"] / peak, 4),
