@@ -163,9 +163,10 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
 // elements of a word as bytes, (w >> 4) & 0x0F0F0F0F the odd ones, and dp4a
 // accumulates exact plane sums S_p = sum nib_i * B_p,i (u8 x u8 for planes 0
 // and 1, |S| <= 122400; u8 x s8 for plane 2, |S2| <= 30720). Then
-//   sum_i q_i X_i = S2 * 65536 + (S1 * 256 + S0 - 8 * sum_i X_i)
-// with the bracket exact in int32; two int->float conversions and one FFMA
-// give the group's dot product, times unit = 2^(e-22).
+//   sum_i q_i X_i = S0 + 256 S1 + 65536 S2 - 8 sum_i X_i,
+// |sum_i q_i X_i| <= 32 * 8 * 2^22 = 2^30: the sum is formed in 32-bit
+// wrap-around arithmetic (terms may leave the int32 range, the result cannot,
+// so it is exact), converted to float once and scaled by unit = 2^(e-22).
 struct XPlanes {
     uint32_t lo[3][4];  // plane p, word j: byte p of X for elements 8j, 8j+2, 8j+4, 8j+6
     uint32_t hi[3][4];  // plane p, word j: byte p of X for elements 8j+1, 8j+3, 8j+5, 8j+7
@@ -241,8 +242,9 @@ __device__ __forceinline__ float dot32(const uint4 w, const XPlanes &g) {
         s1 = dp4a_uu(hi, g.hi[1][j], s1);
         s2 = dp4a_us(hi, g.hi[2][j], s2);
     }
-    const int low = s1 * 256 + s0 + g.m8sum;
-    return fmaf((float)s2, 65536.0f, (float)low) * g.unit;
+    const uint32_t t = (uint32_t)s0 + ((uint32_t)s1 << 8) + ((uint32_t)s2 << 16) +
+                       (uint32_t)g.m8sum;
+    return (float)(int)t * g.unit;
 }
 
 // x staged in shared memory padded to 33 floats per group of 32, so lane l

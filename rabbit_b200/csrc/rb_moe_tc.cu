@@ -16,10 +16,11 @@
 //     of the MMA's B operand (k_tc_images);
 //   * one tcgen05.mma (M = 128 weight rows, N = 3 x pairs rounded up to 16,
 //     K = 32) per group and 128-row tile gives the exact plane sums
-//     S_p = sum 16 q D_p (|S_p| <= 2^19) in s32; the readout warps combine
-//     them, 16 sum q X = S0 + 256 S1 + 65536 S2, with one rounding
-//     (fmaf(S2, 65536, S1 * 256 + S0)), and accumulate scale_g * that over
-//     the groups in order in fp32; the row's result is acc * 2^(e-22) / 16.
+//     S_p = sum 16 q D_p (|S_p| <= 2^19, multiples of 16) in s32; the readout
+//     warps combine them exactly in s32, sum q X = S0 / 16 + 16 S1 + 4096 S2
+//     (|sum q X| <= 32 * 8 * 2^22 = 2^30), convert that once to fp32 and
+//     accumulate scale_g * it over the groups in order; the row's result is
+//     acc * 2^(e-22).
 //
 // Rounding: the activation's quantisation error is at most 2^(e-23) per
 // element (e from the row's largest |x|), the per-group sums are exact, and
@@ -462,9 +463,9 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
                             for (int i = 0; i < 8; ++i) v[16 + i] = v8[i];
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
-                                const int lo = v[3 * i + 1] * 256 + v[3 * i];
-                                const float f = fmaf((float)v[3 * i + 2], 65536.0f, (float)lo);
-                                acc[blk * 8 + i] = fmaf(s, f, acc[blk * 8 + i]);
+                                const int qx = (v[3 * i] >> 4) + v[3 * i + 1] * 16 +
+                                               v[3 * i + 2] * 4096;
+                                acc[blk * 8 + i] = fmaf(s, (float)qx, acc[blk * 8 + i]);
                             }
                         }
                     }
@@ -479,12 +480,12 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
                 }
             }
             if (!ok) break;
-            // the item's outputs: acc * 2^(e-22) / 16 per pair
+            // the item's outputs: acc * 2^(e-22) per pair
             const float *unit = GU ? b.xunit : b.munit;
 #pragma unroll
             for (int c = 0; c < kTcUnit; ++c) {
                 if (c >= it.n) break;
-                const float v = acc[c] * (unit[it.off + c] * 0.0625f);
+                const float v = acc[c] * unit[it.off + c];
                 if (GU) {
                     const int TRh = b.tb.TR < 16 ? b.tb.TR : 16;
                     const float up = __shfl_xor_sync(0xffffffffu, v, TRh);
