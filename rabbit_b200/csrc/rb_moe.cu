@@ -1631,10 +1631,10 @@ static int prefill_launch(rabbit_cuda_moe *p, int layer, const float *d_h_in, fl
     ga.b = a;
     ga.tmap = p->tm_gu;
     RB_CUDA(launch_tc(0, wide, dim3(pairs_max), dim3(256), 0, s, &a));
-    RB_CUDA(launch_tc(1, wide, dim3(gemm_ctas), dim3(kTcThreads), tc_gemm_smem(wide), s, &ga));
+    RB_CUDA(launch_tc(1, wide, dim3(gemm_ctas), dim3(tc_threads(wide)), tc_gemm_smem(wide), s, &ga));
     RB_CUDA(launch_tc(2, wide, dim3(pairs_max), dim3(256), 0, s, &a));
     ga.tmap = p->tm_dn;
-    RB_CUDA(launch_tc(3, wide, dim3(gemm_ctas), dim3(kTcThreads), tc_gemm_smem(wide), s, &ga));
+    RB_CUDA(launch_tc(3, wide, dim3(gemm_ctas), dim3(tc_threads(wide)), tc_gemm_smem(wide), s, &ga));
     if (a2a) {  // combine, first half: the received pairs' outputs go back to their senders
         if (V > T) RB_CUDA(launch_batch(3, dim3(V - T, (p->H + 255) / 256), dim3(256), 0, s, a));
         mark(3);

@@ -86,24 +86,26 @@ constexpr int kMaxBatchTokens = 256;
 constexpr int kTcMaxUnit = 32;       // widest work unit (pairs); pair_u = unit * kTcMaxUnit + column
 constexpr int kTcMinUnit = 16;       // narrowest (bounds the number of units)
 constexpr int kTcRows = 256;         // weight rows per work item (two M = 128 MMAs)
-constexpr int kTcThreads = 14 * 32;  // TMA, MMA, 4 unpack and 8 readout warps
 // The tensor-core GEMMs in two configurations, picked per launch by how many
 // pairs an expert can expect:
 //   wide    one CTA per SM: units of up to 32 pairs, 3 staged chunks, 8 A
 //           slots, up to 8 D buffers, 512 tensor-memory columns;
-//   narrow  two CTAs per SM (each 256 columns, 89 KB of shared memory, at
-//           most 72 registers a thread), so one CTA's hand-off latencies
+//   narrow  two CTAs per SM (each 256 columns, 89 KB of shared memory, 10
+//           warps of at most 96 registers), so one CTA's hand-off latencies
 //           overlap the other's work: units of up to 16 pairs, 2 stages, 4 A
 //           slots, up to 4 D buffers. Experts drawing more pairs than that
 //           are read once per unit.
+// Warps: TMA, MMA, 4 unpack, then kReadoutWarps readout warps (8: one item
+// row per thread; 4: two, one in each 128-row half).
 struct TcWide {
     static constexpr int kUnit = 32, kStages = 3, kASlots = 8, kMaxDBufs = 8, kTmemCols = 512,
-                         kCtasPerSm = 1;
+                         kCtasPerSm = 1, kReadoutWarps = 8, kThreads = (6 + kReadoutWarps) * 32;
 };
 struct TcNarrow {
     static constexpr int kUnit = 16, kStages = 2, kASlots = 4, kMaxDBufs = 4, kTmemCols = 256,
-                         kCtasPerSm = 2;
+                         kCtasPerSm = 2, kReadoutWarps = 4, kThreads = (6 + kReadoutWarps) * 32;
 };
+inline int tc_threads(bool wide) { return wide ? TcWide::kThreads : TcNarrow::kThreads; }
 // MMA N of a unit of n pairs: three digit rows per pair, rounded up to 16.
 __host__ __device__ inline int tc_n_of(int n) { return (3 * n + 15) / 16 * 16; }
 

@@ -29,9 +29,10 @@
 //
 // Work items are (unit, 256 weight rows): for gate/up 128 rows of W1 and the
 // same 128 rows of W3 (the pool's GU tiles interleave TRb rows of each), for
-// down 256 rows of one column chunk of W2. Two CTAs share an SM (each half
-// the SM's tensor memory, 91 KB of shared memory, at most 72 registers a
-// thread), so one CTA's hand-off latencies overlap the other's work; a CTA
+// down 256 rows of one column chunk of W2. In the narrow configuration two
+// CTAs share an SM (each half the SM's tensor memory, 91 KB of shared memory,
+// 10 warps of at most 96 registers a thread), so one CTA's hand-off latencies
+// overlap the other's work; the wide one has one CTA of 14 warps per SM. A CTA
 // takes a contiguous run of items whose summed cost (a fixed part per group plus the
 // readout's 8-pair blocks) is 1 / grid of the launch's, and runs it through a
 // warp-specialised pipeline:
@@ -45,7 +46,9 @@
 //                its D buffer full);
 //   warps 2..5   unpack: two weight rows per thread (one of each 128-row
 //                half), nibbles -> A in TMEM;
-//   warps 6..13  readout: one weight row per thread, accumulators in
+//   warps 6..    readout (C::kReadoutWarps: 8 with one weight row per
+//                thread, or 4 with two, one in each 128-row half, so the
+//                per-group wait, fences and arrival serve both), accumulators in
 //                registers; the item's outputs at its end (gate/up: mid =
 //                silu(gate) * up, the partner row in the same warp, taken
 //                by a shuffle; down: the chunk's rows of each pair).
@@ -225,7 +228,7 @@ __device__ void cta_items(const MoeBatchArgs &b, int bx, int grid, int *i0, int 
 }  // namespace
 
 template <bool GU, class C>
-__global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
+__global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     k_tc_gemm(const __grid_constant__ TcGemmArgs a) {
     using P = TcPlan<C>;
     constexpr int kTcUnit = C::kUnit, kTcStages = C::kStages, kTcASlots = C::kASlots;
@@ -250,7 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
             mbar_init(&ss.gdone[j], 1);
         }
         for (int d = 0; d < kTcMaxDBufs; ++d) {
-            mbar_init(&ss.dempty[d], 8);
+            mbar_init(&ss.dempty[d], C::kReadoutWarps);
         }
         mbar_init(&ss.mdone, 1);
         ss.abort = 0;
@@ -394,8 +397,12 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
         }
     } else {
         // ------------------------------------------------------ readout --
-        const int w = warp - kWarpReadout, t = w >> 2, q = warp & 3;
-        const int m = t * 128 + q * 32 + lane;  // the item row this thread reads out
+        // RPT item rows per thread: with 8 readout warps one (warps 6..9 the
+        // rows 0..127, warps 10..13 the rows 128..255), with 4 two, one in
+        // each 128-row half, so the per-group waits, fences and arrivals are
+        // paid once for both.
+        constexpr int RPT = 8 / C::kReadoutWarps;
+        const int w = warp - kWarpReadout, q = warp & 3;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         int g = 0;
         int d = 0;
@@ -403,69 +410,87 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
         bool ok = true;
         for (int item = i0; item < i1 && ok; ++item) {
             const Item it = item_of<GU>(a, item);
-            // this row's scales and output position
-            int tile, j, out_row, gate = 0;
-            bool valid;
-            const float *srow;
-            if (GU) {
-                const int TR = b.tb.TR;
-                int p, h;
-                const int r = gu_row(m, TR, &p, &h);
-                gate = h == 0;
-                tile = it.t0 + r / (2 * TR);
-                j = r % (2 * TR);  // row of the tile: gate rows, then up rows
-                out_row = it.t0 * TR + p;
-                valid = tile < b.tb.ntiles && out_row < b.I;
-                srow = reinterpret_cast<const float *>(
-                    b.pool + (size_t)it.rec * b.rec_stride + (size_t)tile * b.tb.tile_stride +
-                    (size_t)TR * b.H + (size_t)j * (b.H / 8));
-            } else {
-                const int TR = b.tc.TR;
-                tile = it.t0 + m / TR;
-                j = m % TR;
-                out_row = tile * TR + j;
-                valid = tile < b.tc.rtiles && out_row < b.H;
-                srow = reinterpret_cast<const float *>(
-                    b.pool + (size_t)it.rec * b.rec_stride + b.off_d +
-                    (size_t)(it.c * b.tc.rtiles + tile) * b.tc.tile_stride +
-                    (size_t)TR * (b.tc.cols / 2) + (size_t)j * (b.tc.cols / 8));
-            }
-            float acc[kTcUnit];
+            // each row's scales and output position
+            int out_row[RPT], gate[RPT];
+            bool valid[RPT];
+            const float *srow[RPT];
 #pragma unroll
-            for (int c = 0; c < kTcUnit; ++c) acc[c] = 0.f;
+            for (int r = 0; r < RPT; ++r) {
+                const int t = RPT == 1 ? w >> 2 : r;
+                const int m = t * 128 + q * 32 + lane;  // the item row
+                gate[r] = 0;
+                if (GU) {
+                    const int TR = b.tb.TR;
+                    int p, h;
+                    const int sr = gu_row(m, TR, &p, &h);
+                    gate[r] = h == 0;
+                    const int tile = it.t0 + sr / (2 * TR);
+                    const int j = sr % (2 * TR);  // row of the tile: gate rows, then up rows
+                    out_row[r] = it.t0 * TR + p;
+                    valid[r] = tile < b.tb.ntiles && out_row[r] < b.I;
+                    srow[r] = reinterpret_cast<const float *>(
+                        b.pool + (size_t)it.rec * b.rec_stride + (size_t)tile * b.tb.tile_stride +
+                        (size_t)TR * b.H + (size_t)j * (b.H / 8));
+                } else {
+                    const int TR = b.tc.TR;
+                    const int tile = it.t0 + m / TR;
+                    const int j = m % TR;
+                    out_row[r] = tile * TR + j;
+                    valid[r] = tile < b.tc.rtiles && out_row[r] < b.H;
+                    srow[r] = reinterpret_cast<const float *>(
+                        b.pool + (size_t)it.rec * b.rec_stride + b.off_d +
+                        (size_t)(it.c * b.tc.rtiles + tile) * b.tc.tile_stride +
+                        (size_t)TR * (b.tc.cols / 2) + (size_t)j * (b.tc.cols / 8));
+                }
+            }
+            float acc[RPT][kTcUnit];
+#pragma unroll
+            for (int r = 0; r < RPT; ++r)
+#pragma unroll
+                for (int c = 0; c < kTcUnit; ++c) acc[r][c] = 0.f;
             const int nblk = (it.n + 7) >> 3;
-            // the group's scale, fetched one group ahead
-            float s_next = valid ? __ldg(srow) : 0.f;
+            // the group's scales, fetched one group ahead
+            float s_next[RPT];
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) s_next[r] = valid[r] ? __ldg(srow[r]) : 0.f;
             for (int ch = 0; ch < it.nchunks && ok; ++ch) {
                 const int ng = min(8, it.G - ch * 8);
 #pragma unroll 1
                 for (int gi = 0; gi < ng; ++gi) {
-                    const float s = s_next;
-                    {
-                        const int gn = ch * 8 + gi + 1;
-                        s_next = valid && gn < it.G ? __ldg(srow + gn) : 0.f;
+                    float s[RPT];
+                    const int gn = ch * 8 + gi + 1;
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        s[r] = s_next[r];
+                        s_next[r] = valid[r] && gn < it.G ? __ldg(srow[r] + gn) : 0.f;
                     }
                     if (!(ok = tc_wait_warp(&ss.gdone[g % kTcASlots], (g / kTcASlots) & 1, a, abort)))
                         break;
                     tc_fence_after();
-                    const uint32_t dt = tmem + lane_base + kColD + (uint32_t)((2 * d + t) * NW);
 #pragma unroll
-                    for (int blk = 0; blk < kTcUnit / 8; ++blk) {
-                        if (blk < nblk) {
-                            int v16[16], v8[8];
-                            tmem_ld16(dt, v16, blk * 24);
-                            tmem_ld8(dt, v8, blk * 24 + 16);
-                            tmem_wait_ld();
-                            int v[24];
+                    for (int r = 0; r < RPT; ++r) {
+                        const int t = RPT == 1 ? w >> 2 : r;
+                        const uint32_t dt =
+                            tmem + lane_base + kColD + (uint32_t)((2 * d + t) * NW);
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) v[i] = v16[i];
+                        for (int blk = 0; blk < kTcUnit / 8; ++blk) {
+                            if (blk < nblk) {
+                                int v16[16], v8[8];
+                                tmem_ld16(dt, v16, blk * 24);
+                                tmem_ld8(dt, v8, blk * 24 + 16);
+                                tmem_wait_ld();
+                                int v[24];
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) v[16 + i] = v8[i];
+                                for (int i = 0; i < 16; ++i) v[i] = v16[i];
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const int qx = (v[3 * i] >> 4) + v[3 * i + 1] * 16 +
-                                               v[3 * i + 2] * 4096;
-                                acc[blk * 8 + i] = fmaf(s, (float)qx, acc[blk * 8 + i]);
+                                for (int i = 0; i < 8; ++i) v[16 + i] = v8[i];
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const int qx = (v[3 * i] >> 4) + v[3 * i + 1] * 16 +
+                                                   v[3 * i + 2] * 4096;
+                                    acc[r][blk * 8 + i] =
+                                        fmaf(s[r], (float)qx, acc[r][blk * 8 + i]);
+                                }
                             }
                         }
                     }
@@ -483,16 +508,19 @@ __global__ void __launch_bounds__(kTcThreads, C::kCtasPerSm)
             // the item's outputs: acc * 2^(e-22) per pair
             const float *unit = GU ? b.xunit : b.munit;
 #pragma unroll
-            for (int c = 0; c < kTcUnit; ++c) {
-                if (c >= it.n) break;
-                const float v = acc[c] * unit[it.off + c];
-                if (GU) {
-                    const int TRh = b.tb.TR < 16 ? b.tb.TR : 16;
-                    const float up = __shfl_xor_sync(0xffffffffu, v, TRh);
-                    if (valid && gate)
-                        b.mid[(size_t)(it.off + c) * b.I + out_row] = silu_mul(v, up);
-                } else if (valid) {
-                    b.down[((size_t)(it.off + c) * b.tc.KC + it.c) * b.H + out_row] = v;
+            for (int r = 0; r < RPT; ++r) {
+#pragma unroll
+                for (int c = 0; c < kTcUnit; ++c) {
+                    if (c >= it.n) break;
+                    const float v = acc[r][c] * unit[it.off + c];
+                    if (GU) {
+                        const int TRh = b.tb.TR < 16 ? b.tb.TR : 16;
+                        const float up = __shfl_xor_sync(0xffffffffu, v, TRh);
+                        if (valid[r] && gate[r])
+                            b.mid[(size_t)(it.off + c) * b.I + out_row[r]] = silu_mul(v, up);
+                    } else if (valid[r]) {
+                        b.down[((size_t)(it.off + c) * b.tc.KC + it.c) * b.H + out_row[r]] = v;
+                    }
                 }
             }
         }
