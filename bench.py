@@ -186,6 +186,7 @@ def cpu_baseline_single(layer) -> dict:
 
 # ------------------------------------------------------------ GEMV ---------
 GEMV_ROWS = GEMV_COLS = 4096  # the single int4 grouped GEMV (quant.c:152-188)
+HOST_AHEAD_CYCLES = 20_000_000  # ~10 ms of device sleep before a timed launch chain
 
 
 def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 200) -> dict:
@@ -204,6 +205,13 @@ def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 2
         m.gemv_dev(x.data_ptr(), y.data_ptr(), s)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # One dependent GEMV lasts about as long as the host's own cost of one
+    # call through ctypes, so a slow or busy host would set the pace. A
+    # device-side sleep queued first lets the host enqueue every launch
+    # before the first timed one starts: the events then time the device
+    # chain alone (ev0 is recorded after the sleep).
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(HOST_AHEAD_CYCLES)
     ev0.record(stream)
     for i in range(iters):
         mats[i % copies].gemv_dev(x.data_ptr(), y.data_ptr(), s)
@@ -220,6 +228,8 @@ def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 2
         capi.gemv_batch_dev(mats, xp, yp, s)
     torch.cuda.synchronize()
     biters = max(1, iters // copies)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(HOST_AHEAD_CYCLES)
     ev0.record(stream)
     for _ in range(biters):
         capi.gemv_batch_dev(mats, xp, yp, s)
@@ -233,7 +243,8 @@ def gemv_item(capi, synth, stream, peak: float, copies: int = 16, iters: int = 2
             "unit": "GB/s", "us_per_gemv": round(sec * 1e6, 3), "bytes_per_gemv": nbytes,
             "frac_of_hbm_peak": round(gbs / peak, 4), "launches": iters,
             "l2": f"{copies} distinct matrices in rotation ({copies * nbytes / 1e6:.0f} MB)",
-            "kernel": "k_gemv_g32", "mode": "one GEMV per launch, each after the previous",
+            "kernel": "k_gemv_g32", "mode": "one GEMV per launch, each after the previous "
+                                            "(all launches enqueued before the first runs)",
             "batched": {"value": round(bgbs, 1), "unit": "GB/s",
                         "us_per_gemv": round(bsec * 1e6, 3),
                         "frac_of_hbm_peak": round(bgbs / peak, 4),
